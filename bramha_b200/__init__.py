@@ -1,0 +1,13 @@
+"""B200-native (sm_100a) dequantize-fused linear-layer path for Bramha.
+
+The product is the C ABI in ``include/bramha_cuda.h`` (``libbramha_cuda.so``,
+built by ``python -m bramha_b200.build``); this package is its Python host
+side, mirroring the reference's compute-plane interface.
+"""
+from ._lib import FMT, BramhaError, header_symbols, last_error, lib
+from .plane import CudaComputePlane, Weight, get_cuda_plane, packed_nbytes
+
+__all__ = [
+    "FMT", "BramhaError", "CudaComputePlane", "Weight", "get_cuda_plane", "header_symbols", "last_error", "lib",
+    "packed_nbytes",
+]

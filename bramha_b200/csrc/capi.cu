@@ -1,0 +1,561 @@
+// capi.cu -- the extern "C" boundary declared in include/bramha_cuda.h.
+//
+// Host-side equivalent of the reference's `WgpuComputePlane`
+// (src/compute/wgpu_backend.rs:100-1728): a per-device context with a
+// persistent weight registry keyed by "model:layer" (get_or_create_op,
+// :603-722), least-recently-used eviction under a device-memory cap
+// (ModelBuffers, :25-82), and synchronous host-buffer GEMV calls with the
+// reference's error behaviour (size mismatch -> error string, :1096-1104;
+// N == 0 or K == 0 -> zeros, :1092-1095).  Every entry point returns a status
+// and records a message for bramha_cuda_last_error(); nothing throws across
+// the boundary.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <list>
+#include <mutex>
+#include <new>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "common.cuh"
+
+using namespace bramha;
+
+struct bramha_weight {
+    std::string key;
+    int fmt = 0;
+    int64_t N = 0, K = 0;
+    int64_t row_bytes = 0, ldq = 0;
+    uint8_t* q = nullptr;
+    float* scales = nullptr;
+    size_t bytes = 0;
+    bool live = true;
+    bool keyed = false;
+    bramha_ctx* ctx = nullptr;
+    std::list<std::string>::iterator lru_it;
+};
+
+struct bramha_ctx {
+    int device = 0;
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;
+    std::mutex mu;  // registry + LRU
+    std::unordered_map<std::string, bramha_weight*> reg;
+    std::list<std::string> lru;          // front = least recently used
+    std::vector<bramha_weight*> dead;    // evicted handles: stale pointers fail cleanly
+    size_t cap = 0, used = 0;
+    std::mutex io_mu;                    // device staging for host-buffer calls
+    float* dev_x = nullptr;
+    float* dev_y = nullptr;
+    size_t dev_x_cap = 0, dev_y_cap = 0;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    cudaGetLastError();  // clear a sticky launch error so the next call can proceed
+    return fail(e == cudaErrorMemoryAllocation ? BRAMHA_ERR_OOM : BRAMHA_ERR_CUDA, "CUDA error in %s: %s", what,
+                cudaGetErrorString(e));
+}
+
+#define CK(call, what)                                   \
+    do {                                                 \
+        cudaError_t e_ = (call);                         \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+const char* fmt_name(int fmt) {
+    switch (fmt) {
+        case BRAMHA_FMT_F32: return "F32";
+        case BRAMHA_FMT_W8: return "INT8";
+        case BRAMHA_FMT_W4ZP8: return "INT4";
+        case BRAMHA_FMT_LOG4: return "LOG4";
+        default: return "?";
+    }
+}
+
+bool valid_fmt(int fmt) { return fmt >= BRAMHA_FMT_F32 && fmt <= BRAMHA_FMT_LOG4; }
+
+// Expected packed length, with the reference's wording for mismatches.
+int check_sizes(int fmt, int64_t N, int64_t K, size_t q_bytes, size_t n_scales, bool scales_given) {
+    if (!valid_fmt(fmt)) return fail(BRAMHA_ERR_INVALID, "unknown weight format %d", fmt);
+    if (N < 0 || K < 0) return fail(BRAMHA_ERR_INVALID, "negative shape %lld x %lld", (long long)N, (long long)K);
+    const int64_t rb = row_bytes_of(fmt, K);
+    const int64_t unit = fmt == BRAMHA_FMT_F32 ? 4 : 1;
+    const uint64_t expect = (uint64_t)N * (uint64_t)rb;
+    if ((uint64_t)q_bytes != expect) {
+        if (fmt == BRAMHA_FMT_W4ZP8 || fmt == BRAMHA_FMT_LOG4)
+            return fail(BRAMHA_ERR_SIZE,
+                        "Quantized %s weight size mismatch: weight length is %zu, expected %lld x (%lld / 2) = %llu",
+                        fmt_name(fmt), q_bytes, (long long)N, (long long)K, (unsigned long long)expect);
+        if (fmt == BRAMHA_FMT_W8)
+            return fail(BRAMHA_ERR_SIZE,
+                        "Quantized INT8 weight size mismatch: weight length is %zu, expected %lld x %lld = %llu",
+                        q_bytes, (long long)N, (long long)K, (unsigned long long)expect);
+        return fail(BRAMHA_ERR_SIZE, "Weight size mismatch: weight length is %zu, expected %lld x %lld = %llu",
+                    q_bytes / unit, (long long)N, (long long)K, (unsigned long long)(expect / unit));
+    }
+    if (fmt != BRAMHA_FMT_F32) {
+        if (!scales_given && N > 0) return fail(BRAMHA_ERR_INVALID, "scales pointer is NULL");
+        if ((int64_t)n_scales != N)
+            return fail(BRAMHA_ERR_SIZE, "Scale length mismatch: scales length is %zu, expected %lld", n_scales,
+                        (long long)N);
+    }
+    return BRAMHA_OK;
+}
+
+void free_weight_memory(bramha_weight* w) {
+    if (w->q) cudaFree(w->q);
+    if (w->scales) cudaFree(w->scales);
+    w->q = nullptr;
+    w->scales = nullptr;
+    w->live = false;
+}
+
+// Caller holds ctx->mu.
+void evict_locked(bramha_ctx* ctx, const std::string& key) {
+    auto it = ctx->reg.find(key);
+    if (it == ctx->reg.end()) return;
+    bramha_weight* w = it->second;
+    cudaStreamSynchronize(ctx->stream);  // no launch may still read it
+    ctx->used -= w->bytes;
+    ctx->lru.erase(w->lru_it);
+    ctx->reg.erase(it);
+    free_weight_memory(w);
+    ctx->dead.push_back(w);
+}
+
+void touch_locked(bramha_ctx* ctx, bramha_weight* w) { ctx->lru.splice(ctx->lru.end(), ctx->lru, w->lru_it); }
+
+// Allocates and uploads (H2D when host, D2D otherwise) into the padded layout.
+int upload(bramha_ctx* ctx, bramha_weight* w, const void* q, const float* scales, bool from_device,
+           cudaStream_t st) {
+    w->row_bytes = row_bytes_of(w->fmt, w->K);
+    w->ldq = pitch_of(w->row_bytes);
+    const size_t qbytes = (size_t)w->N * (size_t)w->ldq;
+    const size_t sbytes = w->fmt == BRAMHA_FMT_F32 ? 0 : (size_t)w->N * sizeof(float);
+    w->bytes = qbytes + sbytes;
+    if (qbytes > 0) CK(cudaMalloc(&w->q, qbytes), "cudaMalloc(weight)");
+    if (sbytes > 0) {
+        cudaError_t e = cudaMalloc(&w->scales, sbytes);
+        if (e != cudaSuccess) {
+            free_weight_memory(w);
+            return cuda_fail(e, "cudaMalloc(scales)");
+        }
+    }
+    const cudaMemcpyKind kind = from_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    cudaError_t e = cudaSuccess;
+    if (qbytes > 0) {
+        if (w->ldq != w->row_bytes) e = cudaMemsetAsync(w->q, 0, qbytes, st);
+        if (e == cudaSuccess && w->row_bytes > 0)
+            e = cudaMemcpy2DAsync(w->q, (size_t)w->ldq, q, (size_t)w->row_bytes, (size_t)w->row_bytes,
+                                  (size_t)w->N, kind, st);
+    }
+    if (e == cudaSuccess && sbytes > 0) e = cudaMemcpyAsync(w->scales, scales, sbytes, kind, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        free_weight_memory(w);
+        return cuda_fail(e, "weight upload");
+    }
+    return BRAMHA_OK;
+}
+
+int register_impl(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K, const void* q,
+                  size_t q_bytes, const float* scales, size_t n_scales, bool from_device, cudaStream_t st,
+                  bramha_weight** out) {
+    if (!ctx || !out) return fail(BRAMHA_ERR_INVALID, "null context or output pointer");
+    if (!key) return fail(BRAMHA_ERR_INVALID, "null weight key");
+    int rc = check_sizes(fmt, N, K, q_bytes, n_scales, scales != nullptr);
+    if (rc) return rc;
+    if (!q && q_bytes > 0) return fail(BRAMHA_ERR_INVALID, "weight pointer is NULL");
+    DeviceGuard g(ctx->device);
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    auto it = ctx->reg.find(key);
+    if (it != ctx->reg.end()) {
+        bramha_weight* w = it->second;
+        if (w->fmt != fmt || w->N != N || w->K != K)
+            return fail(BRAMHA_ERR_SIZE, "key '%s' is registered with a different shape or format", key);
+        touch_locked(ctx, w);
+        *out = w;
+        return BRAMHA_OK;
+    }
+    const size_t need = (size_t)N * (size_t)pitch_of(row_bytes_of(fmt, K)) +
+                        (fmt == BRAMHA_FMT_F32 ? 0 : (size_t)N * sizeof(float));
+    // enforce_limits (wgpu_backend.rs:65-81): evict least recently used first.
+    while (ctx->cap > 0 && ctx->used + need > ctx->cap && !ctx->lru.empty()) evict_locked(ctx, ctx->lru.front());
+    bramha_weight* w = new (std::nothrow) bramha_weight();
+    if (!w) return fail(BRAMHA_ERR_OOM, "host allocation failed");
+    w->key = key;
+    w->fmt = fmt;
+    w->N = N;
+    w->K = K;
+    w->keyed = true;
+    w->ctx = ctx;
+    rc = upload(ctx, w, q, scales, from_device, st ? st : ctx->stream);
+    if (rc) {
+        delete w;
+        return rc;
+    }
+    ctx->used += w->bytes;
+    ctx->lru.push_back(w->key);
+    w->lru_it = std::prev(ctx->lru.end());
+    ctx->reg.emplace(w->key, w);
+    *out = w;
+    return BRAMHA_OK;
+}
+
+int check_weight(const bramha_ctx* ctx, const bramha_weight* w) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (!w) return fail(BRAMHA_ERR_INVALID, "null weight");
+    if (w->ctx != ctx) return fail(BRAMHA_ERR_INVALID, "weight belongs to another context");
+    if (!w->live) return fail(BRAMHA_ERR_NOT_FOUND, "weight '%s' was evicted", w->key.c_str());
+    return BRAMHA_OK;
+}
+
+// Core device GEMV over several weights sharing x.  x must be 16-byte aligned
+// with row pitch ldx (a multiple of 4 floats when batch > 1).
+int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const float* x, int64_t ldx,
+                int64_t batch, float* const* ys, cudaStream_t st) {
+    const int fmt = ws[0]->fmt;
+    const int64_t K = ws[0]->K;
+    if (batch <= 0) return BRAMHA_OK;
+    if (K == 0) {
+        for (int i = 0; i < n; ++i)
+            if (ws[i]->N > 0) CK(cudaMemsetAsync(ys[i], 0, sizeof(float) * ws[i]->N * batch, st), "memset(y)");
+        return BRAMHA_OK;
+    }
+    if (K > 0x7fffffffLL) return fail(BRAMHA_ERR_UNSUPPORTED, "K too large");
+    for (int64_t b0 = 0; b0 < batch; b0 += kMaxGemvBatch) {
+        const int bc = (int)((batch - b0) < kMaxGemvBatch ? (batch - b0) : kMaxGemvBatch);
+        GemvArgs a{};
+        a.x = x + b0 * ldx;
+        a.ldx = ldx;
+        // Columns the packed rows actually hold: with odd K a nibble row has
+        // K/2 bytes and the last activation is ignored (cpu_engine.rs:1364).
+        a.K = (int)((fmt == BRAMHA_FMT_W4ZP8 || fmt == BRAMHA_FMT_LOG4) ? (K / 2) * 2 : K);
+        a.batch = bc;
+        a.nseg = 0;
+        a.ldq_min = 0x7fffffff;
+        for (int i = 0; i < n; ++i) {
+            if (ws[i]->N == 0) continue;
+            if (ws[i]->N > 0x7fffffffLL) return fail(BRAMHA_ERR_UNSUPPORTED, "N too large");
+            GemvSeg& s = a.seg[a.nseg++];
+            s.q = ws[i]->q;
+            s.scales = ws[i]->scales;
+            s.ldq = ws[i]->ldq;
+            s.ldy = ws[i]->N;
+            s.y = ys[i] + b0 * ws[i]->N;
+            s.N = (int)ws[i]->N;
+            if (ws[i]->ldq < a.ldq_min) a.ldq_min = (int)ws[i]->ldq;
+        }
+        if (a.nseg == 0) return BRAMHA_OK;
+        CK(launch_gemv(fmt, a, ctx->num_sms, st), "gemv launch");
+    }
+    return BRAMHA_OK;
+}
+
+int ensure_staging(bramha_ctx* ctx, size_t x_elems, size_t y_elems) {
+    if (x_elems > ctx->dev_x_cap) {
+        if (ctx->dev_x) cudaFree(ctx->dev_x);
+        ctx->dev_x = nullptr;
+        ctx->dev_x_cap = 0;
+        CK(cudaMalloc(&ctx->dev_x, x_elems * sizeof(float)), "cudaMalloc(x staging)");
+        ctx->dev_x_cap = x_elems;
+    }
+    if (y_elems > ctx->dev_y_cap) {
+        if (ctx->dev_y) cudaFree(ctx->dev_y);
+        ctx->dev_y = nullptr;
+        ctx->dev_y_cap = 0;
+        CK(cudaMalloc(&ctx->dev_y, y_elems * sizeof(float)), "cudaMalloc(y staging)");
+        ctx->dev_y_cap = y_elems;
+    }
+    return BRAMHA_OK;
+}
+
+// Host-buffer GEMV/GEMM: H2D x, launch, D2H y, wait.
+int gemv_host(bramha_ctx* ctx, const bramha_weight* w, const float* x_host, int64_t batch, float* y_host) {
+    if (batch < 0) return fail(BRAMHA_ERR_INVALID, "negative batch");
+    if (batch > 0 && ((!x_host && w->K > 0) || (!y_host && w->N > 0)))
+        return fail(BRAMHA_ERR_INVALID, "null host buffer");
+    if (batch == 0 || w->N == 0) return BRAMHA_OK;
+    if (w->K == 0) {
+        memset(y_host, 0, sizeof(float) * (size_t)(w->N * batch));
+        return BRAMHA_OK;
+    }
+    DeviceGuard g(ctx->device);
+    std::lock_guard<std::mutex> lk(ctx->io_mu);
+    const int64_t ldx = (w->K + 3) / 4 * 4;
+    int rc = ensure_staging(ctx, (size_t)(ldx * batch), (size_t)(w->N * batch));
+    if (rc) return rc;
+    cudaStream_t st = ctx->stream;
+    CK(cudaMemcpy2DAsync(ctx->dev_x, ldx * sizeof(float), x_host, w->K * sizeof(float), w->K * sizeof(float),
+                         (size_t)batch, cudaMemcpyHostToDevice, st),
+       "H2D x");
+    const bramha_weight* ws[1] = {w};
+    float* ys[1] = {ctx->dev_y};
+    rc = gemv_device(ctx, 1, ws, ctx->dev_x, ldx, batch, ys, st);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(y_host, ctx->dev_y, sizeof(float) * (size_t)(w->N * batch), cudaMemcpyDeviceToHost, st),
+       "D2H y");
+    CK(cudaStreamSynchronize(st), "stream sync");
+    return BRAMHA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* bramha_cuda_last_error(void) { return g_last_error.c_str(); }
+
+int bramha_cuda_abi_version(void) { return BRAMHA_CUDA_ABI_VERSION; }
+
+int bramha_cuda_init(int device, bramha_ctx** out) {
+    if (!out) return fail(BRAMHA_ERR_INVALID, "null output pointer");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(BRAMHA_ERR_CUDA, "no CUDA device available (%s)", cudaGetErrorString(e));
+    }
+    if (device < 0 || device >= n) return fail(BRAMHA_ERR_INVALID, "device %d out of range (%d devices)", device, n);
+    cudaDeviceProp p;
+    CK(cudaGetDeviceProperties(&p, device), "cudaGetDeviceProperties");
+    if (p.major != 10)
+        return fail(BRAMHA_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only", device,
+                    p.major, p.minor);
+    bramha_ctx* ctx = new (std::nothrow) bramha_ctx();
+    if (!ctx) return fail(BRAMHA_ERR_OOM, "host allocation failed");
+    ctx->device = device;
+    ctx->num_sms = p.multiProcessorCount;
+    DeviceGuard g(device);
+    e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete ctx;
+        return cuda_fail(e, "cudaStreamCreate");
+    }
+    *out = ctx;
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_destroy(bramha_ctx* ctx) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    DeviceGuard g(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        for (auto& kv : ctx->reg) {
+            free_weight_memory(kv.second);
+            delete kv.second;
+        }
+        for (bramha_weight* w : ctx->dead) delete w;
+        ctx->reg.clear();
+        ctx->dead.clear();
+    }
+    if (ctx->dev_x) cudaFree(ctx->dev_x);
+    if (ctx->dev_y) cudaFree(ctx->dev_y);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_set_memory_cap(bramha_ctx* ctx, size_t bytes) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    DeviceGuard g(ctx->device);
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    ctx->cap = bytes;
+    while (ctx->cap > 0 && ctx->used > ctx->cap && !ctx->lru.empty()) evict_locked(ctx, ctx->lru.front());
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_memory_used(bramha_ctx* ctx, size_t* bytes) {
+    if (!ctx || !bytes) return fail(BRAMHA_ERR_INVALID, "null argument");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    *bytes = ctx->used;
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_register_weight(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K, const void* q,
+                                size_t q_bytes, const float* scales, size_t n_scales, bramha_weight** out) {
+    return register_impl(ctx, key, fmt, N, K, q, q_bytes, scales, n_scales, false, nullptr, out);
+}
+
+int bramha_cuda_register_weight_dev(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K,
+                                    const void* q_dev, size_t q_bytes, const float* scales_dev, size_t n_scales,
+                                    void* stream, bramha_weight** out) {
+    return register_impl(ctx, key, fmt, N, K, q_dev, q_bytes, scales_dev, n_scales, true,
+                         static_cast<cudaStream_t>(stream), out);
+}
+
+int bramha_cuda_lookup_weight(bramha_ctx* ctx, const char* key, bramha_weight** out) {
+    if (!ctx || !key || !out) return fail(BRAMHA_ERR_INVALID, "null argument");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    auto it = ctx->reg.find(key);
+    if (it == ctx->reg.end()) return fail(BRAMHA_ERR_NOT_FOUND, "no weight registered under '%s'", key);
+    touch_locked(ctx, it->second);
+    *out = it->second;
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_evict_weight(bramha_ctx* ctx, const char* key) {
+    if (!ctx || !key) return fail(BRAMHA_ERR_INVALID, "null argument");
+    DeviceGuard g(ctx->device);
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (ctx->reg.find(key) == ctx->reg.end()) return fail(BRAMHA_ERR_NOT_FOUND, "no weight registered under '%s'", key);
+    evict_locked(ctx, key);
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_clear(bramha_ctx* ctx) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    DeviceGuard g(ctx->device);
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    while (!ctx->lru.empty()) evict_locked(ctx, ctx->lru.front());
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_weight_info(const bramha_weight* w, int* fmt, int64_t* N, int64_t* K, size_t* device_bytes) {
+    if (!w) return fail(BRAMHA_ERR_INVALID, "null weight");
+    if (!w->live) return fail(BRAMHA_ERR_NOT_FOUND, "weight '%s' was evicted", w->key.c_str());
+    if (fmt) *fmt = w->fmt;
+    if (N) *N = w->N;
+    if (K) *K = w->K;
+    if (device_bytes) *device_bytes = w->bytes;
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_gemv(bramha_ctx* ctx, const bramha_weight* w, const float* x_host, int64_t batch, float* y_host) {
+    int rc = check_weight(ctx, w);
+    if (rc) return rc;
+    return gemv_host(ctx, w, x_host, batch, y_host);
+}
+
+int bramha_cuda_gemv_dev(bramha_ctx* ctx, const bramha_weight* w, const float* x_dev, int64_t batch, float* y_dev,
+                         void* stream) {
+    const bramha_weight* ws[1] = {w};
+    float* ys[1] = {y_dev};
+    return bramha_cuda_gemv_multi_dev(ctx, 1, ws, x_dev, batch, ys, stream);
+}
+
+int bramha_cuda_gemv_multi_dev(bramha_ctx* ctx, int n_weights, const bramha_weight* const* ws, const float* x_dev,
+                               int64_t batch, float* const* y_devs, void* stream) {
+    if (!ctx || !ws || !y_devs) return fail(BRAMHA_ERR_INVALID, "null argument");
+    if (n_weights < 1 || n_weights > kMaxSegments)
+        return fail(BRAMHA_ERR_INVALID, "n_weights must be in 1..%d", kMaxSegments);
+    if (batch < 0) return fail(BRAMHA_ERR_INVALID, "negative batch");
+    for (int i = 0; i < n_weights; ++i) {
+        int rc = check_weight(ctx, ws[i]);
+        if (rc) return rc;
+        if (ws[i]->fmt != ws[0]->fmt || ws[i]->K != ws[0]->K)
+            return fail(BRAMHA_ERR_SIZE, "fused weights must share format and K");
+        if (!y_devs[i] && ws[i]->N > 0 && batch > 0) return fail(BRAMHA_ERR_INVALID, "null output pointer");
+    }
+    const int64_t K = ws[0]->K;
+    if (batch > 0 && K > 0) {
+        if (!x_dev) return fail(BRAMHA_ERR_INVALID, "null input pointer");
+        if ((reinterpret_cast<uintptr_t>(x_dev) & 15) != 0 || (batch > 1 && (K & 3) != 0))
+            return fail(BRAMHA_ERR_INVALID,
+                        "x_dev must be 16-byte aligned (and K a multiple of 4 when batch > 1); "
+                        "use bramha_cuda_gemv for unaligned input");
+    }
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    return gemv_device(ctx, n_weights, ws, x_dev, K, batch, y_devs, st);
+}
+
+int bramha_cuda_matvec(bramha_ctx* ctx, int fmt, const float* h, int64_t K, const void* q_weight, size_t q_bytes,
+                       const float* scales, size_t n_scales, int64_t N, const char* model_name,
+                       const char* layer_name, float* out) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (!valid_fmt(fmt)) return fail(BRAMHA_ERR_INVALID, "unknown weight format %d", fmt);
+    if (N < 0 || K < 0) return fail(BRAMHA_ERR_INVALID, "negative shape");
+    if (N > 0 && !out) return fail(BRAMHA_ERR_INVALID, "null output pointer");
+    // wgpu_backend.rs:1092-1095: an empty input or output gives zeros.
+    if (K == 0 || N == 0) {
+        if (N > 0) memset(out, 0, sizeof(float) * (size_t)N);
+        return BRAMHA_OK;
+    }
+    int rc = check_sizes(fmt, N, K, q_bytes, n_scales, scales != nullptr);
+    if (rc) return rc;
+    if (model_name && layer_name) {
+        std::string key = std::string(model_name) + ":" + layer_name;
+        bramha_weight* w = nullptr;
+        rc = register_impl(ctx, key.c_str(), fmt, N, K, q_weight, q_bytes, scales, n_scales, false, nullptr, &w);
+        if (rc) return rc;
+        return gemv_host(ctx, w, h, 1, out);
+    }
+    // Temporary buffers for this call only (wgpu_backend.rs:1118-1171).
+    DeviceGuard g(ctx->device);
+    bramha_weight tmp;
+    tmp.fmt = fmt;
+    tmp.N = N;
+    tmp.K = K;
+    tmp.ctx = ctx;
+    tmp.key = "<temporary>";
+    rc = upload(ctx, &tmp, q_weight, scales, false, ctx->stream);
+    if (rc) return rc;
+    rc = gemv_host(ctx, &tmp, h, 1, out);
+    free_weight_memory(&tmp);
+    return rc;
+}
+
+int bramha_cuda_gemm(bramha_ctx* ctx, const bramha_weight* w, const float* h_host, int64_t M, float* out_host) {
+    int rc = check_weight(ctx, w);
+    if (rc) return rc;
+    return gemv_host(ctx, w, h_host, M, out_host);
+}
+
+int bramha_cuda_gemm_dev(bramha_ctx* ctx, const bramha_weight* w, const void* x_dev, int x_dtype, int64_t M,
+                         float* y_dev, void* stream) {
+    int rc = check_weight(ctx, w);
+    if (rc) return rc;
+    if (x_dtype != BRAMHA_DTYPE_F32)
+        return fail(BRAMHA_ERR_UNSUPPORTED, "gemm_dev: activation dtype %d not supported by this build", x_dtype);
+    return bramha_cuda_gemv_dev(ctx, w, static_cast<const float*>(x_dev), M, y_dev, stream);
+}
+
+int bramha_cuda_quantize_dev(bramha_ctx* ctx, int fmt, int64_t N, int64_t K, const float* w_dev, void* q_dev,
+                             float* scales_dev, void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (fmt != BRAMHA_FMT_W8 && fmt != BRAMHA_FMT_W4ZP8 && fmt != BRAMHA_FMT_LOG4)
+        return fail(BRAMHA_ERR_INVALID, "quantize: format %d is not a quantized format", fmt);
+    if (N < 0 || K < 0) return fail(BRAMHA_ERR_INVALID, "negative shape");
+    if ((fmt == BRAMHA_FMT_W4ZP8 || fmt == BRAMHA_FMT_LOG4) && (K % 2) != 0)
+        return fail(BRAMHA_ERR_INVALID, "in_features must be a multiple of 2 for %s packing", fmt_name(fmt));
+    if (N == 0 || K == 0) return BRAMHA_OK;
+    if (!w_dev || !q_dev || !scales_dev) return fail(BRAMHA_ERR_INVALID, "null device pointer");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    CK(launch_quantize(fmt, N, K, w_dev, static_cast<uint8_t*>(q_dev), scales_dev, st), "quantize launch");
+    return BRAMHA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,8 @@
+// gemv_log4.cu -- instantiates the decode GEMV (gemv_impl.cuh) for BRAMHA_FMT_LOG4.
+#include "gemv_impl.cuh"
+
+namespace bramha {
+cudaError_t launch_gemv_log4(const GemvArgs& a, int num_sms, cudaStream_t stream) {
+    return dispatch_batch<BRAMHA_FMT_LOG4>(a, num_sms, stream);
+}
+}  // namespace bramha

@@ -1,0 +1,227 @@
+"""`CudaComputePlane`: the reference's GPU compute-plane interface on the C ABI.
+
+Mirrors `WgpuComputePlane` (src/compute/wgpu_backend.rs:100-1728) method by
+method, same argument meaning and error behaviour:
+
+* ``matvec_mul(h, weight, out_features, model_name=None, layer_name=None)``  (:734)
+* ``matvec_mul_int8(h, q_weight, scales, out_features, model_name, layer_name)``  (:906)
+* ``matvec_mul_int4(h, q_weight, scales, out_features, model_name, layer_name)``  (:1083)
+* ``matvec_mul_log4(...)``: the same for SPANDA 4-bit log codes
+  (decoder spanda-engine/src/lib.rs:332-342; no GPU arm exists in the reference)
+* ``gemm(fmt, h_block, q, scales, block_size, in_features, out_features)``:
+  the prefill GEMM that `gemm_cpu` (src/inference/cpu_engine.rs:565) computes
+* ``clear_persistent_buffers()`` (:725)
+
+Where the reference returns ``Err(String)`` this raises :class:`BramhaError`;
+``Ok(vec![0; N])`` for an empty input or output becomes a zero array.  When both
+``model_name`` and ``layer_name`` are given, the weight is cached on the device
+under ``"model:layer"`` (get_or_create_op, :603-722) and later calls skip the
+upload.  ``get_cuda_plane()`` mirrors ``get_wgpu_plane()`` (:1710-1728): it
+returns ``None`` when ``BRAMHA_CPU`` is set or the device cannot be opened.
+
+The device-pointer methods (``register_dev``, ``gemv_dev``, ``quantize_dev``)
+take torch CUDA tensors; torch only supplies memory and streams.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional, Sequence
+
+import numpy as np
+
+from ._lib import DTYPE, FMT, BramhaError, check, lib
+
+_vp = ctypes.c_void_p
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+class Weight:
+    """A weight registered on the device (an opaque `bramha_weight*`)."""
+
+    def __init__(self, plane: "CudaComputePlane", handle: int, key: str, fmt: str, n: int, k: int):
+        self.plane, self.handle, self.key, self.fmt, self.N, self.K = plane, handle, key, fmt, n, k
+
+    @property
+    def device_bytes(self) -> int:
+        nb = ctypes.c_size_t()
+        check(lib().bramha_cuda_weight_info(self.handle, None, None, None, ctypes.byref(nb)))
+        return nb.value
+
+    def __repr__(self):
+        return f"Weight({self.key!r}, {self.fmt}, N={self.N}, K={self.K})"
+
+
+class CudaComputePlane:
+    def __init__(self, device: int = 0):
+        ctx = _vp()
+        check(lib().bramha_cuda_init(device, ctypes.byref(ctx)))
+        self._ctx = ctx
+        self.device = device
+
+    # ------------------------------------------------------------------ life
+    def close(self):
+        if getattr(self, "_ctx", None):
+            lib().bramha_cuda_destroy(self._ctx)
+            self._ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def ctx(self):
+        return self._ctx
+
+    def set_memory_cap(self, nbytes: int):
+        check(lib().bramha_cuda_set_memory_cap(self._ctx, nbytes))
+
+    def memory_used(self) -> int:
+        v = ctypes.c_size_t()
+        check(lib().bramha_cuda_memory_used(self._ctx, ctypes.byref(v)))
+        return v.value
+
+    def clear_persistent_buffers(self):
+        check(lib().bramha_cuda_clear(self._ctx))
+
+    # ------------------------------------------------------------ registry
+    def register(self, key: str, fmt: str, out_features: int, in_features: int, q, scales=None) -> Weight:
+        """Upload packed host weights (numpy) under `key` (idempotent)."""
+        qa = np.ascontiguousarray(q)
+        sa = None if scales is None else _f32(scales)
+        h = _vp()
+        check(lib().bramha_cuda_register_weight(
+            self._ctx, key.encode(), FMT[fmt], out_features, in_features, qa.ctypes.data, qa.nbytes,
+            None if sa is None else sa.ctypes.data, 0 if sa is None else sa.size, ctypes.byref(h)))
+        return Weight(self, h.value, key, fmt, out_features, in_features)
+
+    def register_dev(self, key: str, fmt: str, out_features: int, in_features: int, q, scales=None,
+                     stream=None) -> Weight:
+        """Register from torch CUDA tensors (device-to-device copy)."""
+        h = _vp()
+        check(lib().bramha_cuda_register_weight_dev(
+            self._ctx, key.encode(), FMT[fmt], out_features, in_features, q.data_ptr(),
+            q.numel() * q.element_size(), None if scales is None else scales.data_ptr(),
+            0 if scales is None else scales.numel(), _stream(stream), ctypes.byref(h)))
+        return Weight(self, h.value, key, fmt, out_features, in_features)
+
+    def lookup(self, key: str) -> Weight:
+        h = _vp()
+        check(lib().bramha_cuda_lookup_weight(self._ctx, key.encode(), ctypes.byref(h)))
+        f, n, k = ctypes.c_int(), ctypes.c_int64(), ctypes.c_int64()
+        check(lib().bramha_cuda_weight_info(h, ctypes.byref(f), ctypes.byref(n), ctypes.byref(k), None))
+        return Weight(self, h.value, key, {v: s for s, v in FMT.items()}[f.value], n.value, k.value)
+
+    def evict(self, key: str):
+        check(lib().bramha_cuda_evict_weight(self._ctx, key.encode()))
+
+    # ------------------------------------------------- reference-shaped API
+    def _matvec(self, fmt, h, q, scales, out_features, model_name, layer_name):
+        h = _f32(h).reshape(-1)
+        qa = np.ascontiguousarray(q)
+        sa = None if scales is None else _f32(scales)
+        out = np.zeros(out_features, np.float32)
+        check(lib().bramha_cuda_matvec(
+            self._ctx, FMT[fmt], h.ctypes.data, h.size, qa.ctypes.data, qa.nbytes,
+            None if sa is None else sa.ctypes.data, 0 if sa is None else sa.size, out_features,
+            None if model_name is None else model_name.encode(),
+            None if layer_name is None else layer_name.encode(), out.ctypes.data))
+        return out
+
+    def matvec_mul(self, h, weight, out_features, model_name: Optional[str] = None,
+                   layer_name: Optional[str] = None) -> np.ndarray:
+        return self._matvec("f32", h, _f32(weight), None, out_features, model_name, layer_name)
+
+    def matvec_mul_int8(self, h, q_weight, scales, out_features, model_name=None, layer_name=None):
+        return self._matvec("w8", h, np.ascontiguousarray(q_weight, np.int8), scales, out_features,
+                            model_name, layer_name)
+
+    def matvec_mul_int4(self, h, q_weight, scales, out_features, model_name=None, layer_name=None):
+        return self._matvec("w4zp8", h, np.ascontiguousarray(q_weight, np.uint8), scales, out_features,
+                            model_name, layer_name)
+
+    def matvec_mul_log4(self, h, q_weight, scales, out_features, model_name=None, layer_name=None):
+        return self._matvec("log4", h, np.ascontiguousarray(q_weight, np.uint8), scales, out_features,
+                            model_name, layer_name)
+
+    # ------------------------------------------------------- host-buffer ops
+    def gemv(self, w: Weight, x) -> np.ndarray:
+        """y[b] = W x[b] for x of shape [batch, K] (or [K]); synchronous."""
+        x = _f32(x)
+        batch = 1 if x.ndim == 1 else x.shape[0]
+        if x.size != batch * w.K:
+            raise BramhaError(-2, f"input has {x.size} elements, expected {batch} x {w.K}")
+        y = np.empty((batch, w.N), np.float32)
+        check(lib().bramha_cuda_gemv(self._ctx, w.handle, x.ctypes.data, batch, y.ctypes.data))
+        return y.reshape(-1) if x.ndim == 1 else y
+
+    def gemm(self, w: Weight, h_block, block_size: int) -> np.ndarray:
+        """gemm_cpu(h_block, weight, block_size, in_features, out_features) -> [M*N]."""
+        hb = _f32(h_block).reshape(-1)
+        if hb.size != block_size * w.K:
+            raise BramhaError(-2, f"h_block has {hb.size} elements, expected {block_size} x {w.K}")
+        out = np.empty(block_size * w.N, np.float32)
+        check(lib().bramha_cuda_gemm(self._ctx, w.handle, hb.ctypes.data, block_size, out.ctypes.data))
+        return out
+
+    # ---------------------------------------------------- device-pointer ops
+    def gemv_dev(self, w: Weight, x, y, stream=None):
+        """x: CUDA f32 [batch, K]; y: CUDA f32 [batch, N]; stream-ordered."""
+        batch = 1 if x.dim() == 1 else x.shape[0]
+        check(lib().bramha_cuda_gemv_dev(self._ctx, w.handle, x.data_ptr(), batch, y.data_ptr(), _stream(stream)))
+
+    def gemv_multi_dev(self, ws: Sequence[Weight], x, ys, stream=None):
+        n = len(ws)
+        harr = (ctypes.c_void_p * n)(*[w.handle for w in ws])
+        yarr = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+        batch = 1 if x.dim() == 1 else x.shape[0]
+        check(lib().bramha_cuda_gemv_multi_dev(self._ctx, n, harr, x.data_ptr(), batch, yarr, _stream(stream)))
+
+    def gemm_dev(self, w: Weight, x, y, stream=None):
+        dt = DTYPE["bf16"] if str(x.dtype) == "torch.bfloat16" else DTYPE["f32"]
+        check(lib().bramha_cuda_gemm_dev(self._ctx, w.handle, x.data_ptr(), dt, x.shape[0], y.data_ptr(),
+                                         _stream(stream)))
+
+    def quantize_dev(self, fmt: str, w, q, scales, stream=None):
+        n, k = w.shape
+        check(lib().bramha_cuda_quantize_dev(self._ctx, FMT[fmt], n, k, w.data_ptr(), q.data_ptr(),
+                                             scales.data_ptr(), _stream(stream)))
+
+
+def _stream(stream) -> Optional[int]:
+    if stream is None:
+        try:
+            import torch
+            if torch.cuda.is_available():
+                return torch.cuda.current_stream().cuda_stream
+        except Exception:
+            pass
+        return None
+    return getattr(stream, "cuda_stream", stream)
+
+
+_PLANES: dict = {}
+_PLANES_LOCK = threading.Lock()
+
+
+def get_cuda_plane(device: int = 0) -> Optional[CudaComputePlane]:
+    """Process-wide plane for `device`, or None (BRAMHA_CPU set / init failed)."""
+    if os.environ.get("BRAMHA_CPU") is not None:
+        return None
+    with _PLANES_LOCK:
+        if device not in _PLANES:
+            try:
+                _PLANES[device] = CudaComputePlane(device)
+            except (BramhaError, RuntimeError):
+                _PLANES[device] = None
+        return _PLANES[device]
+
+
+def packed_nbytes(fmt: str, n: int, k: int) -> int:
+    return {"f32": n * k * 4, "w8": n * k, "w4zp8": n * (k // 2), "log4": n * (k // 2)}[fmt]

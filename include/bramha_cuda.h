@@ -1,0 +1,179 @@
+/*
+ * bramha_cuda.h -- C ABI of the B200 (sm_100a) quantized linear-layer plane.
+ *
+ * This is the drop-in boundary for the GPU arm of the reference's compute
+ * layer (akshaybhlrp/bramha): it replaces `WgpuComputePlane`
+ * (src/compute/wgpu_backend.rs:100-1728) and the dead GPU dispatch inside
+ * `matvec_mul` (src/inference/cpu_engine.rs:380-454), and adds the prefill
+ * GEMM that `gemm_cpu` (src/inference/cpu_engine.rs:565-912) computes on the
+ * host.  Plain C types only: a Rust `extern "C"` block, ctypes or cgo can bind
+ * it without CUDA or torch headers.  Streams are passed as `void*` holding a
+ * `cudaStream_t` (NULL = the context's own stream).
+ *
+ * Conventions (mirroring the reference):
+ *  - every call returns BRAMHA_OK (0) or a negative BRAMHA_ERR_* status and
+ *    never aborts; no C++ exception crosses this boundary;
+ *  - the message of the last failure on the calling thread is returned by
+ *    bramha_cuda_last_error() (the reference returns `Err(String)`);
+ *  - size mismatches are errors (wgpu_backend.rs:1096-1104); N == 0 or K == 0
+ *    returns zeros (wgpu_backend.rs:1092-1095);
+ *  - weights are copied once into a persistent device buffer keyed by
+ *    "model:layer" (get_or_create_op, wgpu_backend.rs:603-722) and evicted in
+ *    least-recently-used order above a device-memory cap (ModelBuffers,
+ *    wgpu_backend.rs:25-82);
+ *  - the registry is thread-safe; host-buffer calls are synchronous (they
+ *    return once the result is in host memory), like the reference's
+ *    `device.poll(Wait)` round trip (wgpu_backend.rs:1244).
+ *
+ * Weight formats (row-major, one fp32 scale per output row):
+ *  - BRAMHA_FMT_F32   : f32 [N][K]                          (matvec_mul, wgpu_backend.rs:734)
+ *  - BRAMHA_FMT_W8    : i8  [N][K], w = q * s_row           (quantize_to_int8, src/models/quantization.rs:7-38)
+ *  - BRAMHA_FMT_W4ZP8 : u8  [N][K/2], even column in the high nibble,
+ *                       w = (nibble - 8) * s_row            (quantize_to_int4, quantization.rs:41-83)
+ *  - BRAMHA_FMT_LOG4  : u8  [N][K/2], high nibble first,
+ *                       w = (2^code - 1) * s_row            (dequantize_log4, spanda-engine/src/lib.rs:332-342)
+ */
+#ifndef BRAMHA_CUDA_H
+#define BRAMHA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BRAMHA_CUDA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define BRAMHA_API __attribute__((visibility("default")))
+#else
+#define BRAMHA_API
+#endif
+
+enum bramha_format {
+    BRAMHA_FMT_F32 = 0,
+    BRAMHA_FMT_W8 = 1,
+    BRAMHA_FMT_W4ZP8 = 2,
+    BRAMHA_FMT_LOG4 = 3
+};
+
+enum bramha_dtype { BRAMHA_DTYPE_F32 = 0, BRAMHA_DTYPE_BF16 = 1 };
+
+enum bramha_status {
+    BRAMHA_OK = 0,
+    BRAMHA_ERR_INVALID = -1,     /* null pointer, bad enum, negative size   */
+    BRAMHA_ERR_SIZE = -2,        /* buffer length does not match the shape  */
+    BRAMHA_ERR_CUDA = -3,        /* a CUDA runtime call failed              */
+    BRAMHA_ERR_OOM = -4,         /* device memory exhausted / above the cap */
+    BRAMHA_ERR_UNSUPPORTED = -5, /* shape or format this build cannot run   */
+    BRAMHA_ERR_NOT_FOUND = -6,   /* unknown weight key                      */
+    BRAMHA_ERR_TIMEOUT = -7,     /* a bounded device-side wait gave up      */
+    BRAMHA_ERR_NCCL = -8         /* a collective failed                     */
+};
+
+typedef struct bramha_ctx bramha_ctx;
+typedef struct bramha_weight bramha_weight;
+
+/* ---------------------------------------------------------------- context */
+
+/* Replaces WgpuComputePlane::new (wgpu_backend.rs:121) / get_wgpu_plane
+ * (wgpu_backend.rs:1710-1728): binds `device`, creates the context stream and
+ * the weight registry.  Fails with BRAMHA_ERR_UNSUPPORTED on a device that is
+ * not sm_100 (the kernels are built for sm_100a only). */
+BRAMHA_API int bramha_cuda_init(int device, bramha_ctx** out);
+
+/* Frees every registered weight and the context. */
+BRAMHA_API int bramha_cuda_destroy(bramha_ctx* ctx);
+
+/* Message of the last failed call on this thread ("" if none).  The
+ * reference's `Err(String)` payloads (wgpu_backend.rs:1096-1104). */
+BRAMHA_API const char* bramha_cuda_last_error(void);
+
+BRAMHA_API int bramha_cuda_abi_version(void);
+
+/* Device-memory cap for registered weights, in bytes (ModelBuffers::new,
+ * wgpu_backend.rs:41-56; the reference caps at 3 GB). 0 = no cap. */
+BRAMHA_API int bramha_cuda_set_memory_cap(bramha_ctx* ctx, size_t bytes);
+BRAMHA_API int bramha_cuda_memory_used(bramha_ctx* ctx, size_t* bytes);
+
+/* ---------------------------------------------------------------- weights */
+
+/* get_or_create_op (wgpu_backend.rs:603-722): copies the packed weight and
+ * its per-row scales from HOST memory into a persistent device buffer under
+ * `key`.  Idempotent per key: a second call with the same key returns the
+ * cached weight and refreshes its LRU position.  `scales` may be NULL for
+ * BRAMHA_FMT_F32.  q_bytes must equal N*K*4 (F32), N*K (W8) or N*(K/2)
+ * (W4ZP8, LOG4); n_scales must equal N. */
+BRAMHA_API int bramha_cuda_register_weight(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K,
+                                const void* q, size_t q_bytes, const float* scales, size_t n_scales,
+                                bramha_weight** out);
+
+/* Same, from DEVICE memory (device-to-device copy on `stream`). */
+BRAMHA_API int bramha_cuda_register_weight_dev(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K,
+                                    const void* q_dev, size_t q_bytes, const float* scales_dev,
+                                    size_t n_scales, void* stream, bramha_weight** out);
+
+/* Looks up a registered weight (refreshes its LRU position). */
+BRAMHA_API int bramha_cuda_lookup_weight(bramha_ctx* ctx, const char* key, bramha_weight** out);
+
+/* Evicts one key, or all (clear_persistent_buffers, wgpu_backend.rs:725-731). */
+BRAMHA_API int bramha_cuda_evict_weight(bramha_ctx* ctx, const char* key);
+BRAMHA_API int bramha_cuda_clear(bramha_ctx* ctx);
+
+/* Shape / format / device footprint of a registered weight. */
+BRAMHA_API int bramha_cuda_weight_info(const bramha_weight* w, int* fmt, int64_t* N, int64_t* K, size_t* device_bytes);
+
+/* -------------------------------------------------------- decode GEMV path */
+
+/* matvec_mul_int4 / matvec_mul_int8 / matvec_mul (wgpu_backend.rs:1083, 906,
+ * 734) in one entry point: y[b][j] = sum_i x[b][i] * dq(w[j][i]) for
+ * b < batch, host buffers, synchronous.  `x_host` is [batch][K] f32,
+ * `y_host` is [batch][N] f32. */
+BRAMHA_API int bramha_cuda_gemv(bramha_ctx* ctx, const bramha_weight* w, const float* x_host, int64_t batch,
+                     float* y_host);
+
+/* Device-pointer, stream-ordered variant (asynchronous). */
+BRAMHA_API int bramha_cuda_gemv_dev(bramha_ctx* ctx, const bramha_weight* w, const float* x_dev, int64_t batch,
+                         float* y_dev, void* stream);
+
+/* fused_qkv_mul_into (cpu_engine.rs:3342-3354) generalised: several weights
+ * that share one input x (same K), computed by ONE kernel launch.  y_devs[i]
+ * is [batch][N_i]. At most 8 weights. */
+BRAMHA_API int bramha_cuda_gemv_multi_dev(bramha_ctx* ctx, int n_weights, const bramha_weight* const* ws,
+                               const float* x_dev, int64_t batch, float* const* y_devs, void* stream);
+
+/* The reference's keyed one-shot call, e.g.
+ * `matvec_mul_int4(h, q_weight, scales, out_features, model_name, layer_name)`
+ * (wgpu_backend.rs:1083-1091): when both names are non-NULL the weight is
+ * cached under "model:layer"; otherwise it is uploaded for this call only.
+ * K is the length of h; out is [N]. */
+BRAMHA_API int bramha_cuda_matvec(bramha_ctx* ctx, int fmt, const float* h, int64_t K, const void* q_weight,
+                       size_t q_bytes, const float* scales, size_t n_scales, int64_t N,
+                       const char* model_name, const char* layer_name, float* out);
+
+/* ------------------------------------------------------- prefill GEMM path */
+
+/* gemm_cpu (cpu_engine.rs:565-912): out[m][j] = sum_i h[m][i] * dq(w[j][i]),
+ * h_block [M][K] f32 host, out [M][N] f32 host, synchronous. */
+BRAMHA_API int bramha_cuda_gemm(bramha_ctx* ctx, const bramha_weight* w, const float* h_host, int64_t M,
+                     float* out_host);
+
+/* Device variant: x_dev is [M][K] of `x_dtype` (BRAMHA_DTYPE_F32 or _BF16). */
+BRAMHA_API int bramha_cuda_gemm_dev(bramha_ctx* ctx, const bramha_weight* w, const void* x_dev, int x_dtype, int64_t M,
+                         float* y_dev, void* stream);
+
+/* ------------------------------------------------------------ packers (GPU) */
+
+/* quantize_to_int8 / quantize_to_int4 (src/models/quantization.rs:7-83) and
+ * the log4 encoder this project defines, on the device, bit-exact with the
+ * reference's rounding (half away from zero) and nibble order.  w_dev is
+ * f32 [N][K]; q_dev receives the packed bytes, scales_dev [N] the scales. */
+BRAMHA_API int bramha_cuda_quantize_dev(bramha_ctx* ctx, int fmt, int64_t N, int64_t K, const float* w_dev, void* q_dev,
+                             float* scales_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BRAMHA_CUDA_H */

@@ -1,0 +1,253 @@
+"""CPU oracle for the quantized linear-layer path -- TEST INFRASTRUCTURE ONLY.
+
+numpy/ctypes wrappers around ``liboracle.so``, the plain-C restatement of the
+reference's CPU arithmetic (akshaybhlrp/bramha):
+
+* packers / dequantizers: ``src/models/quantization.rs:7-122``
+* log4 decoder: ``spanda-engine/src/lib.rs:332-342`` (encoder defined here)
+* decode GEMV ``matvec_mul_into``: ``src/inference/cpu_engine.rs:1307-1444``
+* allocating GEMV ``matvec_mul``: ``src/inference/cpu_engine.rs:355-562``
+* prefill GEMM ``gemm_cpu``: ``src/inference/cpu_engine.rs:565-706``
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline and
+reference legs may import this package.  The product path (``bramha_b200``)
+never does: it fails loudly when its CUDA library is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_i8p = ctypes.POINTER(ctypes.c_int8)
+_i64 = ctypes.c_int64
+
+
+def build(force: bool = False) -> str:
+    """Compile liboracle.so with its Makefile (gcc, no fast-math, no FMA contraction)."""
+    if force or not os.path.exists(_LIB_PATH) or (
+        os.path.getmtime(_LIB_PATH) < os.path.getmtime(os.path.join(_HERE, "bramha_oracle.c"))
+    ):
+        subprocess.run(["make", "-s", "-C", _HERE, "-B" if force else "liboracle.so"], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(_LIB_PATH)
+        sig = {
+            "bro_quantize_to_int8": (None, [_f32p, _i64, _i64, _i8p, _f32p]),
+            "bro_quantize_to_int4": (ctypes.c_int, [_f32p, _i64, _i64, _u8p, _f32p]),
+            "bro_quantize_to_log4": (ctypes.c_int, [_f32p, _i64, _i64, _u8p, _f32p]),
+            "bro_dequantize_int8": (None, [_i8p, _f32p, _i64, _i64, _f32p]),
+            "bro_dequantize_int4": (None, [_u8p, _f32p, _i64, _i64, _f32p]),
+            "bro_dequantize_log4": (None, [_u8p, _i64, ctypes.c_float, _f32p]),
+            "bro_dequantize_log4_rows": (None, [_u8p, _f32p, _i64, _i64, _f32p]),
+            "bro_matvec_into_f32": (None, [_f32p, _i64, _f32p, _i64, _f32p, ctypes.c_int]),
+            "bro_matvec_into_i8": (None, [_f32p, _i64, _i8p, _f32p, _i64, _f32p, ctypes.c_int]),
+            "bro_matvec_into_u4": (None, [_f32p, _i64, _u8p, _f32p, _i64, _f32p, ctypes.c_int]),
+            "bro_matvec_into_log4": (None, [_f32p, _i64, _u8p, _f32p, _i64, _f32p, ctypes.c_int]),
+            "bro_matvec_fused_log4": (None, [_f32p, _i64, _u8p, _f32p, _i64, _f32p, ctypes.c_int]),
+            "bro_matvec_f32": (None, [_f32p, _i64, _f32p, _i64, _f32p]),
+            "bro_matvec_i8": (None, [_f32p, _i64, _i8p, _f32p, _i64, _f32p]),
+            "bro_matvec_u4": (None, [_f32p, _i64, _u8p, _f32p, _i64, _f32p]),
+            "bro_gemm_f32": (None, [_f32p, _i64, _i64, _f32p, _i64, _f32p]),
+            "bro_gemm_i8": (None, [_f32p, _i64, _i64, _i8p, _f32p, _i64, _f32p]),
+            "bro_gemm_u4": (None, [_f32p, _i64, _i64, _u8p, _f32p, _i64, _f32p]),
+            "bro_gemm_log4": (None, [_f32p, _i64, _i64, _u8p, _f32p, _i64, _f32p]),
+            "bro_gemm_u4_par": (None, [_f32p, _i64, _i64, _u8p, _f32p, _i64, _f32p, ctypes.c_int]),
+            "bro_max_threads": (ctypes.c_int, []),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a, t):
+    return a.ctypes.data_as(t)
+
+
+def _c(a, dtype):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+# ----------------------------------------------------------------------------- packers
+def quantize_to_int8(w: np.ndarray, out_features: int, in_features: int):
+    w = _c(w, np.float32)
+    q = np.empty(out_features * in_features, np.int8)
+    s = np.empty(out_features, np.float32)
+    lib().bro_quantize_to_int8(_p(w, _f32p), out_features, in_features, _p(q, _i8p), _p(s, _f32p))
+    return q, s
+
+
+def quantize_to_int4(w: np.ndarray, out_features: int, in_features: int):
+    w = _c(w, np.float32)
+    q = np.empty(out_features * (in_features // 2), np.uint8)
+    s = np.empty(out_features, np.float32)
+    rc = lib().bro_quantize_to_int4(_p(w, _f32p), out_features, in_features, _p(q, _u8p), _p(s, _f32p))
+    if rc != 0:
+        raise ValueError("in_features must be a multiple of 2 for INT4 packing")
+    return q, s
+
+
+def quantize_to_log4(w: np.ndarray, out_features: int, in_features: int):
+    w = _c(w, np.float32)
+    q = np.empty(out_features * (in_features // 2), np.uint8)
+    s = np.empty(out_features, np.float32)
+    rc = lib().bro_quantize_to_log4(_p(w, _f32p), out_features, in_features, _p(q, _u8p), _p(s, _f32p))
+    if rc != 0:
+        raise ValueError("in_features must be a multiple of 2 for LOG4 packing")
+    return q, s
+
+
+def dequantize_int8(q, scales, in_features: int):
+    q = _c(q, np.int8)
+    scales = _c(scales, np.float32)
+    n = scales.size
+    out = np.empty(n * in_features, np.float32)
+    lib().bro_dequantize_int8(_p(q, _i8p), _p(scales, _f32p), n, in_features, _p(out, _f32p))
+    return out
+
+
+def dequantize_int4(q, scales, in_features: int):
+    q = _c(q, np.uint8)
+    scales = _c(scales, np.float32)
+    n = scales.size
+    out = np.zeros(n * in_features, np.float32)
+    lib().bro_dequantize_int4(_p(q, _u8p), _p(scales, _f32p), n, in_features, _p(out, _f32p))
+    return out
+
+
+def dequantize_log4(data, scale: float):
+    data = _c(data, np.uint8)
+    out = np.empty(data.size * 2, np.float32)
+    lib().bro_dequantize_log4(_p(data, _u8p), data.size, ctypes.c_float(scale), _p(out, _f32p))
+    return out
+
+
+def dequantize_log4_rows(q, scales, in_features: int):
+    q = _c(q, np.uint8)
+    scales = _c(scales, np.float32)
+    n = scales.size
+    out = np.zeros(n * in_features, np.float32)
+    lib().bro_dequantize_log4_rows(_p(q, _u8p), _p(scales, _f32p), n, in_features, _p(out, _f32p))
+    return out
+
+
+# ----------------------------------------------------------------------------- GEMV / GEMM
+FORMATS = ("f32", "w8", "w4zp8", "log4")
+
+
+def matvec_mul_into(fmt: str, h, q, scales, out_features: int, threads: int = 0):
+    """Decode GEMV as `matvec_mul_into` computes it (4 interleaved accumulators)."""
+    h = _c(h, np.float32)
+    K = h.size
+    out = np.empty(out_features, np.float32)
+    L = lib()
+    if fmt == "f32":
+        w = _c(q, np.float32)
+        L.bro_matvec_into_f32(_p(h, _f32p), K, _p(w, _f32p), out_features, _p(out, _f32p), threads)
+        return out
+    scales = _c(scales, np.float32)
+    if fmt == "w8":
+        L.bro_matvec_into_i8(_p(h, _f32p), K, _p(_c(q, np.int8), _i8p), _p(scales, _f32p), out_features,
+                             _p(out, _f32p), threads)
+    elif fmt == "w4zp8":
+        L.bro_matvec_into_u4(_p(h, _f32p), K, _p(_c(q, np.uint8), _u8p), _p(scales, _f32p), out_features,
+                             _p(out, _f32p), threads)
+    elif fmt == "log4":
+        L.bro_matvec_into_log4(_p(h, _f32p), K, _p(_c(q, np.uint8), _u8p), _p(scales, _f32p), out_features,
+                               _p(out, _f32p), threads)
+    else:
+        raise ValueError(fmt)
+    return out
+
+
+def matvec_fused_log4(h, q, scales, out_features: int, threads: int = 0):
+    h = _c(h, np.float32)
+    out = np.empty(out_features, np.float32)
+    lib().bro_matvec_fused_log4(_p(h, _f32p), h.size, _p(_c(q, np.uint8), _u8p), _p(_c(scales, np.float32), _f32p),
+                                out_features, _p(out, _f32p), threads)
+    return out
+
+
+def matvec_mul(fmt: str, h, q, scales, out_features: int):
+    """`matvec_mul` (single accumulator, cpu_engine.rs:456-561)."""
+    h = _c(h, np.float32)
+    K = h.size
+    out = np.empty(out_features, np.float32)
+    L = lib()
+    if fmt == "f32":
+        L.bro_matvec_f32(_p(h, _f32p), K, _p(_c(q, np.float32), _f32p), out_features, _p(out, _f32p))
+    elif fmt == "w8":
+        L.bro_matvec_i8(_p(h, _f32p), K, _p(_c(q, np.int8), _i8p), _p(_c(scales, np.float32), _f32p),
+                        out_features, _p(out, _f32p))
+    elif fmt == "w4zp8":
+        L.bro_matvec_u4(_p(h, _f32p), K, _p(_c(q, np.uint8), _u8p), _p(_c(scales, np.float32), _f32p),
+                        out_features, _p(out, _f32p))
+    else:
+        raise ValueError(fmt)
+    return out
+
+
+def gemm_cpu(fmt: str, h_block, q, scales, block_size: int, in_features: int, out_features: int):
+    """`gemm_cpu` sequential branch: out[b][j] = s_j * sum_i h[b][i] * dq(w_ji)."""
+    hb = _c(h_block, np.float32)
+    out = np.empty(block_size * out_features, np.float32)
+    L = lib()
+    args = (_p(hb, _f32p), block_size, in_features)
+    if fmt == "f32":
+        L.bro_gemm_f32(*args, _p(_c(q, np.float32), _f32p), out_features, _p(out, _f32p))
+    elif fmt == "w8":
+        L.bro_gemm_i8(*args, _p(_c(q, np.int8), _i8p), _p(_c(scales, np.float32), _f32p), out_features,
+                      _p(out, _f32p))
+    elif fmt == "w4zp8":
+        L.bro_gemm_u4(*args, _p(_c(q, np.uint8), _u8p), _p(_c(scales, np.float32), _f32p), out_features,
+                      _p(out, _f32p))
+    elif fmt == "log4":
+        L.bro_gemm_log4(*args, _p(_c(q, np.uint8), _u8p), _p(_c(scales, np.float32), _f32p), out_features,
+                        _p(out, _f32p))
+    else:
+        raise ValueError(fmt)
+    return out
+
+
+def quantize(fmt: str, w, out_features: int, in_features: int):
+    if fmt == "w8":
+        return quantize_to_int8(w, out_features, in_features)
+    if fmt == "w4zp8":
+        return quantize_to_int4(w, out_features, in_features)
+    if fmt == "log4":
+        return quantize_to_log4(w, out_features, in_features)
+    if fmt == "f32":
+        return _c(w, np.float32).reshape(-1).copy(), None
+    raise ValueError(fmt)
+
+
+def dequantize(fmt: str, q, scales, in_features: int):
+    if fmt == "w8":
+        return dequantize_int8(q, scales, in_features)
+    if fmt == "w4zp8":
+        return dequantize_int4(q, scales, in_features)
+    if fmt == "log4":
+        return dequantize_log4_rows(q, scales, in_features)
+    if fmt == "f32":
+        return _c(q, np.float32)
+    raise ValueError(fmt)
+
+
+def max_threads() -> int:
+    return int(lib().bro_max_threads())

@@ -1,0 +1,428 @@
+/*
+ * bramha_oracle.c -- TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain-C restatement of the reference's CPU arithmetic for the quantized
+ * linear-layer path (akshaybhlrp/bramha).  The reference is Rust and cannot be
+ * compiled in this environment, so this file restates it operation by
+ * operation: same loop structure, same accumulator interleave, same fp32
+ * rounding points.  It must be compiled WITHOUT -ffast-math and WITH
+ * -ffp-contract=off: Rust/LLVM neither reassociates nor contracts a*b+c into
+ * an FMA, and gcc does contract by default in GNU C mode.
+ *
+ * Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
+ * arm may load this library, and only as the checker or the timed CPU
+ * baseline.  The CUDA product path never calls it.
+ *
+ * Parity pinning: the reference's own known-answer test for this path is
+ * `test_quantization_correctness` (src/inference/cpu_engine.rs:3501-3682);
+ * tests/test_oracle.py restates it against this file.  The log4 decoder
+ * (spanda-engine/src/lib.rs:332-342) has no reference test: it is pinned only
+ * by the reference code itself and by the independent numpy restatement that
+ * generated tests/golden/.
+ *
+ * Threading mirrors Rayon's `par_iter_mut().with_min_len(256)` over output
+ * rows with OpenMP dynamic chunks of 256 rows; each row's arithmetic is
+ * independent of the thread that runs it, so results do not depend on the
+ * thread count.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stddef.h>
+#include <string.h>
+#include <stdlib.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define BRO_API __attribute__((visibility("default")))
+
+/* ------------------------------------------------------------------------- */
+/* Rust `f32 as u8` / `f32 as i8` casts saturate and map NaN to 0.            */
+static inline uint8_t rust_f32_as_u8(float v) {
+    if (isnan(v)) return 0;
+    if (v <= 0.0f) return 0;
+    if (v >= 255.0f) return 255;
+    return (uint8_t)v; /* truncation toward zero, as Rust */
+}
+static inline int8_t rust_f32_as_i8(float v) {
+    if (isnan(v)) return 0;
+    if (v <= -128.0f) return -128;
+    if (v >= 127.0f) return 127;
+    return (int8_t)v;
+}
+/* Rust `f32::clamp(lo, hi)`: NaN stays NaN. */
+static inline float rust_clamp(float v, float lo, float hi) {
+    if (v < lo) v = lo;
+    if (v > hi) v = hi;
+    return v;
+}
+/* Rust `f32::round`: half away from zero == C roundf. */
+static inline float rust_round(float v) { return roundf(v); }
+
+/* Row max |w| exactly as the reference loop: `if abs > max_abs` (NaN never wins). */
+static inline float row_max_abs(const float* row, int64_t K) {
+    float m = 0.0f;
+    for (int64_t i = 0; i < K; ++i) {
+        float a = fabsf(row[i]);
+        if (a > m) m = a;
+    }
+    return m;
+}
+
+/* ------------------------------------------------------------------------- */
+/* quantize_to_int8  -- src/models/quantization.rs:7-38                        */
+BRO_API void bro_quantize_to_int8(const float* w, int64_t N, int64_t K, int8_t* q, float* scales) {
+    for (int64_t j = 0; j < N; ++j) {
+        const float* row = w + j * K;
+        float max_abs = row_max_abs(row, K);
+        float scale = (max_abs == 0.0f) ? 1.0f : max_abs / 127.0f;
+        scales[j] = scale;
+        for (int64_t i = 0; i < K; ++i) {
+            float v = rust_clamp(rust_round(row[i] / scale), -127.0f, 127.0f);
+            q[j * K + i] = rust_f32_as_i8(v);
+        }
+    }
+}
+
+/* quantize_to_int4  -- src/models/quantization.rs:41-83
+ * Returns -1 when K is odd (the reference asserts, :46-49). */
+BRO_API int bro_quantize_to_int4(const float* w, int64_t N, int64_t K, uint8_t* q, float* scales) {
+    if (K % 2 != 0) return -1;
+    const int64_t half = K / 2;
+    for (int64_t j = 0; j < N; ++j) {
+        const float* row = w + j * K;
+        float max_abs = row_max_abs(row, K);
+        float scale = (max_abs == 0.0f) ? 1.0f : max_abs / 7.0f;
+        scales[j] = scale;
+        for (int64_t i = 0; i < half; ++i) {
+            float x1 = row[2 * i], x2 = row[2 * i + 1];
+            uint8_t q1 = rust_f32_as_u8(rust_clamp(rust_round(x1 / scale), -7.0f, 7.0f) + 8.0f);
+            uint8_t q2 = rust_f32_as_u8(rust_clamp(rust_round(x2 / scale), -7.0f, 7.0f) + 8.0f);
+            /* `(q1 << 4) | (q2 & 0x0F)` on u8: q1 << 4 wraps modulo 256 in the
+             * reference only in debug-panic terms; q1 <= 15 so it never does. */
+            q[j * half + i] = (uint8_t)(((q1 << 4) & 0xFF) | (q2 & 0x0F));
+        }
+    }
+    return 0;
+}
+
+/* dequantize_int8 -- src/models/quantization.rs:86-99 */
+BRO_API void bro_dequantize_int8(const int8_t* q, const float* scales, int64_t N, int64_t K, float* out) {
+    for (int64_t j = 0; j < N; ++j)
+        for (int64_t i = 0; i < K; ++i) out[j * K + i] = (float)q[j * K + i] * scales[j];
+}
+
+/* dequantize_int4 -- src/models/quantization.rs:102-122 */
+BRO_API void bro_dequantize_int4(const uint8_t* q, const float* scales, int64_t N, int64_t K, float* out) {
+    const int64_t half = K / 2;
+    for (int64_t j = 0; j < N; ++j) {
+        float s = scales[j];
+        for (int64_t i = 0; i < half; ++i) {
+            uint8_t b = q[j * half + i];
+            float q1 = (float)((b >> 4) & 0x0F) - 8.0f;
+            float q2 = (float)(b & 0x0F) - 8.0f;
+            out[j * K + 2 * i] = q1 * s;
+            out[j * K + 2 * i + 1] = q2 * s;
+        }
+    }
+}
+
+/* dequantize_log4 -- spanda-engine/src/lib.rs:332-342
+ * For code c (high nibble first): signum(c) * (2^|c| - 1) * scale.
+ * c >= 0 and f32::signum(+0.0) == +1.0, so the value is ((2^c - 1) * 1) * scale,
+ * evaluated left to right as the reference does: (signum * (pow - 1)) * scale. */
+static inline float log4_decode(unsigned c, float scale) {
+    float v = (float)c;
+    float sg = 1.0f;                      /* signum of a non-negative float */
+    float p = ldexpf(1.0f, (int)c);       /* 2.0f32.powf(c) is exact for c in 0..15 */
+    (void)v;
+    return (sg * (p - 1.0f)) * scale;
+}
+
+BRO_API void bro_dequantize_log4(const uint8_t* data, int64_t nbytes, float scale, float* out) {
+    for (int64_t i = 0; i < nbytes; ++i) {
+        uint8_t b = data[i];
+        out[2 * i] = log4_decode((unsigned)(b >> 4), scale);
+        out[2 * i + 1] = log4_decode((unsigned)(b & 0x0F), scale);
+    }
+}
+
+/* Row-wise log4 dequantization with one scale per output row (the format this
+ * project registers: scales.len() == N). */
+BRO_API void bro_dequantize_log4_rows(const uint8_t* q, const float* scales, int64_t N, int64_t K, float* out) {
+    const int64_t half = K / 2;
+    for (int64_t j = 0; j < N; ++j) bro_dequantize_log4(q + j * half, half, scales[j], out + j * K);
+}
+
+/* quantize_to_log4 -- DEFINED BY THIS PROJECT (the reference has no encoder).
+ * Per row: s = max|w| / 32767 (1.0 for an all-zero row), so the largest code
+ * (15 -> 2^15 - 1 = 32767) reproduces max|w|.  Each |w| maps to the code whose
+ * decoded value fl((2^c - 1) * s) is nearest, ties to the lower code.  The
+ * sign is dropped because the reference decoder cannot represent it.  Byte i
+ * of a row holds column 2i in the high nibble, column 2i+1 in the low nibble.
+ * Returns -1 when K is odd. */
+BRO_API int bro_quantize_to_log4(const float* w, int64_t N, int64_t K, uint8_t* q, float* scales) {
+    if (K % 2 != 0) return -1;
+    const int64_t half = K / 2;
+    for (int64_t j = 0; j < N; ++j) {
+        const float* row = w + j * K;
+        float max_abs = row_max_abs(row, K);
+        float s = (max_abs == 0.0f) ? 1.0f : max_abs / 32767.0f;
+        scales[j] = s;
+        float d[16];
+        for (unsigned c = 0; c < 16; ++c) d[c] = log4_decode(c, s);
+        for (int64_t i = 0; i < half; ++i) {
+            unsigned code[2];
+            for (int t = 0; t < 2; ++t) {
+                float a = fabsf(row[2 * i + t]);
+                unsigned best = 0;
+                float best_err = fabsf(a - d[0]);
+                for (unsigned c = 1; c < 16; ++c) {
+                    float e = fabsf(a - d[c]);
+                    if (e < best_err) { best = c; best_err = e; }
+                }
+                code[t] = best;
+            }
+            q[j * half + i] = (uint8_t)((code[0] << 4) | code[1]);
+        }
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------------------- */
+/* LUT_Q1 / LUT_Q2 -- src/inference/cpu_engine.rs:108-126 */
+static float LUT_Q1[256], LUT_Q2[256];
+static float LUT_L1[256], LUT_L2[256]; /* log4 analogue: 2^c - 1 */
+static void luts_init(void) {
+    static int done = 0;
+    if (done) return;
+    for (int i = 0; i < 256; ++i) {
+        LUT_Q1[i] = (float)((i >> 4) & 0x0F) - 8.0f;
+        LUT_Q2[i] = (float)(i & 0x0F) - 8.0f;
+        LUT_L1[i] = ldexpf(1.0f, (i >> 4) & 0x0F) - 1.0f;
+        LUT_L2[i] = ldexpf(1.0f, i & 0x0F) - 1.0f;
+    }
+    done = 1;
+}
+
+static inline void set_threads(int threads) {
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#else
+    (void)threads;
+#endif
+}
+
+/* matvec_mul_into, Float branch -- cpu_engine.rs:1311-1335 */
+static inline float row_dot_f32_into(const float* h, const float* w, int64_t K) {
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    int64_t chunks = K / 4, rem = K % 4;
+    for (int64_t i = 0; i < chunks; ++i) {
+        int64_t b = i * 4;
+        s0 += h[b] * w[b];
+        s1 += h[b + 1] * w[b + 1];
+        s2 += h[b + 2] * w[b + 2];
+        s3 += h[b + 3] * w[b + 3];
+    }
+    for (int64_t i = chunks * 4; i < chunks * 4 + rem; ++i) s0 += h[i] * w[i];
+    return s0 + s1 + s2 + s3;
+}
+
+/* matvec_mul_into, QuantizedI8 branch -- cpu_engine.rs:1337-1361 */
+static inline float row_dot_i8_into(const float* h, const int8_t* w, int64_t K) {
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    int64_t chunks = K / 4, rem = K % 4;
+    for (int64_t i = 0; i < chunks; ++i) {
+        int64_t b = i * 4;
+        s0 += h[b] * (float)w[b];
+        s1 += h[b + 1] * (float)w[b + 1];
+        s2 += h[b + 2] * (float)w[b + 2];
+        s3 += h[b + 3] * (float)w[b + 3];
+    }
+    for (int64_t i = chunks * 4; i < chunks * 4 + rem; ++i) s0 += h[i] * (float)w[i];
+    return s0 + s1 + s2 + s3;
+}
+
+/* matvec_mul_into, QuantizedU4 branch -- cpu_engine.rs:1363-1411.
+ * Also used with the log4 tables for the fused log4 CPU baseline. */
+static inline float row_dot_nib_into(const float* h, const uint8_t* rb, int64_t half,
+                                     const float* L1, const float* L2) {
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    int64_t chunks = half / 8;
+    for (int64_t c = 0; c < chunks; ++c) {
+        int64_t bb = c * 8, bh = c * 16;
+        uint8_t b0 = rb[bb], b1 = rb[bb + 1], b2 = rb[bb + 2], b3 = rb[bb + 3];
+        uint8_t b4 = rb[bb + 4], b5 = rb[bb + 5], b6 = rb[bb + 6], b7 = rb[bb + 7];
+        s0 += h[bh] * L1[b0] + h[bh + 1] * L2[b0];
+        s1 += h[bh + 2] * L1[b1] + h[bh + 3] * L2[b1];
+        s2 += h[bh + 4] * L1[b2] + h[bh + 5] * L2[b2];
+        s3 += h[bh + 6] * L1[b3] + h[bh + 7] * L2[b3];
+        s0 += h[bh + 8] * L1[b4] + h[bh + 9] * L2[b4];
+        s1 += h[bh + 10] * L1[b5] + h[bh + 11] * L2[b5];
+        s2 += h[bh + 12] * L1[b6] + h[bh + 13] * L2[b6];
+        s3 += h[bh + 14] * L1[b7] + h[bh + 15] * L2[b7];
+    }
+    float sum = s0 + s1 + s2 + s3;
+    for (int64_t i = chunks * 8; i < half; ++i) {
+        uint8_t b = rb[i];
+        sum += h[2 * i] * L1[b] + h[2 * i + 1] * L2[b];
+    }
+    return sum;
+}
+
+BRO_API void bro_matvec_into_f32(const float* h, int64_t K, const float* w, int64_t N, float* out, int threads) {
+    set_threads(threads);
+#pragma omp parallel for schedule(dynamic, 256) if (threads != 1)
+    for (int64_t j = 0; j < N; ++j) out[j] = row_dot_f32_into(h, w + j * K, K);
+}
+
+BRO_API void bro_matvec_into_i8(const float* h, int64_t K, const int8_t* q, const float* scales, int64_t N,
+                                float* out, int threads) {
+    set_threads(threads);
+#pragma omp parallel for schedule(dynamic, 256) if (threads != 1)
+    for (int64_t j = 0; j < N; ++j) out[j] = row_dot_i8_into(h, q + j * K, K) * scales[j];
+}
+
+BRO_API void bro_matvec_into_u4(const float* h, int64_t K, const uint8_t* q, const float* scales, int64_t N,
+                                float* out, int threads) {
+    luts_init();
+    const int64_t half = K / 2;
+    set_threads(threads);
+#pragma omp parallel for schedule(dynamic, 256) if (threads != 1)
+    for (int64_t j = 0; j < N; ++j) out[j] = row_dot_nib_into(h, q + j * half, half, LUT_Q1, LUT_Q2) * scales[j];
+}
+
+/* log4 GEMV as the reference would run it: dequantize_log4 of each row with
+ * that row's scale (spanda-engine/src/lib.rs:332-342), then the Float branch
+ * of matvec_mul_into (cpu_engine.rs:1311-1335).  This is the parity oracle. */
+BRO_API void bro_matvec_into_log4(const float* h, int64_t K, const uint8_t* q, const float* scales, int64_t N,
+                                  float* out, int threads) {
+    const int64_t half = K / 2;
+    set_threads(threads);
+#pragma omp parallel
+    {
+        float* row = (float*)malloc(sizeof(float) * (size_t)(K > 0 ? K : 1));
+#pragma omp for schedule(dynamic, 256)
+        for (int64_t j = 0; j < N; ++j) {
+            bro_dequantize_log4(q + j * half, half, scales[j], row);
+            if (K % 2) row[K - 1] = 0.0f; /* odd K: the packed row covers K-1 columns */
+            out[j] = row_dot_f32_into(h, row, K);
+        }
+        free(row);
+    }
+}
+
+/* Fused log4 GEMV in the reference's U4 loop style (same 8-byte chunking and
+ * accumulator interleave, tables 2^c - 1 instead of q - 8, scale at the end).
+ * It is the timed CPU baseline for log4: the reference has no fused log4
+ * GEMV, and dequantizing each row first would only make the CPU slower. */
+BRO_API void bro_matvec_fused_log4(const float* h, int64_t K, const uint8_t* q, const float* scales, int64_t N,
+                                   float* out, int threads) {
+    luts_init();
+    const int64_t half = K / 2;
+    set_threads(threads);
+#pragma omp parallel for schedule(dynamic, 256) if (threads != 1)
+    for (int64_t j = 0; j < N; ++j) out[j] = row_dot_nib_into(h, q + j * half, half, LUT_L1, LUT_L2) * scales[j];
+}
+
+/* ------------------------------------------------------------------------- */
+/* matvec_mul (allocating variant, single accumulator) -- cpu_engine.rs:355-562 */
+BRO_API void bro_matvec_f32(const float* h, int64_t K, const float* w, int64_t N, float* out) {
+    for (int64_t j = 0; j < N; ++j) {
+        float s = 0.0f;
+        for (int64_t i = 0; i < K; ++i) s += h[i] * w[j * K + i];
+        out[j] = s;
+    }
+}
+BRO_API void bro_matvec_i8(const float* h, int64_t K, const int8_t* q, const float* scales, int64_t N, float* out) {
+    for (int64_t j = 0; j < N; ++j) {
+        float s = 0.0f;
+        for (int64_t i = 0; i < K; ++i) s += h[i] * (float)q[j * K + i];
+        out[j] = s * scales[j];
+    }
+}
+BRO_API void bro_matvec_u4(const float* h, int64_t K, const uint8_t* q, const float* scales, int64_t N, float* out) {
+    const int64_t half = K / 2;
+    for (int64_t j = 0; j < N; ++j) {
+        float s = 0.0f;
+        for (int64_t i = 0; i < half; ++i) {
+            uint8_t b = q[j * half + i];
+            float q1 = (float)((b >> 4) & 0x0F) - 8.0f;
+            float q2 = (float)(b & 0x0F) - 8.0f;
+            s += h[2 * i] * q1 + h[2 * i + 1] * q2;
+        }
+        out[j] = s * scales[j];
+    }
+}
+
+/* ------------------------------------------------------------------------- */
+/* gemm_cpu, sequential branch -- cpu_engine.rs:565-706.  Loop j outer, b inner. */
+BRO_API void bro_gemm_f32(const float* hb, int64_t M, int64_t K, const float* w, int64_t N, float* out) {
+    for (int64_t j = 0; j < N; ++j) {
+        const float* ws = w + j * K;
+        for (int64_t b = 0; b < M; ++b) {
+            const float* hr = hb + b * K;
+            float s = 0.0f;
+            for (int64_t i = 0; i < K; ++i) s += hr[i] * ws[i];
+            out[b * N + j] = s;
+        }
+    }
+}
+BRO_API void bro_gemm_i8(const float* hb, int64_t M, int64_t K, const int8_t* q, const float* scales, int64_t N,
+                         float* out) {
+    for (int64_t j = 0; j < N; ++j) {
+        const int8_t* ws = q + j * K;
+        float sc = scales[j];
+        for (int64_t b = 0; b < M; ++b) {
+            const float* hr = hb + b * K;
+            float s = 0.0f;
+            for (int64_t i = 0; i < K; ++i) s += hr[i] * (float)ws[i];
+            out[b * N + j] = s * sc;
+        }
+    }
+}
+BRO_API void bro_gemm_u4(const float* hb, int64_t M, int64_t K, const uint8_t* q, const float* scales, int64_t N,
+                         float* out) {
+    luts_init();
+    const int64_t half = K / 2;
+    for (int64_t j = 0; j < N; ++j) {
+        const uint8_t* rb = q + j * half;
+        float sc = scales[j];
+        for (int64_t b = 0; b < M; ++b)
+            out[b * N + j] = row_dot_nib_into(hb + b * K, rb, half, LUT_Q1, LUT_Q2) * sc;
+    }
+}
+/* log4 prefill as the reference would run it: dequantize, then gemm_cpu Float. */
+BRO_API void bro_gemm_log4(const float* hb, int64_t M, int64_t K, const uint8_t* q, const float* scales, int64_t N,
+                           float* out) {
+    float* w = (float*)malloc(sizeof(float) * (size_t)(N * K > 0 ? N * K : 1));
+    bro_dequantize_log4_rows(q, scales, N, K, w);
+    if (K % 2)
+        for (int64_t j = 0; j < N; ++j) w[j * K + K - 1] = 0.0f;
+    bro_gemm_f32(hb, M, K, w, N, out);
+    free(w);
+}
+
+/* Multi-threaded row-parallel variant of the gemm used only for timing large
+ * CPU samples (gemm_cpu itself is sequential in the reference). */
+BRO_API void bro_gemm_u4_par(const float* hb, int64_t M, int64_t K, const uint8_t* q, const float* scales,
+                             int64_t N, float* out, int threads) {
+    luts_init();
+    const int64_t half = K / 2;
+    set_threads(threads);
+#pragma omp parallel for schedule(dynamic, 16)
+    for (int64_t j = 0; j < N; ++j) {
+        const uint8_t* rb = q + j * half;
+        float sc = scales[j];
+        for (int64_t b = 0; b < M; ++b)
+            out[b * N + j] = row_dot_nib_into(hb + b * K, rb, half, LUT_Q1, LUT_Q2) * sc;
+    }
+}
+
+BRO_API int bro_max_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}

@@ -1,0 +1,57 @@
+"""The C-ABI library: it loads, exports every declared symbol, and fails with a
+status (never an abort) on bad arguments.  No GPU needed."""
+import ctypes
+import subprocess
+
+import pytest
+
+import bramha_b200 as bb
+from bramha_b200 import _lib
+
+
+def test_library_exports_every_header_symbol():
+    L = bb.lib()
+    syms = bb.header_symbols()
+    assert len(syms) >= 19
+    for s in syms:
+        assert hasattr(L, s), s
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    assert set(syms) <= exported
+    # nothing else leaks out of the library except the ABI (C++ internals are hidden)
+    ours = {s for s in exported if s.startswith("bramha")}
+    assert ours == set(syms)
+
+
+def test_every_header_symbol_has_a_binding():
+    assert set(bb.header_symbols()) == set(_lib._SIGNATURES)
+
+
+def test_abi_version():
+    assert bb.lib().bramha_cuda_abi_version() == 1
+
+
+def test_null_arguments_return_status_not_abort():
+    L = bb.lib()
+    assert L.bramha_cuda_init(0, None) == -1
+    assert "null" in bb.last_error()
+    assert L.bramha_cuda_destroy(None) == -1
+    assert L.bramha_cuda_gemv(None, None, None, 1, None) == -1
+    assert L.bramha_cuda_clear(None) == -1
+    assert L.bramha_cuda_weight_info(None, None, None, None, None) == -1
+
+
+def test_init_without_usable_device_is_an_error_status():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    ctx = ctypes.c_void_p()
+    rc = bb.lib().bramha_cuda_init(0, ctypes.byref(ctx))
+    assert rc in (-3, -5) and not ctx.value
+    assert bb.last_error()
+
+
+def test_get_cuda_plane_respects_bramha_cpu(monkeypatch):
+    from bramha_b200 import plane
+    monkeypatch.setenv("BRAMHA_CPU", "1")
+    assert plane.get_cuda_plane(0) is None
