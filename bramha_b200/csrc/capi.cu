@@ -52,6 +52,7 @@ struct bramha_ctx {
     float* dev_x = nullptr;
     float* dev_y = nullptr;
     size_t dev_x_cap = 0, dev_y_cap = 0;
+    int* d_err = nullptr;                // device error word written by bounded waits
 };
 
 namespace {
@@ -179,6 +180,8 @@ int upload(bramha_ctx* ctx, bramha_weight* w, const void* q, const float* scales
             e = cudaMemcpy2DAsync(w->q, (size_t)w->ldq, q, (size_t)w->row_bytes, (size_t)w->row_bytes,
                                   (size_t)w->N, kind, st);
     }
+    if (e == cudaSuccess && qbytes > 0 && (w->fmt == BRAMHA_FMT_W4ZP8 || w->fmt == BRAMHA_FMT_LOG4))
+        e = launch_repack_nibbles(w->q, (int64_t)qbytes, st);
     if (e == cudaSuccess && sbytes > 0) e = cudaMemcpyAsync(w->scales, scales, sbytes, kind, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) {
@@ -282,6 +285,46 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
     return BRAMHA_OK;
 }
 
+// After the stream is idle: report (and clear) a device-side failure.
+int check_device_error(bramha_ctx* ctx, cudaStream_t st) {
+    int h = 0;
+    CK(cudaMemcpyAsync(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, st), "read error word");
+    CK(cudaStreamSynchronize(st), "stream sync");
+    if (h != 0) {
+        cudaMemsetAsync(ctx->d_err, 0, sizeof(int), st);
+        cudaStreamSynchronize(st);
+        return fail(h == BRAMHA_ERR_TIMEOUT ? BRAMHA_ERR_TIMEOUT : BRAMHA_ERR_CUDA,
+                    "a kernel gave up a bounded wait (device error word %d)", h);
+    }
+    return BRAMHA_OK;
+}
+
+// Prefill GEMM on the tensor cores for the quantized formats; dense f32
+// weights go through the GEMV kernels in batch chunks.
+int gemm_device(bramha_ctx* ctx, const bramha_weight* w, const void* x, int x_is_f32, int64_t ldx, int64_t M,
+                float* y, cudaStream_t st) {
+    if (M <= 0 || w->N == 0) return BRAMHA_OK;
+    if (w->K == 0) {
+        CK(cudaMemsetAsync(y, 0, sizeof(float) * w->N * M, st), "memset(y)");
+        return BRAMHA_OK;
+    }
+    if (w->fmt == BRAMHA_FMT_F32) {
+        if (!x_is_f32) return fail(BRAMHA_ERR_UNSUPPORTED, "f32 weights take f32 activations");
+        const bramha_weight* ws[1] = {w};
+        float* ys[1] = {y};
+        return gemv_device(ctx, 1, ws, static_cast<const float*>(x), ldx, M, ys, st);
+    }
+    const int64_t keff = (w->fmt == BRAMHA_FMT_W4ZP8 || w->fmt == BRAMHA_FMT_LOG4) ? (w->K / 2) * 2 : w->K;
+    if (keff == 0) {
+        CK(cudaMemsetAsync(y, 0, sizeof(float) * w->N * M, st), "memset(y)");
+        return BRAMHA_OK;
+    }
+    CK(launch_gemm_tcgen05(w->fmt, w->q, w->ldq, w->scales, w->N, keff, x, x_is_f32, ldx, M, y, w->N, ctx->d_err,
+                           st),
+       "tcgen05 gemm launch");
+    return BRAMHA_OK;
+}
+
 int ensure_staging(bramha_ctx* ctx, size_t x_elems, size_t y_elems) {
     if (x_elems > ctx->dev_x_cap) {
         if (ctx->dev_x) cudaFree(ctx->dev_x);
@@ -362,6 +405,13 @@ int bramha_cuda_init(int device, bramha_ctx** out) {
         delete ctx;
         return cuda_fail(e, "cudaStreamCreate");
     }
+    e = cudaMalloc(&ctx->d_err, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        cudaStreamDestroy(ctx->stream);
+        delete ctx;
+        return cuda_fail(e, "cudaMalloc(error word)");
+    }
     *out = ctx;
     return BRAMHA_OK;
 }
@@ -382,6 +432,7 @@ int bramha_cuda_destroy(bramha_ctx* ctx) {
     }
     if (ctx->dev_x) cudaFree(ctx->dev_x);
     if (ctx->dev_y) cudaFree(ctx->dev_y);
+    if (ctx->d_err) cudaFree(ctx->d_err);
     cudaStreamDestroy(ctx->stream);
     delete ctx;
     return BRAMHA_OK;
@@ -530,16 +581,51 @@ int bramha_cuda_matvec(bramha_ctx* ctx, int fmt, const float* h, int64_t K, cons
 int bramha_cuda_gemm(bramha_ctx* ctx, const bramha_weight* w, const float* h_host, int64_t M, float* out_host) {
     int rc = check_weight(ctx, w);
     if (rc) return rc;
-    return gemv_host(ctx, w, h_host, M, out_host);
+    if (M < 0) return fail(BRAMHA_ERR_INVALID, "negative block size");
+    if (M == 0 || w->N == 0) return BRAMHA_OK;
+    if (w->K == 0) {
+        memset(out_host, 0, sizeof(float) * (size_t)(w->N * M));
+        return BRAMHA_OK;
+    }
+    if (!h_host || !out_host) return fail(BRAMHA_ERR_INVALID, "null host buffer");
+    DeviceGuard g(ctx->device);
+    std::lock_guard<std::mutex> lk(ctx->io_mu);
+    const int64_t ldx = (w->K + 3) / 4 * 4;
+    rc = ensure_staging(ctx, (size_t)(ldx * M), (size_t)(w->N * M));
+    if (rc) return rc;
+    cudaStream_t st = ctx->stream;
+    CK(cudaMemcpy2DAsync(ctx->dev_x, ldx * sizeof(float), h_host, w->K * sizeof(float), w->K * sizeof(float),
+                         (size_t)M, cudaMemcpyHostToDevice, st),
+       "H2D h_block");
+    rc = gemm_device(ctx, w, ctx->dev_x, 1, ldx, M, ctx->dev_y, st);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(out_host, ctx->dev_y, sizeof(float) * (size_t)(w->N * M), cudaMemcpyDeviceToHost, st),
+       "D2H out");
+    return check_device_error(ctx, st);
 }
 
 int bramha_cuda_gemm_dev(bramha_ctx* ctx, const bramha_weight* w, const void* x_dev, int x_dtype, int64_t M,
                          float* y_dev, void* stream) {
     int rc = check_weight(ctx, w);
     if (rc) return rc;
-    if (x_dtype != BRAMHA_DTYPE_F32)
-        return fail(BRAMHA_ERR_UNSUPPORTED, "gemm_dev: activation dtype %d not supported by this build", x_dtype);
-    return bramha_cuda_gemv_dev(ctx, w, static_cast<const float*>(x_dev), M, y_dev, stream);
+    if (x_dtype != BRAMHA_DTYPE_F32 && x_dtype != BRAMHA_DTYPE_BF16)
+        return fail(BRAMHA_ERR_INVALID, "gemm_dev: unknown activation dtype %d", x_dtype);
+    if (M < 0) return fail(BRAMHA_ERR_INVALID, "negative block size");
+    if (M > 0 && w->N > 0 && (!x_dev || !y_dev)) return fail(BRAMHA_ERR_INVALID, "null device pointer");
+    if (x_dtype == BRAMHA_DTYPE_F32 && M > 0 && w->K > 0 &&
+        ((reinterpret_cast<uintptr_t>(x_dev) & 15) != 0 || (M > 1 && (w->K & 3) != 0)))
+        return fail(BRAMHA_ERR_INVALID, "f32 x_dev must be 16-byte aligned (and K a multiple of 4 when M > 1)");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    return gemm_device(ctx, w, x_dev, x_dtype == BRAMHA_DTYPE_F32 ? 1 : 0, w->K, M, y_dev, st);
+}
+
+int bramha_cuda_stream_sync(bramha_ctx* ctx, void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    CK(cudaStreamSynchronize(st), "stream sync");
+    return check_device_error(ctx, st);
 }
 
 int bramha_cuda_quantize_dev(bramha_ctx* ctx, int fmt, int64_t N, int64_t K, const float* w_dev, void* q_dev,

@@ -1,12 +1,12 @@
 // common.cuh -- definitions shared by the kernels and the C-ABI host code.
 //
 // Device weight layout (HBM): one buffer per registered weight, rows in the
-// reference's order and byte layout (src/models/quantization.rs:41-83 for
-// nibbles: byte i of a row = column 2i in the high nibble, column 2i+1 in the
-// low nibble), each row padded to a pitch `ldq` that is a multiple of 16 bytes
-// so every 16-byte vector load is aligned.  Padding bytes are zero; the kernels
-// read the matching activation columns as zero, so padding contributes nothing.
-// Scales: f32 [N], one per output row.
+// reference's order, each row padded to a pitch `ldq` that is a multiple of 16
+// bytes so every 16-byte vector load is aligned.  Padding bytes are zero; the
+// kernels read the matching activation columns as zero, so padding contributes
+// nothing.  Int8 and f32 rows keep the reference's byte layout; the two 4-bit
+// formats are rearranged inside each 32-bit word (repack.cu): even columns in
+// bits 0-15, odd columns in bits 16-31.  Scales: f32 [N], one per output row.
 #pragma once
 
 #include <cstdint>
@@ -52,10 +52,20 @@ struct GemvArgs {
     int ldq_min;           // smallest pitch among segments (all equal for one K/format)
     int nsteps;            // vector steps per row
     int ntiles;            // tiles over all segments
+    uint32_t mul[8];       // log4: powers of two moving each code to bit 23 (set by the launcher)
 };
 
 // Launch a GEMV over the segments; chooses the tiling from the shape.
 cudaError_t launch_gemv(int fmt, const GemvArgs& a, int num_sms, cudaStream_t stream);
+
+// Rearranges 4-bit rows into the device word layout, in place (repack.cu).
+cudaError_t launch_repack_nibbles(uint8_t* q, int64_t nbytes, cudaStream_t stream);
+
+// Prefill GEMM on tcgen05 (gemm_tcgen05.cu).  K = columns held by the packed
+// rows; x is bf16 (x_is_f32 = 0) or f32 (split into two bf16 passes).
+cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const float* scales, int64_t N, int64_t K,
+                                const void* x, int x_is_f32, int64_t ldx, int64_t M, float* y, int64_t ldy, int* err,
+                                cudaStream_t stream);
 
 // GPU packers (quant.cu).
 cudaError_t launch_quantize(int fmt, int64_t N, int64_t K, const float* w, uint8_t* q, float* scales,

@@ -3,6 +3,6 @@
 
 namespace bramha {
 cudaError_t launch_gemv_log4(const GemvArgs& a, int num_sms, cudaStream_t stream) {
-    return dispatch_batch<BRAMHA_FMT_LOG4>(a, num_sms, stream);
+    return run_gemv<BRAMHA_FMT_LOG4>(a, num_sms, stream);
 }
 }  // namespace bramha

@@ -8,7 +8,7 @@
 //
 // One CTA per row.  All arithmetic uses explicitly rounded intrinsics
 // (__fdiv_rn, __fmul_rn, __fsub_rn) so no multiply-add is ever contracted and
-// every value is the IEEE result the reference's f32 code produces.  roundf
+// every value is the IEEE result the reference's f32 code produces.  Rounding
 // is half away from zero, like Rust's f32::round.
 #include <cuda_runtime.h>
 #include <cstdint>
@@ -31,6 +31,15 @@ __device__ __forceinline__ int rust_as_i8(float v) {
     if (v <= -128.f) return -128;
     if (v >= 127.f) return 127;
     return (int)v;
+}
+// Rust f32::round: nearest integer, halves away from zero.  Built from the
+// exact primitives trunc and subtract (x - trunc(x) is exact in fp32), so
+// values just below a half (e.g. 0.49999997) can never round up.
+__device__ __forceinline__ float round_half_away(float x) {
+    float t = truncf(x);
+    const float d = __fsub_rn(x, t);
+    if (fabsf(d) >= 0.5f) t = __fadd_rn(t, copysignf(1.0f, x));
+    return t;
 }
 // Rust f32::clamp (NaN passes through).
 __device__ __forceinline__ float rclamp(float v, float lo, float hi) {
@@ -75,7 +84,7 @@ __global__ void __launch_bounds__(kThreads) quant_int8_kernel(const float* __res
     const float scale = (m == 0.f) ? 1.0f : __fdiv_rn(m, 127.0f);
     if (threadIdx.x == 0) scales[j] = scale;
     for (int64_t i = threadIdx.x; i < K; i += blockDim.x)
-        q[j * K + i] = (int8_t)rust_as_i8(rclamp(roundf(__fdiv_rn(row[i], scale)), -127.f, 127.f));
+        q[j * K + i] = (int8_t)rust_as_i8(rclamp(round_half_away(__fdiv_rn(row[i], scale)), -127.f, 127.f));
 }
 
 __global__ void __launch_bounds__(kThreads) quant_int4_kernel(const float* __restrict__ w, int64_t K,
@@ -87,9 +96,9 @@ __global__ void __launch_bounds__(kThreads) quant_int4_kernel(const float* __res
     const float scale = (m == 0.f) ? 1.0f : __fdiv_rn(m, 7.0f);
     if (threadIdx.x == 0) scales[j] = scale;
     for (int64_t i = threadIdx.x; i < half; i += blockDim.x) {
-        const uint32_t q1 = rust_as_u8(__fadd_rn(rclamp(roundf(__fdiv_rn(row[2 * i], scale)), -7.f, 7.f), 8.0f));
+        const uint32_t q1 = rust_as_u8(__fadd_rn(rclamp(round_half_away(__fdiv_rn(row[2 * i], scale)), -7.f, 7.f), 8.0f));
         const uint32_t q2 =
-            rust_as_u8(__fadd_rn(rclamp(roundf(__fdiv_rn(row[2 * i + 1], scale)), -7.f, 7.f), 8.0f));
+            rust_as_u8(__fadd_rn(rclamp(round_half_away(__fdiv_rn(row[2 * i + 1], scale)), -7.f, 7.f), 8.0f));
         q[j * half + i] = (uint8_t)(((q1 << 4) & 0xFFu) | (q2 & 0x0Fu));
     }
 }

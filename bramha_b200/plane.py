@@ -188,22 +188,38 @@ class CudaComputePlane:
         check(lib().bramha_cuda_gemm_dev(self._ctx, w.handle, x.data_ptr(), dt, x.shape[0], y.data_ptr(),
                                          _stream(stream)))
 
+    def stream_sync(self, stream=None):
+        """Wait for the stream and raise if a kernel reported a device-side failure."""
+        check(lib().bramha_cuda_stream_sync(self._ctx, _stream(stream)))
+
     def quantize_dev(self, fmt: str, w, q, scales, stream=None):
         n, k = w.shape
         check(lib().bramha_cuda_quantize_dev(self._ctx, FMT[fmt], n, k, w.data_ptr(), q.data_ptr(),
                                              scales.data_ptr(), _stream(stream)))
 
 
+_STREAM_LEGACY = 0x1  # cudaStreamLegacy: the legacy default stream, valid in any CUDA runtime
+
+
 def _stream(stream) -> Optional[int]:
+    """The cudaStream_t to pass: torch's current stream unless one is given.
+
+    torch's default stream has handle 0, which the C ABI reads as "the
+    context's own stream" -- a different, non-blocking stream.  The legacy
+    default stream is passed explicitly instead so the call stays ordered
+    after torch's work on that stream.
+    """
     if stream is None:
         try:
             import torch
             if torch.cuda.is_available():
-                return torch.cuda.current_stream().cuda_stream
+                stream = torch.cuda.current_stream()
         except Exception:
-            pass
-        return None
-    return getattr(stream, "cuda_stream", stream)
+            return None
+        if stream is None:
+            return None
+    handle = getattr(stream, "cuda_stream", stream)
+    return _STREAM_LEGACY if handle == 0 else handle
 
 
 _PLANES: dict = {}

@@ -159,9 +159,19 @@ BRAMHA_API int bramha_cuda_matvec(bramha_ctx* ctx, int fmt, const float* h, int6
 BRAMHA_API int bramha_cuda_gemm(bramha_ctx* ctx, const bramha_weight* w, const float* h_host, int64_t M,
                      float* out_host);
 
-/* Device variant: x_dev is [M][K] of `x_dtype` (BRAMHA_DTYPE_F32 or _BF16). */
+/* Device variant, stream-ordered: x_dev is [M][K] of `x_dtype`.  BF16 input
+ * runs one tcgen05 pass (bf16 tiles, fp32 accumulation); F32 input is split
+ * into bf16 hi + lo parts and runs two accumulating passes (~2^-16 relative).
+ * Weights are dequantized exactly (int4 -> q-8, int8 -> q, log4 -> 2^c), so
+ * the activation rounding is the only approximation. */
 BRAMHA_API int bramha_cuda_gemm_dev(bramha_ctx* ctx, const bramha_weight* w, const void* x_dev, int x_dtype, int64_t M,
                          float* y_dev, void* stream);
+
+/* Waits for `stream` (NULL = the context stream) and reports a failure that a
+ * kernel recorded on the device: the tensor-core GEMM bounds every wait and
+ * returns BRAMHA_ERR_TIMEOUT here instead of hanging.  Host-buffer calls
+ * already check this before returning. */
+BRAMHA_API int bramha_cuda_stream_sync(bramha_ctx* ctx, void* stream);
 
 /* ------------------------------------------------------------ packers (GPU) */
 

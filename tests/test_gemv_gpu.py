@@ -60,7 +60,9 @@ def test_packers_bit_exact(plane, fmt, n, k):
     w[0, :] = 0.0                     # all-zero row -> scale 1.0
     if n > 2:
         w[1, :4] = [0.5, -0.5, 1.5, -2.5]  # exact halves: round half away from zero
-        w[2, 0] = 7.0
+        w[2, 0] = 7.0                      # row max 7 -> int4 scale exactly 1.0
+        # just below / at halves: Rust's round never rounds 0.49999997 up
+        w[2, 1:6] = [np.float32(0.49999997), -np.float32(0.49999997), np.nextafter(np.float32(1.5), 0), 2.5, -3.5]
     q_ref, s_ref = oracle.quantize(fmt, w.reshape(-1), n, k)
     wd = dev(w)
     qd = torch.zeros(q_ref.size, dtype=torch.uint8, device="cuda")
