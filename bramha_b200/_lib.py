@@ -61,6 +61,7 @@ _SIGNATURES = {
     "bramha_cuda_gemm_dev": [_vp, _vp, _vp, _int, _i64, _vp, _vp],
     "bramha_cuda_quantize_dev": [_vp, _int, _i64, _i64, _vp, _vp, _vp, _vp],
     "bramha_cuda_stream_sync": [_vp, _vp],
+    "bramha_cuda_gemm_noalloc_dev": [_vp, _vp, _vp, _i64, _vp, _vp],
 }
 
 _lib = None

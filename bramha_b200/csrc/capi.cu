@@ -620,6 +620,34 @@ int bramha_cuda_gemm_dev(bramha_ctx* ctx, const bramha_weight* w, const void* x_
     return gemm_device(ctx, w, x_dev, x_dtype == BRAMHA_DTYPE_F32 ? 1 : 0, w->K, M, y_dev, st);
 }
 
+int bramha_cuda_gemm_noalloc_dev(bramha_ctx* ctx, const bramha_weight* w, const void* x_dev, int64_t M,
+                                 float* y_dev, void* stream) {
+    int rc = check_weight(ctx, w);
+    if (rc) return rc;
+    if (M < 0) return fail(BRAMHA_ERR_INVALID, "negative block size");
+    if (M > kNoAllocMaxTokens)
+        return fail(BRAMHA_ERR_UNSUPPORTED,
+                    "gemm_noalloc_dev: M = %lld tokens exceeds the fixed scratch of this entry point "
+                    "(%lld tokens); split the block or use bramha_cuda_gemm_dev",
+                    (long long)M, (long long)kNoAllocMaxTokens);
+    if (w->fmt == BRAMHA_FMT_F32)
+        return fail(BRAMHA_ERR_UNSUPPORTED, "gemm_noalloc_dev: dense f32 weights are not supported");
+    if (M == 0 || w->N == 0) return BRAMHA_OK;
+    if (!x_dev || !y_dev) return fail(BRAMHA_ERR_INVALID, "null device pointer");
+    const int64_t keff = (w->fmt == BRAMHA_FMT_W4ZP8 || w->fmt == BRAMHA_FMT_LOG4) ? (w->K / 2) * 2 : w->K;
+    if ((w->K % 8) != 0 || (reinterpret_cast<uintptr_t>(x_dev) & 15) != 0)
+        return fail(BRAMHA_ERR_INVALID,
+                    "gemm_noalloc_dev: x_dev must be 16-byte aligned bf16 [M][K] with K a multiple of 8");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    float* scratch = nullptr;
+    if (w->fmt == BRAMHA_FMT_LOG4) CK(noalloc_rowsum_scratch(ctx->device, &scratch), "cudaGetSymbolAddress(scratch)");
+    CK(launch_gemm_tcgen05_bf16_noalloc(w->fmt, w->q, w->ldq, w->scales, w->N, keff, x_dev, w->K, M, y_dev, w->N,
+                                        ctx->d_err, scratch, st),
+       "tcgen05 gemm (no-alloc) launch");
+    return BRAMHA_OK;
+}
+
 int bramha_cuda_stream_sync(bramha_ctx* ctx, void* stream) {
     if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
     DeviceGuard g(ctx->device);

@@ -67,6 +67,17 @@ cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const fl
                                 const void* x, int x_is_f32, int64_t ldx, int64_t M, float* y, int64_t ldy, int* err,
                                 cudaStream_t stream);
 
+// bf16-activation GEMM that allocates nothing: the log4 per-token sums go to
+// `rowsum_scratch` (at least M floats, caller-owned); x must be 16-byte
+// aligned with a row pitch that is a multiple of 8 elements.
+cudaError_t launch_gemm_tcgen05_bf16_noalloc(int fmt, const uint8_t* q, int64_t ldq, const float* scales, int64_t N,
+                                             int64_t K, const void* x, int64_t ldx, int64_t M, float* y,
+                                             int64_t ldy, int* err, float* rowsum_scratch, cudaStream_t stream);
+
+// Fixed scratch of bramha_cuda_gemm_noalloc_dev (noalloc.cu).
+constexpr int64_t kNoAllocMaxTokens = 16384;
+cudaError_t noalloc_rowsum_scratch(int device, float** out);
+
 // GPU packers (quant.cu).
 cudaError_t launch_quantize(int fmt, int64_t N, int64_t K, const float* w, uint8_t* q, float* scales,
                             cudaStream_t stream);

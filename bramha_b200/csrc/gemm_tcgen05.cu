@@ -548,4 +548,41 @@ cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const fl
     return e;
 }
 
+cudaError_t launch_gemm_tcgen05_bf16_noalloc(int fmt, const uint8_t* q, int64_t ldq, const float* scales, int64_t N,
+                                             int64_t K, const void* x, int64_t ldx, int64_t M, float* y,
+                                             int64_t ldy, int* err, float* rowsum_scratch, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return cudaSuccess;
+    if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff || K <= 0) return cudaErrorInvalidValue;
+    if ((ldx % 8) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0) return cudaErrorInvalidValue;
+    if (!encode_fn()) return cudaErrorNotSupported;
+    cudaError_t e = cudaSuccess;
+    float* rs = nullptr;
+    if (fmt == BRAMHA_FMT_LOG4) {
+        if (!rowsum_scratch) return cudaErrorInvalidValue;
+        rs = rowsum_scratch;
+        const int wpb = 8;
+        const unsigned blocks = (unsigned)((M + wpb - 1) / wpb);
+        // every one of the M sums is written here before the GEMM reads it
+        prep_kernel<false><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, K, nullptr, nullptr, rs, nullptr);
+        e = cudaGetLastError();
+    }
+    const int bn = gemm_tile_n(M);
+    CUtensorMap tmW, tmX;
+    if (e == cudaSuccess) e = make_w_map(&tmW, q, ldq, N, fmt);
+    if (e == cudaSuccess) e = make_x_map(&tmX, x, K, M, ldx, bn);
+    if (e != cudaSuccess) return e;
+    GemmArgs g;
+    g.scales = scales;
+    g.rowsum = rs;
+    g.y = y;
+    g.ldy = ldy;
+    g.M = (int)M;
+    g.N = (int)N;
+    g.K = (int)K;
+    g.k_steps = (int)((K + BK - 1) / BK);
+    g.accumulate = 0;
+    g.err = err;
+    return run_pass(fmt, bn, tmX, tmW, g, st);
+}
+
 }  // namespace bramha

@@ -167,6 +167,25 @@ BRAMHA_API int bramha_cuda_gemm(bramha_ctx* ctx, const bramha_weight* w, const f
 BRAMHA_API int bramha_cuda_gemm_dev(bramha_ctx* ctx, const bramha_weight* w, const void* x_dev, int x_dtype, int64_t M,
                          float* y_dev, void* stream);
 
+/* Allocation-free variant of bramha_cuda_gemm_dev, for callers that cannot let
+ * a library allocate device memory during a call -- for example an engine that
+ * reserves all of HBM for its own weight and KV-cache pools at start-up and
+ * must not grow the CUDA memory pool afterwards, or a latency-bound serving
+ * path where a pool growth could block.  It has no counterpart in the
+ * reference.  Same computation as bramha_cuda_gemm_dev with BF16 activations:
+ * x_dev is bf16 [M][K] (16-byte aligned, K a multiple of 8), y_dev f32 [M][N],
+ * stream-ordered.  Its only scratch (the per-token activation sums of the log4
+ * correction) lives in a fixed device array compiled into the library, sized
+ * for at most 16384 tokens: larger M is rejected with BRAMHA_ERR_UNSUPPORTED.
+ * The array is held by every GPU that loads the library until exit.  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress),
+ * so make that first call before any stream capture.  All calls share the one
+ * array (each call overwrites the sums it reads, nothing needs to start at
+ * zero): calls whose work overlaps on the GPU race with each other, so order
+ * them on one stream.  Int4 and int8 weights use no scratch at all. */
+BRAMHA_API int bramha_cuda_gemm_noalloc_dev(bramha_ctx* ctx, const bramha_weight* w, const void* x_dev, int64_t M,
+                                            float* y_dev, void* stream);
+
 /* Waits for `stream` (NULL = the context stream) and reports a failure that a
  * kernel recorded on the device: the tensor-core GEMM bounds every wait and
  * returns BRAMHA_ERR_TIMEOUT here instead of hanging.  Host-buffer calls

@@ -12,7 +12,7 @@ from bramha_b200 import _lib
 def test_library_exports_every_header_symbol():
     L = bb.lib()
     syms = bb.header_symbols()
-    assert len(syms) >= 20
+    assert len(syms) >= 21
     for s in syms:
         assert hasattr(L, s), s
     out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True).stdout
