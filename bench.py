@@ -218,6 +218,58 @@ def cpu_baseline_sample(fmt, batch, qs, seconds=8.0):
                       "matvec_mul_into (cpu_engine.rs:1307-1444) with log4 tables, OpenMP over rows"}
 
 
+# ------------------------------------------------------------------ prefill (config 3)
+QWEN05 = [("q", 896, 896), ("k", 128, 896), ("v", 128, 896), ("o", 896, 896), ("gate", 4864, 896),
+          ("up", 4864, 896), ("down", 896, 4864), ("lm_head", 151936, 896)]
+
+
+def prefill_bench(plane, dev, reps=10, m=2048):
+    """tcgen05 dequant-GEMM, M = 2048 bf16 tokens on the Qwen2-0.5B
+    linears (log4 and int8 weights ~N(0,0.02)); TFLOP/s = 2*M*N*K / CUDA-event time."""
+    import torch
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {"bf16_tflops": 1590.0}
+    out = {"workload": f"qwen2-0.5b linears, M={m} bf16 tokens", "peak_tflops": peaks["bf16_tflops"],
+           "peak_source": "measured bf16_tflops (burst)", "shapes": {}}
+    gen = torch.Generator(device=dev).manual_seed(5)
+    stream = torch.cuda.Stream(device=dev)
+    for fmt in ("log4", "w8"):
+        tot_flop, tot_ms = 0.0, 0.0
+        for name, n, k in QWEN05:
+            wf = torch.randn((n, k), generator=gen, device=dev) * 0.02
+            nb = n * k * (4 if fmt == "log4" else 8) // 8
+            qd = torch.empty(nb, dtype=torch.uint8, device=dev)
+            sd = torch.empty(n, dtype=torch.float32, device=dev)
+            plane.quantize_dev(fmt, wf, qd, sd)
+            del wf
+            w = plane.register_dev(f"pf:{fmt}:{name}", fmt, n, k, qd, sd)
+            x = torch.randn((m, k), generator=gen, device=dev).to(torch.bfloat16)
+            y = torch.empty((m, n), dtype=torch.float32, device=dev)
+            torch.cuda.synchronize()
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    plane.gemm_dev(w, x, y)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(reps):
+                    plane.gemm_dev(w, x, y)
+                e1.record()
+            torch.cuda.synchronize()
+            plane.stream_sync(stream)
+            ms = e0.elapsed_time(e1) / reps
+            flop = 2.0 * m * n * k
+            tot_flop += flop
+            tot_ms += ms
+            out["shapes"][f"{fmt}:{name}"] = {"n": n, "k": k, "us": round(ms * 1e3, 2),
+                                              "tflops": round(flop / (ms * 1e-3) / 1e12, 1)}
+            plane.evict(w.key)
+            del qd, sd, x, y
+        out[f"{fmt}_total_tflops"] = round(tot_flop / (tot_ms * 1e-3) / 1e12, 1)
+    lm = out["shapes"]["log4:lm_head"]["tflops"]
+    out["frac_lm_head_log4"] = round(lm / out["peak_tflops"], 3)
+    return out
+
+
 # ------------------------------------------------------------------ our arm
 def run_ours(args, ws, rank, local):
     import torch
@@ -276,15 +328,10 @@ def run_ours(args, ws, rank, local):
 
     stream = torch.cuda.Stream(device=dev)
 
-    def step(record=None):
+    def step():
         for entry in layers:
             for gname, wts, x, ys, y_full in entry:
-                if record is not None:
-                    record.append((gname, torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
-                    record[-1][1].record()
                 plane.gemv_multi_dev(wts, x, ys)
-                if record is not None:
-                    record[-1][2].record()
                 if ws > 1:
                     local_y = torch.cat([y.reshape(-1) for y in ys]) if len(ys) > 1 else ys[0].reshape(-1)
                     dist.all_gather_into_tensor(y_full.view(-1), local_y)
@@ -334,14 +381,31 @@ def run_ours(args, ws, rank, local):
         ms = float(t.item())
     value = step_bytes / (ms * 1e-3) / 1e9
 
-    # ---- per-launch durations (separate instrumented pass, same stream)
-    rec = []
-    with torch.cuda.stream(stream):
-        step(record=rec)
-    torch.cuda.synchronize()
+    # ---- per-launch durations: each group's launches (e.g. the 28 gate|up GEMVs)
+    # captured in their own CUDA graph and replayed, so host launch latency is
+    # not part of the measurement; mean device time per launch
+    groups = {}
+    for entry in layers:
+        for gname, wts, x, ys, _ in entry:
+            groups.setdefault(gname, []).append((wts, x, ys))
     per = {}
-    for gname, a, b in rec:
-        per.setdefault(gname, []).append(a.elapsed_time(b) * 1e3)
+    reps = 5
+    for gname, items in groups.items():
+        gg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gg, stream=stream):
+            for wts, x, ys in items:
+                plane.gemv_multi_dev(wts, x, ys)
+        gg.replay()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a_.record()
+            for _ in range(reps):
+                gg.replay()
+            b_.record()
+        torch.cuda.synchronize()
+        per[gname] = [a_.elapsed_time(b_) * 1e3 / (reps * len(items))] * len(items)
+        del gg
     group_bytes = {}
     for gname, parts, k in GROUPS + [("lm_head", [("lm_head", V)], H)]:
         nloc = sum(shard(n)[1] - shard(n)[0] for _, n in parts)
@@ -399,6 +463,10 @@ def run_ours(args, ws, rank, local):
         e2e_s = float(t.item())
     e2e_val = step_bytes / e2e_s / 1e9
 
+    prefill = None
+    if rank == 0 and ws == 1 and not args.no_prefill:
+        prefill = prefill_bench(plane, dev)
+
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_sample(fmt, B, layer0_host)
@@ -414,7 +482,8 @@ def run_ours(args, ws, rank, local):
                        "batch": B, "fmt": fmt, "hidden": H, "intermediate": I, "vocab": V, "layers": args.layers,
                        "parallelism": f"column-shard x{ws} + NCCL all-gather" if ws > 1 else "single GPU",
                        "l2": f"no flush: {step_bytes / 1e9:.2f} GB of packed weights per step >> 126 MB L2",
-                       "cuda_graph": graph is not None},
+                       "cuda_graph": graph is not None,
+                       "gemv_kernel": "tc_gemv_kernel (tcgen05, tile-major weights)"},
             "tokens_per_s": round(B * 1e3 / ms, 2),
             "gpu_launches": launches_per_step * args.steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -428,6 +497,7 @@ def run_ours(args, ws, rank, local):
                     "api": "bramha_cuda_gemv (host buffers, synchronous), one call per linear",
                     "tokens_per_s": round(B / e2e_s, 2)},
             "cpu_baseline": cpu,
+            "prefill": prefill,
             "setup_s": round(setup_s, 1),
         }
         print(json.dumps(line), flush=True)
@@ -446,6 +516,7 @@ def main():
     ap.add_argument("--fmt", choices=list(BITS), default="log4")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill GEMM measurement")
     ap.add_argument("--layers", type=int, default=LAYERS, help="decoder layers (smaller = profiling case)")
     args = ap.parse_args()
     ws, rank, local = dist_setup(args)

@@ -156,12 +156,16 @@ void evict_locked(bramha_ctx* ctx, const std::string& key) {
 
 void touch_locked(bramha_ctx* ctx, bramha_weight* w) { ctx->lru.splice(ctx->lru.end(), ctx->lru, w->lru_it); }
 
-// Allocates and uploads (H2D when host, D2D otherwise) into the padded layout.
+// Allocates and uploads (H2D when host, D2D otherwise) into the device
+// layout: quantized formats are tiled by a kernel (from a temporary
+// row-major copy when the source is in host memory); f32 rows are padded.
 int upload(bramha_ctx* ctx, bramha_weight* w, const void* q, const float* scales, bool from_device,
            cudaStream_t st) {
     w->row_bytes = row_bytes_of(w->fmt, w->K);
     w->ldq = pitch_of(w->row_bytes);
-    const size_t qbytes = (size_t)w->N * (size_t)w->ldq;
+    const bool tiled = is_tiled(w->fmt);
+    const size_t qbytes = tiled ? (size_t)tiled_bytes(w->fmt, w->N, held_columns(w->fmt, w->K))
+                                : (size_t)w->N * (size_t)w->ldq;
     const size_t sbytes = w->fmt == BRAMHA_FMT_F32 ? 0 : (size_t)w->N * sizeof(float);
     w->bytes = qbytes + sbytes;
     if (qbytes > 0) CK(cudaMalloc(&w->q, qbytes), "cudaMalloc(weight)");
@@ -174,16 +178,25 @@ int upload(bramha_ctx* ctx, bramha_weight* w, const void* q, const float* scales
     }
     const cudaMemcpyKind kind = from_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
     cudaError_t e = cudaSuccess;
-    if (qbytes > 0) {
+    uint8_t* staging = nullptr;
+    if (qbytes > 0 && tiled) {
+        const uint8_t* src = static_cast<const uint8_t*>(q);
+        const size_t raw = (size_t)w->N * (size_t)w->row_bytes;
+        if (!from_device && raw > 0) {
+            e = cudaMalloc(&staging, raw);
+            if (e == cudaSuccess) e = cudaMemcpyAsync(staging, q, raw, cudaMemcpyHostToDevice, st);
+            src = staging;
+        }
+        if (e == cudaSuccess) e = launch_tile_weights(w->fmt, src, w->row_bytes, w->N, w->K, w->q, st);
+    } else if (qbytes > 0) {
         if (w->ldq != w->row_bytes) e = cudaMemsetAsync(w->q, 0, qbytes, st);
         if (e == cudaSuccess && w->row_bytes > 0)
             e = cudaMemcpy2DAsync(w->q, (size_t)w->ldq, q, (size_t)w->row_bytes, (size_t)w->row_bytes,
                                   (size_t)w->N, kind, st);
     }
-    if (e == cudaSuccess && qbytes > 0 && (w->fmt == BRAMHA_FMT_W4ZP8 || w->fmt == BRAMHA_FMT_LOG4))
-        e = launch_repack_nibbles(w->q, (int64_t)qbytes, st);
     if (e == cudaSuccess && sbytes > 0) e = cudaMemcpyAsync(w->scales, scales, sbytes, kind, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (staging) cudaFree(staging);
     if (e != cudaSuccess) {
         free_weight_memory(w);
         return cuda_fail(e, "weight upload");
@@ -210,7 +223,8 @@ int register_impl(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t 
         *out = w;
         return BRAMHA_OK;
     }
-    const size_t need = (size_t)N * (size_t)pitch_of(row_bytes_of(fmt, K)) +
+    const size_t need = (is_tiled(fmt) ? (size_t)tiled_bytes(fmt, N, held_columns(fmt, K))
+                                       : (size_t)N * (size_t)pitch_of(row_bytes_of(fmt, K))) +
                         (fmt == BRAMHA_FMT_F32 ? 0 : (size_t)N * sizeof(float));
     // enforce_limits (wgpu_backend.rs:65-81): evict least recently used first.
     while (ctx->cap > 0 && ctx->used + need > ctx->cap && !ctx->lru.empty()) evict_locked(ctx, ctx->lru.front());
@@ -263,7 +277,7 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
         a.ldx = ldx;
         // Columns the packed rows actually hold: with odd K a nibble row has
         // K/2 bytes and the last activation is ignored (cpu_engine.rs:1364).
-        a.K = (int)((fmt == BRAMHA_FMT_W4ZP8 || fmt == BRAMHA_FMT_LOG4) ? (K / 2) * 2 : K);
+        a.K = (int)held_columns(fmt, K);
         a.batch = bc;
         a.nseg = 0;
         a.ldq_min = 0x7fffffff;
@@ -280,7 +294,11 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
             if (ws[i]->ldq < a.ldq_min) a.ldq_min = (int)ws[i]->ldq;
         }
         if (a.nseg == 0) return BRAMHA_OK;
-        CK(launch_gemv(fmt, a, ctx->num_sms, st), "gemv launch");
+        a.err = ctx->d_err;
+        if (is_tiled(fmt))
+            CK(launch_gemv_tc(fmt, a, ctx->num_sms, st), "tensor-core gemv launch");
+        else
+            CK(launch_gemv_f32(a, ctx->num_sms, st), "gemv launch");
     }
     return BRAMHA_OK;
 }

@@ -1,12 +1,14 @@
 // common.cuh -- definitions shared by the kernels and the C-ABI host code.
 //
-// Device weight layout (HBM): one buffer per registered weight, rows in the
-// reference's order, each row padded to a pitch `ldq` that is a multiple of 16
-// bytes so every 16-byte vector load is aligned.  Padding bytes are zero; the
-// kernels read the matching activation columns as zero, so padding contributes
-// nothing.  Int8 and f32 rows keep the reference's byte layout; the two 4-bit
-// formats are rearranged inside each 32-bit word (repack.cu): even columns in
-// bits 0-15, odd columns in bits 16-31.  Scales: f32 [N], one per output row.
+// Device weight layout (HBM), one buffer per registered weight:
+//  * quantized formats (int8, int4, log4): TILE-MAJOR (repack.cu) -- 128-row
+//    tiles cut into k-steps of 64 columns; block (tile t, step s) holds the 128
+//    row slices of those columns contiguously (32 bytes per row for 4-bit, 64
+//    for int8), so each pipeline stage is one contiguous 4 KB / 8 KB read.
+//    4-bit words are rearranged (even columns in bits 0-15, odd in 16-31).
+//    Rows past N and columns past K are zero.
+//  * dense f32: row-major, rows padded to a 16-byte pitch.
+// Scales: f32 [N], one per output row.
 #pragma once
 
 #include <cstdint>
@@ -16,7 +18,7 @@
 
 namespace bramha {
 
-constexpr int kMaxGemvBatch = 8;     // CUDA-core GEMV handles batch 1..8
+constexpr int kMaxGemvBatch = 8;     // GEMV kernels take batch 1..8 per launch
 constexpr int kMaxSegments = 8;      // weights fused into one GEMV launch
 
 // Bytes of one packed row (without padding) for a format.
@@ -31,9 +33,27 @@ inline int64_t row_bytes_of(int fmt, int64_t K) {
 }
 inline int64_t pitch_of(int64_t row_bytes) { return (row_bytes + 15) / 16 * 16; }
 
+// Tile-major layout of the quantized formats.
+constexpr int kTileRows = 128;   // rows per tile (= UMMA M)
+constexpr int kTileK = 64;       // columns per k-step
+__host__ __device__ constexpr int tile_slice_bytes(int fmt) {
+    return fmt == BRAMHA_FMT_W8 ? 64 : (fmt == BRAMHA_FMT_W4ZP8 || fmt == BRAMHA_FMT_LOG4) ? 32 : 0;
+}
+// K here is the number of columns the packed rows hold.
+__host__ __device__ constexpr int64_t k_steps(int64_t K) { return (K + kTileK - 1) / kTileK; }
+__host__ __device__ constexpr int64_t row_tiles(int64_t N) { return (N + kTileRows - 1) / kTileRows; }
+inline int64_t tiled_bytes(int fmt, int64_t N, int64_t K) {
+    return row_tiles(N) * k_steps(K) * kTileRows * tile_slice_bytes(fmt);
+}
+inline bool is_tiled(int fmt) { return tile_slice_bytes(fmt) > 0; }
+// Columns held by a packed row: K/2 bytes of 4-bit codes cover 2*(K/2) columns.
+inline int64_t held_columns(int fmt, int64_t K) {
+    return (fmt == BRAMHA_FMT_W4ZP8 || fmt == BRAMHA_FMT_LOG4) ? (K / 2) * 2 : K;
+}
+
 // One weight inside a (possibly fused) GEMV launch.
 struct GemvSeg {
-    const uint8_t* q;      // device rows, pitch ldq
+    const uint8_t* q;      // device weight: tile-major (quantized) or rows of pitch ldq (f32)
     const float* scales;   // [N]
     float* y;              // [batch][ldy]
     int64_t ldq;
@@ -53,13 +73,16 @@ struct GemvArgs {
     int nsteps;            // vector steps per row
     int ntiles;            // tiles over all segments
     uint32_t mul[8];       // log4: powers of two moving each code to bit 23 (set by the launcher)
+    int* err;              // device error word for bounded waits (tensor-core kernels)
 };
 
-// Launch a GEMV over the segments; chooses the tiling from the shape.
-cudaError_t launch_gemv(int fmt, const GemvArgs& a, int num_sms, cudaStream_t stream);
+// CUDA-core GEMV for dense f32 weights (gemv_f32.cu).
+cudaError_t launch_gemv_f32(const GemvArgs& a, int num_sms, cudaStream_t stream);
 
-// Rearranges 4-bit rows into the device word layout, in place (repack.cu).
-cudaError_t launch_repack_nibbles(uint8_t* q, int64_t nbytes, cudaStream_t stream);
+// Reference row-major packed rows (row_bytes per row) -> tile-major device
+// layout of tiled_bytes(fmt, N, held_columns(fmt, K)) bytes (repack.cu).
+cudaError_t launch_tile_weights(int fmt, const uint8_t* src, int64_t row_bytes, int64_t N, int64_t K, uint8_t* dst,
+                                cudaStream_t stream);
 
 // Prefill GEMM on tcgen05 (gemm_tcgen05.cu).  K = columns held by the packed
 // rows; x is bf16 (x_is_f32 = 0) or f32 (split into two bf16 passes).
@@ -77,6 +100,9 @@ cudaError_t launch_gemm_tcgen05_bf16_noalloc(int fmt, const uint8_t* q, int64_t 
 // Fixed scratch of bramha_cuda_gemm_noalloc_dev (noalloc.cu).
 constexpr int64_t kNoAllocMaxTokens = 16384;
 cudaError_t noalloc_rowsum_scratch(int device, float** out);
+
+// Tensor-core GEMV for the quantized formats, batch 1..8 (gemv_tc.cu).
+cudaError_t launch_gemv_tc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t stream);
 
 // GPU packers (quant.cu).
 cudaError_t launch_quantize(int fmt, int64_t N, int64_t K, const float* w, uint8_t* q, float* scales,

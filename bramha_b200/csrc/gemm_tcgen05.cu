@@ -11,8 +11,9 @@
 //
 // One CTA computes a 128 (weight rows) x BN (tokens) tile: D = W_tile * X_tile^T
 // ("weights as the M operand"), looping over K in steps of 64.
-//   warp 0      TMA producer: X tile (bf16, 128-byte swizzle) and the packed
-//               weight tile (raw bytes) per stage, mbarrier complete_tx.
+//   warp 0      TMA producer: X tile (bf16, 128-byte swizzle, tensor map) and
+//               the packed weight block (one contiguous bulk copy from the
+//               tile-major layout) per stage, mbarrier complete_tx.
 //   warp 1      allocates TMEM (BN fp32 columns), one lane issues tcgen05.mma
 //               (M=128, N=BN, K=16, both operands K-major SW128 in shared
 //               memory) and tcgen05.commit to release stages.
@@ -31,6 +32,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace bramha {
 namespace {
@@ -38,9 +40,9 @@ namespace {
 constexpr int BM = 128;          // weight rows per tile (UMMA M)
 constexpr int BK = 64;           // K per stage: 64 bf16 = 128 bytes = one swizzle row
 constexpr int kThreads = 192;    // 6 warps
-constexpr uint64_t kTimeoutNs = 2000000000ull;
 
 struct GemmArgs {
+    const uint8_t* q;      // tile-major weight (repack.cu)
     const float* scales;   // [N]
     const float* rowsum;   // [M] sum of the bf16 activations (log4 only)
     float* y;              // [M][ldy]
@@ -50,99 +52,6 @@ struct GemmArgs {
     int accumulate;        // 0: y = result, 1: y += result (second half of a hi/lo split)
     int* err;              // device error word (0 = ok)
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ uint64_t globaltimer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(b)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait for the phase with `parity` to complete.  On timeout (or when
-// another thread already gave up) records the error and returns false.
-__device__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err) {
-    if (mbar_try_wait(b, parity)) return true;
-    const uint64_t t0 = globaltimer();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(b, parity)) return true;
-        if ((i & 63) == 0) {
-            if (*abort_flag) return false;
-            if (globaltimer() - t0 > kTimeoutNs) {
-                *abort_flag = 1;
-                atomicCAS(err, 0, (int)BRAMHA_ERR_TIMEOUT);
-                return false;
-            }
-        }
-    }
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-            smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
-        : "memory");
-}
-
-// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (SBO), version 1 (sm_100).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
-           (2ull << 61);
-}
-// Instruction descriptor, kind::f16: D f32, A/B bf16, both K-major, N, M.
-template <int BN>
-__device__ __forceinline__ constexpr uint32_t idesc_bf16() {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
 
 // Packed weight bytes per row per stage.
 template <int FMT>
@@ -216,8 +125,7 @@ struct Layout {
 
 template <int FMT, int BN, int S>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                const __grid_constant__ GemmArgs a) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ GemmArgs a) {
     using L = Layout<FMT, BN, S>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -267,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (it >= S && !mbar_wait(&empty[s], ((it / S) & 1) ^ 1, abort_flag, a.err)) break;
                 mbar_expect_tx(&full_tma[s], kTx);
                 tma_load_2d(Xs + s * L::kX, &tmX, &full_tma[s], it * BK, m0);
-                tma_load_2d(Ps + s * L::kP, &tmW, &full_tma[s], it * packed_bytes<FMT>(), n0);
+                bulk_load(Ps + s * L::kP, a.q + ((int64_t)blockIdx.x * ksteps + it) * L::kP, L::kP, &full_tma[s]);
             }
             // drain: every issued copy has landed before the CTA can exit
             for (int j = (it > S ? it - S : 0); j < it; ++j)
@@ -276,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16<BN>();
+            constexpr uint32_t idesc = idesc_bf16<BM, BN>();
             for (int it = 0; it < ksteps; ++it) {
                 const int s = it % S;
                 const uint32_t ph = (it / S) & 1;
@@ -413,13 +321,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 template <int FMT, int BN, int S>
-cudaError_t launch_tiles(const CUtensorMap& tmX, const CUtensorMap& tmW, const GemmArgs& g, cudaStream_t st) {
+cudaError_t launch_tiles(const CUtensorMap& tmX, const GemmArgs& g, cudaStream_t st) {
     using L = Layout<FMT, BN, S>;
     auto kern = gemm_kernel<FMT, BN, S>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
     if (e != cudaSuccess) return e;
     dim3 grid((g.N + BM - 1) / BM, (g.M + BN - 1) / BN);
-    kern<<<grid, kThreads, L::kAlloc, st>>>(tmX, tmW, g);
+    kern<<<grid, kThreads, L::kAlloc, st>>>(tmX, g);
     return cudaGetLastError();
 }
 
@@ -434,12 +342,12 @@ constexpr int stages_for() {
 }
 
 template <int FMT>
-cudaError_t launch_fmt(int bn, const CUtensorMap& tmX, const CUtensorMap& tmW, const GemmArgs& g, cudaStream_t st) {
+cudaError_t launch_fmt(int bn, const CUtensorMap& tmX, const GemmArgs& g, cudaStream_t st) {
     switch (bn) {
-        case 256: return launch_tiles<FMT, 256, stages_for<FMT, 256>()>(tmX, tmW, g, st);
-        case 128: return launch_tiles<FMT, 128, stages_for<FMT, 128>()>(tmX, tmW, g, st);
-        case 64: return launch_tiles<FMT, 64, stages_for<FMT, 64>()>(tmX, tmW, g, st);
-        default: return launch_tiles<FMT, 32, stages_for<FMT, 32>()>(tmX, tmW, g, st);
+        case 256: return launch_tiles<FMT, 256, stages_for<FMT, 256>()>(tmX, g, st);
+        case 128: return launch_tiles<FMT, 128, stages_for<FMT, 128>()>(tmX, g, st);
+        case 64: return launch_tiles<FMT, 64, stages_for<FMT, 64>()>(tmX, g, st);
+        default: return launch_tiles<FMT, 32, stages_for<FMT, 32>()>(tmX, g, st);
     }
 }
 
@@ -459,23 +367,11 @@ cudaError_t make_x_map(CUtensorMap* m, const void* xg, int64_t K, int64_t M, int
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
-cudaError_t make_w_map(CUtensorMap* m, const uint8_t* q, int64_t ldq, int64_t N, int fmt) {
-    const int pb = fmt == BRAMHA_FMT_W8 ? BK : BK / 2;
-    cuuint64_t dims[2] = {(cuuint64_t)ldq, (cuuint64_t)N};
-    cuuint64_t strides[1] = {(cuuint64_t)ldq};
-    cuuint32_t box[2] = {(cuuint32_t)pb, (cuuint32_t)BM};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(q), dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
-}
-cudaError_t run_pass(int fmt, int bn, const CUtensorMap& tmX, const CUtensorMap& tmW, const GemmArgs& g,
-                     cudaStream_t st) {
+cudaError_t run_pass(int fmt, int bn, const CUtensorMap& tmX, const GemmArgs& g, cudaStream_t st) {
     switch (fmt) {
-        case BRAMHA_FMT_LOG4: return launch_fmt<BRAMHA_FMT_LOG4>(bn, tmX, tmW, g, st);
-        case BRAMHA_FMT_W4ZP8: return launch_fmt<BRAMHA_FMT_W4ZP8>(bn, tmX, tmW, g, st);
-        case BRAMHA_FMT_W8: return launch_fmt<BRAMHA_FMT_W8>(bn, tmX, tmW, g, st);
+        case BRAMHA_FMT_LOG4: return launch_fmt<BRAMHA_FMT_LOG4>(bn, tmX, g, st);
+        case BRAMHA_FMT_W4ZP8: return launch_fmt<BRAMHA_FMT_W4ZP8>(bn, tmX, g, st);
+        case BRAMHA_FMT_W8: return launch_fmt<BRAMHA_FMT_W8>(bn, tmX, g, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -521,14 +417,14 @@ cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const fl
         e = cudaGetLastError();
     }
     const int bn = gemm_tile_n(M);
-    CUtensorMap tmW;
-    if (e == cudaSuccess) e = make_w_map(&tmW, q, ldq, N, fmt);
+    if ((reinterpret_cast<uintptr_t>(q) & 15) != 0) e = cudaErrorInvalidValue;
     for (int pass = 0; pass < npass && e == cudaSuccess; ++pass) {
         const void* xg = need_copy ? static_cast<const void*>(xb[pass]) : x;
         CUtensorMap tmX;
         e = make_x_map(&tmX, xg, K, M, need_copy ? kp : ldx, bn);
         if (e != cudaSuccess) break;
         GemmArgs g;
+        g.q = q;
         g.scales = scales;
         g.rowsum = rs[pass];
         g.y = y;
@@ -539,7 +435,7 @@ cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const fl
         g.k_steps = (int)((K + BK - 1) / BK);
         g.accumulate = pass;
         g.err = err;
-        e = run_pass(fmt, bn, tmX, tmW, g, st);
+        e = run_pass(fmt, bn, tmX, g, st);
     }
     if (scratch) {
         cudaError_t e2 = cudaFreeAsync(scratch, st);
@@ -567,11 +463,12 @@ cudaError_t launch_gemm_tcgen05_bf16_noalloc(int fmt, const uint8_t* q, int64_t 
         e = cudaGetLastError();
     }
     const int bn = gemm_tile_n(M);
-    CUtensorMap tmW, tmX;
-    if (e == cudaSuccess) e = make_w_map(&tmW, q, ldq, N, fmt);
+    CUtensorMap tmX;
+    if (e == cudaSuccess && (reinterpret_cast<uintptr_t>(q) & 15) != 0) e = cudaErrorInvalidValue;
     if (e == cudaSuccess) e = make_x_map(&tmX, x, K, M, ldx, bn);
     if (e != cudaSuccess) return e;
     GemmArgs g;
+    g.q = q;
     g.scales = scales;
     g.rowsum = rs;
     g.y = y;
@@ -582,7 +479,7 @@ cudaError_t launch_gemm_tcgen05_bf16_noalloc(int fmt, const uint8_t* q, int64_t 
     g.k_steps = (int)((K + BK - 1) / BK);
     g.accumulate = 0;
     g.err = err;
-    return run_pass(fmt, bn, tmX, tmW, g, st);
+    return run_pass(fmt, bn, tmX, g, st);
 }
 
 }  // namespace bramha

@@ -1,14 +1,23 @@
-// repack.cu -- device word layout of the 4-bit formats.
+// repack.cu -- device layout of the quantized formats (done once, at registration).
 //
-// The reference packs two codes per byte, column 2i in the high nibble and
-// column 2i+1 in the low nibble (src/models/quantization.rs:74-78,
-// spanda-engine/src/lib.rs:335-339).  At registration each 32-bit word
-// (columns c0..c7) is rearranged in place so that the even columns c0,c2,c4,c6
-// occupy bits 0-15 and the odd columns c1,c3,c5,c7 bits 16-31, nibble j of
-// each half holding column 2j / 2j+1.  Column pairs (2j, 2j+1) are then 16 bits
-// apart, which lets the kernels build two dequantized values with one shift
-// and one logic operation (a bf16x2 pair for the tensor-core GEMM).  The
-// transform is a bijection on words; padding words (zero) stay zero.
+// The reference stores a quantized weight row-major: row j, then row j+1, with
+// two 4-bit codes per byte, column 2i in the high nibble and column 2i+1 in the
+// low nibble (src/models/quantization.rs:74-78, spanda-engine/src/lib.rs:335-339),
+// or one int8 per byte (quantization.rs:7-38).
+//
+// On the device the weight is TILE-MAJOR: 128-row tiles, each cut into k-steps
+// of 64 columns, and each (tile, k-step) block stored as 128 consecutive row
+// slices:
+//     block(t, s) = rows 128t .. 128t+127, columns 64s .. 64s+63
+//     offset      = (t * ksteps + s) * 128 * slice,  slice = 32 B (4-bit) / 64 B (int8)
+// so every pipeline stage of the kernels is ONE contiguous 4 KB (8 KB) read:
+// a single bulk copy, sequential DRAM pages.  Rows past N and columns past K
+// are zero (the kernels drop those rows and see zero activations there).
+//
+// 4-bit words are also rearranged inside each 32-bit word (columns c0..c7):
+// even columns c0,c2,c4,c6 in bits 0-15, odd columns c1,c3,c5,c7 in bits 16-31,
+// nibble j of each half = column 2j / 2j+1.  A column pair is then 16 bits
+// apart: one shift and one logic op give a bf16x2 pair.
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -27,20 +36,41 @@ __host__ __device__ inline uint32_t to_device_word(uint32_t w) {
     return e16 | (o16 << 16);
 }
 
-__global__ void repack_kernel(uint32_t* __restrict__ q, int64_t nwords) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nwords; i += (int64_t)gridDim.x * blockDim.x)
-        q[i] = to_device_word(q[i]);
+// One thread per 32-bit word of the tiled buffer.  `src` is the reference
+// row-major layout with `row_bytes` bytes per row (no alignment assumed).
+__global__ void tile_kernel(const uint8_t* __restrict__ src, int64_t row_bytes, int64_t N, int64_t ksteps,
+                            int slice, int nibbles, uint32_t* __restrict__ dst, int64_t nwords) {
+    const int words_per_slice = slice / 4;
+    for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < nwords; o += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t wi = o % words_per_slice;
+        const int64_t row_in_tile = (o / words_per_slice) % kTileRows;
+        const int64_t block = o / (words_per_slice * kTileRows);
+        const int64_t tile = block / ksteps, step = block % ksteps;
+        const int64_t row = tile * kTileRows + row_in_tile;
+        const int64_t b0 = step * slice + wi * 4;  // source byte offset in the row
+        uint32_t w = 0;
+        if (row < N) {
+            const uint8_t* r = src + row * row_bytes;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (b0 + i < row_bytes) w |= (uint32_t)r[b0 + i] << (8 * i);
+        }
+        dst[o] = nibbles ? to_device_word(w) : w;
+    }
 }
 
 }  // namespace
 
-cudaError_t launch_repack_nibbles(uint8_t* q, int64_t nbytes, cudaStream_t st) {
-    if (nbytes <= 0) return cudaSuccess;
-    if (nbytes % 4) return cudaErrorInvalidValue;  // rows are padded to 16 bytes
+cudaError_t launch_tile_weights(int fmt, const uint8_t* src, int64_t row_bytes, int64_t N, int64_t K, uint8_t* dst,
+                                cudaStream_t st) {
+    const int slice = tile_slice_bytes(fmt);
+    if (slice <= 0) return cudaErrorInvalidValue;
+    const int64_t nbytes = tiled_bytes(fmt, N, K);
+    if (nbytes == 0) return cudaSuccess;
     const int64_t nwords = nbytes / 4;
     const int64_t blocks = (nwords + 255) / 256;
-    repack_kernel<<<(unsigned)(blocks < 65535 * 8 ? blocks : 65535 * 8), 256, 0, st>>>(reinterpret_cast<uint32_t*>(q),
-                                                                                      nwords);
+    tile_kernel<<<(unsigned)(blocks < 65535 * 8 ? blocks : 65535 * 8), 256, 0, st>>>(
+        src, row_bytes, N, k_steps(K), slice, fmt != BRAMHA_FMT_W8, reinterpret_cast<uint32_t*>(dst), nwords);
     return cudaGetLastError();
 }
 
