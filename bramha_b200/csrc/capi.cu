@@ -53,6 +53,8 @@ struct bramha_ctx {
     float* dev_y = nullptr;
     size_t dev_x_cap = 0, dev_y_cap = 0;
     int* d_err = nullptr;                // device error word written by bounded waits
+    float* split_ws = nullptr;           // K-split partials of the tensor-core GEMV
+    int* split_tickets = nullptr;        // per-tile arrival counters (kept zero between launches)
 };
 
 namespace {
@@ -295,6 +297,10 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
         }
         if (a.nseg == 0) return BRAMHA_OK;
         a.err = ctx->d_err;
+        a.split_ws = ctx->split_ws;
+        a.split_ws_floats = kSplitWsFloats;
+        a.split_tickets = ctx->split_tickets;
+        a.split_tickets_n = kSplitTickets;
         if (is_tiled(fmt))
             CK(launch_gemv_tc(fmt, a, ctx->num_sms, st), "tensor-core gemv launch");
         else
@@ -310,6 +316,8 @@ int check_device_error(bramha_ctx* ctx, cudaStream_t st) {
     CK(cudaStreamSynchronize(st), "stream sync");
     if (h != 0) {
         cudaMemsetAsync(ctx->d_err, 0, sizeof(int), st);
+        // an aborted launch may leave K-split tickets taken
+        cudaMemsetAsync(ctx->split_tickets, 0, sizeof(int) * (size_t)kSplitTickets, st);
         cudaStreamSynchronize(st);
         return fail(h == BRAMHA_ERR_TIMEOUT ? BRAMHA_ERR_TIMEOUT : BRAMHA_ERR_CUDA,
                     "a kernel gave up a bounded wait (device error word %d)", h);
@@ -425,10 +433,16 @@ int bramha_cuda_init(int device, bramha_ctx** out) {
     }
     e = cudaMalloc(&ctx->d_err, sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->split_ws, sizeof(float) * (size_t)kSplitWsFloats);
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->split_tickets, sizeof(int) * (size_t)kSplitTickets);
+    if (e == cudaSuccess) e = cudaMemset(ctx->split_tickets, 0, sizeof(int) * (size_t)kSplitTickets);
     if (e != cudaSuccess) {
+        if (ctx->d_err) cudaFree(ctx->d_err);
+        if (ctx->split_ws) cudaFree(ctx->split_ws);
+        if (ctx->split_tickets) cudaFree(ctx->split_tickets);
         cudaStreamDestroy(ctx->stream);
         delete ctx;
-        return cuda_fail(e, "cudaMalloc(error word)");
+        return cuda_fail(e, "cudaMalloc(context scratch)");
     }
     *out = ctx;
     return BRAMHA_OK;
@@ -451,6 +465,8 @@ int bramha_cuda_destroy(bramha_ctx* ctx) {
     if (ctx->dev_x) cudaFree(ctx->dev_x);
     if (ctx->dev_y) cudaFree(ctx->dev_y);
     if (ctx->d_err) cudaFree(ctx->d_err);
+    if (ctx->split_ws) cudaFree(ctx->split_ws);
+    if (ctx->split_tickets) cudaFree(ctx->split_tickets);
     cudaStreamDestroy(ctx->stream);
     delete ctx;
     return BRAMHA_OK;

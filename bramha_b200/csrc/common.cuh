@@ -74,7 +74,16 @@ struct GemvArgs {
     int ntiles;            // tiles over all segments
     uint32_t mul[8];       // log4: powers of two moving each code to bit 23 (set by the launcher)
     int* err;              // device error word for bounded waits (tensor-core kernels)
+    // K-split combine of the tensor-core GEMV (context-owned): per-split
+    // partial results and per-tile arrival tickets (zero between launches)
+    float* split_ws;
+    int64_t split_ws_floats;
+    int* split_tickets;
+    int split_tickets_n;
 };
+
+constexpr int64_t kSplitWsFloats = 8 << 20;   // 32 MB of partial results per context
+constexpr int kSplitTickets = 1 << 18;         // tiles per launch that may be K-split
 
 // CUDA-core GEMV for dense f32 weights (gemv_f32.cu).
 cudaError_t launch_gemv_f32(const GemvArgs& a, int num_sms, cudaStream_t stream);

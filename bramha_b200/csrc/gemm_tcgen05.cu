@@ -213,7 +213,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if constexpr (FMT == BRAMHA_FMT_W8) {
 #pragma unroll
                 for (int h = 0; h < 4; ++h) {
-                    const uint4 p = *reinterpret_cast<const uint4*>(prow + 16 * h);
+                    // int8 slices are stored 64-byte-swizzled (repack.cu)
+                    const uint4 p = *reinterpret_cast<const uint4*>(prow + 16 * (h ^ ((row >> 1) & 3)));
                     const int c0 = 2 * h, c1 = 2 * h + 1;
                     *reinterpret_cast<uint4*>(arow + ((c0 ^ (row & 7)) << 4)) = dq_int8(p.x, p.y);
                     *reinterpret_cast<uint4*>(arow + ((c1 ^ (row & 7)) << 4)) = dq_int8(p.z, p.w);

@@ -1,38 +1,53 @@
-// gemv_tc.cu -- decode GEMV for the quantized formats (batch 1..8) with the
-// multiply-accumulate on the tensor cores and only the dequantization on the
-// CUDA cores.
+// gemv_tc.cu -- decode GEMV for the quantized formats (batch 1..8) on the
+// tensor cores, with 8-bit operands.
 //
 // Same result as `matvec_mul_into` (src/inference/cpu_engine.rs:1307-1444) on
 // int4 (quantize_to_int4, src/models/quantization.rs:41-83), int8
 // (quantize_to_int8, :7-38) or log4 (dequantize_log4,
 // spanda-engine/src/lib.rs:332-342) weights.
 //
-// Why tensor cores for a bandwidth-bound GEMV: dequantizing on CUDA cores and
-// accumulating with FMAs costs >= 2.6 issue slots per 4-bit code for log4,
-// which at full HBM bandwidth is ~94% of an SM's issue rate (ncu measured 4.4
-// on the CUDA-core kernel).  Here the CUDA cores only turn two codes into a
-// bf16 pair (one shift + one logic op), the pairs go to TMEM with tcgen05.st,
-// and tcgen05.mma (A = weights in TMEM, B = activations in shared memory)
-// does the products, so the decode costs ~1 issue slot per code.
+// A tcgen05.mma with M = 128 costs the same ~51 cycles for any N <= 64, so a
+// GEMV (N = batch) is bound by how many MMAs its weight bytes need.  8-bit
+// operands take K = 32 per MMA, half the MMAs of bf16 (K = 16):
+//   int8  (W8)    kind::i8, A = the int8 block exactly as stored (the repack
+//                 writes it in the 64-byte-swizzle operand order), read by the
+//                 MMA straight from the shared-memory ring: no dequantization.
+//   int4  (W4ZP8) kind::i8, A = u8 q (0..15) in TMEM: one mask per 4 codes.
+//   log4          kind::f8f6f4, A = e5m2 2^(c-14) in TMEM (exact; byte
+//                 (c+1)*4): one mask + one multiply-add per 4 codes.
+// The weights are exact in these types.  The activations become B columns of
+// several 8-bit terms per batch row, scaled per row by a power of two s chosen
+// from max|x| over the CTA's K range:
+//   int8 terms: x*s = t1 + t2/128 + t3/16384 (abs. error <= 2^-22 max|x|),
+//               integer accumulation, exact;
+//   e4m3 terms: x*s = t1 + t2/16 + t3/256 + t4/4096 (rel. error ~2^-16),
+//               fp32 accumulation.
+// The epilogue folds the terms, the zero points (int4 -8, log4 -1, with the
+// row's sum(x)) and the row scale.
 //
-// Exactness: weights are exact in bf16 (log4 -> 2^(c-15), int4 -> 128 + q,
-// both corrected in the epilogue with sum(x)); each activation is split into
-// bf16 hi + lo (x = hi + lo to ~2^-16), so batch row b uses B columns 2b and
-// 2b+1 of the N = 16 MMA and results match fp32 to ~1e-5.
-//
-// Tile: 128 weight rows x a K-range.  grid = (tiles over all fused weights,
-// ksplit); with ksplit > 1 the partial results of a tile are added into y
-// (zeroed first) with fp32 atomics.
-//   warp 0      bulk copy: one contiguous (tile, k-step) block of the tile-major
-//               weight per step (4 KB 4-bit / 8 KB int8) into a 64 KB ring
-//   warp 1      TMEM alloc; lane 0 issues tcgen05.mma (kind::f16, M=128, N=16)
-//   warp 2      activations: f32 -> bf16 hi/lo B tile (128-byte swizzle), sum(x)
-//   warps 4-11  dequantize: two groups take alternate steps; per row 64 codes
-//               -> 32 bf16 pairs -> tcgen05.st (store wait overlapped)
-//   warps 4-7   epilogue: tcgen05.ld of the accumulator, scale, store
-// All mbarrier waits are bounded (tc_common.cuh).
+// Work: 128-row tiles of the tile-major weight (repack.cu) x a K range (a
+// "split").  One persistent CTA per SM; grid = ksplit x CTAs per split; a CTA
+// walks the tiles of its split back to back.  With ksplit > 1 each split
+// writes its partial tile result to a context-owned workspace and takes a
+// ticket; the last split to arrive adds the partials in split order and writes
+// y, so results do not depend on timing.  A ring slot is 8 KB: two
+// 64-column blocks of a 4-bit tile (K = 128) or one int8 block (K = 64).
+//   warp 0       bulk copy into the 128 KB ring (16 slots)
+//   warp 1       TMEM alloc; lane 0 issues the MMAs (M=128, N=16/32, K=32)
+//   warps 4-19   (4-bit) dequantize: four groups take slots g, g+4, ...; a
+//                warp owns one TMEM lane quarter: 128 codes per row -> 32
+//                words -> one tcgen05.st into one of 14 A stages
+//   warps 20-23  epilogue: tcgen05.ld of the finished (double-buffered)
+//                accumulator, fold, scale, store
+//   all warps    prologue: the split's activations are loaded once (ahead of
+//                the weight stream, staged raw in the ring's tail), reduced to
+//                max|x| and sum(x), and written as 8-bit B terms (K-major,
+//                128-byte swizzle, one 128-column atom per 128 K).
+// Every mbarrier wait is bounded (tc_common.cuh).
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -44,16 +59,35 @@
 namespace bramha {
 namespace {
 
-constexpr int TM = 128;                  // weight rows per tile (UMMA M)
-constexpr int TK = 64;                   // K per step (4 x UMMA K=16)
-constexpr int TN = 16;                   // UMMA N: x_hi / x_lo for up to 8 batch rows
-constexpr int kRingBytes = 64 * 1024;    // packed weight ring in shared memory
-constexpr int kSX = 8;                   // activation stages
-constexpr int kSA = 6;                   // dequantized stages in TMEM (32 columns each)
-constexpr int kDCol = 0;                 // accumulator columns [0, 16)
-constexpr int kACol = 32;                // A stages from column 32
-constexpr int kTmemCols = 256;
-constexpr int kThreads = 384;            // 12 warps
+constexpr int TM = 128;                   // weight rows per tile (UMMA M)
+constexpr int kSlotBytes = 8192;
+constexpr int kSW = 16;                   // ring slots
+constexpr int kFirstFill = 4;             // slots requested before the prologue
+constexpr int kStageFloats = (kSW - kFirstFill) * kSlotBytes / 4;  // raw activation staging
+constexpr int kSA = 14;                   // A stages in TMEM (4-bit), 32 columns each
+constexpr int kACol = 64;                 // A stages from column 64; accumulators at 0 / 32
+constexpr int kGroups = 4;                // dequant groups (4 warps each)
+constexpr int kDeqWarp0 = 4;
+constexpr int kEpiWarp0 = kDeqWarp0 + 4 * kGroups;  // 20
+constexpr int kThreads = (kEpiWarp0 + 4) * 32;      // 768
+constexpr int kXBytes = 64 * 1024;        // B terms of one split
+static_assert(kACol + kSA * 32 <= 512, "TMEM columns");
+static_assert(kSW % kGroups == 0, "a ring slot must always belong to the same dequant group");
+
+// Per-format constants.
+template <int FMT>
+struct F {
+    static constexpr bool kDeq = FMT != BRAMHA_FMT_W8;          // A through TMEM
+    static constexpr int kStepsPerSlot = kDeq ? 2 : 1;           // 64-column blocks per slot
+    static constexpr int kBlock = kTileRows * tile_slice_bytes(FMT);  // 4 KB / 8 KB
+    static constexpr int kMmaPerSlot = kDeq ? 4 : 2;             // K = 32 each
+    static constexpr int kTerms = FMT == BRAMHA_FMT_LOG4 ? 4 : 3;
+};
+template <int FMT, int B>
+struct NB {
+    static constexpr int N = (B * F<FMT>::kTerms <= 16) ? 16 : 32;  // MMA N (B columns)
+    static constexpr int kXSlot = N * 128;                           // B bytes per 128 K
+};
 
 struct TcSeg {
     const uint8_t* q;      // tile-major weight (repack.cu)
@@ -72,31 +106,24 @@ struct TcGemvParams {
     int nseg;
     int ntiles;
     int K;                 // columns held by the packed rows
-    int ksteps;            // ceil(K / 64)
+    int ksteps;            // 64-column blocks per tile row
     int steps_per_split;
-    int atomic_out;        // 1 when gridDim.y > 1
+    int ctas_per_split;
+    int ksplit;
+    float* ws;             // [ntiles][ksplit][B][128] partials (ksplit > 1)
+    int* tickets;          // [ntiles] arrivals, zero between launches
 };
 
-// Per-format stage geometry: one stage = one (tile, k-step) block of the
-// tile-major layout, read with a single bulk copy.
-template <int FMT>
-struct Geo {
-    static constexpr int kSlice = tile_slice_bytes(FMT);  // bytes per row per step
-    static constexpr int kStage = TM * kSlice;            // 4 KB (4-bit) / 8 KB (int8)
-    static constexpr int kSW = kRingBytes / kStage;       // ring depth
-};
-
-template <int FMT>
-struct TcSmem {
-    uint8_t w[Geo<FMT>::kSW][Geo<FMT>::kStage];
-    uint8_t x[kSX][TN * 128];            // 2 KB each, SW128 K-major (rows 2B..15 stay zero)
-    uint64_t w_full[Geo<FMT>::kSW], w_empty[Geo<FMT>::kSW];
-    uint64_t x_full[kSX], x_empty[kSX];
+struct alignas(1024) TcSmem {
+    uint8_t w[kSW][kSlotBytes];
+    uint8_t x[kXBytes];
+    uint64_t w_full[kSW], w_empty[kSW];
     uint64_t a_full[kSA], a_empty[kSA];
-    uint64_t acc_full, sx_ready;
-    float sx[8];
+    uint64_t acc_full[2], d_empty[2], mma_done;
+    float amax[8], sx[8], inv_s[8];
     uint32_t tmem;
     int abort_flag;
+    int last_split;
 };
 
 // Every lane polls; the warp proceeds only if all lanes saw the phase (so the
@@ -106,101 +133,243 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     return __all_sync(0xffffffffu, ok);
 }
 
-// Two 4-bit codes per bf16x2 pair (device word layout, repack.cu): even
-// columns in bits 0-15, odd in 16-31.  log4 -> 2^(c-15); int4 -> 128 + q.
+// UMMA descriptor, K-major: 128-byte swizzle (B terms, 8-row groups 1 KB
+// apart) or 64-byte swizzle (int8 weight blocks, 8-row groups 512 B apart).
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+__device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | ((uint64_t)(512 >> 4) << 32) | (1ull << 46) |
+           (4ull << 61);
+}
+
+// Instruction descriptors (M = 128): kind::i8 (D s32, A u8/s8, B s8) and
+// kind::f8f6f4 (D f32, A e5m2, B e4m3).
+template <int FMT, int N>
+__device__ __forceinline__ constexpr uint32_t idesc8() {
+    constexpr uint32_t mn = ((uint32_t)(N >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+    if constexpr (FMT == BRAMHA_FMT_LOG4) return (1u << 4) | (1u << 7) | (0u << 10) | mn;
+    else if constexpr (FMT == BRAMHA_FMT_W4ZP8) return (2u << 4) | (0u << 7) | (1u << 10) | mn;
+    else return (2u << 4) | (1u << 7) | (1u << 10) | mn;
+}
+
 template <int FMT>
-__device__ __forceinline__ void dq_word(uint32_t w, uint32_t* o) {
-    if constexpr (FMT == BRAMHA_FMT_LOG4) {
-        constexpr uint32_t M = 0x07800780u, E = 0x38003800u;
-        o[0] = ((w << 7) & M) | E;
-        o[1] = ((w << 3) & M) | E;
-        o[2] = ((w >> 1) & M) | E;
-        o[3] = ((w >> 5) & M) | E;
-    } else {
-        constexpr uint32_t M = 0x000F000Fu, E = 0x43004300u;
-        o[0] = (w & M) | E;
-        o[1] = ((w >> 4) & M) | E;
-        o[2] = ((w >> 8) & M) | E;
-        o[3] = ((w >> 12) & M) | E;
+__device__ __forceinline__ void mma8(uint32_t d, uint32_t a_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                     uint32_t acc) {
+    if constexpr (FMT == BRAMHA_FMT_LOG4)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+            "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc)
+            : "memory");
+    else if constexpr (FMT == BRAMHA_FMT_W4ZP8)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+            "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc)
+            : "memory");
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc)
+            : "memory");
+}
+
+// One device word (8 codes; repack.cu) -> two words of four 8-bit A values,
+// K order (c0, c4, c1, c5) and (c2, c6, c3, c7).
+template <int FMT>
+__device__ __forceinline__ void dq_word8(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    constexpr uint32_t M = 0x0F0F0F0Fu;
+    if constexpr (FMT == BRAMHA_FMT_LOG4) {  // e5m2 byte (c + 1) * 4 = 2^(c - 14)
+        lo = (w & M) * 4u + 0x04040404u;
+        hi = ((w >> 2) & 0x3C3C3C3Cu) + 0x04040404u;
+    } else {                                 // u8 q
+        lo = w & M;
+        hi = (w >> 4) & M;
     }
 }
 
-// int8 -> bf16 pair: bytes of u are q + 128; 0x4B000000 | byte is 2^23 + q + 128.
-__device__ __forceinline__ uint32_t i8_pair(uint32_t u, uint32_t sel_lo, uint32_t sel_hi) {
-    const float a = __uint_as_float(__byte_perm(u, 0x4Bu, sel_lo)) - 8388736.0f;
-    const float b = __uint_as_float(__byte_perm(u, 0x4Bu, sel_hi)) - 8388736.0f;
-    __nv_bfloat162 r = __floats2bfloat162_rn(a, b);  // |q| <= 127: exact
-    return *reinterpret_cast<uint32_t*>(&r);
-}
-
-// A row's 64 codes of one step -> 32 bf16 pairs.
+// Position p of a 128-K B atom <-> column of the K range: 4-bit A words hold
+// their codes in the order above, int8 A in natural order.
 template <int FMT>
-__device__ __forceinline__ void dq_row(const uint8_t* slice, uint32_t (&v)[32]) {
-    if constexpr (FMT == BRAMHA_FMT_W8) {
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-            const uint4 p = *reinterpret_cast<const uint4*>(slice + 16 * h);
-            const uint32_t wv[4] = {p.x ^ 0x80808080u, p.y ^ 0x80808080u, p.z ^ 0x80808080u, p.w ^ 0x80808080u};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                v[8 * h + 2 * i] = i8_pair(wv[i], 0x4550, 0x4551);
-                v[8 * h + 2 * i + 1] = i8_pair(wv[i], 0x4552, 0x4553);
-            }
-        }
-    } else {
-        const uint4 p0 = *reinterpret_cast<const uint4*>(slice);
-        const uint4 p1 = *reinterpret_cast<const uint4*>(slice + 16);
-        dq_word<FMT>(p0.x, v + 0);
-        dq_word<FMT>(p0.y, v + 4);
-        dq_word<FMT>(p0.z, v + 8);
-        dq_word<FMT>(p0.w, v + 12);
-        dq_word<FMT>(p1.x, v + 16);
-        dq_word<FMT>(p1.y, v + 20);
-        dq_word<FMT>(p1.z, v + 24);
-        dq_word<FMT>(p1.w, v + 28);
+__device__ __forceinline__ int pos_to_col(int p) {
+    if constexpr (FMT == BRAMHA_FMT_W8) return p;
+    else {
+        const int m = p & 7;
+        return (p & ~7) + ((m >> 1) | ((m & 1) << 2));  // 0,4,1,5,2,6,3,7
     }
 }
 
-template <int FMT, int B>
-__global__ void __launch_bounds__(kThreads, 2) tc_gemv_kernel(const __grid_constant__ TcGemvParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    using G = Geo<FMT>;
-    constexpr int kSW = G::kSW;
-    TcSmem<FMT>& S = *reinterpret_cast<TcSmem<FMT>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    volatile int* abort_flag = &S.abort_flag;
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile = blockIdx.x;
+__device__ __forceinline__ int seg_of(const TcGemvParams& p, int tile) {
     int si = 0;
     for (int i = 1; i < p.nseg; ++i)
         if (tile >= p.seg[i].tile_begin) si = i;
-    const TcSeg& sg = p.seg[si];
-    const int row0 = (tile - sg.tile_begin) * TM;  // first row inside weight si
-    const int step0 = blockIdx.y * p.steps_per_split;
-    const int nsteps = min(p.steps_per_split, p.ksteps - step0);
+    return si;
+}
 
+__device__ __forceinline__ float e4m3_value(__nv_fp8_storage_t b) {
+    return __half2float(__half(__nv_cvt_fp8_to_halfraw(b, __NV_E4M3)));
+}
+
+template <int FMT, int B>
+__global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_constant__ TcGemvParams p) {
+    using Fm = F<FMT>;
+    constexpr int N = NB<FMT, B>::N;
+    constexpr int kXSlot = NB<FMT, B>::kXSlot;
+    constexpr int T = Fm::kTerms;
+    extern __shared__ uint8_t smem_raw[];
+    TcSmem& S = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    volatile int* abort_flag = &S.abort_flag;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int split = blockIdx.x / p.ctas_per_split;
+    const int ci = blockIdx.x % p.ctas_per_split;
+    const int step0 = split * p.steps_per_split;
+    const int nsteps = min(p.steps_per_split, p.ksteps - step0);          // 64-column blocks per tile
+    const int nslots = (nsteps + Fm::kStepsPerSlot - 1) / Fm::kStepsPerSlot;
+    const int nkb = (nsteps + 1) >> 1;                                     // 128-K B atoms
+    const int ntile_cta = (p.ntiles - 1 - ci) / p.ctas_per_split + 1;       // ci < ntiles (host)
+    const int total = ntile_cta * nslots;                                  // slots this CTA streams
+    const int k0 = step0 * kTileK;                                         // first column of the split
+    const int nk = nsteps * kTileK;                                        // columns of the split
+
+    // source and size of this CTA's g-th slot
+    auto slot_src = [&](int g, uint32_t& bytes) -> const uint8_t* {
+        const int i = g / nslots, j = g - i * nslots;
+        const int tile = ci + i * p.ctas_per_split;
+        const TcSeg& sg = p.seg[seg_of(p, tile)];
+        const int s = j * Fm::kStepsPerSlot;
+        bytes = (uint32_t)(min(Fm::kStepsPerSlot, nsteps - s) * Fm::kBlock);
+        return sg.q + ((int64_t)(tile - sg.tile_begin) * p.ksteps + step0 + s) * Fm::kBlock;
+    };
+
+    // ---------------- prologue 1: barriers, TMEM, zeroed B area
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSW; ++s) {
             mbar_init(&S.w_full[s], 1);
-            mbar_init(&S.w_empty[s], 4);
-        }
-        for (int s = 0; s < kSX; ++s) {
-            mbar_init(&S.x_full[s], 1);
-            mbar_init(&S.x_empty[s], 1);
+            mbar_init(&S.w_empty[s], Fm::kDeq ? 4 : 1);
         }
         for (int s = 0; s < kSA; ++s) {
             mbar_init(&S.a_full[s], 4);
             mbar_init(&S.a_empty[s], 1);
         }
-        mbar_init(&S.acc_full, 1);
-        mbar_init(&S.sx_ready, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&S.acc_full[i], 1);
+            mbar_init(&S.d_empty[i], 4);
+        }
+        mbar_init(&S.mma_done, 1);
+        for (int b = 0; b < 8; ++b) {
+            S.amax[b] = 0.f;
+            S.sx[b] = 0.f;
+        }
         S.abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    // zero the activation tiles once: rows >= 2B are never written again
-    for (int i = threadIdx.x; i < kSX * TN * 128 / 16; i += kThreads)
-        reinterpret_cast<uint4*>(&S.x[0][0])[i] = make_uint4(0, 0, 0, 0);
-    if (warp == 1) tmem_alloc(&S.tmem, kTmemCols);
+    if (warp == 1) tmem_alloc(&S.tmem, 512);
+    {
+        uint4* xz = reinterpret_cast<uint4*>(&S.x[0]);
+        const int nz = nkb * kXSlot / 16;
+        for (int i = threadIdx.x; i < nz; i += kThreads) xz[i] = make_uint4(0, 0, 0, 0);
+    }
+
+    // ---------------- prologue 2: activations -> staging (ring tail), max|x|, sum(x)
+    // The loads are issued before the first weight copies so they do not
+    // queue behind them.
+    float* stage = reinterpret_cast<float*>(&S.w[kFirstFill][0]);
+    {
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            const float* xr = p.x + (int64_t)b * p.ldx + k0;
+            const int kv = min(nk, p.K - k0);  // valid columns
+            float am = 0.f, sm = 0.f;
+#pragma unroll 4
+            for (int k = threadIdx.x; k < nk; k += kThreads) {
+                const float v = k < kv ? __ldg(xr + k) : 0.f;
+                stage[b * nk + k] = v;
+                am = fmaxf(am, fabsf(v));
+                sm += v;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+                sm += __shfl_xor_sync(0xffffffffu, sm, o);
+            }
+            if (lane == 0) {
+                atomicMax(reinterpret_cast<int*>(&S.amax[b]), __float_as_int(am));  // am >= 0
+                atomicAdd(&S.sx[b], sm);
+            }
+        }
+    }
+    __syncthreads();
+    const int first = min(kFirstFill, total);
+    if (threadIdx.x == 0)
+        for (int g = 0; g < first; ++g) {
+            uint32_t bytes;
+            const uint8_t* src = slot_src(g, bytes);
+            mbar_expect_tx(&S.w_full[g], bytes);
+            bulk_load(&S.w[g][0], src, bytes, &S.w_full[g]);
+        }
+
+    // ---------------- prologue 3: B terms
+    {
+        float scl[B];
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            // s = 2^e with max|x*s| < 128 (int8 terms) or < 256 (e4m3 terms)
+            const float am = S.amax[b];
+            float s = 1.f;
+            if (am > 0.f) {
+                const int e = ((__float_as_int(am) >> 23) & 0xFF) - 127;  // am in [2^e, 2^(e+1))
+                s = ldexpf(1.f, min((FMT == BRAMHA_FMT_LOG4 ? 7 : 6) - e, 126));
+                if (FMT != BRAMHA_FMT_LOG4 && am * s >= 127.5f) s *= 0.5f;
+            }
+            scl[b] = s;
+            if (threadIdx.x == 0) S.inv_s[b] = 1.f / s;
+        }
+        const int npos4 = nkb * 32;  // 4-position groups
+        for (int i = threadIdx.x; i < B * npos4; i += kThreads) {
+            const int b = i / npos4, g4 = i - b * npos4;
+            const int p0 = g4 * 4;                      // position in the split
+            const int kb = p0 >> 7, pin = p0 & 127;     // atom, position in the atom
+            float s = scl[0];
+#pragma unroll
+            for (int bb = 1; bb < B; ++bb)
+                if (b == bb) s = scl[bb];
+            uint32_t word[T];
+#pragma unroll
+            for (int j = 0; j < T; ++j) word[j] = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int col = (kb << 7) + pos_to_col<FMT>(pin + e);
+                const float v = col < nk ? stage[b * nk + col] : 0.f;
+                float a = v * s;
+                if constexpr (FMT == BRAMHA_FMT_LOG4) {
+#pragma unroll
+                    for (int j = 0; j < T; ++j) {
+                        const __nv_fp8_storage_t t = __nv_cvt_float_to_fp8(a, __NV_SATFINITE, __NV_E4M3);
+                        word[j] |= (uint32_t)t << (8 * e);
+                        a = (a - e4m3_value(t)) * 16.f;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < T; ++j) {
+                        const int t = __float2int_rn(a);
+                        word[j] |= (uint32_t)(t & 0xFF) << (8 * e);
+                        a = (a - (float)t) * 128.f;
+                    }
+                }
+            }
+            uint8_t* atom = &S.x[kb * kXSlot];
+#pragma unroll
+            for (int j = 0; j < T; ++j) {
+                const int n = b * T + j;
+                *reinterpret_cast<uint32_t*>(atom + (n >> 3) * 1024 + (n & 7) * 128 + (((pin >> 4) ^ (n & 7)) << 4) +
+                                             (pin & 15)) = word[j];
+            }
+        }
+    }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -208,154 +377,182 @@ __global__ void __launch_bounds__(kThreads, 2) tc_gemv_kernel(const __grid_const
     const uint32_t tmem = S.tmem;
 
     if (warp == 0) {
-        // ---------------- bulk-copy producer: one contiguous block per step
+        // ---------------- bulk-copy producer
         if (lane == 0) {
-            const uint8_t* src = sg.q + ((int64_t)(tile - sg.tile_begin) * p.ksteps + step0) * G::kStage;
-            int it = 0;
-            for (; it < nsteps; ++it) {
-                const int s = it % kSW;
-                if (it >= kSW && !mbar_wait(&S.w_empty[s], ((it / kSW) & 1) ^ 1, abort_flag, p.err)) break;
-                mbar_expect_tx(&S.w_full[s], G::kStage);
-                bulk_load(&S.w[s][0], src + (int64_t)it * G::kStage, G::kStage, &S.w_full[s]);
+            int g = first;
+            for (; g < total; ++g) {
+                const int st = g % kSW;
+                if (g >= kSW && !mbar_wait(&S.w_empty[st], ((g / kSW) & 1) ^ 1, abort_flag, p.err)) break;
+                uint32_t bytes;
+                const uint8_t* src = slot_src(g, bytes);
+                mbar_expect_tx(&S.w_full[st], bytes);
+                bulk_load(&S.w[st][0], src, bytes, &S.w_full[st]);
             }
-            for (int j = (it > kSW ? it - kSW : 0); j < it; ++j)
-                mbar_wait(&S.w_full[j % kSW], (j / kSW) & 1, abort_flag, p.err);
+            // every issued copy lands before the CTA exits
+            const uint64_t deadline = globaltimer() + kTimeoutNs;
+            for (int j = (g > kSW ? g - kSW : 0); j < g; ++j)
+                if (!mbar_wait_until(&S.w_full[j % kSW], (j / kSW) & 1, deadline)) break;
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16<TM, TN>();
-            for (int it = 0; it < nsteps; ++it) {
-                const int sa = it % kSA, sx = it % kSX;
-                if (!mbar_wait(&S.a_full[sa], (it / kSA) & 1, abort_flag, p.err)) break;
-                if (!mbar_wait(&S.x_full[sx], (it / kSX) & 1, abort_flag, p.err)) break;
+            constexpr uint32_t idesc = idesc8<FMT, N>();
+            const uint32_t xbase = smem_u32(&S.x[0]);
+            bool ok = true;
+            int g = 0;
+            for (int i = 0; i < ntile_cta && ok; ++i) {
+                const int buf = i & 1;
+                if (i >= 2 && !mbar_wait(&S.d_empty[buf], ((i >> 1) - 1) & 1, abort_flag, p.err)) break;
                 tc_fence_after();
-                const uint32_t xb = smem_u32(&S.x[sx][0]);
+                const uint32_t dcol = tmem + buf * 32;
+                for (int j = 0; j < nslots; ++j, ++g) {
+                    if constexpr (Fm::kDeq) {
+                        const int sa = g % kSA;
+                        if (!mbar_wait(&S.a_full[sa], (g / kSA) & 1, abort_flag, p.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t xt = xbase + j * kXSlot;
 #pragma unroll
-                for (int kk = 0; kk < TK / 16; ++kk)
-                    umma_bf16_ts(tmem + kDCol, tmem + kACol + sa * 32 + kk * 8, sw128_desc(xb + kk * 32), idesc,
-                                 (it > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(&S.a_empty[sa]);
-                umma_commit(&S.x_empty[sx]);
+                        for (int kk = 0; kk < Fm::kMmaPerSlot; ++kk)
+                            mma8<FMT>(dcol, tmem + kACol + sa * 32 + kk * 8, 0, desc_sw128(xt + kk * 32), idesc,
+                                      (j > 0 || kk > 0) ? 1u : 0u);
+                        umma_commit(&S.a_empty[sa]);
+                    } else {
+                        const int st = g % kSW;
+                        if (!mbar_wait(&S.w_full[st], (g / kSW) & 1, abort_flag, p.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t xt = xbase + (j >> 1) * kXSlot + (j & 1) * 64;
+                        const uint32_t wa = smem_u32(&S.w[st][0]);
+#pragma unroll
+                        for (int kk = 0; kk < Fm::kMmaPerSlot; ++kk)
+                            mma8<FMT>(dcol, 0, desc_sw64(wa + kk * 32), desc_sw128(xt + kk * 32), idesc,
+                                      (j > 0 || kk > 0) ? 1u : 0u);
+                        umma_commit(&S.w_empty[st]);
+                    }
+                }
+                if (ok) umma_commit(&S.acc_full[buf]);
             }
-            umma_commit(&S.acc_full);
+            // all MMAs issued have completed before TMEM and the ring are released
+            umma_commit(&S.mma_done);
+            mbar_wait_until(&S.mma_done, 0, globaltimer() + kTimeoutNs);
         }
-    } else if (warp == 2) {
-        // ---------------- activations: hi/lo bf16 B tile per step, sum(x)
-        // The loads for PF steps are issued together so one L2 round trip
-        // covers several steps (a step's tile is needed every few hundred cycles).
-        constexpr int PF = B <= 1 ? 8 : B <= 2 ? 4 : B <= 4 ? 2 : 1;  // steps per round trip
-        float sxp[B];
+    } else if (warp >= kDeqWarp0 && warp < kEpiWarp0) {
+        if constexpr (Fm::kDeq) {
+            // ---------------- dequantize into TMEM
+            // The wait for a slot's tcgen05.st is deferred until the group's
+            // next slot is decoded, so the store latency overlaps work.
+            const int q4 = warp & 3;                         // TMEM lane quarter
+            const int grp = (warp - kDeqWarp0) >> 2;
+            const int row = q4 * 32 + lane;
+            const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+            int pending = -1;
+            for (int g = grp; g < total; g += kGroups) {
+                const int st = g % kSW, sa = g % kSA;
+                if (!warp_wait(&S.w_full[st], (g / kSW) & 1, abort_flag, p.err)) break;
+                uint32_t v[32];
 #pragma unroll
-        for (int b = 0; b < B; ++b) sxp[b] = 0.f;
-        const int chunk = lane >> 2, within = (lane & 3) * 4;
-        bool ok = true;
-        for (int base = 0; base < nsteps && ok; base += PF) {
-            float2 v[PF][B];
+                for (int h = 0; h < 2; ++h) {  // the slot's two 64-column blocks
+                    const uint8_t* sl = &S.w[st][h * Fm::kBlock + row * 32];
+                    const uint4 p0 = *reinterpret_cast<const uint4*>(sl);
+                    const uint4 p1 = *reinterpret_cast<const uint4*>(sl + 16);
+                    const uint32_t wv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
-            for (int j = 0; j < PF; ++j) {
-                const int k = (step0 + base + j) * TK + 2 * lane;
-#pragma unroll
-                for (int b = 0; b < B; ++b) {
-                    const float* xr = p.x + (int64_t)b * p.ldx;
-                    v[j][b].x = (base + j < nsteps && k < p.K) ? __ldg(xr + k) : 0.f;
-                    v[j][b].y = (base + j < nsteps && k + 1 < p.K) ? __ldg(xr + k + 1) : 0.f;
+                    for (int i = 0; i < 8; ++i) dq_word8<FMT>(wv[i], v[16 * h + 2 * i], v[16 * h + 2 * i + 1]);
                 }
-            }
-#pragma unroll
-            for (int j = 0; j < PF; ++j) {
-                const int it = base + j;
-                if (it >= nsteps) break;
-                const int sx = it % kSX;
-                if (it >= kSX && !warp_wait(&S.x_empty[sx], ((it / kSX) & 1) ^ 1, abort_flag, p.err)) {
-                    ok = false;
-                    break;
-                }
-                uint8_t* tile_x = &S.x[sx][0];
-#pragma unroll
-                for (int b = 0; b < B; ++b) {
-                    const __nv_bfloat162 hi = __floats2bfloat162_rn(v[j][b].x, v[j][b].y);
-                    const float2 hf = __bfloat1622float2(hi);
-                    const __nv_bfloat162 lo = __floats2bfloat162_rn(v[j][b].x - hf.x, v[j][b].y - hf.y);
-                    const float2 lf = __bfloat1622float2(lo);
-                    sxp[b] += (hf.x + lf.x) + (hf.y + lf.y);
-                    const int rh = 2 * b, rl = 2 * b + 1;
-                    *reinterpret_cast<__nv_bfloat162*>(tile_x + rh * 128 + ((chunk ^ (rh & 7)) << 4) + within) = hi;
-                    *reinterpret_cast<__nv_bfloat162*>(tile_x + rl * 128 + ((chunk ^ (rl & 7)) << 4) + within) = lo;
-                }
+                // the slot's bytes were read through the generic proxy; the next
+                // bulk copy into it is an async-proxy write
                 fence_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&S.x_full[sx]);
+                if (lane == 0) mbar_arrive(&S.w_empty[st]);
+                if (pending >= 0) {
+                    tmem_st_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&S.a_full[pending]);
+                    pending = -1;
+                }
+                if (g >= kSA && !warp_wait(&S.a_empty[sa], ((g / kSA) & 1) ^ 1, abort_flag, p.err)) break;
+                tc_fence_after();  // the store follows the MMAs that read this stage
+                tmem_st32(tmem + lane_base + kACol + sa * 32, v);
+                pending = sa;
             }
-        }
-#pragma unroll
-        for (int b = 0; b < B; ++b) {
-            float v = sxp[b];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0) S.sx[b] = v;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.sx_ready);
-    } else if (warp >= 4) {
-        // ---------------- dequantize into TMEM
-        // Two groups of four warps (one warp per TMEM lane quarter) take
-        // alternate steps; each thread turns its row's 64 codes into 32 bf16
-        // pairs.  The wait for a step's tcgen05.st is deferred until the next
-        // step's codes are decoded, so the store latency overlaps work.
-        const int q4 = warp & 3;               // TMEM lane quarter of this warp
-        const int grp = (warp - 4) >> 2;       // steps grp, grp + 2, ...
-        const int row = q4 * 32 + lane;
-        const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-        int pending = -1;                      // stage whose store is not yet published
-        for (int it = grp; it < nsteps; it += 2) {
-            const int sw = it % kSW, sa = it % kSA;
-            if (!warp_wait(&S.w_full[sw], (it / kSW) & 1, abort_flag, p.err)) break;
-            uint32_t v[32];
-            dq_row<FMT>(&S.w[sw][row * G::kSlice], v);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&S.w_empty[sw]);
             if (pending >= 0) {
                 tmem_st_wait();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&S.a_full[pending]);
-                pending = -1;
             }
-            if (it >= kSA && !warp_wait(&S.a_empty[sa], ((it / kSA) & 1) ^ 1, abort_flag, p.err)) break;
-            tmem_st32(tmem + lane_base + kACol + sa * 32, v);
-            pending = sa;
         }
-        if (pending >= 0) {
-            tmem_st_wait();
+    } else if (warp >= kEpiWarp0) {
+        // ---------------- epilogue, one warp per TMEM lane quarter
+        const int q4 = warp & 3;
+        const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+        for (int i = 0; i < ntile_cta; ++i) {
+            const int buf = i & 1;
+            if (!warp_wait(&S.acc_full[buf], (i >> 1) & 1, abort_flag, p.err)) break;
+            tc_fence_after();
+            uint32_t d[32];
+            tmem_ld16(tmem + lane_base + buf * 32, *reinterpret_cast<uint32_t(*)[16]>(&d[0]));
+            if constexpr (N > 16) tmem_ld16(tmem + lane_base + buf * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&d[16]));
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&S.a_full[pending]);
-        }
-        // ---------------- epilogue (warps 4-7: one per lane quarter)
-        if (grp == 0) {
-            bool ok = true;
-            if (lane == 0) ok = mbar_wait(&S.acc_full, 0, abort_flag, p.err) && mbar_wait(&S.sx_ready, 0, abort_flag, p.err);
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-            if (ok) {
-                tc_fence_after();
-                uint32_t d[16];
-                tmem_ld16(tmem + lane_base + kDCol, d);
-                const int grow = row0 + row;
-                if (grow < sg.N) {
-                    const float sc = __ldg(sg.scales + grow);
+            if (lane == 0) mbar_arrive(&S.d_empty[buf]);
+            const int tile = ci + i * p.ctas_per_split;
+            const TcSeg& sg = p.seg[seg_of(p, tile)];
+            const int row = q4 * 32 + lane;
+            const int grow = (tile - sg.tile_begin) * TM + row;
+            float res[B];
+            if (grow < sg.N) {
+                const float sc = __ldg(sg.scales + grow);
+#pragma unroll
+                for (int b = 0; b < B; ++b) {
+                    float acc = 0.f;
+                    if constexpr (FMT == BRAMHA_FMT_LOG4) {
+#pragma unroll
+                        for (int j = T - 1; j >= 0; --j) acc = acc * 0.0625f + __uint_as_float(d[b * T + j]);
+                    } else {
+#pragma unroll
+                        for (int j = T - 1; j >= 0; --j) acc = acc * 0.0078125f + (float)(int)d[b * T + j];
+                    }
+                    const float xq = acc * S.inv_s[b];  // sum(a * x) with a as stored in A
+                    float dot;
+                    if constexpr (FMT == BRAMHA_FMT_LOG4) dot = fmaf(xq, 16384.0f, -S.sx[b]);  // sum((2^c - 1) x)
+                    else if constexpr (FMT == BRAMHA_FMT_W4ZP8) dot = fmaf(-8.0f, S.sx[b], xq);  // sum((q - 8) x)
+                    else dot = xq;
+                    res[b] = dot * sc;
+                }
+            }
+            if (p.ksplit == 1) {
+                if (grow < sg.N)
+#pragma unroll
+                    for (int b = 0; b < B; ++b) sg.y[(int64_t)b * sg.ldy + grow] = res[b];
+                continue;
+            }
+            // K split: publish this split's partial, take a ticket; the last
+            // split adds all partials in split order
+            float* part = p.ws + (int64_t)tile * p.ksplit * B * TM;
+            if (grow < sg.N)
+#pragma unroll
+                for (int b = 0; b < B; ++b) part[((int64_t)split * B + b) * TM + row] = res[b];
+            __threadfence();
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (row == 0) S.last_split = atomicAdd(&p.tickets[tile], 1) == p.ksplit - 1;
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (S.last_split) {
+                __threadfence();
+                if (grow < sg.N)
 #pragma unroll
                     for (int b = 0; b < B; ++b) {
-                        const float acc = __uint_as_float(d[2 * b]) + __uint_as_float(d[2 * b + 1]);
-                        float dot;
-                        if constexpr (FMT == BRAMHA_FMT_LOG4) dot = fmaf(acc, 32768.0f, -S.sx[b]);
-                        else if constexpr (FMT == BRAMHA_FMT_W4ZP8) dot = fmaf(-136.0f, S.sx[b], acc);
-                        else dot = acc;  // int8 weights are exact in bf16
-                        float* dst = sg.y + (int64_t)b * sg.ldy + grow;
-                        if (p.atomic_out) atomicAdd(dst, dot * sc);
-                        else *dst = dot * sc;
+                        float acc = 0.f;
+                        for (int s = 0; s < p.ksplit; ++s) acc += __ldcg(part + ((int64_t)s * B + b) * TM + row);
+                        sg.y[(int64_t)b * sg.ldy + grow] = acc;
                     }
-                }
+                if (row == 0) p.tickets[tile] = 0;  // ready for the next launch
             }
         }
     }
@@ -363,24 +560,65 @@ __global__ void __launch_bounds__(kThreads, 2) tc_gemv_kernel(const __grid_const
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        tmem_dealloc(tmem, 512);
     }
 }
 
 template <int FMT, int B>
-cudaError_t launch_b(const TcGemvParams& p, int ksplit, cudaStream_t st) {
+cudaError_t launch_b(const TcGemvParams& p, int grid, cudaStream_t st) {
     auto kern = tc_gemv_kernel<FMT, B>;
-    constexpr int smem = (int)sizeof(TcSmem<FMT>) + 1024;
+    constexpr int smem = (int)sizeof(TcSmem) + 1024;
+    static_assert(smem <= 227 * 1024, "shared memory per CTA exceeds 227 KB");
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    kern<<<dim3((unsigned)p.ntiles, (unsigned)ksplit), kThreads, smem, st>>>(p);
+    kern<<<grid, kThreads, smem, st>>>(p);
     return cudaGetLastError();
+}
+
+// Largest K range (64-column blocks) one CTA takes: its B terms fit the B
+// area and its raw activations the staging area.
+int max_split_steps(int fmt, int batch) {
+    const int terms = fmt == BRAMHA_FMT_LOG4 ? 4 : 3;
+    const int n = batch * terms <= 16 ? 16 : 32;
+    const int by_terms = 2 * (kXBytes / (n * 128));
+    const int by_stage = kStageFloats / (batch * kTileK);
+    return by_terms < by_stage ? by_terms : by_stage;
+}
+
+// K split: the one that minimises the time of the busiest CTA (one CTA per
+// SM), counted in 64-column blocks: its blocks, ~1 per tile for the epilogue,
+// and for a split ~2 + ksplit/8 for the combine.  Splits start on even blocks
+// so 4-bit slots stay whole.  False when no split fits.
+bool plan_gemv_tc(int ntiles, int ksteps, int max_steps, int max_ksplit, int num_sms, int* ksplit_out,
+                  int* steps_per_split_out, int* ctas_per_split_out) {
+    int64_t best = INT64_MAX;
+    int bk = 1, bspp = ksteps, bcps = 1;
+    for (int ks = 1; ks <= ksteps && ks <= num_sms && ks <= max_ksplit; ++ks) {
+        int spp = (ksteps + ks - 1) / ks;
+        spp += spp & 1;
+        if (spp > max_steps) continue;
+        const int ks_eff = (ksteps + spp - 1) / spp;
+        if (ks_eff != ks) continue;
+        const int cps = ntiles < num_sms / ks ? ntiles : num_sms / ks;
+        if (cps < 1) continue;
+        const int64_t tpc = (ntiles + cps - 1) / cps;
+        const int64_t cost = 8 * (tpc * (spp + 1)) + (ks > 1 ? 16 + ks : 0);  // eighths of a block
+        if (cost < best) {
+            best = cost;
+            bk = ks;
+            bspp = spp;
+            bcps = cps;
+        }
+    }
+    *ksplit_out = bk;
+    *steps_per_split_out = bspp;
+    *ctas_per_split_out = bcps;
+    return best != INT64_MAX;
 }
 
 }  // namespace
 
 // Tensor-core GEMV over up to 8 fused quantized weights sharing x (batch 1..8).
-// `segs` carry the tile-major device weights, scales and outputs.
 cudaError_t launch_gemv_tc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t st) {
     if (!is_tiled(fmt)) return cudaErrorInvalidValue;
     if (a.batch < 1 || a.batch > 8 || a.nseg < 1 || a.nseg > kMaxSegments || a.K <= 0) return cudaErrorInvalidValue;
@@ -398,6 +636,7 @@ cudaError_t launch_gemv_tc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t
         p.seg[i].tile_begin = ntiles;
         ntiles += (int)row_tiles(s.N);
     }
+    if (ntiles <= 0) return cudaErrorInvalidValue;
     p.x = a.x;
     p.ldx = a.ldx;
     p.err = a.err;
@@ -405,22 +644,21 @@ cudaError_t launch_gemv_tc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t
     p.ntiles = ntiles;
     p.K = a.K;
     p.ksteps = (int)k_steps(a.K);
-    // split K until ~2 CTAs per SM are busy (each split keeps >= 8 steps)
-    int ksplit = 1;
-    while (ksplit < 16 && (int64_t)ntiles * ksplit < 2LL * num_sms && p.ksteps / (ksplit * 2) >= 8) ksplit *= 2;
-    p.steps_per_split = (p.ksteps + ksplit - 1) / ksplit;
-    ksplit = (p.ksteps + p.steps_per_split - 1) / p.steps_per_split;
-    p.atomic_out = ksplit > 1;
-    if (p.atomic_out)
-        for (int i = 0; i < a.nseg; ++i) {
-            cudaError_t e = cudaMemsetAsync(a.seg[i].y, 0, sizeof(float) * (size_t)a.seg[i].ldy * a.batch, st);
-            if (e != cudaSuccess) return e;
-        }
-#define BRAMHA_TC_B(n)                                                                     \
-    case n:                                                                                \
-        return fmt == BRAMHA_FMT_LOG4    ? launch_b<BRAMHA_FMT_LOG4, n>(p, ksplit, st)     \
-               : fmt == BRAMHA_FMT_W4ZP8 ? launch_b<BRAMHA_FMT_W4ZP8, n>(p, ksplit, st)    \
-                                         : launch_b<BRAMHA_FMT_W8, n>(p, ksplit, st);
+    // splits need a workspace slot per (tile, split, batch row) and a ticket per tile
+    int max_ksplit = 1;
+    if (a.split_ws && a.split_tickets && ntiles <= a.split_tickets_n)
+        max_ksplit = (int)(a.split_ws_floats / ((int64_t)ntiles * a.batch * TM));
+    if (!plan_gemv_tc(ntiles, p.ksteps, max_split_steps(fmt, a.batch), max_ksplit, num_sms, &p.ksplit,
+                      &p.steps_per_split, &p.ctas_per_split))
+        return cudaErrorInvalidValue;
+    p.ws = a.split_ws;
+    p.tickets = a.split_tickets;
+    const int grid = p.ksplit * p.ctas_per_split;
+#define BRAMHA_TC_B(n)                                                                    \
+    case n:                                                                               \
+        return fmt == BRAMHA_FMT_LOG4    ? launch_b<BRAMHA_FMT_LOG4, n>(p, grid, st)      \
+               : fmt == BRAMHA_FMT_W4ZP8 ? launch_b<BRAMHA_FMT_W4ZP8, n>(p, grid, st)     \
+                                         : launch_b<BRAMHA_FMT_W8, n>(p, grid, st);
     switch (a.batch) {
         BRAMHA_TC_B(1)
         BRAMHA_TC_B(2)

@@ -17,7 +17,12 @@
 // 4-bit words are also rearranged inside each 32-bit word (columns c0..c7):
 // even columns c0,c2,c4,c6 in bits 0-15, odd columns c1,c3,c5,c7 in bits 16-31,
 // nibble j of each half = column 2j / 2j+1.  A column pair is then 16 bits
-// apart: one shift and one logic op give a bf16x2 pair.
+// apart: one shift and one logic op give a bf16x2 pair; one mask gives four
+// codes as bytes (c0, c4, c1, c5) / (c2, c6, c3, c7).
+//
+// int8 row slices (64 B) are stored in the tensor cores' 64-byte-swizzle
+// order, so a block is an MMA operand as it lands in shared memory: the
+// 16-byte chunk j of row r sits at chunk position j ^ ((r >> 1) & 3).
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -47,7 +52,11 @@ __global__ void tile_kernel(const uint8_t* __restrict__ src, int64_t row_bytes, 
         const int64_t block = o / (words_per_slice * kTileRows);
         const int64_t tile = block / ksteps, step = block % ksteps;
         const int64_t row = tile * kTileRows + row_in_tile;
-        const int64_t b0 = step * slice + wi * 4;  // source byte offset in the row
+        int64_t b0 = step * slice + wi * 4;  // source byte offset in the row
+        if (!nibbles) {                      // int8: chunk position p holds chunk p ^ ((r >> 1) & 3)
+            const int64_t j = (wi >> 2) ^ ((row_in_tile >> 1) & 3);
+            b0 = step * slice + j * 16 + (wi & 3) * 4;
+        }
         uint32_t w = 0;
         if (row < N) {
             const uint8_t* r = src + row * row_bytes;

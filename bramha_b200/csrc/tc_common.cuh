@@ -62,6 +62,16 @@ __device__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag
     }
 }
 
+// Wait used while draining at exit (copies or MMAs already issued must land
+// before shared memory or TMEM is released): ignores the abort flag, gives up
+// at an absolute %globaltimer deadline shared by all the drain waits.
+__device__ bool mbar_wait_until(uint64_t* b, uint32_t parity, uint64_t deadline) {
+    for (;;) {
+        if (mbar_try_wait(b, parity)) return true;
+        if (globaltimer() > deadline) return false;
+    }
+}
+
 // Contiguous global -> shared copy by the TMA engine (no tensor map): both
 // addresses 16-byte aligned, size a multiple of 16.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
