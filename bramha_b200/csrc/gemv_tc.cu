@@ -6,15 +6,18 @@
 // (quantize_to_int8, :7-38) or log4 (dequantize_log4,
 // spanda-engine/src/lib.rs:332-342) weights.
 //
-// A tcgen05.mma with M = 128 costs the same ~51 cycles for any N <= 64, so a
-// GEMV (N = batch) is bound by how many MMAs its weight bytes need.  8-bit
-// operands take K = 32 per MMA, half the MMAs of bf16 (K = 16):
-//   int8  (W8)    kind::i8, A = the int8 block exactly as stored (the repack
+// A GEMV has N = batch, so its MMAs are tiny (M = 128, N = 16/32, K = 32):
+// ~8 cycles of tensor work each, but one issuing thread waits ~55-68 cycles
+// per tcgen05.mma (measured).  So four threads issue, each into its own
+// accumulator (slot g goes to issuer g mod 4): ~17 cycles per MMA in
+// aggregate (measured), several times what HBM can feed.  8-bit operands take
+// K = 32 per MMA:
+//   int8  (W8)    kind::i8: A = the int8 block exactly as stored (the repack
 //                 writes it in the 64-byte-swizzle operand order), read by the
 //                 MMA straight from the shared-memory ring: no dequantization.
-//   int4  (W4ZP8) kind::i8, A = u8 q (0..15) in TMEM: one mask per 4 codes.
-//   log4          kind::f8f6f4, A = e5m2 2^(c-14) in TMEM (exact; byte
-//                 (c+1)*4): one mask + one multiply-add per 4 codes.
+//   int4  (W4ZP8) kind::i8: A = u8 q (0..15) in TMEM (one mask per 4 codes).
+//   log4          kind::f8f6f4: A = e5m2 2^(c-14) in TMEM (exact; byte
+//                 (c+1)*4: one mask + one multiply-add per 4 codes).
 // The weights are exact in these types.  The activations become B columns of
 // several 8-bit terms per batch row, scaled per row by a power of two s chosen
 // from max|x| over the CTA's K range:
@@ -22,30 +25,36 @@
 //               integer accumulation, exact;
 //   e4m3 terms: x*s = t1 + t2/16 + t3/256 + t4/4096 (rel. error ~2^-16),
 //               fp32 accumulation.
-// The epilogue folds the terms, the zero points (int4 -8, log4 -1, with the
-// row's sum(x)) and the row scale.
+// The epilogue adds the four issuers' accumulators (in issuer order), folds
+// the terms, the zero points (int4 -8, log4 -1, with the row's sum(x)) and the
+// row scale.
 //
 // Work: 128-row tiles of the tile-major weight (repack.cu) x a K range (a
-// "split").  One persistent CTA per SM; grid = ksplit x CTAs per split; a CTA
-// walks the tiles of its split back to back.  With ksplit > 1 each split
-// writes its partial tile result to a context-owned workspace and takes a
-// ticket; the last split to arrive adds the partials in split order and writes
-// y, so results do not depend on timing.  A ring slot is 8 KB: two
-// 64-column blocks of a 4-bit tile (K = 128) or one int8 block (K = 64).
-//   warp 0       bulk copy into the 128 KB ring (16 slots)
-//   warp 1       TMEM alloc; lane 0 issues the MMAs (M=128, N=16/32, K=32)
-//   warps 4-19   (4-bit) dequantize: four groups take slots g, g+4, ...; a
+// "split").  Persistent CTAs, one per SM, each walking the tiles of its split
+// back to back.  With ksplit > 1 each split writes its partial tile result to
+// a context-owned workspace and takes a ticket; the last split to arrive adds
+// the partials in split order and writes y, so results do not depend on
+// timing.  A ring slot is 8 KB: two 64-column blocks of a 4-bit tile (K = 128)
+// or one int8 block (K = 64).
+//   warps 0, 5   bulk copies into the 96 KB ring (12 slots; producer p takes
+//                slots g = p, p+2, ...: one thread issuing 8 KB copies tops
+//                out near 4.9 TB/s, two reach the HBM peak -- measured); the
+//                whole ring is requested during the prologue, right after the
+//                activation loads
+//   warps 1-4    MMA issuers (lane 0)
+//   warps 8-23   (4-bit) dequantize: four groups take slots g, g+4, ...; a
 //                warp owns one TMEM lane quarter: 128 codes per row -> 32
-//                words -> one tcgen05.st into one of 14 A stages
-//   warps 20-23  epilogue: tcgen05.ld of the finished (double-buffered)
-//                accumulator, fold, scale, store
-//   all warps    prologue: the split's activations are loaded once (ahead of
-//                the weight stream, staged raw in the ring's tail), reduced to
-//                max|x| and sum(x), and written as 8-bit B terms (K-major,
-//                128-byte swizzle, one 128-column atom per 128 K).
-// Every mbarrier wait is bounded (tc_common.cuh).
+//                words -> one tcgen05.st into an A stage
+//   warps 24-27  epilogue (tcgen05.ld of the double-buffered accumulators)
+//   prologue     all warps load the split's activations once (staged raw),
+//                reduce max|x| and sum(x); warps 1-4, 6, 7 and 24-27 then
+//                write the 8-bit B terms (K-major, 128-byte swizzle, one
+//                128-column atom per 128 K) while the dequant warps start.
+// Ring slots and A stages are multiples of 4 deep, so each one is always
+// consumed by the same dequant group and the same issuer: a parity wait can
+// never see a phase two generations old.  Every mbarrier wait is bounded
+// (tc_common.cuh).
 #include <cuda.h>
-#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
@@ -59,25 +68,29 @@
 namespace bramha {
 namespace {
 
-constexpr int TM = 128;                   // weight rows per tile (UMMA M)
+constexpr int TM = 128;                   // weight rows per tile (UMMA M, TMEM lanes)
 constexpr int kSlotBytes = 8192;
-constexpr int kSW = 16;                   // ring slots
-constexpr int kFirstFill = 4;             // slots requested before the prologue
-constexpr int kStageFloats = (kSW - kFirstFill) * kSlotBytes / 4;  // raw activation staging
-constexpr int kSA = 14;                   // A stages in TMEM (4-bit), 32 columns each
-constexpr int kACol = 64;                 // A stages from column 64; accumulators at 0 / 32
+constexpr int kSW = 12;                   // ring slots
+constexpr int kNI = 4;                    // MMA issuers
 constexpr int kGroups = 4;                // dequant groups (4 warps each)
-constexpr int kDeqWarp0 = 4;
-constexpr int kEpiWarp0 = kDeqWarp0 + 4 * kGroups;  // 20
-constexpr int kThreads = (kEpiWarp0 + 4) * 32;      // 768
+constexpr int kIssWarp0 = 1;
+constexpr int kNP = 2;                    // producers (warps 0 and 5)
+constexpr int kProdWarp1 = 5;
+constexpr int kDeqWarp0 = 8;
+constexpr int kEpiWarp0 = kDeqWarp0 + 4 * kGroups;  // 24
+constexpr int kThreads = (kEpiWarp0 + 4) * 32;      // 896
+constexpr int kBuilders = 10;             // warps 1-4, 6, 7 and 24-27 write the B terms
 constexpr int kXBytes = 64 * 1024;        // B terms of one split
-static_assert(kACol + kSA * 32 <= 512, "TMEM columns");
-static_assert(kSW % kGroups == 0, "a ring slot must always belong to the same dequant group");
+constexpr int kStageFloats = 8192;        // raw activations of one split (32 KB)
+constexpr int kPerThread = 10;            // activation columns a thread loads per batch row
+static_assert(kSW % kGroups == 0 && kSW % kNI == 0 && kSW % kNP == 0,
+              "a ring slot must always have the same producer and consumer");
+static_assert(kDeqWarp0 % 4 == 0 && kEpiWarp0 % 4 == 0, "TMEM lane quarters follow warp % 4");
 
 // Per-format constants.
 template <int FMT>
 struct F {
-    static constexpr bool kDeq = FMT != BRAMHA_FMT_W8;          // A through TMEM
+    static constexpr bool kDeq = FMT != BRAMHA_FMT_W8;           // A through TMEM
     static constexpr int kStepsPerSlot = kDeq ? 2 : 1;           // 64-column blocks per slot
     static constexpr int kBlock = kTileRows * tile_slice_bytes(FMT);  // 4 KB / 8 KB
     static constexpr int kMmaPerSlot = kDeq ? 4 : 2;             // K = 32 each
@@ -87,7 +100,10 @@ template <int FMT, int B>
 struct NB {
     static constexpr int N = (B * F<FMT>::kTerms <= 16) ? 16 : 32;  // MMA N (B columns)
     static constexpr int kXSlot = N * 128;                           // B bytes per 128 K
+    static constexpr int kDCols = kNI * 2 * N;                       // accumulators: issuer x buffer
+    static constexpr int kSA = (512 - kDCols) / 32 / 4 * 4;          // A stages (multiple of 4)
 };
+static_assert(NB<BRAMHA_FMT_LOG4, 1>::kSA == 12 && NB<BRAMHA_FMT_LOG4, 8>::kSA == 8, "TMEM plan");
 
 struct TcSeg {
     const uint8_t* q;      // tile-major weight (repack.cu)
@@ -117,10 +133,11 @@ struct TcGemvParams {
 struct alignas(1024) TcSmem {
     uint8_t w[kSW][kSlotBytes];
     uint8_t x[kXBytes];
+    float stage[kStageFloats];
     uint64_t w_full[kSW], w_empty[kSW];
-    uint64_t a_full[kSA], a_empty[kSA];
-    uint64_t acc_full[2], d_empty[2], mma_done;
-    float amax[8], sx[8], inv_s[8];
+    uint64_t a_full[12], a_empty[12];
+    uint64_t acc_full[2], d_empty[2], mma_done, b_ready;
+    float amax[8], sx[8];
     uint32_t tmem;
     int abort_flag;
     int last_split;
@@ -209,8 +226,49 @@ __device__ __forceinline__ int seg_of(const TcGemvParams& p, int tile) {
     return si;
 }
 
-__device__ __forceinline__ float e4m3_value(__nv_fp8_storage_t b) {
-    return __half2float(__half(__nv_cvt_fp8_to_halfraw(b, __NV_E4M3)));
+// Power-of-two activation scale of a batch row: max|x*s| < 128 (int8 terms)
+// or < 256 (e4m3 terms).
+template <int FMT>
+__device__ __forceinline__ float act_scale(float amax) {
+    if (!(amax > 0.f)) return 1.f;
+    const int e = ((__float_as_int(amax) >> 23) & 0xFF) - 127;  // amax in [2^e, 2^(e+1))
+    float s = ldexpf(1.f, min((FMT == BRAMHA_FMT_LOG4 ? 7 : 6) - e, 126));
+    if (FMT != BRAMHA_FMT_LOG4 && amax * s >= 127.5f) s *= 0.5f;
+    return s;
+}
+
+// Four consecutive positions' scaled values -> T words of 8-bit terms.
+template <int FMT, int T>
+__device__ __forceinline__ void make_terms(float v0, float v1, float v2, float v3, uint32_t (&word)[T]) {
+    if constexpr (FMT == BRAMHA_FMT_LOG4) {
+        float2 a = make_float2(v0, v1), b = make_float2(v2, v3);
+#pragma unroll
+        for (int j = 0; j < T; ++j) {
+            const __nv_fp8x2_storage_t ta = __nv_cvt_float2_to_fp8x2(a, __NV_SATFINITE, __NV_E4M3);
+            const __nv_fp8x2_storage_t tb = __nv_cvt_float2_to_fp8x2(b, __NV_SATFINITE, __NV_E4M3);
+            word[j] = (uint32_t)ta | ((uint32_t)tb << 16);
+            if (j + 1 < T) {
+                // residual * 16, exact: a - t is representable and the scaling is a power of two
+                const float2 fa = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(ta, __NV_E4M3)));
+                const float2 fb = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(tb, __NV_E4M3)));
+                a = make_float2(fmaf(fa.x, -16.f, a.x * 16.f), fmaf(fa.y, -16.f, a.y * 16.f));
+                b = make_float2(fmaf(fb.x, -16.f, b.x * 16.f), fmaf(fb.y, -16.f, b.y * 16.f));
+            }
+        }
+    } else {
+        float a[4] = {v0, v1, v2, v3};
+#pragma unroll
+        for (int j = 0; j < T; ++j) {
+            uint32_t w = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int t = __float2int_rn(a[e]);
+                w |= (uint32_t)(t & 0xFF) << (8 * e);
+                a[e] = (a[e] - (float)t) * 128.f;
+            }
+            word[j] = w;
+        }
+    }
 }
 
 template <int FMT, int B>
@@ -218,7 +276,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
     using Fm = F<FMT>;
     constexpr int N = NB<FMT, B>::N;
     constexpr int kXSlot = NB<FMT, B>::kXSlot;
+    constexpr int kACol = NB<FMT, B>::kDCols;  // A stages after the accumulators
+    constexpr int kSA = NB<FMT, B>::kSA;
     constexpr int T = Fm::kTerms;
+    static_assert(kSA % kGroups == 0 && kSA % kNI == 0 && kSA <= 12, "an A stage must always have the same users");
     extern __shared__ uint8_t smem_raw[];
     TcSmem& S = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     volatile int* abort_flag = &S.abort_flag;
@@ -245,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
         return sg.q + ((int64_t)(tile - sg.tile_begin) * p.ksteps + step0 + s) * Fm::kBlock;
     };
 
-    // ---------------- prologue 1: barriers, TMEM, zeroed B area
+    // ---------------- prologue: barriers, zeroed B area, the whole ring requested
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSW; ++s) {
             mbar_init(&S.w_full[s], 1);
@@ -256,10 +317,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             mbar_init(&S.a_empty[s], 1);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&S.acc_full[i], 1);
+            mbar_init(&S.acc_full[i], kNI);
             mbar_init(&S.d_empty[i], 4);
         }
-        mbar_init(&S.mma_done, 1);
+        mbar_init(&S.mma_done, kNI);
+        mbar_init(&S.b_ready, kBuilders);
         for (int b = 0; b < 8; ++b) {
             S.amax[b] = 0.f;
             S.sx[b] = 0.f;
@@ -267,29 +329,46 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
         S.abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 1) tmem_alloc(&S.tmem, 512);
     {
         uint4* xz = reinterpret_cast<uint4*>(&S.x[0]);
         const int nz = nkb * kXSlot / 16;
         for (int i = threadIdx.x; i < nz; i += kThreads) xz[i] = make_uint4(0, 0, 0, 0);
     }
+    __syncthreads();
+    const int first = min(kSW, total);
+    const bool producer = (warp == 0 || warp == kProdWarp1) && lane == 0;
+    const int pid = warp == 0 ? 0 : 1;
 
-    // ---------------- prologue 2: activations -> staging (ring tail), max|x|, sum(x)
-    // The loads are issued before the first weight copies so they do not
-    // queue behind them.
-    float* stage = reinterpret_cast<float*>(&S.w[kFirstFill][0]);
+    // ---------------- activations -> staging, max|x|, sum(x)
     {
+        const int kv = min(nk, p.K - k0);
 #pragma unroll
         for (int b = 0; b < B; ++b) {
             const float* xr = p.x + (int64_t)b * p.ldx + k0;
-            const int kv = min(nk, p.K - k0);  // valid columns
+            float v[kPerThread];
+#pragma unroll
+            for (int u = 0; u < kPerThread; ++u) {
+                const int k = threadIdx.x + u * kThreads;
+                v[u] = k < kv ? __ldg(xr + k) : 0.f;
+            }
+            if (b == 0) {
+                // the weight ring is requested once the activation loads are out
+                if (producer)
+                    for (int g = pid; g < first; g += kNP) {
+                        uint32_t bytes;
+                        const uint8_t* src = slot_src(g, bytes);
+                        mbar_expect_tx(&S.w_full[g], bytes);
+                        bulk_load(&S.w[g][0], src, bytes, &S.w_full[g]);
+                    }
+                if (warp == 1) tmem_alloc(&S.tmem, 512);
+            }
             float am = 0.f, sm = 0.f;
-#pragma unroll 4
-            for (int k = threadIdx.x; k < nk; k += kThreads) {
-                const float v = k < kv ? __ldg(xr + k) : 0.f;
-                stage[b * nk + k] = v;
-                am = fmaxf(am, fabsf(v));
-                sm += v;
+#pragma unroll
+            for (int u = 0; u < kPerThread; ++u) {
+                const int k = threadIdx.x + u * kThreads;
+                if (k < nk) S.stage[b * nk + k] = v[u];
+                am = fmaxf(am, fabsf(v[u]));
+                sm += v[u];
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
@@ -302,65 +381,34 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             }
         }
     }
+    tc_fence_before();
     __syncthreads();
-    const int first = min(kFirstFill, total);
-    if (threadIdx.x == 0)
-        for (int g = 0; g < first; ++g) {
-            uint32_t bytes;
-            const uint8_t* src = slot_src(g, bytes);
-            mbar_expect_tx(&S.w_full[g], bytes);
-            bulk_load(&S.w[g][0], src, bytes, &S.w_full[g]);
-        }
+    tc_fence_after();
+    const uint32_t tmem = S.tmem;
 
-    // ---------------- prologue 3: B terms
-    {
+    // ---------------- B terms (warps 1-4, 6, 7 and 24-27, while the dequant warps start)
+    if ((warp > 0 && warp < kDeqWarp0 && warp != kProdWarp1) || warp >= kEpiWarp0) {
+        const int bw = warp < kProdWarp1 ? warp - 1 : warp < kDeqWarp0 ? warp - 2 : warp - kEpiWarp0 + 6;
+        const int bt = bw * 32 + lane;
         float scl[B];
 #pragma unroll
-        for (int b = 0; b < B; ++b) {
-            // s = 2^e with max|x*s| < 128 (int8 terms) or < 256 (e4m3 terms)
-            const float am = S.amax[b];
-            float s = 1.f;
-            if (am > 0.f) {
-                const int e = ((__float_as_int(am) >> 23) & 0xFF) - 127;  // am in [2^e, 2^(e+1))
-                s = ldexpf(1.f, min((FMT == BRAMHA_FMT_LOG4 ? 7 : 6) - e, 126));
-                if (FMT != BRAMHA_FMT_LOG4 && am * s >= 127.5f) s *= 0.5f;
-            }
-            scl[b] = s;
-            if (threadIdx.x == 0) S.inv_s[b] = 1.f / s;
-        }
-        const int npos4 = nkb * 32;  // 4-position groups
-        for (int i = threadIdx.x; i < B * npos4; i += kThreads) {
+        for (int b = 0; b < B; ++b) scl[b] = act_scale<FMT>(S.amax[b]);
+        const int npos4 = nkb * 32;  // 4-position groups per batch row
+        for (int i = bt; i < B * npos4; i += kBuilders * 32) {
             const int b = i / npos4, g4 = i - b * npos4;
-            const int p0 = g4 * 4;                      // position in the split
-            const int kb = p0 >> 7, pin = p0 & 127;     // atom, position in the atom
+            const int p0 = g4 * 4, kb = p0 >> 7, pin = p0 & 127;
             float s = scl[0];
 #pragma unroll
             for (int bb = 1; bb < B; ++bb)
                 if (b == bb) s = scl[bb];
-            uint32_t word[T];
-#pragma unroll
-            for (int j = 0; j < T; ++j) word[j] = 0;
+            float v[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int col = (kb << 7) + pos_to_col<FMT>(pin + e);
-                const float v = col < nk ? stage[b * nk + col] : 0.f;
-                float a = v * s;
-                if constexpr (FMT == BRAMHA_FMT_LOG4) {
-#pragma unroll
-                    for (int j = 0; j < T; ++j) {
-                        const __nv_fp8_storage_t t = __nv_cvt_float_to_fp8(a, __NV_SATFINITE, __NV_E4M3);
-                        word[j] |= (uint32_t)t << (8 * e);
-                        a = (a - e4m3_value(t)) * 16.f;
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < T; ++j) {
-                        const int t = __float2int_rn(a);
-                        word[j] |= (uint32_t)(t & 0xFF) << (8 * e);
-                        a = (a - (float)t) * 128.f;
-                    }
-                }
+                v[e] = col < nk ? S.stage[b * nk + col] * s : 0.f;
             }
+            uint32_t word[T];
+            make_terms<FMT, T>(v[0], v[1], v[2], v[3], word);
             uint8_t* atom = &S.x[kb * kXSlot];
 #pragma unroll
             for (int j = 0; j < T; ++j) {
@@ -369,43 +417,44 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
                                              (pin & 15)) = word[j];
             }
         }
+        fence_async_smem();  // generic writes -> MMA reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.b_ready);
     }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = S.tmem;
 
-    if (warp == 0) {
-        // ---------------- bulk-copy producer
+    if (warp == 0 || warp == kProdWarp1) {
+        // ---------------- bulk-copy producer `pid`: slots g = pid, pid + 2, ...
         if (lane == 0) {
-            int g = first;
-            for (; g < total; ++g) {
+            int g = first + ((pid - first % kNP + kNP) % kNP);  // first slot of mine not yet requested
+            for (; g < total; g += kNP) {
                 const int st = g % kSW;
-                if (g >= kSW && !mbar_wait(&S.w_empty[st], ((g / kSW) & 1) ^ 1, abort_flag, p.err)) break;
+                if (!mbar_wait(&S.w_empty[st], ((g / kSW) & 1) ^ 1, abort_flag, p.err)) break;
                 uint32_t bytes;
                 const uint8_t* src = slot_src(g, bytes);
                 mbar_expect_tx(&S.w_full[st], bytes);
                 bulk_load(&S.w[st][0], src, bytes, &S.w_full[st]);
             }
-            // every issued copy lands before the CTA exits
+            // every copy this producer issued lands before the CTA exits
             const uint64_t deadline = globaltimer() + kTimeoutNs;
-            for (int j = (g > kSW ? g - kSW : 0); j < g; ++j)
-                if (!mbar_wait_until(&S.w_full[j % kSW], (j / kSW) & 1, deadline)) break;
+            for (int j = pid; j < g && j < total; j += kNP)
+                if (j + kSW >= g && !mbar_wait_until(&S.w_full[j % kSW], (j / kSW) & 1, deadline)) break;
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer
+    } else if (warp >= kIssWarp0 && warp < kIssWarp0 + kNI) {
+        // ---------------- MMA issuer `me`: slots g with g % kNI == me, into accumulator `me`
         if (lane == 0) {
+            const int me = warp - kIssWarp0;
             constexpr uint32_t idesc = idesc8<FMT, N>();
             const uint32_t xbase = smem_u32(&S.x[0]);
-            bool ok = true;
-            int g = 0;
+            bool ok = mbar_wait(&S.b_ready, 0, abort_flag, p.err);
             for (int i = 0; i < ntile_cta && ok; ++i) {
                 const int buf = i & 1;
                 if (i >= 2 && !mbar_wait(&S.d_empty[buf], ((i >> 1) - 1) & 1, abort_flag, p.err)) break;
                 tc_fence_after();
-                const uint32_t dcol = tmem + buf * 32;
-                for (int j = 0; j < nslots; ++j, ++g) {
+                const uint32_t dcol = tmem + (me * 2 + buf) * N;
+                const int g0 = i * nslots;
+                bool acc = false;
+                for (int j = (me - g0 % kNI + kNI) % kNI; j < nslots; j += kNI) {
+                    const int g = g0 + j;
                     if constexpr (Fm::kDeq) {
                         const int sa = g % kSA;
                         if (!mbar_wait(&S.a_full[sa], (g / kSA) & 1, abort_flag, p.err)) {
@@ -417,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
 #pragma unroll
                         for (int kk = 0; kk < Fm::kMmaPerSlot; ++kk)
                             mma8<FMT>(dcol, tmem + kACol + sa * 32 + kk * 8, 0, desc_sw128(xt + kk * 32), idesc,
-                                      (j > 0 || kk > 0) ? 1u : 0u);
+                                      (acc || kk > 0) ? 1u : 0u);
                         umma_commit(&S.a_empty[sa]);
                     } else {
                         const int st = g % kSW;
@@ -431,11 +480,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
 #pragma unroll
                         for (int kk = 0; kk < Fm::kMmaPerSlot; ++kk)
                             mma8<FMT>(dcol, 0, desc_sw64(wa + kk * 32), desc_sw128(xt + kk * 32), idesc,
-                                      (j > 0 || kk > 0) ? 1u : 0u);
+                                      (acc || kk > 0) ? 1u : 0u);
                         umma_commit(&S.w_empty[st]);
                     }
+                    acc = true;
                 }
-                if (ok) umma_commit(&S.acc_full[buf]);
+                if (ok) umma_commit(&S.acc_full[buf]);  // arrives at once when this issuer had no slot here
             }
             // all MMAs issued have completed before TMEM and the ring are released
             umma_commit(&S.mma_done);
@@ -445,14 +495,23 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
         if constexpr (Fm::kDeq) {
             // ---------------- dequantize into TMEM
             // The wait for a slot's tcgen05.st is deferred until the group's
-            // next slot is decoded, so the store latency overlaps work.
+            // next slot is decoded (so the store latency overlaps work), unless
+            // that slot has not landed yet.
             const int q4 = warp & 3;                         // TMEM lane quarter
             const int grp = (warp - kDeqWarp0) >> 2;
             const int row = q4 * 32 + lane;
             const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
             int pending = -1;
+            auto publish = [&]() {
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.a_full[pending]);
+                pending = -1;
+            };
             for (int g = grp; g < total; g += kGroups) {
                 const int st = g % kSW, sa = g % kSA;
+                if (pending >= 0 && !__all_sync(0xffffffffu, mbar_test(&S.w_full[st], (g / kSW) & 1))) publish();
                 if (!warp_wait(&S.w_full[st], (g / kSW) & 1, abort_flag, p.err)) break;
                 uint32_t v[32];
 #pragma unroll
@@ -469,36 +528,45 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&S.w_empty[st]);
-                if (pending >= 0) {
-                    tmem_st_wait();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&S.a_full[pending]);
-                    pending = -1;
-                }
+                if (pending >= 0) publish();
                 if (g >= kSA && !warp_wait(&S.a_empty[sa], ((g / kSA) & 1) ^ 1, abort_flag, p.err)) break;
                 tc_fence_after();  // the store follows the MMAs that read this stage
                 tmem_st32(tmem + lane_base + kACol + sa * 32, v);
                 pending = sa;
             }
-            if (pending >= 0) {
-                tmem_st_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&S.a_full[pending]);
-            }
+            if (pending >= 0) publish();
         }
     } else if (warp >= kEpiWarp0) {
         // ---------------- epilogue, one warp per TMEM lane quarter
         const int q4 = warp & 3;
         const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+        constexpr int kCols = B * T;  // accumulator columns in use
+        constexpr int kHalves = kCols > 16 ? 2 : 1;
         for (int i = 0; i < ntile_cta; ++i) {
             const int buf = i & 1;
             if (!warp_wait(&S.acc_full[buf], (i >> 1) & 1, abort_flag, p.err)) break;
             tc_fence_after();
-            uint32_t d[32];
-            tmem_ld16(tmem + lane_base + buf * 32, *reinterpret_cast<uint32_t(*)[16]>(&d[0]));
-            if constexpr (N > 16) tmem_ld16(tmem + lane_base + buf * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&d[16]));
+            // add the accumulators of the issuers that had a slot in this tile, in issuer order
+            const int g0 = i * nslots;
+            uint32_t d[16 * kHalves];
+#pragma unroll
+            for (int c = 0; c < 16 * kHalves; ++c) d[c] = 0;
+#pragma unroll
+            for (int me = 0; me < kNI; ++me) {
+                if ((me - g0 % kNI + kNI) % kNI >= nslots) continue;  // no slot of this tile
+#pragma unroll
+                for (int h = 0; h < kHalves; ++h) {
+                    uint32_t t[16];
+                    tmem_ld16(tmem + lane_base + (me * 2 + buf) * N + h * 16, t);
+#pragma unroll
+                    for (int c = 0; c < 16; ++c) {
+                        if constexpr (FMT == BRAMHA_FMT_LOG4)
+                            d[h * 16 + c] = __float_as_uint(__uint_as_float(d[h * 16 + c]) + __uint_as_float(t[c]));
+                        else
+                            d[h * 16 + c] += t[c];  // s32
+                    }
+                }
+            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.d_empty[buf]);
@@ -519,7 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
 #pragma unroll
                         for (int j = T - 1; j >= 0; --j) acc = acc * 0.0078125f + (float)(int)d[b * T + j];
                     }
-                    const float xq = acc * S.inv_s[b];  // sum(a * x) with a as stored in A
+                    const float xq = acc / act_scale<FMT>(S.amax[b]);  // sum(a * x), a as held in A
                     float dot;
                     if constexpr (FMT == BRAMHA_FMT_LOG4) dot = fmaf(xq, 16384.0f, -S.sx[b]);  // sum((2^c - 1) x)
                     else if constexpr (FMT == BRAMHA_FMT_W4ZP8) dot = fmaf(-8.0f, S.sx[b], xq);  // sum((q - 8) x)
@@ -564,31 +632,23 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
     }
 }
 
-template <int FMT, int B>
-cudaError_t launch_b(const TcGemvParams& p, int grid, cudaStream_t st) {
-    auto kern = tc_gemv_kernel<FMT, B>;
-    constexpr int smem = (int)sizeof(TcSmem) + 1024;
-    static_assert(smem <= 227 * 1024, "shared memory per CTA exceeds 227 KB");
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    kern<<<grid, kThreads, smem, st>>>(p);
-    return cudaGetLastError();
-}
-
 // Largest K range (64-column blocks) one CTA takes: its B terms fit the B
-// area and its raw activations the staging area.
+// area and its raw activations the staging area and the threads' loads.
 int max_split_steps(int fmt, int batch) {
     const int terms = fmt == BRAMHA_FMT_LOG4 ? 4 : 3;
     const int n = batch * terms <= 16 ? 16 : 32;
-    const int by_terms = 2 * (kXBytes / (n * 128));
+    int m = 2 * (kXBytes / (n * 128));
     const int by_stage = kStageFloats / (batch * kTileK);
-    return by_terms < by_stage ? by_terms : by_stage;
+    const int by_threads = kPerThread * kThreads / kTileK;
+    if (by_stage < m) m = by_stage;
+    if (by_threads < m) m = by_threads;
+    return m;
 }
 
 // K split: the one that minimises the time of the busiest CTA (one CTA per
-// SM), counted in 64-column blocks: its blocks, ~1 per tile for the epilogue,
-// and for a split ~2 + ksplit/8 for the combine.  Splits start on even blocks
-// so 4-bit slots stay whole.  False when no split fits.
+// SM), counted in 64-column blocks: its blocks, ~1 per tile for the
+// epilogue, and for a split ~2 + ksplit/8 for the combine.  Splits start on
+// even blocks so 4-bit slots stay whole.  False when no split fits.
 bool plan_gemv_tc(int ntiles, int ksteps, int max_steps, int max_ksplit, int num_sms, int* ksplit_out,
                   int* steps_per_split_out, int* ctas_per_split_out) {
     int64_t best = INT64_MAX;
@@ -614,6 +674,20 @@ bool plan_gemv_tc(int ntiles, int ksteps, int max_steps, int max_ksplit, int num
     *steps_per_split_out = bspp;
     *ctas_per_split_out = bcps;
     return best != INT64_MAX;
+}
+
+template <int FMT, int B>
+cudaError_t launch_b(TcGemvParams& p, int max_ksplit, int num_sms, cudaStream_t st) {
+    auto kern = tc_gemv_kernel<FMT, B>;
+    constexpr int smem = (int)sizeof(TcSmem) + 1024;
+    static_assert(smem <= 227 * 1024, "shared memory per CTA exceeds 227 KB");
+    if (!plan_gemv_tc(p.ntiles, p.ksteps, max_split_steps(FMT, B), max_ksplit, num_sms, &p.ksplit,
+                      &p.steps_per_split, &p.ctas_per_split))
+        return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    kern<<<p.ksplit * p.ctas_per_split, kThreads, smem, st>>>(p);
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -644,21 +718,17 @@ cudaError_t launch_gemv_tc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t
     p.ntiles = ntiles;
     p.K = a.K;
     p.ksteps = (int)k_steps(a.K);
+    p.ws = a.split_ws;
+    p.tickets = a.split_tickets;
     // splits need a workspace slot per (tile, split, batch row) and a ticket per tile
     int max_ksplit = 1;
     if (a.split_ws && a.split_tickets && ntiles <= a.split_tickets_n)
         max_ksplit = (int)(a.split_ws_floats / ((int64_t)ntiles * a.batch * TM));
-    if (!plan_gemv_tc(ntiles, p.ksteps, max_split_steps(fmt, a.batch), max_ksplit, num_sms, &p.ksplit,
-                      &p.steps_per_split, &p.ctas_per_split))
-        return cudaErrorInvalidValue;
-    p.ws = a.split_ws;
-    p.tickets = a.split_tickets;
-    const int grid = p.ksplit * p.ctas_per_split;
-#define BRAMHA_TC_B(n)                                                                    \
-    case n:                                                                               \
-        return fmt == BRAMHA_FMT_LOG4    ? launch_b<BRAMHA_FMT_LOG4, n>(p, grid, st)      \
-               : fmt == BRAMHA_FMT_W4ZP8 ? launch_b<BRAMHA_FMT_W4ZP8, n>(p, grid, st)     \
-                                         : launch_b<BRAMHA_FMT_W8, n>(p, grid, st);
+#define BRAMHA_TC_B(n)                                                                                   \
+    case n:                                                                                              \
+        return fmt == BRAMHA_FMT_LOG4    ? launch_b<BRAMHA_FMT_LOG4, n>(p, max_ksplit, num_sms, st)      \
+               : fmt == BRAMHA_FMT_W4ZP8 ? launch_b<BRAMHA_FMT_W4ZP8, n>(p, max_ksplit, num_sms, st)     \
+                                         : launch_b<BRAMHA_FMT_W8, n>(p, max_ksplit, num_sms, st);
     switch (a.batch) {
         BRAMHA_TC_B(1)
         BRAMHA_TC_B(2)

@@ -46,10 +46,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait for the phase with `parity` to complete.  On timeout (or when
-// another thread already gave up) records the error and returns false.
+// Non-blocking test of a phase.
+__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the phase with `parity` to complete (a non-blocking test
+// first: a phase that already completed costs no suspend).  On timeout (or
+// when another thread already gave up) records the error and returns false.
 __device__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err) {
-    if (mbar_try_wait(b, parity)) return true;
+    if (mbar_test(b, parity) || mbar_try_wait(b, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (;;) {
         if (mbar_try_wait(b, parity)) return true;
