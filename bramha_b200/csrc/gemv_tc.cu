@@ -36,20 +36,23 @@
 // the partials in split order and writes y, so results do not depend on
 // timing.  A ring slot is 8 KB: two 64-column blocks of a 4-bit tile (K = 128)
 // or one int8 block (K = 64).
-//   warps 0, 5   bulk copies into the 96 KB ring (12 slots; producer p takes
-//                slots g = p, p+2, ...: one thread issuing 8 KB copies tops
-//                out near 4.9 TB/s, two reach the HBM peak -- measured); the
-//                whole ring is requested during the prologue, right after the
-//                activation loads
+//   warps 0, 5   bulk copies into the 128 KB ring (16 slots of 8 KB, filled and
+//                released in pairs: one barrier and, within a tile, one 16 KB
+//                copy per pair; producer p takes pairs d = p, p+2, ...).  A
+//                thread issuing 8 KB copies tops out near 4.9 TB/s, 16 KB
+//                copies reach the HBM peak (measured).  Slots 0-11 are
+//                requested during the prologue, right after the activation
+//                loads; slots 12-15 hold the raw activations until the
+//                prologue ends
 //   warps 1-4    MMA issuers (lane 0)
 //   warps 8-23   (4-bit) dequantize: four groups take slots g, g+4, ...; a
 //                warp owns one TMEM lane quarter: 128 codes per row -> 32
 //                words -> one tcgen05.st into an A stage
 //   warps 24-27  epilogue (tcgen05.ld of the double-buffered accumulators)
 //   prologue     all warps load the split's activations once (staged raw),
-//                reduce max|x| and sum(x); warps 1-4, 6, 7 and 24-27 then
-//                write the 8-bit B terms (K-major, 128-byte swizzle, one
-//                128-column atom per 128 K) while the dequant warps start.
+//                reduce max|x| and sum(x), and write the 8-bit B terms
+//                (K-major, 128-byte swizzle, one 128-column atom per 128 K)
+//                while the first weights are in flight.
 // Ring slots and A stages are multiples of 4 deep, so each one is always
 // consumed by the same dequant group and the same issuer: a parity wait can
 // never see a phase two generations old.  Every mbarrier wait is bounded
@@ -70,7 +73,9 @@ namespace {
 
 constexpr int TM = 128;                   // weight rows per tile (UMMA M, TMEM lanes)
 constexpr int kSlotBytes = 8192;
-constexpr int kSW = 12;                   // ring slots
+constexpr int kSW = 16;                   // ring slots
+constexpr int kPrologueSlots = 12;        // slots free during the prologue (the rest stage activations)
+constexpr int kSD = kSW / 2;              // ring slot pairs (one barrier each)
 constexpr int kNI = 4;                    // MMA issuers
 constexpr int kGroups = 4;                // dequant groups (4 warps each)
 constexpr int kIssWarp0 = 1;
@@ -79,11 +84,10 @@ constexpr int kProdWarp1 = 5;
 constexpr int kDeqWarp0 = 8;
 constexpr int kEpiWarp0 = kDeqWarp0 + 4 * kGroups;  // 24
 constexpr int kThreads = (kEpiWarp0 + 4) * 32;      // 896
-constexpr int kBuilders = 10;             // warps 1-4, 6, 7 and 24-27 write the B terms
 constexpr int kXBytes = 64 * 1024;        // B terms of one split
-constexpr int kStageFloats = 8192;        // raw activations of one split (32 KB)
+constexpr int kStageFloats = (kSW - kPrologueSlots) * kSlotBytes / 4;  // raw activations of one split
 constexpr int kPerThread = 10;            // activation columns a thread loads per batch row
-static_assert(kSW % kGroups == 0 && kSW % kNI == 0 && kSW % kNP == 0,
+static_assert(kSW % kGroups == 0 && kSW % kNI == 0 && kSD % kNP == 0,
               "a ring slot must always have the same producer and consumer");
 static_assert(kDeqWarp0 % 4 == 0 && kEpiWarp0 % 4 == 0, "TMEM lane quarters follow warp % 4");
 
@@ -131,12 +135,11 @@ struct TcGemvParams {
 };
 
 struct alignas(1024) TcSmem {
-    uint8_t w[kSW][kSlotBytes];
+    uint8_t w[kSW][kSlotBytes];   // slots kPrologueSlots.. double as the activation staging area
     uint8_t x[kXBytes];
-    float stage[kStageFloats];
-    uint64_t w_full[kSW], w_empty[kSW];
+    uint64_t w_full[kSD], w_empty[kSD];  // per slot pair
     uint64_t a_full[12], a_empty[12];
-    uint64_t acc_full[2], d_empty[2], mma_done, b_ready;
+    uint64_t acc_full[2], d_empty[2], mma_done;
     float amax[8], sx[8];
     uint32_t tmem;
     int abort_flag;
@@ -306,11 +309,29 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
         return sg.q + ((int64_t)(tile - sg.tile_begin) * p.ksteps + step0 + s) * Fm::kBlock;
     };
 
+    // copies of slot pair d (slots 2d, 2d + 1) into ring slots 2d % kSW, +1,
+    // completing on w_full[d % kSD]; one copy when the pair is contiguous
+    auto issue_pair = [&](int d) {
+        const int g = 2 * d, st = g % kSW;
+        uint32_t b0 = 0, b1 = 0;
+        const uint8_t* s0 = slot_src(g, b0);
+        const uint8_t* s1 = g + 1 < total ? slot_src(g + 1, b1) : nullptr;
+        uint64_t* bar = &S.w_full[d % kSD];
+        mbar_expect_tx(bar, b0 + b1);
+        if (s1 && b0 == (uint32_t)kSlotBytes && s1 == s0 + kSlotBytes) {
+            bulk_load(&S.w[st][0], s0, b0 + b1, bar);
+        } else {
+            bulk_load(&S.w[st][0], s0, b0, bar);
+            if (s1) bulk_load(&S.w[st + 1][0], s1, b1, bar);
+        }
+    };
+    const int npairs = (total + 1) / 2;
+
     // ---------------- prologue: barriers, zeroed B area, the whole ring requested
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kSW; ++s) {
+        for (int s = 0; s < kSD; ++s) {
             mbar_init(&S.w_full[s], 1);
-            mbar_init(&S.w_empty[s], Fm::kDeq ? 4 : 1);
+            mbar_init(&S.w_empty[s], Fm::kDeq ? 8 : 2);  // both slots' consumers
         }
         for (int s = 0; s < kSA; ++s) {
             mbar_init(&S.a_full[s], 4);
@@ -321,7 +342,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             mbar_init(&S.d_empty[i], 4);
         }
         mbar_init(&S.mma_done, kNI);
-        mbar_init(&S.b_ready, kBuilders);
         for (int b = 0; b < 8; ++b) {
             S.amax[b] = 0.f;
             S.sx[b] = 0.f;
@@ -335,7 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
         for (int i = threadIdx.x; i < nz; i += kThreads) xz[i] = make_uint4(0, 0, 0, 0);
     }
     __syncthreads();
-    const int first = min(kSW, total);
+    const int first = min(kPrologueSlots / 2, npairs);  // slot pairs requested in the prologue
+    float* stage = reinterpret_cast<float*>(&S.w[kPrologueSlots][0]);
     const bool producer = (warp == 0 || warp == kProdWarp1) && lane == 0;
     const int pid = warp == 0 ? 0 : 1;
 
@@ -354,19 +375,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             if (b == 0) {
                 // the weight ring is requested once the activation loads are out
                 if (producer)
-                    for (int g = pid; g < first; g += kNP) {
-                        uint32_t bytes;
-                        const uint8_t* src = slot_src(g, bytes);
-                        mbar_expect_tx(&S.w_full[g], bytes);
-                        bulk_load(&S.w[g][0], src, bytes, &S.w_full[g]);
-                    }
+                    for (int d = pid; d < first; d += kNP) issue_pair(d);
                 if (warp == 1) tmem_alloc(&S.tmem, 512);
             }
             float am = 0.f, sm = 0.f;
 #pragma unroll
             for (int u = 0; u < kPerThread; ++u) {
                 const int k = threadIdx.x + u * kThreads;
-                if (k < nk) S.stage[b * nk + k] = v[u];
+                if (k < nk) stage[b * nk + k] = v[u];
                 am = fmaxf(am, fabsf(v[u]));
                 sm += v[u];
             }
@@ -386,15 +402,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
     tc_fence_after();
     const uint32_t tmem = S.tmem;
 
-    // ---------------- B terms (warps 1-4, 6, 7 and 24-27, while the dequant warps start)
-    if ((warp > 0 && warp < kDeqWarp0 && warp != kProdWarp1) || warp >= kEpiWarp0) {
-        const int bw = warp < kProdWarp1 ? warp - 1 : warp < kDeqWarp0 ? warp - 2 : warp - kEpiWarp0 + 6;
-        const int bt = bw * 32 + lane;
+    // ---------------- B terms (all warps)
+    {
+        const int bt = threadIdx.x;
         float scl[B];
 #pragma unroll
         for (int b = 0; b < B; ++b) scl[b] = act_scale<FMT>(S.amax[b]);
         const int npos4 = nkb * 32;  // 4-position groups per batch row
-        for (int i = bt; i < B * npos4; i += kBuilders * 32) {
+        for (int i = bt; i < B * npos4; i += kThreads) {
             const int b = i / npos4, g4 = i - b * npos4;
             const int p0 = g4 * 4, kb = p0 >> 7, pin = p0 & 127;
             float s = scl[0];
@@ -405,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int col = (kb << 7) + pos_to_col<FMT>(pin + e);
-                v[e] = col < nk ? S.stage[b * nk + col] * s : 0.f;
+                v[e] = col < nk ? stage[b * nk + col] * s : 0.f;
             }
             uint32_t word[T];
             make_terms<FMT, T>(v[0], v[1], v[2], v[3], word);
@@ -417,27 +432,23 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
                                              (pin & 15)) = word[j];
             }
         }
-        fence_async_smem();  // generic writes -> MMA reads
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.b_ready);
     }
+    // B terms: generic writes -> MMA reads; staging reads -> bulk copies into slots 12-15
+    fence_async_smem();
+    __syncthreads();
 
     if (warp == 0 || warp == kProdWarp1) {
-        // ---------------- bulk-copy producer `pid`: slots g = pid, pid + 2, ...
+        // ---------------- bulk-copy producer `pid`: slot pairs d = pid, pid + 2, ...
         if (lane == 0) {
-            int g = first + ((pid - first % kNP + kNP) % kNP);  // first slot of mine not yet requested
-            for (; g < total; g += kNP) {
-                const int st = g % kSW;
-                if (!mbar_wait(&S.w_empty[st], ((g / kSW) & 1) ^ 1, abort_flag, p.err)) break;
-                uint32_t bytes;
-                const uint8_t* src = slot_src(g, bytes);
-                mbar_expect_tx(&S.w_full[st], bytes);
-                bulk_load(&S.w[st][0], src, bytes, &S.w_full[st]);
+            int d = first + ((pid - first % kNP + kNP) % kNP);  // first pair of mine not yet requested
+            for (; d < npairs; d += kNP) {
+                if (!mbar_wait(&S.w_empty[d % kSD], ((d / kSD) & 1) ^ 1, abort_flag, p.err)) break;
+                issue_pair(d);
             }
             // every copy this producer issued lands before the CTA exits
             const uint64_t deadline = globaltimer() + kTimeoutNs;
-            for (int j = pid; j < g && j < total; j += kNP)
-                if (j + kSW >= g && !mbar_wait_until(&S.w_full[j % kSW], (j / kSW) & 1, deadline)) break;
+            for (int j = pid; j < d && j < npairs; j += kNP)
+                if (j + kSD >= d && !mbar_wait_until(&S.w_full[j % kSD], (j / kSD) & 1, deadline)) break;
         }
     } else if (warp >= kIssWarp0 && warp < kIssWarp0 + kNI) {
         // ---------------- MMA issuer `me`: slots g with g % kNI == me, into accumulator `me`
@@ -445,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             const int me = warp - kIssWarp0;
             constexpr uint32_t idesc = idesc8<FMT, N>();
             const uint32_t xbase = smem_u32(&S.x[0]);
-            bool ok = mbar_wait(&S.b_ready, 0, abort_flag, p.err);
+            bool ok = true;
             for (int i = 0; i < ntile_cta && ok; ++i) {
                 const int buf = i & 1;
                 if (i >= 2 && !mbar_wait(&S.d_empty[buf], ((i >> 1) - 1) & 1, abort_flag, p.err)) break;
@@ -469,8 +480,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
                                       (acc || kk > 0) ? 1u : 0u);
                         umma_commit(&S.a_empty[sa]);
                     } else {
-                        const int st = g % kSW;
-                        if (!mbar_wait(&S.w_full[st], (g / kSW) & 1, abort_flag, p.err)) {
+                        const int st = g % kSW, sd = (g >> 1) % kSD;
+                        if (!mbar_wait(&S.w_full[sd], ((g >> 1) / kSD) & 1, abort_flag, p.err)) {
                             ok = false;
                             break;
                         }
@@ -481,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
                         for (int kk = 0; kk < Fm::kMmaPerSlot; ++kk)
                             mma8<FMT>(dcol, 0, desc_sw64(wa + kk * 32), desc_sw128(xt + kk * 32), idesc,
                                       (acc || kk > 0) ? 1u : 0u);
-                        umma_commit(&S.w_empty[st]);
+                        umma_commit(&S.w_empty[sd]);
                     }
                     acc = true;
                 }
@@ -510,9 +521,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
                 pending = -1;
             };
             for (int g = grp; g < total; g += kGroups) {
-                const int st = g % kSW, sa = g % kSA;
-                if (pending >= 0 && !__all_sync(0xffffffffu, mbar_test(&S.w_full[st], (g / kSW) & 1))) publish();
-                if (!warp_wait(&S.w_full[st], (g / kSW) & 1, abort_flag, p.err)) break;
+                const int st = g % kSW, sd = (g >> 1) % kSD, sa = g % kSA;
+                const uint32_t par = ((g >> 1) / kSD) & 1;
+                if (pending >= 0 && !__all_sync(0xffffffffu, mbar_test(&S.w_full[sd], par))) publish();
+                if (!warp_wait(&S.w_full[sd], par, abort_flag, p.err)) break;
                 uint32_t v[32];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {  // the slot's two 64-column blocks
@@ -527,7 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
                 // bulk copy into it is an async-proxy write
                 fence_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&S.w_empty[st]);
+                if (lane == 0) mbar_arrive(&S.w_empty[sd]);
                 if (pending >= 0) publish();
                 if (g >= kSA && !warp_wait(&S.a_empty[sa], ((g / kSA) & 1) ^ 1, abort_flag, p.err)) break;
                 tc_fence_after();  // the store follows the MMAs that read this stage
