@@ -79,8 +79,12 @@ typedef struct bramha_weight bramha_weight;
 
 /* Replaces WgpuComputePlane::new (wgpu_backend.rs:121) / get_wgpu_plane
  * (wgpu_backend.rs:1710-1728): binds `device`, creates the context stream and
- * the weight registry.  Fails with BRAMHA_ERR_UNSUPPORTED on a device that is
- * not sm_100 (the kernels are built for sm_100a only). */
+ * the weight registry, and allocates the context's GEMV scratch (32 MB of
+ * K-split partial results and a ticket array, kept for the context's life).
+ * GEMV calls on one context share that scratch, so GEMVs of one context must
+ * not run concurrently on different streams (use one context per stream for
+ * that).  Fails with BRAMHA_ERR_UNSUPPORTED on a device that is not sm_100
+ * (the kernels are built for sm_100a only). */
 BRAMHA_API int bramha_cuda_init(int device, bramha_ctx** out);
 
 /* Frees every registered weight and the context. */
