@@ -53,6 +53,11 @@
 //                reduce max|x| and sum(x), and write the 8-bit B terms
 //                (K-major, 128-byte swizzle, one 128-column atom per 128 K)
 //                while the first weights are in flight.
+// Launches are programmatically dependent (PDL): a CTA may start on an SM as
+// soon as the previous launch's CTA there has exited, sets up its barriers,
+// TMEM and first weight copies (weights are immutable), and waits for the
+// previous launch to complete (griddepcontrol.wait) before it reads
+// activations or writes outputs or the K-split workspace.
 // Ring slots and A stages are multiples of 4 deep, so each one is always
 // consumed by the same dequant group and the same issuer: a parity wait can
 // never see a phase two generations old.  Every mbarrier wait is bounded
@@ -327,7 +332,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
     };
     const int npairs = (total + 1) / 2;
 
-    // ---------------- prologue: barriers, zeroed B area, the whole ring requested
+    // the next launch may start its own set-up as our CTAs retire
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    // ---------------- prologue: barriers, zeroed B area, the first weights requested
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSD; ++s) {
             mbar_init(&S.w_full[s], 1);
@@ -359,6 +367,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
     float* stage = reinterpret_cast<float*>(&S.w[kPrologueSlots][0]);
     const bool producer = (warp == 0 || warp == kProdWarp1) && lane == 0;
     const int pid = warp == 0 ? 0 : 1;
+    if (producer)
+        for (int d = pid; d < first; d += kNP) issue_pair(d);
+    if (warp == 1) tmem_alloc(&S.tmem, 512);
+    // activations, outputs and the K-split workspace belong to the stream order
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     // ---------------- activations -> staging, max|x|, sum(x)
     {
@@ -371,12 +384,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             for (int u = 0; u < kPerThread; ++u) {
                 const int k = threadIdx.x + u * kThreads;
                 v[u] = k < kv ? __ldg(xr + k) : 0.f;
-            }
-            if (b == 0) {
-                // the weight ring is requested once the activation loads are out
-                if (producer)
-                    for (int d = pid; d < first; d += kNP) issue_pair(d);
-                if (warp == 1) tmem_alloc(&S.tmem, 512);
             }
             float am = 0.f, sm = 0.f;
 #pragma unroll
@@ -698,8 +705,17 @@ cudaError_t launch_b(TcGemvParams& p, int max_ksplit, int num_sms, cudaStream_t 
         return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    kern<<<p.ksplit * p.ctas_per_split, kThreads, smem, st>>>(p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)(p.ksplit * p.ctas_per_split));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, (const TcGemvParams)p);
 }
 
 }  // namespace
