@@ -49,10 +49,11 @@
 //                warp owns one TMEM lane quarter: 128 codes per row -> 32
 //                words -> one tcgen05.st into an A stage
 //   warps 24-27  epilogue (tcgen05.ld of the double-buffered accumulators)
-//   prologue     all warps load the split's activations once (staged raw),
-//                reduce max|x| and sum(x), and write the 8-bit B terms
-//                (K-major, 128-byte swizzle, one 128-column atom per 128 K)
-//                while the first weights are in flight.
+//   prologue     warps 0-7 and 24-27 load the split's activations once
+//                (staged raw), reduce max|x| and sum(x), and write the 8-bit
+//                B terms (K-major, 128-byte swizzle, one 128-column atom per
+//                128 K); meanwhile the dequant warps already decode the first
+//                weights (they touch neither activations nor outputs).
 // Launches are programmatically dependent (PDL): a CTA may start on an SM as
 // soon as the previous launch's CTA there has exited, sets up its barriers,
 // TMEM and first weight copies (weights are immutable), and waits for the
@@ -91,7 +92,8 @@ constexpr int kEpiWarp0 = kDeqWarp0 + 4 * kGroups;  // 24
 constexpr int kThreads = (kEpiWarp0 + 4) * 32;      // 896
 constexpr int kXBytes = 64 * 1024;        // B terms of one split
 constexpr int kStageFloats = (kSW - kPrologueSlots) * kSlotBytes / 4;  // raw activations of one split
-constexpr int kPerThread = 10;            // activation columns a thread loads per batch row
+constexpr int kActThreads = 384;          // warps 0-7 and 24-27 stage the activations and build B
+constexpr int kPerThread = 12;            // activation columns a thread loads per batch row
 static_assert(kSW % kGroups == 0 && kSW % kNI == 0 && kSD % kNP == 0,
               "a ring slot must always have the same producer and consumer");
 static_assert(kDeqWarp0 % 4 == 0 && kEpiWarp0 % 4 == 0, "TMEM lane quarters follow warp % 4");
@@ -146,6 +148,7 @@ struct alignas(1024) TcSmem {
     uint64_t a_full[12], a_empty[12];
     uint64_t acc_full[2], d_empty[2], mma_done;
     float amax[8], sx[8];
+    float sx_part[kActThreads / 32][8];  // per-warp partial sums, added in warp order
     uint32_t tmem;
     int abort_flag;
     int last_split;
@@ -357,92 +360,102 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
         S.abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    if (warp == 1) tmem_alloc(&S.tmem, 512);
     {
         uint4* xz = reinterpret_cast<uint4*>(&S.x[0]);
         const int nz = nkb * kXSlot / 16;
         for (int i = threadIdx.x; i < nz; i += kThreads) xz[i] = make_uint4(0, 0, 0, 0);
     }
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = S.tmem;
     const int first = min(kPrologueSlots / 2, npairs);  // slot pairs requested in the prologue
     float* stage = reinterpret_cast<float*>(&S.w[kPrologueSlots][0]);
     const bool producer = (warp == 0 || warp == kProdWarp1) && lane == 0;
     const int pid = warp == 0 ? 0 : 1;
     if (producer)
         for (int d = pid; d < first; d += kNP) issue_pair(d);
-    if (warp == 1) tmem_alloc(&S.tmem, 512);
-    // activations, outputs and the K-split workspace belong to the stream order
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const bool act = warp < kDeqWarp0 || warp >= kEpiWarp0;       // activation warps
+    const int ta = (warp < kDeqWarp0 ? warp : warp - kEpiWarp0 + kDeqWarp0) * 32 + lane;  // 0..383
 
-    // ---------------- activations -> staging, max|x|, sum(x)
-    {
-        const int kv = min(nk, p.K - k0);
+    if (act) {
+        // activations, outputs and the K-split workspace belong to the stream order
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+
+        // ---------------- activations -> staging, max|x|, sum(x)
+        {
+            const int kv = min(nk, p.K - k0);
 #pragma unroll
-        for (int b = 0; b < B; ++b) {
-            const float* xr = p.x + (int64_t)b * p.ldx + k0;
-            float v[kPerThread];
+            for (int b = 0; b < B; ++b) {
+                const float* xr = p.x + (int64_t)b * p.ldx + k0;
+                float v[kPerThread];
 #pragma unroll
-            for (int u = 0; u < kPerThread; ++u) {
-                const int k = threadIdx.x + u * kThreads;
-                v[u] = k < kv ? __ldg(xr + k) : 0.f;
-            }
-            float am = 0.f, sm = 0.f;
+                for (int u = 0; u < kPerThread; ++u) {
+                    const int k = ta + u * kActThreads;
+                    v[u] = k < kv ? __ldg(xr + k) : 0.f;
+                }
+                float am = 0.f, sm = 0.f;
 #pragma unroll
-            for (int u = 0; u < kPerThread; ++u) {
-                const int k = threadIdx.x + u * kThreads;
-                if (k < nk) stage[b * nk + k] = v[u];
-                am = fmaxf(am, fabsf(v[u]));
-                sm += v[u];
-            }
+                for (int u = 0; u < kPerThread; ++u) {
+                    const int k = ta + u * kActThreads;
+                    if (k < nk) stage[b * nk + k] = v[u];
+                    am = fmaxf(am, fabsf(v[u]));
+                    sm += v[u];
+                }
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-                sm += __shfl_xor_sync(0xffffffffu, sm, o);
-            }
-            if (lane == 0) {
-                atomicMax(reinterpret_cast<int*>(&S.amax[b]), __float_as_int(am));  // am >= 0
-                atomicAdd(&S.sx[b], sm);
+                for (int o = 16; o > 0; o >>= 1) {
+                    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+                    sm += __shfl_xor_sync(0xffffffffu, sm, o);
+                }
+                if (lane == 0) {
+                    atomicMax(reinterpret_cast<int*>(&S.amax[b]), __float_as_int(am));  // am >= 0 (order-free)
+                    S.sx_part[ta >> 5][b] = sm;
+                }
             }
         }
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = S.tmem;
+        asm volatile("bar.sync 2, %0;" ::"n"(kActThreads) : "memory");
+        if (ta < B) {  // sum(x) in a fixed order, so results do not depend on timing
+            float s = 0.f;
+            for (int w = 0; w < kActThreads / 32; ++w) s += S.sx_part[w][ta];
+            S.sx[ta] = s;
+        }
 
-    // ---------------- B terms (all warps)
-    {
-        const int bt = threadIdx.x;
-        float scl[B];
+        // ---------------- B terms
+        {
+            const int bt = ta;
+            float scl[B];
 #pragma unroll
-        for (int b = 0; b < B; ++b) scl[b] = act_scale<FMT>(S.amax[b]);
-        const int npos4 = nkb * 32;  // 4-position groups per batch row
-        for (int i = bt; i < B * npos4; i += kThreads) {
-            const int b = i / npos4, g4 = i - b * npos4;
-            const int p0 = g4 * 4, kb = p0 >> 7, pin = p0 & 127;
-            float s = scl[0];
+            for (int b = 0; b < B; ++b) scl[b] = act_scale<FMT>(S.amax[b]);
+            const int npos4 = nkb * 32;  // 4-position groups per batch row
+            for (int i = bt; i < B * npos4; i += kActThreads) {
+                const int b = i / npos4, g4 = i - b * npos4;
+                const int p0 = g4 * 4, kb = p0 >> 7, pin = p0 & 127;
+                float s = scl[0];
 #pragma unroll
-            for (int bb = 1; bb < B; ++bb)
-                if (b == bb) s = scl[bb];
-            float v[4];
+                for (int bb = 1; bb < B; ++bb)
+                    if (b == bb) s = scl[bb];
+                float v[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int col = (kb << 7) + pos_to_col<FMT>(pin + e);
-                v[e] = col < nk ? stage[b * nk + col] * s : 0.f;
-            }
-            uint32_t word[T];
-            make_terms<FMT, T>(v[0], v[1], v[2], v[3], word);
-            uint8_t* atom = &S.x[kb * kXSlot];
+                for (int e = 0; e < 4; ++e) {
+                    const int col = (kb << 7) + pos_to_col<FMT>(pin + e);
+                    v[e] = col < nk ? stage[b * nk + col] * s : 0.f;
+                }
+                uint32_t word[T];
+                make_terms<FMT, T>(v[0], v[1], v[2], v[3], word);
+                uint8_t* atom = &S.x[kb * kXSlot];
 #pragma unroll
-            for (int j = 0; j < T; ++j) {
-                const int n = b * T + j;
-                *reinterpret_cast<uint32_t*>(atom + (n >> 3) * 1024 + (n & 7) * 128 + (((pin >> 4) ^ (n & 7)) << 4) +
-                                             (pin & 15)) = word[j];
+                for (int j = 0; j < T; ++j) {
+                    const int n = b * T + j;
+                    *reinterpret_cast<uint32_t*>(atom + (n >> 3) * 1024 + (n & 7) * 128 + (((pin >> 4) ^ (n & 7)) << 4) +
+                                                 (pin & 15)) = word[j];
+                }
             }
         }
-    }
-    // B terms: generic writes -> MMA reads; staging reads -> bulk copies into slots 12-15
-    fence_async_smem();
-    __syncthreads();
+        // B terms: generic writes -> MMA reads; staging reads -> bulk copies into slots 12-15
+        fence_async_smem();
+        asm volatile("bar.sync 2, %0;" ::"n"(kActThreads) : "memory");
+    }  // act
 
     if (warp == 0 || warp == kProdWarp1) {
         // ---------------- bulk-copy producer `pid`: slot pairs d = pid, pid + 2, ...
@@ -658,7 +671,7 @@ int max_split_steps(int fmt, int batch) {
     const int n = batch * terms <= 16 ? 16 : 32;
     int m = 2 * (kXBytes / (n * 128));
     const int by_stage = kStageFloats / (batch * kTileK);
-    const int by_threads = kPerThread * kThreads / kTileK;
+    const int by_threads = kPerThread * kActThreads / kTileK;
     if (by_stage < m) m = by_stage;
     if (by_threads < m) m = by_threads;
     return m;
