@@ -303,27 +303,49 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
     const int nslots = (nsteps + Fm::kStepsPerSlot - 1) / Fm::kStepsPerSlot;
     const int nkb = (nsteps + 1) >> 1;                                     // 128-K B atoms
     const int ntile_cta = (p.ntiles - 1 - ci) / p.ctas_per_split + 1;       // ci < ntiles (host)
+    const int nunit_tiles = ntile_cta;
     const int total = ntile_cta * nslots;                                  // slots this CTA streams
     const int k0 = step0 * kTileK;                                         // first column of the split
     const int nk = nsteps * kTileK;                                        // columns of the split
 
     // source and size of this CTA's g-th slot
-    auto slot_src = [&](int g, uint32_t& bytes) -> const uint8_t* {
-        const int i = g / nslots, j = g - i * nslots;
+    // A producer walks its slots with a cursor (tile i, slot j in the tile,
+    // the tile's first block of this split); the kernel-parameter segment
+    // table is read only when the tile changes -- those reads are dependent
+    // memory round trips, and per slot they capped a producer near 5 TB/s.
+    struct Cursor {
+        int i, j;
+        const uint8_t* base;
+    };
+    auto tile_base = [&](int i) -> const uint8_t* {
         const int tile = ci + i * p.ctas_per_split;
         const TcSeg& sg = p.seg[seg_of(p, tile)];
-        const int s = j * Fm::kStepsPerSlot;
-        bytes = (uint32_t)(min(Fm::kStepsPerSlot, nsteps - s) * Fm::kBlock);
-        return sg.q + ((int64_t)(tile - sg.tile_begin) * p.ksteps + step0 + s) * Fm::kBlock;
+        return sg.q + ((int64_t)(tile - sg.tile_begin) * p.ksteps + step0) * Fm::kBlock;
     };
-
-    // copies of slot pair d (slots 2d, 2d + 1) into ring slots 2d % kSW, +1,
-    // completing on w_full[d % kSD]; one copy when the pair is contiguous
-    auto issue_pair = [&](int d) {
+    auto advance = [&](Cursor& c, int n) {
+        c.j += n;
+        if (c.j >= nslots) {
+            do {
+                c.j -= nslots;
+                ++c.i;
+            } while (c.j >= nslots);
+            if (c.i < nunit_tiles) c.base = tile_base(c.i);
+        }
+    };
+    // copies of slot pair d (slots 2d, 2d + 1; cursor c at slot 2d) into ring
+    // slots 2d % kSW, +1, completing on w_full[d % kSD]; one copy when the
+    // pair is contiguous
+    auto issue_pair = [&](int d, Cursor c) {
         const int g = 2 * d, st = g % kSW;
-        uint32_t b0 = 0, b1 = 0;
-        const uint8_t* s0 = slot_src(g, b0);
-        const uint8_t* s1 = g + 1 < total ? slot_src(g + 1, b1) : nullptr;
+        const uint32_t b0 = (uint32_t)(min(Fm::kStepsPerSlot, nsteps - c.j * Fm::kStepsPerSlot) * Fm::kBlock);
+        const uint8_t* s0 = c.base + (int64_t)c.j * Fm::kStepsPerSlot * Fm::kBlock;
+        uint32_t b1 = 0;
+        const uint8_t* s1 = nullptr;
+        if (g + 1 < total) {
+            advance(c, 1);
+            b1 = (uint32_t)(min(Fm::kStepsPerSlot, nsteps - c.j * Fm::kStepsPerSlot) * Fm::kBlock);
+            s1 = c.base + (int64_t)c.j * Fm::kStepsPerSlot * Fm::kBlock;
+        }
         uint64_t* bar = &S.w_full[d % kSD];
         mbar_expect_tx(bar, b0 + b1);
         if (s1 && b0 == (uint32_t)kSlotBytes && s1 == s0 + kSlotBytes) {
@@ -374,8 +396,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
     float* stage = reinterpret_cast<float*>(&S.w[kPrologueSlots][0]);
     const bool producer = (warp == 0 || warp == kProdWarp1) && lane == 0;
     const int pid = warp == 0 ? 0 : 1;
-    if (producer)
-        for (int d = pid; d < first; d += kNP) issue_pair(d);
+    Cursor cur = {0, 0, nullptr};  // producer's cursor: slot 2 * (next pair of mine)
+    if (producer) {
+        cur.base = tile_base(0);
+        advance(cur, 2 * pid);
+        for (int d = pid; d < first; d += kNP) {
+            issue_pair(d, cur);
+            advance(cur, 2 * kNP);
+        }
+    }
     const bool act = warp < kDeqWarp0 || warp >= kEpiWarp0;       // activation warps
     const int ta = (warp < kDeqWarp0 ? warp : warp - kEpiWarp0 + kDeqWarp0) * 32 + lane;  // 0..383
 
@@ -463,7 +492,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             int d = first + ((pid - first % kNP + kNP) % kNP);  // first pair of mine not yet requested
             for (; d < npairs; d += kNP) {
                 if (!mbar_wait(&S.w_empty[d % kSD], ((d / kSD) & 1) ^ 1, abort_flag, p.err)) break;
-                issue_pair(d);
+                issue_pair(d, cur);
+                advance(cur, 2 * kNP);
             }
             // every copy this producer issued lands before the CTA exits
             const uint64_t deadline = globaltimer() + kTimeoutNs;
@@ -548,9 +578,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
                 uint32_t v[32];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {  // the slot's two 64-column blocks
+                    // rows are 32 B apart: rows r and r+4 read their halves in
+                    // opposite order, so each 8-lane phase of a 16-byte load hits
+                    // 32 distinct banks
                     const uint8_t* sl = &S.w[st][h * Fm::kBlock + row * 32];
-                    const uint4 p0 = *reinterpret_cast<const uint4*>(sl);
-                    const uint4 p1 = *reinterpret_cast<const uint4*>(sl + 16);
+                    const int sw = (row >> 2) & 1;
+                    const uint4 c0 = *reinterpret_cast<const uint4*>(sl + 16 * sw);
+                    const uint4 c1 = *reinterpret_cast<const uint4*>(sl + 16 * (sw ^ 1));
+                    const uint4 p0 = sw ? c1 : c0;
+                    const uint4 p1 = sw ? c0 : c1;
                     const uint32_t wv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
                     for (int i = 0; i < 8; ++i) dq_word8<FMT>(wv[i], v[16 * h + 2 * i], v[16 * h + 2 * i + 1]);
