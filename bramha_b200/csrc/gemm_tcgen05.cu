@@ -9,18 +9,24 @@
 //     log4 (dequantize_log4) :  2^(c - 15)   and y = s * (2^15 * acc - sum_k x[m][k])
 // so the only rounding is the fp32 accumulation in TMEM.
 //
-// One CTA computes a 128 (weight rows) x BN (tokens) tile: D = W_tile * X_tile^T
-// ("weights as the M operand"), looping over K in steps of 64.
-//   warp 0      TMA producer: X tile (bf16, 128-byte swizzle, tensor map) and
-//               the packed weight block (one contiguous bulk copy from the
-//               tile-major layout) per stage, mbarrier complete_tx.
-//   warp 1      allocates TMEM (BN fp32 columns), one lane issues tcgen05.mma
-//               (M=128, N=BN, K=16, both operands K-major SW128 in shared
-//               memory) and tcgen05.commit to release stages.
-//   warps 2-5   dequantize: thread t owns weight row t of the tile, reads its
-//               packed bytes, writes 8 x 16-byte bf16 chunks in the swizzled
-//               K-major layout the MMA descriptor describes; then the epilogue
-//               (tcgen05.ld of its TMEM lane, scale, store fp32).
+// Tiles are 128 weight rows x BN tokens: D = W_tile * X_tile^T ("weights as the
+// M operand"), K in steps of 64.  The kernel is persistent (one CTA per SM walks
+// tiles blockIdx.x, +gridDim.x, ...) and keeps two accumulators in TMEM, so the
+// epilogue of one tile overlaps the main loop of the next.
+//   warp 0      producer: per K step one TMA load of the X tile (bf16, 128-byte
+//               swizzle) and one bulk copy of the packed weight block (tile-major
+//               layout, repack.cu) into the load ring.
+//   warp 1      allocates TMEM (2 x BN fp32 columns); one lane issues
+//               tcgen05.mma (M=128, N=BN, K=16, both operands K-major SW128 in
+//               shared memory) and tcgen05.commit releases the ring slots and
+//               hands finished accumulators to the epilogue.
+//   warps 2-5   dequantize: thread t owns weight row t, reads its packed bytes
+//               from the load ring and writes 8 x 16-byte bf16 chunks into the
+//               swizzled K-major layout of the operand ring.
+//   warps 6-9   epilogue: tcgen05.ld of their TMEM lane quarter, scale (and the
+//               log4 correction), fp32 stores; then release the accumulator.
+// f32 activations are split x = hi + lo (both bf16) and laid side by side along
+// K, so one pass over 2K accumulates both halves.
 // Every mbarrier wait is bounded (~2 s of %globaltimer): on timeout the kernel
 // records BRAMHA_ERR_TIMEOUT in an error word, drains, frees TMEM and returns.
 #include <cuda.h>
@@ -28,6 +34,8 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
+#include <climits>
 #include <cstdint>
 #include <mutex>
 
@@ -39,17 +47,18 @@ namespace {
 
 constexpr int BM = 128;          // weight rows per tile (UMMA M)
 constexpr int BK = 64;           // K per stage: 64 bf16 = 128 bytes = one swizzle row
-constexpr int kThreads = 192;    // 6 warps
+constexpr int kThreads = 320;    // 10 warps
 
 struct GemmArgs {
     const uint8_t* q;      // tile-major weight (repack.cu)
     const float* scales;   // [N]
-    const float* rowsum;   // [M] sum of the bf16 activations (log4 only)
+    const float* rowsum;   // [M] sum of the activations the MMA sees (log4 only)
     float* y;              // [M][ldy]
     int64_t ldy;
-    int M, N, K;
-    int k_steps;
-    int accumulate;        // 0: y = result, 1: y += result (second half of a hi/lo split)
+    int M, N;
+    int k_steps;           // 64-column weight blocks per tile row
+    int x_steps;           // K steps per tile: k_steps, or 2 * k_steps for a hi|lo split
+    int n_tiles, m_tiles;  // tiles along the weight rows and along the tokens
     int* err;              // device error word (0 = ok)
 };
 
@@ -106,194 +115,269 @@ __device__ __forceinline__ uint4 dq_int8(uint32_t w0, uint32_t w1) {
     return o;
 }
 
-template <int FMT, int BN, int S>
+// Shared memory: a load ring (X tile + packed weight block per slot, filled by
+// the producer, freed by the MMA commit) and an operand ring (dequantized bf16
+// weight tile per slot, filled by the dequant warps, freed by the MMA commit).
+template <int FMT, int BN>
 struct Layout {
-    static constexpr int kX = BN * 128;                   // bytes per X stage
-    static constexpr int kA = BM * 128;                   // bytes per dequantized W stage
-    static constexpr int kP = BM * packed_bytes<FMT>();   // bytes per packed W stage
+    static constexpr int kX = BN * 128;                   // bytes per X slot
+    static constexpr int kA = BM * 128;                   // bytes per dequantized W slot
+    static constexpr int kP = BM * packed_bytes<FMT>();   // bytes per packed W slot
+    static constexpr int kBudget = 227 * 1024 - 1024 - 512;  // alignment slack, barriers
+    static constexpr int S2 = 4;                          // operand ring depth
+    static constexpr int kS1 = (kBudget - S2 * kA) / (kX + kP);
+    static constexpr int S1 = kS1 > 6 ? 6 : kS1;          // load ring depth
     static constexpr int offX = 0;
-    static constexpr int offA = offX + S * kX;
-    static constexpr int offP = offA + S * kA;
-    static constexpr int offBar = offP + S * kP;          // full_tma[S], full_a[S], empty[S], acc_full
-    static constexpr int offTmem = offBar + (3 * S + 1) * 8;
+    static constexpr int offA = offX + S1 * kX;
+    static constexpr int offP = offA + S2 * kA;
+    // full_tma[S1], empty_x[S1], full_a[S2], empty_a[S2], acc_full[2], acc_empty[2], mma_done
+    static constexpr int offBar = offP + S1 * kP;
+    static constexpr int offTmem = offBar + (2 * S1 + 2 * S2 + 5) * 8;
     static constexpr int offAbort = offTmem + 4;
     static constexpr int kBytes = offAbort + 4;
-    static constexpr int kAlloc = kBytes + 1024;           // slack to align the base to 1024
+    static constexpr int kAlloc = kBytes + 1024;          // slack to align the base to 1024
+    static constexpr uint32_t kTmemCols = 2 * BN;         // two accumulators
     static_assert(kAlloc <= 227 * 1024, "shared memory per CTA exceeds 227 KB");
-    static_assert(S >= 2, "need at least two stages");
+    static_assert(S1 >= 3, "load ring too shallow");
 };
 
-template <int FMT, int BN, int S>
+template <int FMT, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ GemmArgs a) {
-    using L = Layout<FMT, BN, S>;
+    using L = Layout<FMT, BN>;
+    constexpr int S1 = L::S1, S2 = L::S2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* Xs = smem + L::offX;
     uint8_t* As = smem + L::offA;
     uint8_t* Ps = smem + L::offP;
     uint64_t* full_tma = reinterpret_cast<uint64_t*>(smem + L::offBar);
-    uint64_t* full_a = full_tma + S;
-    uint64_t* empty = full_a + S;
-    uint64_t* acc_full = empty + S;
+    uint64_t* empty_x = full_tma + S1;
+    uint64_t* full_a = empty_x + S1;
+    uint64_t* empty_a = full_a + S2;
+    uint64_t* acc_full = empty_a + S2;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* mma_done = acc_empty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::offTmem);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::offAbort);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BM;   // first weight row
-    const int m0 = blockIdx.y * BN;   // first token
-    const int ksteps = a.k_steps;
+    const int ntiles = a.n_tiles * a.m_tiles;
+    const int xs = a.x_steps;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
+        for (int s = 0; s < S1; ++s) {
             mbar_init(&full_tma[s], 1);
-            mbar_init(&full_a[s], 128);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty_x[s], 1);
         }
-        mbar_init(acc_full, 1);
+        for (int s = 0; s < S2; ++s) {
+            mbar_init(&full_a[s], 128);
+            mbar_init(&empty_a[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        mbar_init(mma_done, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(BN)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
+    if (warp == 1) tmem_alloc(tmem_slot, L::kTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // ---------------- TMA producer
+        // ---------------- producer
         if (lane == 0) {
             constexpr uint32_t kTx = L::kX + L::kP;
-            int it = 0;
-            for (; it < ksteps; ++it) {
-                const int s = it % S;
-                if (it >= S && !mbar_wait(&empty[s], ((it / S) & 1) ^ 1, abort_flag, a.err)) break;
-                mbar_expect_tx(&full_tma[s], kTx);
-                tma_load_2d(Xs + s * L::kX, &tmX, &full_tma[s], it * BK, m0);
-                bulk_load(Ps + s * L::kP, a.q + ((int64_t)blockIdx.x * ksteps + it) * L::kP, L::kP, &full_tma[s]);
+            int g = 0;  // K steps issued by this CTA, over all its tiles
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int nt = t % a.n_tiles, mt = t / a.n_tiles;
+                const uint8_t* wsrc = a.q + (int64_t)nt * a.k_steps * L::kP;
+                for (int kx = 0; kx < xs; ++kx, ++g) {
+                    const int s = g % S1;
+                    if (g >= S1 && !mbar_wait(&empty_x[s], ((g / S1) & 1) ^ 1, abort_flag, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&full_tma[s], kTx);
+                    tma_load_2d(Xs + s * L::kX, &tmX, &full_tma[s], kx * BK, mt * BN);
+                    const int kw = kx < a.k_steps ? kx : kx - a.k_steps;
+                    bulk_load(Ps + s * L::kP, wsrc + (int64_t)kw * L::kP, L::kP, &full_tma[s]);
+                }
             }
-            // drain: every issued copy has landed before the CTA can exit
-            for (int j = (it > S ? it - S : 0); j < it; ++j)
-                mbar_wait(&full_tma[j % S], (j / S) & 1, abort_flag, a.err);
+            // every issued copy lands before the CTA can exit
+            const uint64_t deadline = globaltimer() + kTimeoutNs;
+            for (int j = (g > S1 ? g - S1 : 0); j < g; ++j) mbar_wait_until(&full_tma[j % S1], (j / S1) & 1, deadline);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16<BM, BN>();
-            for (int it = 0; it < ksteps; ++it) {
-                const int s = it % S;
-                const uint32_t ph = (it / S) & 1;
-                if (!mbar_wait(&full_a[s], ph, abort_flag, a.err)) break;
-                if (!mbar_wait(&full_tma[s], ph, abort_flag, a.err)) break;
+            int g = 0, lt = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++lt) {
+                const int buf = lt & 1;
+                if (lt >= 2 && !mbar_wait(&acc_empty[buf], ((lt >> 1) & 1) ^ 1, abort_flag, a.err)) break;
                 tc_fence_after();
-                const uint32_t a_base = smem_u32(As + s * L::kA);
-                const uint32_t b_base = smem_u32(Xs + s * L::kX);
+                const uint32_t d = tmem + (uint32_t)(buf * BN);
+                for (int kx = 0; kx < xs; ++kx, ++g) {
+                    const int s1 = g % S1, s2 = g % S2;
+                    if (!mbar_wait(&full_a[s2], (g / S2) & 1, abort_flag, a.err) ||
+                        !mbar_wait(&full_tma[s1], (g / S1) & 1, abort_flag, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_base = smem_u32(As + s2 * L::kA);
+                    const uint32_t b_base = smem_u32(Xs + s1 * L::kX);
 #pragma unroll
-                for (int kk = 0; kk < BK / 16; ++kk)
-                    umma_bf16(tmem, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32), idesc,
-                              (it > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(&empty[s]);
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        umma_bf16(d, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32), idesc,
+                                  (kx > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit(&empty_x[s1]);
+                    umma_commit(&empty_a[s2]);
+                }
+                if (ok) umma_commit(&acc_full[buf]);
             }
-            umma_commit(acc_full);  // fires when every MMA issued above has completed
+            // every MMA issued above completes before TMEM is freed
+            umma_commit(mma_done);
+            mbar_wait_until(mma_done, 0, globaltimer() + kTimeoutNs);
+        }
+    } else if (warp < 6) {
+        // ---------------- dequantize (threads 64..191 -> tile rows)
+        const int row = (warp - 2) * 32 + lane;
+        int g = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            for (int kx = 0; kx < xs; ++kx, ++g) {
+                const int s1 = g % S1, s2 = g % S2;
+                if (!mbar_wait(&full_tma[s1], (g / S1) & 1, abort_flag, a.err) ||
+                    (g >= S2 && !mbar_wait(&empty_a[s2], ((g / S2) & 1) ^ 1, abort_flag, a.err))) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* prow = Ps + s1 * L::kP + row * packed_bytes<FMT>();
+                uint8_t* arow = As + s2 * L::kA + row * 128;
+                if constexpr (FMT == BRAMHA_FMT_W8) {
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                        // int8 slices are stored 64-byte-swizzled (repack.cu)
+                        const uint4 p = *reinterpret_cast<const uint4*>(prow + 16 * (h ^ ((row >> 1) & 3)));
+                        const int c0 = 2 * h, c1 = 2 * h + 1;
+                        *reinterpret_cast<uint4*>(arow + ((c0 ^ (row & 7)) << 4)) = dq_int8(p.x, p.y);
+                        *reinterpret_cast<uint4*>(arow + ((c1 ^ (row & 7)) << 4)) = dq_int8(p.z, p.w);
+                    }
+                } else {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint4 p = *reinterpret_cast<const uint4*>(prow + 16 * h);
+                        const uint32_t wv[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int c = 4 * h + i;
+                            const uint4 o = (FMT == BRAMHA_FMT_LOG4) ? dq_log4(wv[i]) : dq_int4(wv[i]);
+                            *reinterpret_cast<uint4*>(arow + ((c ^ (row & 7)) << 4)) = o;
+                        }
+                    }
+                }
+                fence_async_smem();  // generic-proxy writes -> visible to the tensor core
+                mbar_arrive(&full_a[s2]);
+            }
         }
     } else {
-        // ---------------- dequantize (threads 64..191 -> tile rows)
-        const int q4 = warp & 3;                 // TMEM lane quarter this warp may access
-        const int row = q4 * 32 + lane;          // row of the tile == TMEM lane
-        for (int it = 0; it < ksteps; ++it) {
-            const int s = it % S;
-            if (!mbar_wait(&full_tma[s], (it / S) & 1, abort_flag, a.err)) break;
-            const uint8_t* prow = Ps + s * L::kP + row * packed_bytes<FMT>();
-            uint8_t* arow = As + s * L::kA + row * 128;
-            if constexpr (FMT == BRAMHA_FMT_W8) {
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    // int8 slices are stored 64-byte-swizzled (repack.cu)
-                    const uint4 p = *reinterpret_cast<const uint4*>(prow + 16 * (h ^ ((row >> 1) & 3)));
-                    const int c0 = 2 * h, c1 = 2 * h + 1;
-                    *reinterpret_cast<uint4*>(arow + ((c0 ^ (row & 7)) << 4)) = dq_int8(p.x, p.y);
-                    *reinterpret_cast<uint4*>(arow + ((c1 ^ (row & 7)) << 4)) = dq_int8(p.z, p.w);
-                }
-            } else {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const uint4 p = *reinterpret_cast<const uint4*>(prow + 16 * h);
-                    const uint32_t wv[4] = {p.x, p.y, p.z, p.w};
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int c = 4 * h + i;
-                        const uint4 o = (FMT == BRAMHA_FMT_LOG4) ? dq_log4(wv[i]) : dq_int4(wv[i]);
-                        *reinterpret_cast<uint4*>(arow + ((c ^ (row & 7)) << 4)) = o;
-                    }
-                }
-            }
-            fence_async_smem();  // generic-proxy writes -> visible to the tensor core
-            mbar_arrive(&full_a[s]);
-        }
         // ---------------- epilogue (warp-uniform: tcgen05.ld is .sync.aligned)
-        bool ok = true;
-        if (lane == 0) ok = mbar_wait(acc_full, 0, abort_flag, a.err);
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (ok) {
+        const int q4 = warp & 3;  // TMEM lane quarter this warp may access
+        const int row = q4 * 32 + lane;
+        int lt = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++lt) {
+            const int buf = lt & 1;
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&acc_full[buf], (lt >> 1) & 1, abort_flag, a.err);
+            if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
             tc_fence_after();
-            const int grow = n0 + row;
-            const float sc = grow < a.N ? __ldg(a.scales + grow) : 0.f;
-            const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16);
+            const int nt = t % a.n_tiles, mt = t / a.n_tiles;
+            const int grow = nt * BM + row;
+            const int m0 = mt * BN;
+            const bool row_ok = grow < a.N;
+            // a tile inside the matrix stores without per-element bounds checks
+            // (a conditional store per element costs ~4x in issue)
+            const bool full = (int64_t)(nt + 1) * BM <= a.N && (int64_t)m0 + BN <= a.M;
+            const float sc = row_ok ? __ldg(a.scales + grow) : 0.f;
+            float* ycol = a.y + grow;
+            const uint32_t taddr = tmem + (uint32_t)(buf * BN) + ((uint32_t)(q4 * 32) << 16);
+            // log4: per-token sums, one chunk of 32 ahead of its use
+            float rs_next = 0.f;
+            if constexpr (FMT == BRAMHA_FMT_LOG4) rs_next = m0 + lane < a.M ? __ldg(a.rowsum + m0 + lane) : 0.f;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                uint32_t v[16];
-                tmem_ld16(taddr + c0, v);
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                const float rs = rs_next;
+                if constexpr (FMT == BRAMHA_FMT_LOG4) {
+                    const int tl = m0 + c0 + 32 + lane;
+                    if (c0 + 32 < BN) rs_next = tl < a.M ? __ldg(a.rowsum + tl) : 0.f;
+                }
+                uint32_t v[32];
+                tmem_ld32(taddr + c0, v);
+                float o[32];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int tok = m0 + c0 + j;
-                    if (tok < a.M && grow < a.N) {
-                        float acc = __uint_as_float(v[j]);
-                        if constexpr (FMT == BRAMHA_FMT_LOG4) acc = fmaf(acc, 32768.0f, -__ldg(a.rowsum + tok));
-                        float* dst = a.y + (int64_t)tok * a.ldy + grow;
-                        *dst = a.accumulate ? fmaf(acc, sc, *dst) : acc * sc;
-                    }
+                for (int j = 0; j < 32; ++j) {
+                    o[j] = __uint_as_float(v[j]);
+                    if constexpr (FMT == BRAMHA_FMT_LOG4) o[j] = fmaf(o[j], 32768.0f, -__shfl_sync(0xffffffffu, rs, j));
+                    o[j] *= sc;
+                }
+                float* yc = ycol + (int64_t)(m0 + c0) * a.ldy;
+                if (full) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) yc[(int64_t)j * a.ldy] = o[j];
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (row_ok && m0 + c0 + j < a.M) yc[(int64_t)j * a.ldy] = o[j];
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+        tmem_dealloc(tmem, L::kTmemCols);
     }
 }
 
 // ---- activation preparation ------------------------------------------------
-// bf16 copy with a TMA-friendly pitch and per-token sums of exactly the values
-// the MMA sees.  From f32 the activation is split x = hi + lo (hi = bf16(x),
-// lo = bf16(x - hi)), so two accumulating passes reproduce x to ~2^-16.
+// bf16 copy with a TMA-friendly pitch kp (whole K steps) and per-token sums of
+// exactly the values the MMA sees.  From f32 the activation is split
+// x = hi + lo (hi = bf16(x), lo = bf16(x - hi)); hi fills columns [0, kp) and
+// lo columns [kp, 2 kp) of the copy, so one pass over 2 kp reproduces x to ~2^-16.
 template <bool FROM_F32>
-__global__ void prep_kernel(const void* __restrict__ x, int64_t ldx, int M, int K, int64_t ldb,
-                            __nv_bfloat16* __restrict__ xhi, __nv_bfloat16* __restrict__ xlo,
-                            float* __restrict__ rs_hi, float* __restrict__ rs_lo) {
+__global__ void prep_kernel(const void* __restrict__ x, int64_t ldx, int M, int K, int64_t kp,
+                            __nv_bfloat16* __restrict__ xc, float* __restrict__ rs) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= M) return;
+    const int64_t ldc = FROM_F32 ? 2 * kp : kp;
     float sh = 0.f, sl = 0.f;
-    for (int k = lane; k < (int)ldb; k += 32) {
+    for (int k = lane; k < (int)kp; k += 32) {
         float h = 0.f, l = 0.f;
         if (k < K) {
             if constexpr (FROM_F32) {
                 const float v = static_cast<const float*>(x)[(int64_t)warp * ldx + k];
-                const __nv_bfloat16 hb = __float2bfloat16_rn(v);
-                h = __bfloat162float(hb);
+                h = __bfloat162float(__float2bfloat16_rn(v));
                 l = __bfloat162float(__float2bfloat16_rn(v - h));
             } else {
                 h = __bfloat162float(static_cast<const __nv_bfloat16*>(x)[(int64_t)warp * ldx + k]);
             }
         }
-        if (xhi) xhi[(int64_t)warp * ldb + k] = __float2bfloat16_rn(h);
-        if (xlo) xlo[(int64_t)warp * ldb + k] = __float2bfloat16_rn(l);
+        if (xc) {
+            xc[(int64_t)warp * ldc + k] = __float2bfloat16_rn(h);
+            if constexpr (FROM_F32) xc[(int64_t)warp * ldc + kp + k] = __float2bfloat16_rn(l);
+        }
         sh += h;
         sl += l;
     }
@@ -302,10 +386,7 @@ __global__ void prep_kernel(const void* __restrict__ x, int64_t ldx, int M, int 
         sh += __shfl_xor_sync(0xffffffffu, sh, o);
         sl += __shfl_xor_sync(0xffffffffu, sl, o);
     }
-    if (lane == 0) {
-        if (rs_hi) rs_hi[warp] = sh;
-        if (rs_lo) rs_lo[warp] = sl;
-    }
+    if (lane == 0 && rs) rs[warp] = sh + sl;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -321,34 +402,47 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-template <int FMT, int BN, int S>
-cudaError_t launch_tiles(const CUtensorMap& tmX, const GemmArgs& g, cudaStream_t st) {
-    using L = Layout<FMT, BN, S>;
-    auto kern = gemm_kernel<FMT, BN, S>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
-    if (e != cudaSuccess) return e;
-    dim3 grid((g.N + BM - 1) / BM, (g.M + BN - 1) / BN);
-    kern<<<grid, kThreads, L::kAlloc, st>>>(tmX, g);
-    return cudaGetLastError();
+
+// Per-device caches: SM count, and whether a kernel's shared-memory limit has
+// been raised on that device (cudaFuncSetAttribute is per device).
+int sm_count(int dev) {
+    static std::atomic<int> cache[64];
+    if (dev < 0 || dev >= 64) return 148;
+    int n = cache[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev].store(n, std::memory_order_relaxed);
+    }
+    return n;
 }
 
-// Pipeline depth: as many stages as fit in the 227 KB of shared memory a CTA
-// may use (at most 8).
 template <int FMT, int BN>
-constexpr int stages_for() {
-    constexpr int per_stage = BN * 128 + BM * 128 + BM * packed_bytes<FMT>();
-    constexpr int budget = 227 * 1024 - 1024 - 256;  // alignment slack, barriers
-    constexpr int s = budget / per_stage;
-    return s > 8 ? 8 : s;
+cudaError_t launch_tiles(const CUtensorMap& tmX, const GemmArgs& g, cudaStream_t st) {
+    using L = Layout<FMT, BN>;
+    static std::atomic<uint64_t> attr_set{0};
+    auto kern = gemm_kernel<FMT, BN>;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+    if (!bit || !(attr_set.load(std::memory_order_acquire) & bit)) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+        if (e != cudaSuccess) return e;
+        attr_set.fetch_or(bit, std::memory_order_release);
+    }
+    const int64_t ntiles = (int64_t)g.n_tiles * g.m_tiles;
+    const int grid = (int)(ntiles < sm_count(dev) ? ntiles : sm_count(dev));
+    kern<<<grid, kThreads, L::kAlloc, st>>>(tmX, g);
+    return cudaGetLastError();
 }
 
 template <int FMT>
 cudaError_t launch_fmt(int bn, const CUtensorMap& tmX, const GemmArgs& g, cudaStream_t st) {
     switch (bn) {
-        case 256: return launch_tiles<FMT, 256, stages_for<FMT, 256>()>(tmX, g, st);
-        case 128: return launch_tiles<FMT, 128, stages_for<FMT, 128>()>(tmX, g, st);
-        case 64: return launch_tiles<FMT, 64, stages_for<FMT, 64>()>(tmX, g, st);
-        default: return launch_tiles<FMT, 32, stages_for<FMT, 32>()>(tmX, g, st);
+        case 256: return launch_tiles<FMT, 256>(tmX, g, st);
+        case 128: return launch_tiles<FMT, 128>(tmX, g, st);
+        case 64: return launch_tiles<FMT, 64>(tmX, g, st);
+        default: return launch_tiles<FMT, 32>(tmX, g, st);
     }
 }
 
@@ -358,8 +452,9 @@ cudaError_t launch_fmt(int bn, const CUtensorMap& tmX, const GemmArgs& g, cudaSt
 int gemm_tile_n(int64_t M) { return M >= 256 ? 256 : M > 64 ? 128 : M > 32 ? 64 : 32; }
 
 namespace {
-cudaError_t make_x_map(CUtensorMap* m, const void* xg, int64_t K, int64_t M, int64_t xld, int bn) {
-    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+// X tensor map over a bf16 [M][cols] matrix with row pitch xld elements.
+cudaError_t make_x_map(CUtensorMap* m, const void* xg, int64_t cols, int64_t M, int64_t xld, int bn) {
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)M};
     cuuint64_t strides[1] = {(cuuint64_t)(xld * 2)};
     cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)bn};
     cuuint32_t estr[2] = {1, 1};
@@ -368,7 +463,8 @@ cudaError_t make_x_map(CUtensorMap* m, const void* xg, int64_t K, int64_t M, int
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
-cudaError_t run_pass(int fmt, int bn, const CUtensorMap& tmX, const GemmArgs& g, cudaStream_t st) {
+
+cudaError_t run_gemm(int fmt, int bn, const CUtensorMap& tmX, const GemmArgs& g, cudaStream_t st) {
     switch (fmt) {
         case BRAMHA_FMT_LOG4: return launch_fmt<BRAMHA_FMT_LOG4>(bn, tmX, g, st);
         case BRAMHA_FMT_W4ZP8: return launch_fmt<BRAMHA_FMT_W4ZP8>(bn, tmX, g, st);
@@ -376,68 +472,66 @@ cudaError_t run_pass(int fmt, int bn, const CUtensorMap& tmX, const GemmArgs& g,
         default: return cudaErrorInvalidValue;
     }
 }
+
+// Fills the tile counts and steps of a GEMM over K packed columns.
+cudaError_t gemm_args(GemmArgs* g, const uint8_t* q, const float* scales, const float* rowsum, float* y,
+                      int64_t ldy, int64_t M, int64_t N, int64_t K, bool split, int bn, int* err) {
+    const int64_t k_steps = (K + BK - 1) / BK;
+    const int64_t n_tiles = (N + BM - 1) / BM, m_tiles = (M + bn - 1) / bn;
+    if (n_tiles * m_tiles > INT_MAX || 2 * k_steps > INT_MAX) return cudaErrorInvalidValue;
+    g->q = q;
+    g->scales = scales;
+    g->rowsum = rowsum;
+    g->y = y;
+    g->ldy = ldy;
+    g->M = (int)M;
+    g->N = (int)N;
+    g->k_steps = (int)k_steps;
+    g->x_steps = (int)(split ? 2 * k_steps : k_steps);
+    g->n_tiles = (int)n_tiles;
+    g->m_tiles = (int)m_tiles;
+    g->err = err;
+    return cudaSuccess;
+}
 }  // namespace
 
 // y[M][ldy] = dequant(W)[N][K] applied to x[M][ldx] (bf16, or f32 split into
-// two bf16 passes).  K is the number of columns the packed rows hold.
-// Scratch (bf16 copies, per-token sums) comes from the stream-ordered pool.
+// bf16 hi + lo).  K is the number of columns the packed rows hold.
+// Scratch (bf16 copy, per-token sums) comes from the stream-ordered pool.
 cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const float* scales, int64_t N, int64_t K,
                                 const void* x, int x_is_f32, int64_t ldx, int64_t M, float* y, int64_t ldy, int* err,
                                 cudaStream_t st) {
     if (M <= 0 || N <= 0) return cudaSuccess;
     if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff || K <= 0) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(q) & 15) != 0) return cudaErrorInvalidValue;
     if (!encode_fn()) return cudaErrorNotSupported;
-    const int64_t kp = (K + BK - 1) / BK * BK;  // bf16 copy pitch: whole K steps
+    const int64_t kp = (K + BK - 1) / BK * BK;  // copy pitch per half: whole K steps
     const bool need_copy = x_is_f32 || (ldx % 8) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0;
     const bool log4 = fmt == BRAMHA_FMT_LOG4;
-    const int npass = x_is_f32 ? 2 : 1;
-    // scratch: [npass] bf16 copies, [npass] row sums
-    size_t bytes = 0;
-    if (need_copy) bytes += (size_t)npass * M * kp * sizeof(__nv_bfloat16);
-    if (log4) bytes += (size_t)npass * M * sizeof(float);
+    const int64_t cols = x_is_f32 ? 2 * kp : kp;  // columns of the bf16 copy
+    size_t copy_bytes = need_copy ? (size_t)M * cols * sizeof(__nv_bfloat16) : 0;
+    const size_t bytes = copy_bytes + (log4 ? (size_t)M * sizeof(float) : 0);
     uint8_t* scratch = nullptr;
     cudaError_t e = bytes ? cudaMallocAsync(reinterpret_cast<void**>(&scratch), bytes, st) : cudaSuccess;
     if (e != cudaSuccess) return e;
-    __nv_bfloat16* xb[2] = {nullptr, nullptr};
-    float* rs[2] = {nullptr, nullptr};
-    uint8_t* p = scratch;
-    if (need_copy)
-        for (int i = 0; i < npass; ++i, p += (size_t)M * kp * sizeof(__nv_bfloat16))
-            xb[i] = reinterpret_cast<__nv_bfloat16*>(p);
-    if (log4)
-        for (int i = 0; i < npass; ++i, p += (size_t)M * sizeof(float)) rs[i] = reinterpret_cast<float*>(p);
+    __nv_bfloat16* xc = need_copy ? reinterpret_cast<__nv_bfloat16*>(scratch) : nullptr;
+    float* rs = log4 ? reinterpret_cast<float*>(scratch + copy_bytes) : nullptr;
     if (need_copy || log4) {
         const int wpb = 8;
         const unsigned blocks = (unsigned)((M + wpb - 1) / wpb);
-        const int64_t ldb = need_copy ? kp : K;
         if (x_is_f32)
-            prep_kernel<true><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, ldb, xb[0], xb[1], rs[0], rs[1]);
+            prep_kernel<true><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
         else
-            prep_kernel<false><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, ldb, xb[0], nullptr, rs[0],
-                                                           nullptr);
+            prep_kernel<false><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, need_copy ? kp : K, xc, rs);
         e = cudaGetLastError();
     }
     const int bn = gemm_tile_n(M);
-    if ((reinterpret_cast<uintptr_t>(q) & 15) != 0) e = cudaErrorInvalidValue;
-    for (int pass = 0; pass < npass && e == cudaSuccess; ++pass) {
-        const void* xg = need_copy ? static_cast<const void*>(xb[pass]) : x;
-        CUtensorMap tmX;
-        e = make_x_map(&tmX, xg, K, M, need_copy ? kp : ldx, bn);
-        if (e != cudaSuccess) break;
-        GemmArgs g;
-        g.q = q;
-        g.scales = scales;
-        g.rowsum = rs[pass];
-        g.y = y;
-        g.ldy = ldy;
-        g.M = (int)M;
-        g.N = (int)N;
-        g.K = (int)K;
-        g.k_steps = (int)((K + BK - 1) / BK);
-        g.accumulate = pass;
-        g.err = err;
-        e = run_pass(fmt, bn, tmX, g, st);
-    }
+    GemmArgs g;
+    CUtensorMap tmX;
+    if (e == cudaSuccess) e = gemm_args(&g, q, scales, rs, y, ldy, M, N, K, x_is_f32 != 0, bn, err);
+    if (e == cudaSuccess)
+        e = need_copy ? make_x_map(&tmX, xc, cols, M, cols, bn) : make_x_map(&tmX, x, K, M, ldx, bn);
+    if (e == cudaSuccess) e = run_gemm(fmt, bn, tmX, g, st);
     if (scratch) {
         cudaError_t e2 = cudaFreeAsync(scratch, st);
         if (e == cudaSuccess) e = e2;
@@ -451,6 +545,7 @@ cudaError_t launch_gemm_tcgen05_bf16_noalloc(int fmt, const uint8_t* q, int64_t 
     if (M <= 0 || N <= 0) return cudaSuccess;
     if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff || K <= 0) return cudaErrorInvalidValue;
     if ((ldx % 8) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(q) & 15) != 0) return cudaErrorInvalidValue;
     if (!encode_fn()) return cudaErrorNotSupported;
     cudaError_t e = cudaSuccess;
     float* rs = nullptr;
@@ -460,27 +555,16 @@ cudaError_t launch_gemm_tcgen05_bf16_noalloc(int fmt, const uint8_t* q, int64_t 
         const int wpb = 8;
         const unsigned blocks = (unsigned)((M + wpb - 1) / wpb);
         // every one of the M sums is written here before the GEMM reads it
-        prep_kernel<false><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, K, nullptr, nullptr, rs, nullptr);
+        prep_kernel<false><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, K, nullptr, rs);
         e = cudaGetLastError();
     }
     const int bn = gemm_tile_n(M);
-    CUtensorMap tmX;
-    if (e == cudaSuccess && (reinterpret_cast<uintptr_t>(q) & 15) != 0) e = cudaErrorInvalidValue;
-    if (e == cudaSuccess) e = make_x_map(&tmX, x, K, M, ldx, bn);
-    if (e != cudaSuccess) return e;
     GemmArgs g;
-    g.q = q;
-    g.scales = scales;
-    g.rowsum = rs;
-    g.y = y;
-    g.ldy = ldy;
-    g.M = (int)M;
-    g.N = (int)N;
-    g.K = (int)K;
-    g.k_steps = (int)((K + BK - 1) / BK);
-    g.accumulate = 0;
-    g.err = err;
-    return run_pass(fmt, bn, tmX, g, st);
+    CUtensorMap tmX;
+    if (e == cudaSuccess) e = gemm_args(&g, q, scales, rs, y, ldy, M, N, K, false, bn, err);
+    if (e == cudaSuccess) e = make_x_map(&tmX, x, K, M, ldx, bn);
+    if (e == cudaSuccess) e = run_gemm(fmt, bn, tmX, g, st);
+    return e;
 }
 
 }  // namespace bramha
