@@ -59,6 +59,7 @@ struct GemmArgs {
     int k_steps;           // 64-column weight blocks per tile row
     int x_steps;           // K steps per tile: k_steps, or 2 * k_steps for a hi|lo split
     int n_tiles, m_tiles;  // tiles along the weight rows and along the tokens
+    int n_blocks;          // 128-row blocks of the repacked weight (ceil(N / 128))
     int* err;              // device error word (0 = ok)
 };
 
@@ -351,6 +352,278 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---- SM-pair kernel ------------------------------------------------------------
+// A tile of 256 weight rows x 256 tokens is computed by a cluster of two CTAs
+// with tcgen05.mma.cta_group::2 (M=256, N=256, K=16), issued by one thread of
+// CTA 0.  CTA r holds weight rows r*128.. of the tile (its own dequantized
+// operand) and tokens r*128.. of the X tile (its half of B); each CTA's TMEM
+// receives its 128 rows of D.  Per pair and K step the X tile crosses L2 once
+// (each CTA loads half), so the L2 -> SM traffic per flop is ~1.8x lower than
+// the single-CTA 128 x 256 tile, and each MMA instruction covers twice the work.
+// Synchronisation across the pair: every copy completes on a barrier of its own
+// CTA; each dequant warp, once its rows are written and this CTA's X half has
+// landed, arrives on CTA 0's full_a barrier (through the cluster address for
+// CTA 1), so full_a alone tells the MMA issuer that both CTAs' operands are in
+// place; epilogue warps release an accumulator the same way (acc_empty); the
+// MMA commits are multicast to the barrier at the same offset in both CTAs.
+// Remote barrier traffic is one arrival per warp and step.  No TMA multicast.
+constexpr int kPairTok = 256;  // tokens per pair tile (N of the MMA)
+template <int FMT>
+struct PairLayout {
+    static constexpr int kX = (kPairTok / 2) * 128;       // this CTA's half of the X tile
+    static constexpr int kA = BM * 128;                   // this CTA's dequantized weight rows
+    static constexpr int kP = BM * packed_bytes<FMT>();   // this CTA's packed weight block
+    static constexpr int kSlot = kX + kA + kP;
+    static constexpr int kBudget = 227 * 1024 - 1024 - 512;
+    static constexpr int S = kBudget / kSlot > 6 ? 6 : kBudget / kSlot;
+    static constexpr int offX = 0;
+    static constexpr int offA = offX + S * kX;
+    static constexpr int offP = offA + S * kA;
+    // full_x[S] (this CTA's X half), full_p[S] (this CTA's packed block), full_a[S] (CTA 0: 8 warps),
+    // empty[S] (multicast commit), acc_full[2] (multicast commit), acc_empty[2] (CTA 0: 8 warps), mma_done
+    static constexpr int offBar = offP + S * kP;
+    static constexpr int offTmem = offBar + (4 * S + 5) * 8;
+    static constexpr int offAbort = offTmem + 4;
+    static constexpr int kBytes = offAbort + 4;
+    static constexpr int kAlloc = kBytes + 1024;
+    static constexpr int kThreads = 320;                  // producer, MMA, 4 dequant, 4 epilogue warps
+    static constexpr uint32_t kTmemCols = 512;            // two 256-column accumulators
+    static_assert(kAlloc <= 227 * 1024, "shared memory per CTA exceeds 227 KB");
+    static_assert(S >= 4, "ring too shallow");
+};
+
+template <int FMT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<FMT>::kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ GemmArgs a) {
+    using L = PairLayout<FMT>;
+    constexpr int S = L::S;
+    constexpr int BNP = kPairTok;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* Xs = smem + L::offX;
+    uint8_t* As = smem + L::offA;
+    uint8_t* Ps = smem + L::offP;
+    uint64_t* full_x = reinterpret_cast<uint64_t*>(smem + L::offBar);
+    uint64_t* full_p = full_x + S;
+    uint64_t* full_a = full_p + S;
+    uint64_t* empty = full_a + S;
+    uint64_t* acc_full = empty + S;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* mma_done = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::offTmem);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::offAbort);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int ntiles = a.n_tiles * a.m_tiles;
+    const int xs = a.x_steps;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full_x[s], 1);
+            mbar_init(&full_p[s], 1);
+            mbar_init(&full_a[s], 8);  // 4 dequant warps of each CTA
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 8);  // 4 epilogue warps of each CTA
+        }
+        mbar_init(mma_done, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) tmem_alloc_pair(tmem_slot, L::kTmemCols);
+    tc_fence_before();
+    cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- producer (both CTAs): this CTA's X half and weight block
+        if (lane == 0) {
+            int g = 0;
+            bool ok = true;
+            for (int t = pair; t < ntiles && ok; t += npairs) {
+                const int nt = t / a.m_tiles, mt = t % a.m_tiles;
+                const int blk = nt * 2 + (int)rank;
+                const bool has_w = blk < a.n_blocks;
+                const uint8_t* wsrc = a.q + (int64_t)blk * a.k_steps * L::kP;
+                for (int kx = 0; kx < xs; ++kx, ++g) {
+                    const int s = g % S;
+                    if (g >= S && !mbar_wait(&empty[s], ((g / S) & 1) ^ 1, abort_flag, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&full_x[s], L::kX);
+                    tma_load_2d(Xs + s * L::kX, &tmX, &full_x[s], kx * BK, mt * BNP + (int)rank * (BNP / 2));
+                    mbar_expect_tx(&full_p[s], has_w ? L::kP : 0);
+                    const int kw = kx < a.k_steps ? kx : kx - a.k_steps;
+                    if (has_w) bulk_load(Ps + s * L::kP, wsrc + (int64_t)kw * L::kP, L::kP, &full_p[s]);
+                }
+            }
+            // copies in flight land before the CTA can exit
+            const uint64_t deadline = globaltimer() + kTimeoutNs;
+            for (int j = (g > S ? g - S : 0); j < g; ++j) {
+                mbar_wait_until(&full_p[j % S], (j / S) & 1, deadline);
+                mbar_wait_until(&full_x[j % S], (j / S) & 1, deadline);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (CTA 0)
+        if (leader && lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16<256, BNP>();
+            int g = 0, lt = 0;
+            bool ok = true;
+            for (int t = pair; t < ntiles && ok; t += npairs, ++lt) {
+                const int buf = lt & 1;
+                if (lt >= 2 && !mbar_wait(&acc_empty[buf], ((lt >> 1) & 1) ^ 1, abort_flag, a.err)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(buf * BNP);
+                for (int kx = 0; kx < xs; ++kx, ++g) {
+                    const int s = g % S;
+                    if (!mbar_wait(&full_a[s], (g / S) & 1, abort_flag, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_base = smem_u32(As + s * L::kA);
+                    const uint32_t b_base = smem_u32(Xs + s * L::kX);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        umma_bf16_pair(d, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32), idesc,
+                                       (kx > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit_pair(&empty[s], 0x3);
+                }
+                if (ok) umma_commit_pair(&acc_full[buf], 0x3);
+            }
+            // every MMA issued above completes before the pair's TMEM and shared memory go away
+            asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             smem_u32(mma_done))
+                         : "memory");
+            mbar_wait_until(mma_done, 0, globaltimer() + kTimeoutNs);
+        }
+    } else if (warp < 6) {
+        // ---------------- dequantize (both CTAs, thread = weight row of this CTA's block)
+        const int row = (warp - 2) * 32 + lane;
+        int g = 0;
+        bool ok = true;
+        for (int t = pair; t < ntiles && ok; t += npairs) {
+            for (int kx = 0; kx < xs; ++kx, ++g) {
+                const int s = g % S;
+                // outcomes are made warp-uniform: the step ends in a warp-collective arrival
+                if (!__all_sync(0xffffffffu, mbar_wait(&full_p[s], (g / S) & 1, abort_flag, a.err))) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* prow = Ps + s * L::kP + row * packed_bytes<FMT>();
+                uint8_t* arow = As + s * L::kA + row * 128;
+                if constexpr (FMT == BRAMHA_FMT_W8) {
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                        // int8 slices are stored 64-byte-swizzled (repack.cu)
+                        const uint4 p = *reinterpret_cast<const uint4*>(prow + 16 * (h ^ ((row >> 1) & 3)));
+                        const int c0 = 2 * h, c1 = 2 * h + 1;
+                        *reinterpret_cast<uint4*>(arow + ((c0 ^ (row & 7)) << 4)) = dq_int8(p.x, p.y);
+                        *reinterpret_cast<uint4*>(arow + ((c1 ^ (row & 7)) << 4)) = dq_int8(p.z, p.w);
+                    }
+                } else {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint4 p = *reinterpret_cast<const uint4*>(prow + 16 * h);
+                        const uint32_t wv[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int c = 4 * h + i;
+                            const uint4 o = (FMT == BRAMHA_FMT_LOG4) ? dq_log4(wv[i]) : dq_int4(wv[i]);
+                            *reinterpret_cast<uint4*>(arow + ((c ^ (row & 7)) << 4)) = o;
+                        }
+                    }
+                }
+                fence_async_smem();  // generic-proxy writes -> visible to the tensor core
+                // the arrival below also certifies this CTA's X half of the step
+                if (!__all_sync(0xffffffffu, mbar_wait(&full_x[s], (g / S) & 1, abort_flag, a.err))) {
+                    ok = false;
+                    break;
+                }
+                __syncwarp();  // orders every lane's writes before lane 0's arrival
+                if (lane == 0) {
+                    if (leader)
+                        mbar_arrive(&full_a[s]);
+                    else
+                        mbar_arrive_cluster(mapa_shared(smem_u32(&full_a[s]), 0));
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue (both CTAs: this CTA's 128 rows x 256 tokens)
+        const int q4 = warp & 3;
+        int lt = 0;
+        for (int t = pair; t < ntiles; t += npairs, ++lt) {
+            const int buf = lt & 1;
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&acc_full[buf], (lt >> 1) & 1, abort_flag, a.err);
+            if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
+            tc_fence_after();
+            const int nt = t / a.m_tiles, mt = t % a.m_tiles;
+            const int64_t row0 = (int64_t)nt * 256 + rank * 128;
+            const int64_t grow = row0 + q4 * 32 + lane;
+            const int m0 = mt * BNP;
+            const bool row_ok = grow < a.N;
+            // a tile inside the matrix stores without per-element bounds checks
+            const bool full = row0 + 128 <= a.N && (int64_t)m0 + BNP <= a.M;
+            const float sc = row_ok ? __ldg(a.scales + grow) : 0.f;
+            float* ycol = a.y + grow;
+            const uint32_t taddr = tmem + (uint32_t)(buf * BNP) + ((uint32_t)(q4 * 32) << 16);
+            float rs_next = 0.f;
+            if constexpr (FMT == BRAMHA_FMT_LOG4) rs_next = m0 + lane < a.M ? __ldg(a.rowsum + m0 + lane) : 0.f;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BNP; c0 += 32) {
+                const float rs = rs_next;
+                if constexpr (FMT == BRAMHA_FMT_LOG4) {
+                    const int tl = m0 + c0 + 32 + lane;
+                    if (c0 + 32 < BNP) rs_next = tl < a.M ? __ldg(a.rowsum + tl) : 0.f;
+                }
+                uint32_t v[32];
+                tmem_ld32(taddr + c0, v);
+                float o[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    o[j] = __uint_as_float(v[j]);
+                    if constexpr (FMT == BRAMHA_FMT_LOG4) o[j] = fmaf(o[j], 32768.0f, -__shfl_sync(0xffffffffu, rs, j));
+                    o[j] *= sc;
+                }
+                float* yc = ycol + (int64_t)(m0 + c0) * a.ldy;
+                if (full) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) yc[(int64_t)j * a.ldy] = o[j];
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (row_ok && m0 + c0 + j < a.M) yc[(int64_t)j * a.ldy] = o[j];
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (leader)
+                    mbar_arrive(&acc_empty[buf]);
+                else
+                    mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[buf]), 0));
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // the pair's remote arrivals and MMA reads of both CTAs are over
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, L::kTmemCols);
+    }
+}
+
 // ---- activation preparation ------------------------------------------------
 // bf16 copy with a TMA-friendly pitch kp (whole K steps) and per-token sums of
 // exactly the values the MMA sees.  From f32 the activation is split
@@ -446,6 +719,46 @@ cudaError_t launch_fmt(int bn, const CUtensorMap& tmX, const GemmArgs& g, cudaSt
     }
 }
 
+// Pairs of CTAs that can be resident at once (cached per device and format).
+template <int FMT>
+int max_pairs(int dev) {
+    static std::atomic<int> cache[64];
+    if (dev < 0 || dev >= 64) return sm_count(dev) / 2;
+    int n = cache[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)sm_count(dev));
+        cfg.blockDim = dim3(PairLayout<FMT>::kThreads);
+        cfg.dynamicSmemBytes = PairLayout<FMT>::kAlloc;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<FMT>, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = sm_count(dev) / 2;
+        }
+        cache[dev].store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
+
+template <int FMT>
+cudaError_t launch_pair(const CUtensorMap& tmX, const GemmArgs& g, cudaStream_t st) {
+    using L = PairLayout<FMT>;
+    static std::atomic<uint64_t> attr_set{0};
+    auto kern = gemm_pair_kernel<FMT>;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+    if (!bit || !(attr_set.load(std::memory_order_acquire) & bit)) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+        if (e != cudaSuccess) return e;
+        attr_set.fetch_or(bit, std::memory_order_release);
+    }
+    const int64_t ntiles = (int64_t)g.n_tiles * g.m_tiles;
+    const int pairs = (int)(ntiles < max_pairs<FMT>(dev) ? ntiles : max_pairs<FMT>(dev));
+    kern<<<2 * pairs, L::kThreads, L::kAlloc, st>>>(tmX, g);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 // Tokens per tile for M tokens.
@@ -464,7 +777,23 @@ cudaError_t make_x_map(CUtensorMap* m, const void* xg, int64_t cols, int64_t M, 
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// The SM-pair kernel takes GEMMs with at least four rounds of pair tiles on
+// the GPU (lm_head-sized); with fewer, the single-CTA kernel's smaller tiles
+// balance the SMs better.
+bool use_pair(int64_t M, int64_t N, int sms) {
+    const int64_t tiles = ((N + 2 * BM - 1) / (2 * BM)) * ((M + kPairTok - 1) / kPairTok);
+    return M > 128 && N > BM && tiles >= 4 * (sms / 2);
+}
+
 cudaError_t run_gemm(int fmt, int bn, const CUtensorMap& tmX, const GemmArgs& g, cudaStream_t st) {
+    if (bn == 0) {  // SM-pair kernel
+        switch (fmt) {
+            case BRAMHA_FMT_LOG4: return launch_pair<BRAMHA_FMT_LOG4>(tmX, g, st);
+            case BRAMHA_FMT_W4ZP8: return launch_pair<BRAMHA_FMT_W4ZP8>(tmX, g, st);
+            case BRAMHA_FMT_W8: return launch_pair<BRAMHA_FMT_W8>(tmX, g, st);
+            default: return cudaErrorInvalidValue;
+        }
+    }
     switch (fmt) {
         case BRAMHA_FMT_LOG4: return launch_fmt<BRAMHA_FMT_LOG4>(bn, tmX, g, st);
         case BRAMHA_FMT_W4ZP8: return launch_fmt<BRAMHA_FMT_W4ZP8>(bn, tmX, g, st);
@@ -476,8 +805,10 @@ cudaError_t run_gemm(int fmt, int bn, const CUtensorMap& tmX, const GemmArgs& g,
 // Fills the tile counts and steps of a GEMM over K packed columns.
 cudaError_t gemm_args(GemmArgs* g, const uint8_t* q, const float* scales, const float* rowsum, float* y,
                       int64_t ldy, int64_t M, int64_t N, int64_t K, bool split, int bn, int* err) {
+    // bn == 0 selects the SM-pair tiles: 256 weight rows x kPairTok tokens
     const int64_t k_steps = (K + BK - 1) / BK;
-    const int64_t n_tiles = (N + BM - 1) / BM, m_tiles = (M + bn - 1) / bn;
+    const int64_t rows = bn == 0 ? 2 * BM : BM, toks = bn == 0 ? kPairTok : bn;
+    const int64_t n_tiles = (N + rows - 1) / rows, m_tiles = (M + toks - 1) / toks;
     if (n_tiles * m_tiles > INT_MAX || 2 * k_steps > INT_MAX) return cudaErrorInvalidValue;
     g->q = q;
     g->scales = scales;
@@ -489,6 +820,7 @@ cudaError_t gemm_args(GemmArgs* g, const uint8_t* q, const float* scales, const 
     g->k_steps = (int)k_steps;
     g->x_steps = (int)(split ? 2 * k_steps : k_steps);
     g->n_tiles = (int)n_tiles;
+    g->n_blocks = (int)((N + BM - 1) / BM);
     g->m_tiles = (int)m_tiles;
     g->err = err;
     return cudaSuccess;
@@ -525,12 +857,15 @@ cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const fl
             prep_kernel<false><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, need_copy ? kp : K, xc, rs);
         e = cudaGetLastError();
     }
-    const int bn = gemm_tile_n(M);
+    int dev = 0;
+    if (e == cudaSuccess) e = cudaGetDevice(&dev);
+    const int bn = use_pair(M, N, sm_count(dev)) ? 0 : gemm_tile_n(M);
+    const int box = bn == 0 ? kPairTok / 2 : bn;  // X rows per TMA box (each CTA of a pair loads half a tile)
     GemmArgs g;
     CUtensorMap tmX;
     if (e == cudaSuccess) e = gemm_args(&g, q, scales, rs, y, ldy, M, N, K, x_is_f32 != 0, bn, err);
     if (e == cudaSuccess)
-        e = need_copy ? make_x_map(&tmX, xc, cols, M, cols, bn) : make_x_map(&tmX, x, K, M, ldx, bn);
+        e = need_copy ? make_x_map(&tmX, xc, cols, M, cols, box) : make_x_map(&tmX, x, K, M, ldx, box);
     if (e == cudaSuccess) e = run_gemm(fmt, bn, tmX, g, st);
     if (scratch) {
         cudaError_t e2 = cudaFreeAsync(scratch, st);
@@ -558,11 +893,13 @@ cudaError_t launch_gemm_tcgen05_bf16_noalloc(int fmt, const uint8_t* q, int64_t 
         prep_kernel<false><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, K, nullptr, rs);
         e = cudaGetLastError();
     }
-    const int bn = gemm_tile_n(M);
+    int dev = 0;
+    if (e == cudaSuccess) e = cudaGetDevice(&dev);
+    const int bn = use_pair(M, N, sm_count(dev)) ? 0 : gemm_tile_n(M);
     GemmArgs g;
     CUtensorMap tmX;
     if (e == cudaSuccess) e = gemm_args(&g, q, scales, rs, y, ldy, M, N, K, false, bn, err);
-    if (e == cudaSuccess) e = make_x_map(&tmX, x, K, M, ldx, bn);
+    if (e == cudaSuccess) e = make_x_map(&tmX, x, K, M, ldx, bn == 0 ? kPairTok / 2 : bn);
     if (e == cudaSuccess) e = run_gemm(fmt, bn, tmX, g, st);
     return e;
 }

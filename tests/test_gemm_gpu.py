@@ -106,6 +106,30 @@ def test_gemm_f32_split_matches_fp32(plane, fmt):
     plane.evict(w.key)
 
 
+@pytest.mark.parametrize("fmt", ["log4", "w8", "w4zp8"])
+@pytest.mark.parametrize("xdt", ["bf16", "f32"])
+def test_gemm_sm_pair_ragged(plane, fmt, xdt):
+    """The SM-pair kernel (tcgen05.mma.cta_group::2, taken for >= 4 rounds of
+    256 x 256 tiles) on ragged rows (N % 256 = 100, the last tile's second
+    128-row block absent), tokens (M % 256 = 219) and K (900 = 14 steps + 4),
+    with bf16 activations and with the f32 hi|lo split (two K halves)."""
+    n, k, m = 9828, 900, 2011
+    _, q, s = make_weight(fmt, n, k, seed=21)
+    if xdt == "bf16":
+        x = bf16_x(m, k, seed=22).cuda()
+        xf = x.float()
+    else:
+        x = torch.from_numpy(rng(23).normal(0, 1, (m, k)).astype(np.float32)).cuda()
+        xf = x
+    w = plane.register(f"pair:{fmt}:{xdt}", fmt, n, k, q, s)
+    y = run_gemm_dev(plane, w, x)
+    ref = torch_ref(fmt, q, s, n, k, xf)
+    err = normwise_err(y, ref)
+    assert err <= (GEMM_BF16_TOL if xdt == "bf16" else GEMV_TOL)
+    assert err <= 1e-4
+    plane.evict(w.key)
+
+
 def test_gemm_lm_head_full_size_properties(plane):
     """Qwen2-0.5B lm_head (151936 x 896), M = 256, log4: a row slice against
     the oracle, and linearity in the activations (full output)."""
