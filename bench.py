@@ -330,13 +330,23 @@ def run_ours(args, ws, rank, local):
                     layer0_host.append((hi - lo, k, qd.cpu().numpy(), sd.cpu().numpy()))
                 del qd, sd
                 wts.append(w)
-                ys.append(torch.empty((B, hi - lo), dtype=torch.float32, device=dev))
+                ys.append(hi - lo)
                 step_bytes += gemv_bytes(n, k, B, bits)  # whole-job algorithmic bytes
             gen.manual_seed(7 + li * 13 + len(entry))
             x = torch.randn((B, k), generator=gen, device=dev, dtype=torch.float32)
             ntot = sum(w.N for w in wts)
+            # batch 1: the parts' outputs are consecutive views of one buffer, which is
+            # also the all-gather send buffer (no concatenation copy)
+            ybuf = torch.empty((B * ntot,), dtype=torch.float32, device=dev)
+            if B == 1:
+                offs = [0]
+                for nloc in ys:
+                    offs.append(offs[-1] + nloc)
+                ys = [ybuf[offs[i]:offs[i + 1]].view(1, -1) for i in range(len(ys))]
+            else:
+                ys = [torch.empty((B, nloc), dtype=torch.float32, device=dev) for nloc in ys]
             y_full = torch.empty((ws, B * ntot), dtype=torch.float32, device=dev) if ws > 1 else None
-            entry.append((gname, wts, x, ys, y_full))
+            entry.append((gname, wts, x, ys, (ybuf, y_full)))
         layers.append(entry)
     torch.cuda.synchronize()
     setup_s = time.time() - t_setup
@@ -346,22 +356,26 @@ def run_ours(args, ws, rank, local):
 
     def step():
         for entry in layers:
-            for gname, wts, x, ys, y_full in entry:
+            for gname, wts, x, ys, (ybuf, y_full) in entry:
                 plane.gemv_multi_dev(wts, x, ys)
                 if ws > 1:
-                    local_y = torch.cat([y.reshape(-1) for y in ys]) if len(ys) > 1 else ys[0].reshape(-1)
+                    if B == 1:
+                        local_y = ybuf
+                    else:
+                        local_y = torch.cat([y.reshape(-1) for y in ys]) if len(ys) > 1 else ys[0].reshape(-1)
                     dist.all_gather_into_tensor(y_full.view(-1), local_y)
 
-    # ---- capture one step in a CUDA graph (single GPU); replay it K times
-    graph = None
+    # ---- capture one step (GEMVs and, on several GPUs, the NCCL all-gathers) in a
+    # CUDA graph; replay it K times
     with torch.cuda.stream(stream):
-        step()  # warm the launch path (occupancy queries etc.) before capture
+        step()  # warm the launch path (occupancy queries, NCCL communicators) before capture
     torch.cuda.synchronize()
-    if ws == 1:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            step()
-        torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier(device_ids=[local])
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    torch.cuda.synchronize()
 
     def run_step():
         if graph is not None:
