@@ -286,6 +286,95 @@ def prefill_bench(plane, dev, reps=10, m=2048):
     return out
 
 
+# ------------------------------------------------------------------ decode step (config 2)
+def decode_step_bench(plane, dev, prompt_len=512, new_tokens=128):
+    """a full Qwen2-0.5B-architecture decode step (24 layers,
+    hidden 896, 14/2 heads of 64, SwiGLU 4864, RMSNorm 1e-6, RoPE 1e6, vocab
+    151936) with random weights in log4, KV cache prefilled to `prompt_len` from
+    uniform-random token ids (teacher forced), then `new_tokens` greedy tokens
+    (repetition penalty 1.15, EOS stop disabled).  Each token is one replay of
+    the step's CUDA graph; tokens/s from CUDA events over the greedy tokens.
+    gemv_share = device time of the step's GEMV launches alone (their own graph)
+    / the step's time."""
+    import torch
+    from bramha_b200 import DecodeConfig, DecodeLayer, DecodeModel
+
+    cfg = DecodeConfig()
+    gen = torch.Generator(device=dev).manual_seed(2024)
+    qd, kvd, H, I, V = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim, cfg.hidden, cfg.intermediate, cfg.vocab
+    keys = []
+
+    def lin(name, n, k):
+        wf = torch.randn((n, k), generator=gen, device=dev) * 0.02
+        qb = torch.empty(n * k // 2, dtype=torch.uint8, device=dev)
+        sb = torch.empty(n, dtype=torch.float32, device=dev)
+        plane.quantize_dev("log4", wf, qb, sb)
+        w = plane.register_dev(f"c2:{name}", "log4", n, k, qb, sb)
+        keys.append(w.key)
+        return w
+
+    vec = lambda n, mean, std: torch.randn(n, generator=gen, device=dev) * std + mean
+    layers = [DecodeLayer(vec(H, 1, 0.1), lin(f"{i}.q", qd, H), lin(f"{i}.k", kvd, H), lin(f"{i}.v", kvd, H),
+                          vec(qd, 0, 0.1), vec(kvd, 0, 0.1), vec(kvd, 0, 0.1), lin(f"{i}.o", H, qd), vec(H, 1, 0.1),
+                          lin(f"{i}.g", I, H), lin(f"{i}.u", I, H), lin(f"{i}.d", H, I)) for i in range(cfg.layers)]
+    embed = torch.randn((V, H), generator=gen, device=dev)
+    dm = DecodeModel(plane, cfg, layers, embed, vec(H, 1, 0.1), lin("lm", V, H),
+                     max_ctx=prompt_len + new_tokens, max_generated=new_tokens)
+    dm.capture()
+    prompt = torch.randint(0, V, (prompt_len,), generator=torch.Generator().manual_seed(7)).tolist()
+    dm.reset()
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    with torch.cuda.stream(dm.stream):
+        e[0].record()
+        for tok in prompt[:-1]:
+            dm.set_token(tok)
+            dm.step(greedy=False)
+        e[1].record()
+        dm.set_token(prompt[-1])
+        e[2].record()
+        for _ in range(new_tokens):
+            dm.step(greedy=True)
+        e[3].record()
+    dm.sync()
+    ms_tok = e[2].elapsed_time(e[3]) / new_tokens
+    prefill_ms = e[0].elapsed_time(e[1]) / (prompt_len - 1)
+    toks = dm.generated_tokens()
+    # the step's GEMV launches alone, in their own graph
+    gg = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gg, stream=dm.stream):
+        for lw in dm.layers:
+            plane.gemv_multi_dev([lw.q, lw.k, lw.v], dm.h, [dm.q, dm.k, dm.v], stream=dm.stream)
+            plane.gemv_multi_dev([lw.o], dm.attn, [dm.o], stream=dm.stream)
+            plane.gemv_multi_dev([lw.gate, lw.up], dm.h, [dm.g, dm.u], stream=dm.stream)
+            plane.gemv_multi_dev([lw.down], dm.m, [dm.d], stream=dm.stream)
+        plane.gemv_multi_dev([dm.lm_head], dm.h, [dm.logits], stream=dm.stream)
+    reps = 20
+    with torch.cuda.stream(dm.stream):
+        gg.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            gg.replay()
+        b.record()
+    dm.sync()
+    gemv_ms = a.elapsed_time(b) / reps
+    del gg
+    dm.release()
+    out = {"workload": f"qwen2-0.5b decode step ({cfg.layers} layers, log4 linears, f32 norms/biases/embedding), "
+                       f"KV prefilled to {prompt_len} from uniform-random ids, {new_tokens} greedy tokens",
+           "tokens_per_s": round(1e3 / ms_tok, 1), "ms_per_token": round(ms_tok, 4),
+           "prefill_ms_per_token": round(prefill_ms, 4), "gemv_ms_per_token": round(gemv_ms, 4),
+           "gemv_share": round(gemv_ms / ms_tok, 3), "kernel_launches_per_token": dm.kernel_launches_per_step(),
+           "cuda_graph": True, "distinct_generated": len(set(toks)),
+           "data": "synthetic: weights N(0,0.02) packed on the device, norms 1+N(0,0.1), biases N(0,0.1), "
+                   "embedding N(0,1)"}
+    for k in keys:
+        plane.evict(k)
+    del dm, layers, embed
+    torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------------ our arm
 def run_ours(args, ws, rank, local):
     import torch
@@ -496,6 +585,9 @@ def run_ours(args, ws, rank, local):
     prefill = None
     if rank == 0 and ws == 1 and not args.no_prefill:
         prefill = prefill_bench(plane, dev, m=args.prefill_m)
+    decode_step = None
+    if rank == 0 and ws == 1 and not args.no_decode_step:
+        decode_step = decode_step_bench(plane, dev)
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -530,6 +622,7 @@ def run_ours(args, ws, rank, local):
                     "tokens_per_s": round(B / e2e_s, 2)},
             "cpu_baseline": cpu,
             "prefill": prefill,
+            "decode_step": decode_step,
             "setup_s": round(setup_s, 1),
         }
         print(json.dumps(line), flush=True)
@@ -549,6 +642,7 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill GEMM measurement")
+    ap.add_argument("--no-decode-step", action="store_true", help="skip the config-2 decode-step measurement")
     ap.add_argument("--layers", type=int, default=LAYERS, help="decoder layers (smaller = profiling case)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the config-3 prefill GEMM measurement (profiling case) and print its JSON")

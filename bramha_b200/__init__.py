@@ -6,8 +6,9 @@ side, mirroring the reference's compute-plane interface.
 """
 from ._lib import FMT, BramhaError, header_symbols, last_error, lib
 from .plane import CudaComputePlane, Weight, get_cuda_plane, packed_nbytes
+from .decode import DecodeConfig, DecodeLayer, DecodeModel
 
 __all__ = [
-    "FMT", "BramhaError", "CudaComputePlane", "Weight", "get_cuda_plane", "header_symbols", "last_error", "lib",
-    "packed_nbytes",
+    "FMT", "BramhaError", "CudaComputePlane", "DecodeConfig", "DecodeLayer", "DecodeModel", "Weight",
+    "get_cuda_plane", "header_symbols", "last_error", "lib", "packed_nbytes",
 ]

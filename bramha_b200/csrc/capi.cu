@@ -706,4 +706,88 @@ int bramha_cuda_quantize_dev(bramha_ctx* ctx, int fmt, int64_t N, int64_t K, con
     return BRAMHA_OK;
 }
 
+// ---- decode-step operations (decode.cu) -----------------------------------
+namespace {
+cudaStream_t op_stream(bramha_ctx* ctx, void* stream) {
+    return stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+}
+}  // namespace
+
+int bramha_cuda_op_embed(bramha_ctx* ctx, const float* table_dev, int64_t vocab, int64_t hidden,
+                         const int32_t* token_dev, float* x_dev, void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (vocab <= 0 || hidden <= 0) return fail(BRAMHA_ERR_INVALID, "embed: empty table");
+    if (!table_dev || !token_dev || !x_dev) return fail(BRAMHA_ERR_INVALID, "null device pointer");
+    DeviceGuard g(ctx->device);
+    CK(launch_embed(table_dev, vocab, hidden, token_dev, x_dev, op_stream(ctx, stream)), "embed launch");
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_op_rmsnorm(bramha_ctx* ctx, float* x_dev, const float* delta_dev, const float* weight_dev, int64_t n,
+                           float eps, float* out_dev, void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (n <= 0 || n > (1 << 24)) return fail(BRAMHA_ERR_INVALID, "rmsnorm: size %lld out of range", (long long)n);
+    if (!x_dev || !weight_dev || !out_dev) return fail(BRAMHA_ERR_INVALID, "null device pointer");
+    DeviceGuard g(ctx->device);
+    CK(launch_rmsnorm(x_dev, delta_dev, weight_dev, n, eps, out_dev, op_stream(ctx, stream)), "rmsnorm launch");
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_op_qkv_rope(bramha_ctx* ctx, float* q_dev, const float* k_dev, const float* v_dev,
+                            const float* bq_dev, const float* bk_dev, const float* bv_dev, int num_q_heads,
+                            int num_kv_heads, int head_dim, float rope_theta, const int32_t* pos_dev, int64_t max_ctx,
+                            float* k_cache_dev, float* v_cache_dev, void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || head_dim <= 0 || (head_dim & 1) ||
+        max_ctx <= 0)
+        return fail(BRAMHA_ERR_INVALID, "qkv_rope: bad head layout");
+    if (!q_dev || !k_dev || !v_dev || !pos_dev || !k_cache_dev || !v_cache_dev)
+        return fail(BRAMHA_ERR_INVALID, "null device pointer");
+    DeviceGuard g(ctx->device);
+    CK(launch_qkv_rope(q_dev, k_dev, v_dev, bq_dev, bk_dev, bv_dev, num_q_heads, num_kv_heads, head_dim, rope_theta,
+                       pos_dev, max_ctx, k_cache_dev, v_cache_dev, op_stream(ctx, stream)),
+       "qkv_rope launch");
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_op_attention(bramha_ctx* ctx, const float* q_dev, const float* k_cache_dev, const float* v_cache_dev,
+                             const int32_t* pos_dev, int num_q_heads, int num_kv_heads, int head_dim, int64_t max_ctx,
+                             float* out_dev, void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || head_dim <= 0 || head_dim > 128 ||
+        max_ctx <= 0 || max_ctx > 51200)
+        return fail(BRAMHA_ERR_INVALID, "attention: heads, head_dim (<= 128) or max_ctx (<= 51200) out of range");
+    if (!q_dev || !k_cache_dev || !v_cache_dev || !pos_dev || !out_dev)
+        return fail(BRAMHA_ERR_INVALID, "null device pointer");
+    DeviceGuard g(ctx->device);
+    CK(launch_attention(q_dev, k_cache_dev, v_cache_dev, pos_dev, num_q_heads, num_kv_heads, head_dim, max_ctx, out_dev,
+                        op_stream(ctx, stream)),
+       "attention launch");
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_op_silu_mul(bramha_ctx* ctx, const float* g_dev, const float* u_dev, int64_t n, float* out_dev,
+                            void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (n < 0) return fail(BRAMHA_ERR_INVALID, "negative size");
+    if (n > 0 && (!g_dev || !u_dev || !out_dev)) return fail(BRAMHA_ERR_INVALID, "null device pointer");
+    DeviceGuard g(ctx->device);
+    CK(launch_silu_mul(g_dev, u_dev, n, out_dev, op_stream(ctx, stream)), "silu_mul launch");
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_op_select(bramha_ctx* ctx, float* logits_dev, int64_t vocab, int32_t* generated_dev,
+                          int32_t* count_dev, int64_t max_generated, float penalty, int greedy, int32_t* token_dev,
+                          int32_t* pos_dev, void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (vocab <= 0 || max_generated < 0) return fail(BRAMHA_ERR_INVALID, "select: bad sizes");
+    if (!pos_dev || (greedy && (!logits_dev || !generated_dev || !count_dev || !token_dev)))
+        return fail(BRAMHA_ERR_INVALID, "null device pointer");
+    DeviceGuard g(ctx->device);
+    CK(launch_select(logits_dev, vocab, generated_dev, count_dev, max_generated, penalty, greedy, token_dev, pos_dev,
+                     op_stream(ctx, stream)),
+       "select launch");
+    return BRAMHA_OK;
+}
+
 }  // extern "C"

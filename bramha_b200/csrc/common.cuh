@@ -113,6 +113,20 @@ cudaError_t noalloc_rowsum_scratch(int device, float** out);
 // Tensor-core GEMV for the quantized formats, batch 1..8 (gemv_tc.cu).
 cudaError_t launch_gemv_tc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t stream);
 
+// Decode-step operations (decode.cu); token and position live in device memory.
+cudaError_t launch_embed(const float* table, int64_t vocab, int64_t hidden, const int32_t* token, float* x,
+                         cudaStream_t stream);
+cudaError_t launch_rmsnorm(float* x, const float* delta, const float* w, int64_t n, float eps, float* out,
+                           cudaStream_t stream);
+cudaError_t launch_qkv_rope(float* q, const float* k, const float* v, const float* bq, const float* bk,
+                            const float* bv, int nq, int nkv, int hd, float rope_theta, const int32_t* pos,
+                            int64_t max_ctx, float* k_cache, float* v_cache, cudaStream_t stream);
+cudaError_t launch_attention(const float* q, const float* k_cache, const float* v_cache, const int32_t* pos, int nq,
+                             int nkv, int hd, int64_t max_ctx, float* out, cudaStream_t stream);
+cudaError_t launch_silu_mul(const float* g, const float* u, int64_t n, float* out, cudaStream_t stream);
+cudaError_t launch_select(float* logits, int64_t vocab, int32_t* generated, int32_t* count, int64_t max_gen,
+                          float penalty, int greedy, int32_t* token, int32_t* pos, cudaStream_t stream);
+
 // GPU packers (quant.cu).
 cudaError_t launch_quantize(int fmt, int64_t N, int64_t K, const float* w, uint8_t* q, float* scales,
                             cudaStream_t stream);

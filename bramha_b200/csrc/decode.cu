@@ -1,0 +1,358 @@
+// decode.cu -- the per-token operations of a decoder-only model's single-token
+// decode step around the quantized GEMVs, restating the
+// reference's fast decode path, src/inference/cpu_engine.rs:2819-3064:
+//   embedding lookup (:2821-2825), RMSNorm (:1292-1302), bias + RoPE
+//   (:2895-2903, :1682-1698, thetas :1515-1530) + KV append (:2909),
+//   single-token GQA attention (:1450-1509), SiLU * up (:2023-2026), and the
+//   repetition penalty 1.15 + greedy argmax (:2985-3031).
+// Every kernel reads the token id and position from device memory, so a whole
+// decode step (these kernels and the GEMV launches) can be captured once in a
+// CUDA graph and replayed token after token without host work.  All are
+// programmatically dependent launches (see pdl_entry).
+// Floating-point expressions keep the reference's operation order; products
+// and sums that the reference writes separately are kept separate
+// (__fmul_rn / __fadd_rn: no FMA contraction) where a kernel restates a
+// formula term by term.  Reductions (RMSNorm, attention, argmax) use a fixed
+// tree order, so results are bit-reproducible run to run.
+#include <cuda_runtime.h>
+
+#include <cfloat>
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace bramha {
+namespace {
+
+constexpr int kNormThreads = 1024;
+
+// Programmatic dependent launch: every kernel here is launched with the PDL
+// attribute.  At entry it lets the next kernel of the stream be scheduled, then
+// waits for the previous one to complete (and its writes to be visible) before
+// touching any data, so the launch latency of consecutive kernels overlaps.
+__device__ __forceinline__ void pdl_entry() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+// Block-wide sum in a fixed order (warp trees, then warp 0 over the partials).
+template <int THREADS>
+__device__ float block_sum(float v, float* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    v = lane < THREADS / 32 ? red[lane] : 0.f;
+    if (warp == 0) v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+    __syncthreads();
+    v = red[0];
+    __syncthreads();
+    return v;
+}
+
+// x = table[(token mod vocab)]
+__global__ void embed_kernel(const float* __restrict__ table, int64_t vocab, int64_t hidden,
+                             const int32_t* __restrict__ token, float* __restrict__ x) {
+    pdl_entry();
+    const uint32_t t = (uint32_t)*token;
+    const int64_t row = (int64_t)(t % (uint64_t)vocab);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < hidden; i += (int64_t)gridDim.x * blockDim.x)
+        x[i] = table[row * hidden + i];
+}
+
+// x += delta (when given: the residual of the previous block), then
+// out = x * (1 / sqrt(mean(x^2) + eps)) * w.  One CTA.
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ delta,
+                                                               const float* __restrict__ w, int n, float eps,
+                                                               float* __restrict__ out) {
+    __shared__ float red[32];
+    pdl_entry();
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += kNormThreads) {
+        float v = x[i];
+        if (delta) {
+            v = __fadd_rn(v, delta[i]);
+            x[i] = v;
+        }
+        ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+    const float var = block_sum<kNormThreads>(ss, red) / (float)n;
+    const float scale = 1.0f / sqrtf(__fadd_rn(var, eps));
+    for (int i = threadIdx.x; i < n; i += kNormThreads) out[i] = __fmul_rn(__fmul_rn(x[i], scale), w[i]);
+}
+
+// Biases, RoPE of q and k at position *pos (half-split pairs (i, i + hd/2)),
+// then k and v appended to the caches at row *pos (rows >= max_ctx are not
+// written: the host keeps positions below the cache capacity).
+__global__ void qkv_rope_kernel(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                                const float* __restrict__ bq, const float* __restrict__ bk,
+                                const float* __restrict__ bv, int nq, int nkv, int hd, float rope_theta,
+                                const int32_t* __restrict__ pos_ptr, int64_t max_ctx, float* __restrict__ k_cache,
+                                float* __restrict__ v_cache) {
+    pdl_entry();
+    const int pos = *pos_ptr;
+    const bool store_kv = pos >= 0 && pos < max_ctx;
+    const int half = hd / 2;
+    const int64_t row = (int64_t)pos * nkv * hd;
+    const int npairs = (nq + nkv) * half;
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < npairs; idx += gridDim.x * blockDim.x) {
+        const int h = idx / half, i = idx - h * half;
+        const float theta = 1.0f / powf(rope_theta, (float)(2 * i) / (float)hd);
+        const float freq = __fmul_rn((float)pos, theta);
+        const float c = cosf(freq), s = sinf(freq);
+        if (h < nq) {
+            const int a = h * hd + i, b = a + half;
+            const float x1 = bq ? __fadd_rn(q[a], bq[a]) : q[a];
+            const float x2 = bq ? __fadd_rn(q[b], bq[b]) : q[b];
+            q[a] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+            q[b] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+        } else {
+            const int hk = h - nq;
+            const int a = hk * hd + i, b = a + half;
+            const float x1 = bk ? __fadd_rn(k[a], bk[a]) : k[a];
+            const float x2 = bk ? __fadd_rn(k[b], bk[b]) : k[b];
+            if (store_kv) {
+                k_cache[row + a] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+                k_cache[row + b] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+                v_cache[row + a] = bv ? __fadd_rn(v[a], bv[a]) : v[a];
+                v_cache[row + b] = bv ? __fadd_rn(v[b], bv[b]) : v[b];
+            }
+        }
+    }
+}
+
+// Single-token attention, one CTA per query head: scores of the *pos + 1
+// cached tokens, softmax, weighted sum of the values (grouped-query: query
+// head h reads kv head h / (nq / nkv)).  Scores are kept in shared memory
+// (max_ctx floats; the token count is clamped to it).
+constexpr int kAttnThreads = 128;
+constexpr int kAttnMaxHd = 128;
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __restrict__ q,
+                                                                 const float* __restrict__ k_cache,
+                                                                 const float* __restrict__ v_cache,
+                                                                 const int32_t* __restrict__ pos_ptr, int64_t max_ctx,
+                                                                 int nq, int nkv, int hd, float* __restrict__ out) {
+    extern __shared__ float sc[];  // [kv_len] scores, then probabilities
+    __shared__ float qs[kAttnMaxHd];
+    __shared__ float red[32];
+    __shared__ float part[kAttnThreads / 32][kAttnMaxHd];
+    pdl_entry();
+    const int head = blockIdx.x;
+    const int kvh = head / (nq / nkv);
+    const int kv_len = (int)min((int64_t)max(*pos_ptr + 1, 1), max_ctx);
+    const int ld = nkv * hd;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int d = threadIdx.x; d < hd; d += kAttnThreads) qs[d] = q[head * hd + d];
+    __syncthreads();
+    const float scale = 1.0f / sqrtf((float)hd);
+    // scores: thread per token, dot product in d order
+    float mx = -INFINITY;
+    for (int t = threadIdx.x; t < kv_len; t += kAttnThreads) {
+        const float* kr = k_cache + (int64_t)t * ld + kvh * hd;
+        float dot = 0.f;
+        for (int d = 0; d < hd; ++d) dot = __fadd_rn(dot, __fmul_rn(qs[d], kr[d]));
+        const float s = __fmul_rn(dot, scale);
+        sc[t] = s;
+        mx = fmaxf(mx, s);
+    }
+    mx = warp_max(mx);
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = lane < kAttnThreads / 32 ? red[lane] : -INFINITY;
+    mx = warp_max(mx);
+    __syncthreads();
+    float sum = 0.f;
+    for (int t = threadIdx.x; t < kv_len; t += kAttnThreads) {
+        const float p = expf(sc[t] - mx);
+        sc[t] = p;
+        sum = __fadd_rn(sum, p);
+    }
+    sum = block_sum<kAttnThreads>(sum, red);
+    // weighted values: warp w takes tokens w, w + 4, ...; lanes split the head dims
+    float acc[kAttnMaxHd / 32];
+#pragma unroll
+    for (int j = 0; j < kAttnMaxHd / 32; ++j) acc[j] = 0.f;
+    for (int t = warp; t < kv_len; t += kAttnThreads / 32) {
+        const float p = sc[t];
+        const float* vr = v_cache + (int64_t)t * ld + kvh * hd;
+#pragma unroll
+        for (int j = 0; j < kAttnMaxHd / 32; ++j) {
+            const int d = lane + 32 * j;
+            if (d < hd) acc[j] = __fadd_rn(acc[j], __fmul_rn(p, vr[d]));
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kAttnMaxHd / 32; ++j) {
+        const int d = lane + 32 * j;
+        if (d < hd) part[warp][d] = acc[j];
+    }
+    __syncthreads();
+    const float inv = 1.0f / sum;
+    for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
+        float o = 0.f;
+#pragma unroll
+        for (int w = 0; w < kAttnThreads / 32; ++w) o = __fadd_rn(o, part[w][d]);
+        out[head * hd + d] = __fmul_rn(o, inv);
+    }
+}
+
+// out = silu(g) * u, silu(g) = g * (1 / (1 + exp(-g)))
+__global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u, int64_t n,
+                                float* __restrict__ out) {
+    pdl_entry();
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float gi = g[i];
+        const float silu = __fmul_rn(gi, 1.0f / __fadd_rn(1.0f, expf(-gi)));
+        out[i] = __fmul_rn(silu, u[i]);
+    }
+}
+
+// Token selection.  greedy != 0: the repetition penalty over every entry of
+// generated[0 .. *count) in order (in place on the logits), then the first
+// index of the maximum becomes the next token; it is appended to `generated`
+// (while *count < max_gen) and written to *token.  In both modes *pos += 1.
+constexpr int kSelThreads = 1024;
+__global__ void __launch_bounds__(kSelThreads) select_kernel(float* __restrict__ logits, int64_t vocab,
+                                                             int32_t* __restrict__ generated,
+                                                             int32_t* __restrict__ count, int64_t max_gen,
+                                                             float penalty, int greedy, int32_t* __restrict__ token,
+                                                             int32_t* __restrict__ pos) {
+    __shared__ float bv[kSelThreads / 32];
+    __shared__ int64_t bi[kSelThreads / 32];
+    pdl_entry();
+    if (greedy) {
+        if (threadIdx.x == 0) {
+            const int n = *count;
+            for (int i = 0; i < n; ++i) {
+                const int64_t idx = (int64_t)(uint32_t)generated[i];
+                if (idx < vocab) {
+                    const float l = logits[idx];
+                    logits[idx] = l > 0.f ? l / penalty : __fmul_rn(l, penalty);
+                }
+            }
+        }
+        __syncthreads();
+        // per thread: its first strict maximum (NaN never wins; all -inf -> index 0)
+        float best = -INFINITY;
+        int64_t besti = 0;
+        for (int64_t i = threadIdx.x; i < vocab; i += kSelThreads) {
+            const float v = logits[i];
+            if (v > best) {
+                best = v;
+                besti = i;
+            }
+        }
+        // the maximum with the smallest index (the reference's first maximum)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int64_t oi = __shfl_xor_sync(0xffffffffu, besti, o);
+            if (ov > best || (ov == best && oi < besti)) {
+                best = ov;
+                besti = oi;
+            }
+        }
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        if (lane == 0) {
+            bv[warp] = best;
+            bi[warp] = besti;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float b = bv[0];
+            int64_t id = bi[0];
+            for (int w = 1; w < kSelThreads / 32; ++w)
+                if (bv[w] > b || (bv[w] == b && bi[w] < id)) {
+                    b = bv[w];
+                    id = bi[w];
+                }
+            const int n = *count;
+            if (n < max_gen) {
+                generated[n] = (int32_t)id;
+                *count = n + 1;
+            }
+            *token = (int32_t)id;
+        }
+    }
+    if (threadIdx.x == 0) *pos += 1;
+}
+
+}  // namespace
+
+cudaError_t launch_embed(const float* table, int64_t vocab, int64_t hidden, const int32_t* token, float* x,
+                         cudaStream_t st) {
+    const int threads = 256;
+    const int blocks = (int)((hidden + threads - 1) / threads);
+    return launch_pdl(embed_kernel, dim3(blocks), dim3(threads), 0, st, table, vocab, hidden, token, x);
+}
+
+cudaError_t launch_rmsnorm(float* x, const float* delta, const float* w, int64_t n, float eps, float* out,
+                           cudaStream_t st) {
+    if (n <= 0 || n > (1 << 24)) return cudaErrorInvalidValue;
+    return launch_pdl(rmsnorm_kernel, dim3(1), dim3(kNormThreads), 0, st, x, delta, w, (int)n, eps, out);
+}
+
+cudaError_t launch_qkv_rope(float* q, const float* k, const float* v, const float* bq, const float* bk,
+                            const float* bv, int nq, int nkv, int hd, float rope_theta, const int32_t* pos,
+                            int64_t max_ctx, float* k_cache, float* v_cache, cudaStream_t st) {
+    if (nq <= 0 || nkv <= 0 || hd <= 0 || (hd & 1) || nq % nkv || max_ctx <= 0) return cudaErrorInvalidValue;
+    const int npairs = (nq + nkv) * (hd / 2);
+    const int threads = 256;
+    return launch_pdl(qkv_rope_kernel, dim3((npairs + threads - 1) / threads), dim3(threads), 0, st, q, k, v, bq, bk,
+                      bv, nq, nkv, hd, rope_theta, pos, max_ctx, k_cache, v_cache);
+}
+
+cudaError_t launch_attention(const float* q, const float* k_cache, const float* v_cache, const int32_t* pos, int nq,
+                             int nkv, int hd, int64_t max_ctx, float* out, cudaStream_t st) {
+    if (nq <= 0 || nkv <= 0 || nq % nkv || hd <= 0 || hd > kAttnMaxHd || max_ctx <= 0) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)max_ctx * sizeof(float);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    return launch_pdl(attention_kernel, dim3(nq), dim3(kAttnThreads), smem, st, q, k_cache, v_cache, pos, max_ctx, nq,
+                      nkv, hd, out);
+}
+
+cudaError_t launch_silu_mul(const float* g, const float* u, int64_t n, float* out, cudaStream_t st) {
+    const int threads = 256;
+    const int blocks = (int)((n + threads - 1) / threads < 4096 ? (n + threads - 1) / threads : 4096);
+    if (n <= 0) return cudaSuccess;
+    return launch_pdl(silu_mul_kernel, dim3(blocks), dim3(threads), 0, st, g, u, n, out);
+}
+
+cudaError_t launch_select(float* logits, int64_t vocab, int32_t* generated, int32_t* count, int64_t max_gen,
+                          float penalty, int greedy, int32_t* token, int32_t* pos, cudaStream_t st) {
+    if (vocab <= 0) return cudaErrorInvalidValue;
+    return launch_pdl(select_kernel, dim3(1), dim3(kSelThreads), 0, st, logits, vocab, generated, count, max_gen,
+                      penalty, greedy, token, pos);
+}
+
+}  // namespace bramha

@@ -205,6 +205,56 @@ BRAMHA_API int bramha_cuda_stream_sync(bramha_ctx* ctx, void* stream);
 BRAMHA_API int bramha_cuda_quantize_dev(bramha_ctx* ctx, int fmt, int64_t N, int64_t K, const float* w_dev, void* q_dev,
                              float* scales_dev, void* stream);
 
+/* ------------------------------------------- decode-step operations (GPU)
+ *
+ * The per-token operations of the reference's single-token decode
+ * (src/inference/cpu_engine.rs:2819-3064) around the quantized GEMVs, so that
+ * a whole decode step -- these calls and bramha_cuda_gemv_multi_dev -- can be
+ * captured once in a CUDA graph and replayed token after token.  The current
+ * token id and position are int32 values in device memory (token_dev,
+ * pos_dev), read by the kernels when they run.  All pointers are device
+ * pointers; stream NULL = the context stream; calls are asynchronous. */
+
+/* x = table[token mod vocab] (cpu_engine.rs:2821-2825); table f32 [vocab][hidden]. */
+BRAMHA_API int bramha_cuda_op_embed(bramha_ctx* ctx, const float* table_dev, int64_t vocab, int64_t hidden,
+                                    const int32_t* token_dev, float* x_dev, void* stream);
+
+/* RMSNorm (rms_norm_into, cpu_engine.rs:1292-1302): if delta_dev is given,
+ * x += delta first (the residual connection, :2937-2939 / :2966-2968), then
+ * out = x * (1 / sqrt(mean(x^2) + eps)) * weight.  n <= 2^24. */
+BRAMHA_API int bramha_cuda_op_rmsnorm(bramha_ctx* ctx, float* x_dev, const float* delta_dev, const float* weight_dev,
+                                      int64_t n, float eps, float* out_dev, void* stream);
+
+/* q, k, v (+ optional biases, :2895-2897), half-split RoPE of q and k at the
+ * position *pos_dev (apply_rope_cpu :1682-1698, theta_i = 1/base^(2i/hd)),
+ * then k and v stored as row *pos_dev of the caches [max_ctx][kv_heads *
+ * head_dim] (:2909).  q is rotated in place. */
+BRAMHA_API int bramha_cuda_op_qkv_rope(bramha_ctx* ctx, float* q_dev, const float* k_dev, const float* v_dev,
+                                       const float* bq_dev, const float* bk_dev, const float* bv_dev, int num_q_heads,
+                                       int num_kv_heads, int head_dim, float rope_theta, const int32_t* pos_dev,
+                                       int64_t max_ctx, float* k_cache_dev, float* v_cache_dev, void* stream);
+
+/* Single-token grouped-query attention over cache rows 0 .. *pos_dev
+ * (flash_attention_single_into, cpu_engine.rs:1450-1509); head_dim <= 128,
+ * max_ctx <= 51200; out [num_q_heads * head_dim]. */
+BRAMHA_API int bramha_cuda_op_attention(bramha_ctx* ctx, const float* q_dev, const float* k_cache_dev,
+                                        const float* v_cache_dev, const int32_t* pos_dev, int num_q_heads,
+                                        int num_kv_heads, int head_dim, int64_t max_ctx, float* out_dev, void* stream);
+
+/* out = silu(g) * u (run_mlp_into, cpu_engine.rs:2023-2026). */
+BRAMHA_API int bramha_cuda_op_silu_mul(bramha_ctx* ctx, const float* g_dev, const float* u_dev, int64_t n,
+                                       float* out_dev, void* stream);
+
+/* Token selection (cpu_engine.rs:2985-3031).  greedy != 0: the repetition
+ * penalty over every entry of generated[0 .. *count) (logit > 0 ? logit /
+ * penalty : logit * penalty, in place), then the first maximum becomes
+ * *token_dev and is appended to generated (while *count < max_generated).
+ * greedy == 0 (teacher forcing: the caller writes the next token): only the
+ * position advances.  Either way *pos_dev += 1. */
+BRAMHA_API int bramha_cuda_op_select(bramha_ctx* ctx, float* logits_dev, int64_t vocab, int32_t* generated_dev,
+                                     int32_t* count_dev, int64_t max_generated, float penalty, int greedy,
+                                     int32_t* token_dev, int32_t* pos_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,6 +8,10 @@ reference's CPU arithmetic (akshaybhlrp/bramha):
 * decode GEMV ``matvec_mul_into``: ``src/inference/cpu_engine.rs:1307-1444``
 * allocating GEMV ``matvec_mul``: ``src/inference/cpu_engine.rs:355-562``
 * prefill GEMM ``gemm_cpu``: ``src/inference/cpu_engine.rs:565-706``
+* decode-step operations (RMSNorm, RoPE, single-token attention, SwiGLU,
+  repetition penalty + argmax): ``src/inference/cpu_engine.rs:1292-1302,
+  1450-1530, 1682-1698, 2023-2026, 2985-3031``; the step itself is in
+  ``oracle/decode.py``
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline and
 reference legs may import this package.  The product path (``bramha_b200``)
@@ -67,6 +71,12 @@ def lib():
             "bro_gemm_log4": (None, [_f32p, _i64, _i64, _u8p, _f32p, _i64, _f32p]),
             "bro_gemm_u4_par": (None, [_f32p, _i64, _i64, _u8p, _f32p, _i64, _f32p, ctypes.c_int]),
             "bro_max_threads": (ctypes.c_int, []),
+            "bro_rms_norm": (None, [_f32p, _f32p, _i64, ctypes.c_float, _f32p]),
+            "bro_rope": (None, [_f32p, _i64, ctypes.c_int, ctypes.c_int, ctypes.c_float]),
+            "bro_attention": (None, [_f32p, _f32p, _f32p, _i64, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p]),
+            "bro_silu_mul": (None, [_f32p, _f32p, _i64, _f32p]),
+            "bro_penalty_argmax": (ctypes.c_int64, [_f32p, _i64, ctypes.POINTER(ctypes.c_int32), _i64,
+                                                    ctypes.c_float]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -251,3 +261,45 @@ def dequantize(fmt: str, q, scales, in_features: int):
 
 def max_threads() -> int:
     return int(lib().bro_max_threads())
+
+
+# ---- decode-step operations (cpu_engine.rs; see bramha_oracle.c) -------------
+def rms_norm(x, w, eps: float):
+    x = _c(x, np.float32)
+    w = _c(w, np.float32)
+    out = np.empty_like(x)
+    lib().bro_rms_norm(_p(x, _f32p), _p(w, _f32p), x.size, eps, _p(out, _f32p))
+    return out
+
+
+def rope_(v, pos: int, num_heads: int, head_dim: int, rope_theta: float):
+    """In-place RoPE of a float32 vector of num_heads * head_dim values."""
+    assert v.dtype == np.float32 and v.flags.c_contiguous
+    lib().bro_rope(_p(v, _f32p), pos, num_heads, head_dim, rope_theta)
+    return v
+
+
+def attention(q, k_cache, v_cache, kv_len: int, num_q_heads: int, num_kv_heads: int, head_dim: int):
+    q = _c(q, np.float32)
+    k_cache = _c(k_cache, np.float32)
+    v_cache = _c(v_cache, np.float32)
+    out = np.empty(num_q_heads * head_dim, np.float32)
+    lib().bro_attention(_p(q, _f32p), _p(k_cache, _f32p), _p(v_cache, _f32p), kv_len, num_q_heads,
+                        num_kv_heads, head_dim, _p(out, _f32p))
+    return out
+
+
+def silu_mul(g, u):
+    g = _c(g, np.float32)
+    u = _c(u, np.float32)
+    out = np.empty_like(g)
+    lib().bro_silu_mul(_p(g, _f32p), _p(u, _f32p), g.size, _p(out, _f32p))
+    return out
+
+
+def penalty_argmax(logits, generated, penalty: float = 1.15):
+    """Applies the repetition penalty to `logits` in place; returns the argmax."""
+    assert logits.dtype == np.float32 and logits.flags.c_contiguous
+    gen = np.ascontiguousarray(np.asarray(generated, dtype=np.int32))
+    return int(lib().bro_penalty_argmax(_p(logits, _f32p), logits.size,
+                                        gen.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), gen.size, penalty))

@@ -426,3 +426,99 @@ BRO_API int bro_max_threads(void) {
     return 1;
 #endif
 }
+
+/* ---- decode step -------------------------------------
+ * The per-token operations around the quantized GEMVs, in the reference's own
+ * loop order (sequential fp32 sums, no FMA contraction). */
+
+/* rms_norm_into, src/inference/cpu_engine.rs:1292-1302 */
+BRO_API void bro_rms_norm(const float* x, const float* w, int64_t n, float eps, float* out) {
+    float variance = 0.0f;
+    for (int64_t i = 0; i < n; ++i) variance += x[i] * x[i];
+    variance /= (float)n;
+    const float scale = 1.0f / sqrtf(variance + eps);
+    for (int64_t i = 0; i < n; ++i) out[i] = x[i] * scale * w[i];
+}
+
+/* apply_rope_cpu, cpu_engine.rs:1682-1698, with get_rope_thetas
+ * (theta_i = 1 / base^(2i / head_dim), cpu_engine.rs:1515-1530): the two
+ * halves of each head rotate together ("half-split"). */
+BRO_API void bro_rope(float* v, int64_t pos, int num_heads, int head_dim, float rope_theta) {
+    const int half = head_dim / 2;
+    for (int h = 0; h < num_heads; ++h) {
+        float* hv = v + (int64_t)h * head_dim;
+        for (int i = 0; i < half; ++i) {
+            const float theta = 1.0f / powf(rope_theta, (float)(2 * i) / (float)head_dim);
+            const float freq = (float)pos * theta;
+            const float c = cosf(freq), s = sinf(freq);
+            const float x1 = hv[i], x2 = hv[i + half];
+            hv[i] = x1 * c - x2 * s;
+            hv[i + half] = x2 * c + x1 * s;
+        }
+    }
+}
+
+/* flash_attention_single_into, cpu_engine.rs:1450-1509: per query head, one
+ * pass over the cached tokens with a running max m, sum l and output o.
+ * k_cache / v_cache are [kv_len][num_kv_heads * head_dim]. */
+BRO_API void bro_attention(const float* q, const float* k_cache, const float* v_cache, int64_t kv_len,
+                           int num_q_heads, int num_kv_heads, int head_dim, float* out) {
+    const float scale = 1.0f / sqrtf((float)head_dim);
+    const int heads_per_kv = num_q_heads / num_kv_heads;
+    float o[256];
+    for (int head = 0; head < num_q_heads; ++head) {
+        const int kv_head = head / heads_per_kv;
+        const float* qh = q + (int64_t)head * head_dim;
+        for (int d = 0; d < head_dim; ++d) o[d] = 0.0f;
+        float m = -INFINITY, l = 0.0f;
+        for (int64_t t = 0; t < kv_len; ++t) {
+            const int64_t off = t * num_kv_heads * head_dim + (int64_t)kv_head * head_dim;
+            float dot = 0.0f;
+            for (int d = 0; d < head_dim; ++d) dot += qh[d] * k_cache[off + d];
+            const float score = dot * scale;
+            if (score > m) {
+                const float e = expf(m - score);
+                l = l * e + 1.0f;
+                for (int d = 0; d < head_dim; ++d) o[d] = o[d] * e + v_cache[off + d];
+                m = score;
+            } else {
+                const float e = expf(score - m);
+                l += e;
+                for (int d = 0; d < head_dim; ++d) o[d] += e * v_cache[off + d];
+            }
+        }
+        const float inv_l = 1.0f / l;
+        for (int d = 0; d < head_dim; ++d) out[(int64_t)head * head_dim + d] = o[d] * inv_l;
+    }
+}
+
+/* SwiGLU of run_mlp_into, cpu_engine.rs:2023-2026 (dense branch of :1775-2035): silu(g) * u with
+ * silu(g) = g * (1 / (1 + exp(-g))). */
+BRO_API void bro_silu_mul(const float* g, const float* u, int64_t n, float* out) {
+    for (int64_t d = 0; d < n; ++d) {
+        const float silu = g[d] * (1.0f / (1.0f + expf(-g[d])));
+        out[d] = silu * u[d];
+    }
+}
+
+/* Repetition penalty 1.15 over every entry of the generated list (an id that
+ * appears twice is penalised twice), then greedy argmax (first maximum);
+ * cpu_engine.rs:2985-3031.  Modifies logits in place. */
+BRO_API int64_t bro_penalty_argmax(float* logits, int64_t vocab, const int32_t* generated, int64_t n_generated,
+                                   float penalty) {
+    for (int64_t i = 0; i < n_generated; ++i) {
+        const int64_t idx = (int64_t)(uint32_t)generated[i];
+        if (idx < vocab) {
+            const float logit = logits[idx];
+            logits[idx] = logit > 0.0f ? logit / penalty : logit * penalty;
+        }
+    }
+    int64_t max_idx = 0;
+    float max_val = -INFINITY;
+    for (int64_t i = 0; i < vocab; ++i)
+        if (logits[i] > max_val) {
+            max_val = logits[i];
+            max_idx = i;
+        }
+    return max_idx;
+}
