@@ -62,11 +62,14 @@ _SIGNATURES = {
     "bramha_cuda_quantize_dev": [_vp, _int, _i64, _i64, _vp, _vp, _vp, _vp],
     "bramha_cuda_stream_sync": [_vp, _vp],
     "bramha_cuda_gemm_noalloc_dev": [_vp, _vp, _vp, _i64, _vp, _vp],
+    "bramha_cuda_set_gemv_kernel": [_vp, _int],
     "bramha_cuda_op_embed": [_vp, _vp, _i64, _i64, _vp, _vp, _vp],
     "bramha_cuda_op_rmsnorm": [_vp, _vp, _vp, _vp, _i64, ctypes.c_float, _vp, _vp],
     "bramha_cuda_op_qkv_rope": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, ctypes.c_float, _vp, _i64,
                                 _vp, _vp, _vp],
     "bramha_cuda_op_attention": [_vp, _vp, _vp, _vp, _vp, _int, _int, _int, _i64, _vp, _vp],
+    "bramha_cuda_op_rope_attention": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, ctypes.c_float, _vp,
+                                      _i64, _vp, _vp, _vp, _vp],
     "bramha_cuda_op_silu_mul": [_vp, _vp, _vp, _i64, _vp, _vp],
     "bramha_cuda_op_select": [_vp, _vp, _i64, _vp, _vp, _i64, ctypes.c_float, _int, _vp, _vp, _vp],
 }

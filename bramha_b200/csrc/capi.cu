@@ -55,6 +55,7 @@ struct bramha_ctx {
     int* d_err = nullptr;                // device error word written by bounded waits
     float* split_ws = nullptr;           // K-split partials of the tensor-core GEMV
     int* split_tickets = nullptr;        // per-tile arrival counters (kept zero between launches)
+    int gemv_kernel = BRAMHA_GEMV_AUTO;  // kernel choice for the tiled formats
 };
 
 namespace {
@@ -301,7 +302,12 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
         a.split_ws_floats = kSplitWsFloats;
         a.split_tickets = ctx->split_tickets;
         a.split_tickets_n = kSplitTickets;
-        if (is_tiled(fmt))
+        const bool cc = ctx->gemv_kernel == BRAMHA_GEMV_CUDA_CORE
+                            ? is_tiled(fmt) && a.batch == 1
+                            : ctx->gemv_kernel == BRAMHA_GEMV_AUTO && gemv_cc_eligible(fmt, a);
+        if (cc)
+            CK(launch_gemv_cc(fmt, a, ctx->num_sms, st), "cuda-core gemv launch");
+        else if (is_tiled(fmt))
             CK(launch_gemv_tc(fmt, a, ctx->num_sms, st), "tensor-core gemv launch");
         else
             CK(launch_gemv_f32(a, ctx->num_sms, st), "gemv launch");
@@ -469,6 +475,14 @@ int bramha_cuda_destroy(bramha_ctx* ctx) {
     if (ctx->split_tickets) cudaFree(ctx->split_tickets);
     cudaStreamDestroy(ctx->stream);
     delete ctx;
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_set_gemv_kernel(bramha_ctx* ctx, int kind) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (kind != BRAMHA_GEMV_AUTO && kind != BRAMHA_GEMV_TENSOR_CORE && kind != BRAMHA_GEMV_CUDA_CORE)
+        return fail(BRAMHA_ERR_INVALID, "unknown GEMV kernel choice %d", kind);
+    ctx->gemv_kernel = kind;
     return BRAMHA_OK;
 }
 
@@ -763,6 +777,24 @@ int bramha_cuda_op_attention(bramha_ctx* ctx, const float* q_dev, const float* k
     CK(launch_attention(q_dev, k_cache_dev, v_cache_dev, pos_dev, num_q_heads, num_kv_heads, head_dim, max_ctx, out_dev,
                         op_stream(ctx, stream)),
        "attention launch");
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_op_rope_attention(bramha_ctx* ctx, const float* q_dev, const float* k_dev, const float* v_dev,
+                                  const float* bq_dev, const float* bk_dev, const float* bv_dev, int num_q_heads,
+                                  int num_kv_heads, int head_dim, float rope_theta, const int32_t* pos_dev,
+                                  int64_t max_ctx, float* k_cache_dev, float* v_cache_dev, float* out_dev,
+                                  void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || head_dim <= 0 || (head_dim & 1) ||
+        head_dim > 128 || max_ctx <= 0 || max_ctx > 51200)
+        return fail(BRAMHA_ERR_INVALID, "rope_attention: heads, head_dim (even, <= 128) or max_ctx (<= 51200) out of range");
+    if (!q_dev || !k_dev || !v_dev || !pos_dev || !k_cache_dev || !v_cache_dev || !out_dev)
+        return fail(BRAMHA_ERR_INVALID, "null device pointer");
+    DeviceGuard g(ctx->device);
+    CK(launch_rope_attention(q_dev, k_dev, v_dev, bq_dev, bk_dev, bv_dev, rope_theta, pos_dev, max_ctx, k_cache_dev,
+                             v_cache_dev, num_q_heads, num_kv_heads, head_dim, out_dev, op_stream(ctx, stream)),
+       "rope_attention launch");
     return BRAMHA_OK;
 }
 

@@ -110,6 +110,11 @@ cudaError_t launch_gemm_tcgen05_bf16_noalloc(int fmt, const uint8_t* q, int64_t 
 constexpr int64_t kNoAllocMaxTokens = 16384;
 cudaError_t noalloc_rowsum_scratch(int device, float** out);
 
+// CUDA-core batch-1 GEMV of the tiled formats for latency-bound (small)
+// launches (gemv_cc.cu); eligible() says whether a launch should take it.
+bool gemv_cc_eligible(int fmt, const GemvArgs& a);
+cudaError_t launch_gemv_cc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t stream);
+
 // Tensor-core GEMV for the quantized formats, batch 1..8 (gemv_tc.cu).
 cudaError_t launch_gemv_tc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t stream);
 
@@ -123,6 +128,10 @@ cudaError_t launch_qkv_rope(float* q, const float* k, const float* v, const floa
                             int64_t max_ctx, float* k_cache, float* v_cache, cudaStream_t stream);
 cudaError_t launch_attention(const float* q, const float* k_cache, const float* v_cache, const int32_t* pos, int nq,
                              int nkv, int hd, int64_t max_ctx, float* out, cudaStream_t stream);
+cudaError_t launch_rope_attention(const float* q, const float* k, const float* v, const float* bq, const float* bk,
+                                  const float* bv, float rope_theta, const int32_t* pos, int64_t max_ctx,
+                                  float* k_cache, float* v_cache, int nq, int nkv, int hd, float* out,
+                                  cudaStream_t stream);
 cudaError_t launch_silu_mul(const float* g, const float* u, int64_t n, float* out, cudaStream_t stream);
 cudaError_t launch_select(float* logits, int64_t vocab, int32_t* generated, int32_t* count, int64_t max_gen,
                           float penalty, int greedy, int32_t* token, int32_t* pos, cudaStream_t stream);

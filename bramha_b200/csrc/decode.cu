@@ -222,6 +222,103 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __
     }
 }
 
+// Fused form of qkv_rope_kernel + attention_kernel, one CTA per query head:
+// the CTA adds the biases and rotates its query head and the current token's
+// key (of its kv head) itself, attends over cache rows 0 .. pos-1 plus that
+// new row (held in shared memory), and the first query head of each kv group
+// appends the new key / value row to the caches (rows the other CTAs of the
+// group do not read).  Same arithmetic as the two kernels.
+__global__ void __launch_bounds__(kAttnThreads) rope_attention_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+    const float* __restrict__ bq, const float* __restrict__ bk, const float* __restrict__ bv, float rope_theta,
+    const int32_t* __restrict__ pos_ptr, int64_t max_ctx, float* __restrict__ k_cache, float* __restrict__ v_cache,
+    int nq, int nkv, int hd, float* __restrict__ out) {
+    extern __shared__ float sc[];  // [kv_len] scores, then probabilities
+    __shared__ float qs[kAttnMaxHd], kn[kAttnMaxHd], vn[kAttnMaxHd];
+    __shared__ float red[32];
+    __shared__ float part[kAttnThreads / 32][kAttnMaxHd];
+    pdl_entry();
+    const int head = blockIdx.x;
+    const int group = nq / nkv;
+    const int kvh = head / group;
+    const int pos = *pos_ptr;
+    const int kv_len = (int)min((int64_t)max(pos + 1, 1), max_ctx);  // rows 0 .. kv_len-2 cached, kv_len-1 new
+    const int ld = nkv * hd;
+    const int half = hd / 2;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < half; i += kAttnThreads) {
+        const float theta = 1.0f / powf(rope_theta, (float)(2 * i) / (float)hd);
+        const float freq = __fmul_rn((float)pos, theta);
+        const float c = cosf(freq), s = sinf(freq);
+        const int a = head * hd + i, b = a + half;
+        float x1 = bq ? __fadd_rn(q[a], bq[a]) : q[a];
+        float x2 = bq ? __fadd_rn(q[b], bq[b]) : q[b];
+        qs[i] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+        qs[i + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+        const int ka = kvh * hd + i, kb = ka + half;
+        x1 = bk ? __fadd_rn(k[ka], bk[ka]) : k[ka];
+        x2 = bk ? __fadd_rn(k[kb], bk[kb]) : k[kb];
+        kn[i] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+        kn[i + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+        vn[i] = bv ? __fadd_rn(v[ka], bv[ka]) : v[ka];
+        vn[i + half] = bv ? __fadd_rn(v[kb], bv[kb]) : v[kb];
+    }
+    __syncthreads();
+    if (head % group == 0 && pos >= 0 && pos < max_ctx)
+        for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
+            k_cache[(int64_t)pos * ld + kvh * hd + d] = kn[d];
+            v_cache[(int64_t)pos * ld + kvh * hd + d] = vn[d];
+        }
+    const float scale = 1.0f / sqrtf((float)hd);
+    float mx = -INFINITY;
+    for (int t = threadIdx.x; t < kv_len; t += kAttnThreads) {
+        const float* kr = t == kv_len - 1 ? kn : k_cache + (int64_t)t * ld + kvh * hd;
+        float dot = 0.f;
+        for (int d = 0; d < hd; ++d) dot = __fadd_rn(dot, __fmul_rn(qs[d], kr[d]));
+        const float sv = __fmul_rn(dot, scale);
+        sc[t] = sv;
+        mx = fmaxf(mx, sv);
+    }
+    mx = warp_max(mx);
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = lane < kAttnThreads / 32 ? red[lane] : -INFINITY;
+    mx = warp_max(mx);
+    __syncthreads();
+    float sum = 0.f;
+    for (int t = threadIdx.x; t < kv_len; t += kAttnThreads) {
+        const float p = expf(sc[t] - mx);
+        sc[t] = p;
+        sum = __fadd_rn(sum, p);
+    }
+    sum = block_sum<kAttnThreads>(sum, red);
+    float acc[kAttnMaxHd / 32];
+#pragma unroll
+    for (int j = 0; j < kAttnMaxHd / 32; ++j) acc[j] = 0.f;
+    for (int t = warp; t < kv_len; t += kAttnThreads / 32) {
+        const float p = sc[t];
+        const float* vr = t == kv_len - 1 ? vn : v_cache + (int64_t)t * ld + kvh * hd;
+#pragma unroll
+        for (int j = 0; j < kAttnMaxHd / 32; ++j) {
+            const int d = lane + 32 * j;
+            if (d < hd) acc[j] = __fadd_rn(acc[j], __fmul_rn(p, vr[d]));
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kAttnMaxHd / 32; ++j) {
+        const int d = lane + 32 * j;
+        if (d < hd) part[warp][d] = acc[j];
+    }
+    __syncthreads();
+    const float inv = 1.0f / sum;
+    for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
+        float o = 0.f;
+#pragma unroll
+        for (int w = 0; w < kAttnThreads / 32; ++w) o = __fadd_rn(o, part[w][d]);
+        out[head * hd + d] = __fmul_rn(o, inv);
+    }
+}
+
 // out = silu(g) * u, silu(g) = g * (1 / (1 + exp(-g)))
 __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u, int64_t n,
                                 float* __restrict__ out) {
@@ -339,6 +436,23 @@ cudaError_t launch_attention(const float* q, const float* k_cache, const float* 
     }
     return launch_pdl(attention_kernel, dim3(nq), dim3(kAttnThreads), smem, st, q, k_cache, v_cache, pos, max_ctx, nq,
                       nkv, hd, out);
+}
+
+cudaError_t launch_rope_attention(const float* q, const float* k, const float* v, const float* bq, const float* bk,
+                                  const float* bv, float rope_theta, const int32_t* pos, int64_t max_ctx,
+                                  float* k_cache, float* v_cache, int nq, int nkv, int hd, float* out,
+                                  cudaStream_t st) {
+    if (nq <= 0 || nkv <= 0 || nq % nkv || hd <= 0 || (hd & 1) || hd > kAttnMaxHd || max_ctx <= 0)
+        return cudaErrorInvalidValue;
+    const size_t smem = (size_t)max_ctx * sizeof(float);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    if (smem > 48 * 1024) {
+        cudaError_t e =
+            cudaFuncSetAttribute(rope_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    return launch_pdl(rope_attention_kernel, dim3(nq), dim3(kAttnThreads), smem, st, q, k, v, bq, bk, bv, rope_theta,
+                      pos, max_ctx, k_cache, v_cache, nq, nkv, hd, out);
 }
 
 cudaError_t launch_silu_mul(const float* g, const float* u, int64_t n, float* out, cudaStream_t st) {

@@ -10,7 +10,8 @@ The step restates the reference's fast decode path
 
 The linears are the tensor-core GEMVs of the quantized formats
 (``bramha_cuda_gemv_multi_dev``: q|k|v and gate|up each one launch); everything
-else is the ``bramha_cuda_op_*`` kernels.  Token id and position live in device
+else is the ``bramha_cuda_op_*`` kernels (bias + RoPE + KV append fused into the
+attention launch).  Token id and position live in device
 memory, so a step is captured once in a CUDA graph and replayed token after
 token with no host work: ``greedy`` steps pick the next token on the device,
 teacher-forced steps (prompt prefill, parity checks) take a token the host
@@ -138,12 +139,10 @@ class DecodeModel:
                                            self.h.data_ptr(), st))
             P.gemv_multi_dev([lw.q, lw.k, lw.v], self.h, [self.q, self.k, self.v], stream=self.stream)
             kc, vc = self.k_cache[li], self.v_cache[li]
-            check(L.bramha_cuda_op_qkv_rope(ctx, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), _p(lw.bq),
-                                            _p(lw.bk), _p(lw.bv), c.heads, c.kv_heads, c.head_dim, c.rope_theta,
-                                            self.pos.data_ptr(), self.max_ctx, kc.data_ptr(), vc.data_ptr(), st))
-            check(L.bramha_cuda_op_attention(ctx, self.q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
-                                             self.pos.data_ptr(), c.heads, c.kv_heads, c.head_dim, self.max_ctx,
-                                             self.attn.data_ptr(), st))
+            check(L.bramha_cuda_op_rope_attention(ctx, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(),
+                                                  _p(lw.bq), _p(lw.bk), _p(lw.bv), c.heads, c.kv_heads, c.head_dim,
+                                                  c.rope_theta, self.pos.data_ptr(), self.max_ctx, kc.data_ptr(),
+                                                  vc.data_ptr(), self.attn.data_ptr(), st))
             P.gemv_multi_dev([lw.o], self.attn, [self.o], stream=self.stream)
             check(L.bramha_cuda_op_rmsnorm(ctx, self.x.data_ptr(), self.o.data_ptr(), lw.ln2.data_ptr(), c.hidden,
                                            c.eps, self.h.data_ptr(), st))
@@ -161,8 +160,8 @@ class DecodeModel:
 
     def kernel_launches_per_step(self) -> int:
         """Launches of this library's kernels in one step: the embedding, per layer
-        4 GEMVs and 5 other kernels, then the final norm, lm_head and selection."""
-        return 1 + 9 * self.cfg.layers + 3
+        4 GEMVs and 4 other kernels, then the final norm, lm_head and selection."""
+        return 1 + 8 * self.cfg.layers + 3
 
     def step(self, greedy: bool = True):
         """One token: eagerly launched, or replayed from the captured graph."""

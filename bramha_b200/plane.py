@@ -188,6 +188,12 @@ class CudaComputePlane:
         check(lib().bramha_cuda_gemm_dev(self._ctx, w.handle, x.data_ptr(), dt, x.shape[0], y.data_ptr(),
                                          _stream(stream)))
 
+    GEMV_KERNELS = {"auto": 0, "tensor_core": 1, "cuda_core": 2}
+
+    def set_gemv_kernel(self, kind: str = "auto"):
+        """'auto' (default), 'tensor_core' or 'cuda_core' for the quantized GEMVs."""
+        check(lib().bramha_cuda_set_gemv_kernel(self._ctx, self.GEMV_KERNELS[kind]))
+
     def stream_sync(self, stream=None):
         """Wait for the stream and raise if a kernel reported a device-side failure."""
         check(lib().bramha_cuda_stream_sync(self._ctx, _stream(stream)))

@@ -101,6 +101,18 @@ BRAMHA_API int bramha_cuda_abi_version(void);
 BRAMHA_API int bramha_cuda_set_memory_cap(bramha_ctx* ctx, size_t bytes);
 BRAMHA_API int bramha_cuda_memory_used(bramha_ctx* ctx, size_t* bytes);
 
+/* Which GEMV kernel the context's calls use for the quantized formats.
+ * AUTO (default): at batch 1, launches with rows of at most 1024 columns and at
+ * most 8 MB of packed weights run on the CUDA cores (latency-bound: weights
+ * preloaded before the launch dependency, fp32 multiply-adds), all others and
+ * batches > 1 on the tensor cores.  TENSOR_CORE / CUDA_CORE pin one kernel (CUDA_CORE applies at batch 1;
+ * other batches stay on the tensor cores).  Both compute y = s * sum x * code
+ * within the path's 1e-3 tolerance of the reference. */
+#define BRAMHA_GEMV_AUTO 0
+#define BRAMHA_GEMV_TENSOR_CORE 1
+#define BRAMHA_GEMV_CUDA_CORE 2
+BRAMHA_API int bramha_cuda_set_gemv_kernel(bramha_ctx* ctx, int kind);
+
 /* ---------------------------------------------------------------- weights */
 
 /* get_or_create_op (wgpu_backend.rs:603-722): copies the packed weight and
@@ -240,6 +252,16 @@ BRAMHA_API int bramha_cuda_op_qkv_rope(bramha_ctx* ctx, float* q_dev, const floa
 BRAMHA_API int bramha_cuda_op_attention(bramha_ctx* ctx, const float* q_dev, const float* k_cache_dev,
                                         const float* v_cache_dev, const int32_t* pos_dev, int num_q_heads,
                                         int num_kv_heads, int head_dim, int64_t max_ctx, float* out_dev, void* stream);
+
+/* bramha_cuda_op_qkv_rope followed by bramha_cuda_op_attention in one launch
+ * (same arithmetic): each query head's CTA rotates its own q and the current
+ * token's k, attends over cache rows 0 .. *pos_dev - 1 plus that new row, and
+ * the new k / v row is stored at row *pos_dev.  q is not modified. */
+BRAMHA_API int bramha_cuda_op_rope_attention(bramha_ctx* ctx, const float* q_dev, const float* k_dev,
+                                             const float* v_dev, const float* bq_dev, const float* bk_dev,
+                                             const float* bv_dev, int num_q_heads, int num_kv_heads, int head_dim,
+                                             float rope_theta, const int32_t* pos_dev, int64_t max_ctx,
+                                             float* k_cache_dev, float* v_cache_dev, float* out_dev, void* stream);
 
 /* out = silu(g) * u (run_mlp_into, cpu_engine.rs:2023-2026). */
 BRAMHA_API int bramha_cuda_op_silu_mul(bramha_ctx* ctx, const float* g_dev, const float* u_dev, int64_t n,

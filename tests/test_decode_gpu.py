@@ -131,3 +131,44 @@ def test_decode_graph_replay_matches_eager(plane):
         assert np.array_equal(a, b)
     assert eager[1] == graph[1]
     dm.release()
+
+
+def test_rope_attention_fused_equals_two_kernels(plane):
+    """bramha_cuda_op_rope_attention == op_qkv_rope then op_attention, bit for bit
+    (outputs and the appended cache row), at a position with cached rows."""
+    from bramha_b200 import lib
+    from bramha_b200._lib import check
+    nq, nkv, hd, ctx_len, pos = 14, 2, 64, 64, 37
+    r = rng(12)
+    dev = torch.device("cuda", 0)
+    mk = lambda *shape: torch.from_numpy(r.normal(0, 1, shape).astype(np.float32)).to(dev)
+    q, k, v = mk(nq * hd), mk(nkv * hd), mk(nkv * hd)
+    bq, bk, bv = mk(nq * hd), mk(nkv * hd), mk(nkv * hd)
+    kc0, vc0 = mk(ctx_len, nkv * hd), mk(ctx_len, nkv * hd)
+    p = torch.tensor([pos], dtype=torch.int32, device=dev)
+    L, c = lib(), plane.ctx
+    # two kernels
+    q1, kc1, vc1, o1 = q.clone(), kc0.clone(), vc0.clone(), torch.empty(nq * hd, device=dev)
+    check(L.bramha_cuda_op_qkv_rope(c, q1.data_ptr(), k.data_ptr(), v.data_ptr(), bq.data_ptr(), bk.data_ptr(),
+                                    bv.data_ptr(), nq, nkv, hd, 1e6, p.data_ptr(), ctx_len, kc1.data_ptr(),
+                                    vc1.data_ptr(), None))
+    check(L.bramha_cuda_op_attention(c, q1.data_ptr(), kc1.data_ptr(), vc1.data_ptr(), p.data_ptr(), nq, nkv, hd,
+                                     ctx_len, o1.data_ptr(), None))
+    # fused
+    kc2, vc2, o2 = kc0.clone(), vc0.clone(), torch.empty(nq * hd, device=dev)
+    check(L.bramha_cuda_op_rope_attention(c, q.data_ptr(), k.data_ptr(), v.data_ptr(), bq.data_ptr(), bk.data_ptr(),
+                                          bv.data_ptr(), nq, nkv, hd, 1e6, p.data_ptr(), ctx_len, kc2.data_ptr(),
+                                          vc2.data_ptr(), o2.data_ptr(), None))
+    plane.stream_sync()
+    assert torch.equal(o1, o2)
+    assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
+    # against the oracle's restatement
+    qn = (q + bq).cpu().numpy().copy()
+    kn = (k + bk).cpu().numpy().copy()
+    oracle.rope_(qn, pos, nq, hd, 1e6)
+    oracle.rope_(kn, pos, nkv, hd, 1e6)
+    kcache = kc0.cpu().numpy()[:pos + 1].copy()
+    vcache = vc0.cpu().numpy()[:pos + 1].copy()
+    kcache[pos], vcache[pos] = kn, (v + bv).cpu().numpy()
+    ref = oracle.attention(qn, kcache, vcache, pos + 1, nq, nkv, hd)
+    assert normwise_err(o2.cpu().numpy(), ref) <= 1e-5

@@ -74,9 +74,17 @@ def test_packers_bit_exact(plane, fmt, n, k):
 
 
 # ------------------------------------------------------------------- GEMV parity
+@pytest.fixture(params=["tensor_core", "cuda_core"])
+def kernel(request, plane):
+    """Batch-1 GEMVs of the quantized formats on each of the two kernels."""
+    plane.set_gemv_kernel(request.param)
+    yield request.param
+    plane.set_gemv_kernel("auto")
+
+
 @pytest.mark.parametrize("fmt", ["w4zp8", "log4", "w8", "f32"])
 @pytest.mark.parametrize("name", list(QWEN05))
-def test_gemv_qwen05_linears(plane, fmt, name):
+def test_gemv_qwen05_linears(plane, kernel, fmt, name):
     n, k = QWEN05[name]
     _, q, s = make_weight(fmt, n, k, seed=sum(map(ord, name)))
     x = make_x(1, k, seed=11)
@@ -89,12 +97,26 @@ def test_gemv_qwen05_linears(plane, fmt, name):
 
 @pytest.mark.parametrize("fmt", ["log4", "w4zp8", "w8"])
 @pytest.mark.parametrize("name", ["q", "k", "o", "down"])
-def test_gemv_qwen7_linears(plane, fmt, name):
+def test_gemv_qwen7_linears(plane, kernel, fmt, name):
     n, k = QWEN7[name]
     _, q, s = make_weight(fmt, n, k, seed=7)
     x = make_x(1, k, seed=12)
     w = plane.register(f"qwen7:{name}:{fmt}", fmt, n, k, q, s)
     y = run_gemv(plane, w, x)
+    assert normwise_err(y, oracle_gemv(fmt, x, q, s, n)) <= GEMV_TOL
+    plane.evict(w.key)
+
+
+@pytest.mark.parametrize("fmt", ["log4", "w4zp8", "w8"])
+@pytest.mark.parametrize("n,k", [(1, 2), (7, 16), (129, 24), (33, 130), (5, 1000), (300, 34), (2, 18946),
+                                 (20000, 4864)])
+def test_gemv_ragged_batch1(plane, kernel, fmt, n, k):
+    """Ragged rows, columns and blocks at batch 1 on both kernels; (20000, 4864)
+    gives the CUDA-core kernel K ranges longer than its register chunk."""
+    _, q, s = make_weight(fmt, n, k, seed=n * 17 + k)
+    x = make_x(1, k, seed=n + 3 * k)
+    w = plane.register(f"ragged1:{fmt}:{n}x{k}", fmt, n, k, q, s)
+    y = plane.gemv(w, x)
     assert normwise_err(y, oracle_gemv(fmt, x, q, s, n)) <= GEMV_TOL
     plane.evict(w.key)
 
@@ -137,7 +159,7 @@ def test_odd_k_ignores_last_column_like_reference(plane):
         assert normwise_err(y, oracle_gemv(fmt, x, q, s, n)) <= GEMV_TOL
 
 
-def test_fused_multi_weight_launch_matches_separate(plane):
+def test_fused_multi_weight_launch_matches_separate(plane, kernel):
     k = 896
     x = make_x(1, k, seed=21)
     ws, refs = [], []
