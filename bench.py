@@ -286,6 +286,118 @@ def prefill_bench(plane, dev, reps=10, m=2048):
     return out
 
 
+# ------------------------------------------------------------------ 2:4 sparse GEMV
+SP_VB = {"f32": 8, "w8": 2, "w4zp8": 1}  # device bytes of one group's kept pair
+
+
+def sp24_bytes(fmt, n, k):
+    """Algorithmic bytes of one 2:4 GEMV launch: kept code pairs + 4-bit column
+    pairs of the K/4 groups, the row scales, x and y."""
+    g = k // 4
+    return n * g * SP_VB[fmt] + n * g // 2 + 4 * n + 4 * k + 4 * n
+
+
+def sparse24_bench(plane, dev, layers=4, reps=5):
+    """2:4 structured-sparse GEMV (sparse_matvec_mul_2_4_tensor_into /
+    sparse_matvec_2_4_compressed) on the Qwen2-7B MLP shapes: gate and up
+    (18944 x 3584) and down (3584 x 18944) of `layers` layers, weights ~N(0,0.02)
+    quantized on the device (f32, w8, w4zp8) and registered as 2:4.  One pass =
+    the 3*layers launches (more bytes than the 126 MB L2 in every format),
+    captured in a CUDA graph and replayed `reps` times between CUDA events;
+    the dense GEMV of the same codes is timed the same way for comparison.
+    The CPU figure is the oracle's restatement (OpenMP over rows, all host
+    threads) on one gate matrix."""
+    import torch
+    import oracle
+    hbm, kind = load_peaks()
+    shapes = [("gate", I, H), ("up", I, H), ("down", H, I)]
+    out = {"workload": f"qwen2-7b mlp (gate, up, down) x {layers} layers, batch 1",
+           "peak_gbs": hbm, "peak_source": f"{kind} hbm_gbs" + (" (MEASURED_PEAKS.json)" if kind == "measured" else
+                                                                    " (6.65 TB/s, MEASURED_PEAKS.json absent)"),
+           "timing": f"CUDA graph of one pass ({3 * layers} launches), {reps} replays, device time",
+           "formats": {}}
+    gen = torch.Generator(device=dev).manual_seed(24)
+    stream = torch.cuda.Stream(device=dev)
+    x_in = {k: torch.randn(k, generator=gen, device=dev) for k in (H, I)}
+    host_sample = None
+    for fmt in ("w4zp8", "w8", "f32"):
+        sp, dense, ys, nbytes, dbytes = [], [], [], 0, 0
+        for l in range(layers):
+            for name, n, k in shapes:
+                wf = torch.randn((n, k), generator=gen, device=dev) * 0.02
+                if fmt == "f32":
+                    qd, sd = wf, None
+                else:
+                    qd = torch.empty(n * k * BITS[fmt] // 8, dtype=torch.uint8, device=dev)
+                    sd = torch.empty(n, dtype=torch.float32, device=dev)
+                    plane.quantize_dev(fmt, wf, qd, sd)
+                    del wf
+                key = f"sp24b:{fmt}:{l}:{name}"
+                sp.append((plane.register_sparse24_dev(key, fmt, n, k, qd, sd), k))
+                dense.append((plane.register_dev(key + ":dense", fmt, n, k, qd, sd), k))
+                ys.append(torch.empty(n, device=dev))
+                nbytes += sp24_bytes(fmt, n, k)
+                dbytes += gemv_bytes(n, k, 1, 32 if fmt == "f32" else BITS[fmt])
+                if fmt == "w4zp8" and l == 0 and name == "gate":
+                    host_sample = (n, k, qd.cpu().numpy(), sd.cpu().numpy())
+                del qd, sd
+        torch.cuda.synchronize()
+
+        def timed(ws_):
+            with torch.cuda.stream(stream):
+                for (w, k), y in zip(ws_, ys):
+                    plane.gemv_dev(w, x_in[k], y)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for (w, k), y in zip(ws_, ys):
+                    plane.gemv_dev(w, x_in[k], y)
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            with torch.cuda.stream(stream):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(reps):
+                    graph.replay()
+                e1.record()
+            torch.cuda.synchronize()
+            plane.stream_sync(stream)
+            del graph
+            return e0.elapsed_time(e1) / reps
+
+        ms = timed(sp)
+        ms_dense = timed(dense)
+        per_launch_us = ms * 1e3 / len(sp)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out["formats"][fmt] = {
+            "us_per_pass": round(ms * 1e3, 1), "us_per_launch": round(per_launch_us, 2),
+            "bytes_per_pass": nbytes, "achieved_gbs": round(gbs, 1), "frac": round(gbs / hbm, 4),
+            "dense_us_per_pass": round(ms_dense * 1e3, 1), "dense_bytes_per_pass": dbytes,
+            "speedup_vs_dense": round(ms_dense / ms, 3)}
+        for (w, _), (d, _) in zip(sp, dense):
+            plane.evict(w.key)
+            plane.evict(d.key)
+        del sp, dense, ys
+    if host_sample is not None:
+        n, k, q, s = host_sample
+        x = np.random.Generator(np.random.PCG64(3)).standard_normal(k, dtype=np.float32)
+        threads = oracle.max_threads()
+        oracle.sparse_matvec_2_4("w4zp8", x, q, s, n, threads=threads)
+        reps_c, t0 = 0, time.perf_counter()
+        while reps_c < 3 or time.perf_counter() - t0 < 4.0:
+            oracle.sparse_matvec_2_4("w4zp8", x, q, s, n, threads=threads)
+            reps_c += 1
+        dt = (time.perf_counter() - t0) / reps_c
+        gpu_us = out["formats"]["w4zp8"]["us_per_launch"]
+        out["cpu_baseline"] = {"us_per_launch": round(dt * 1e6, 1), "cores": threads, "kind": "port",
+                               "sample": f"one w4zp8 gate matrix ({n} x {k}) x {reps_c} reps: C restatement of "
+                                         "sparse_matvec_mul_2_4_tensor_into (cpu_engine.rs:1532-1640), "
+                                         "OpenMP over rows",
+                               "gpu_over_cpu": round(dt * 1e6 / gpu_us, 1)}
+    return out
+
+
 # ------------------------------------------------------------------ decode step (config 2)
 def decode_step_bench(plane, dev, prompt_len=512, new_tokens=128):
     """a full Qwen2-0.5B-architecture decode step (24 layers,
@@ -588,6 +700,9 @@ def run_ours(args, ws, rank, local):
     decode_step = None
     if rank == 0 and ws == 1 and not args.no_decode_step:
         decode_step = decode_step_bench(plane, dev)
+    sparse24 = None
+    if rank == 0 and ws == 1 and not args.no_sparse:
+        sparse24 = sparse24_bench(plane, dev, layers=args.sparse_layers)
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -623,6 +738,7 @@ def run_ours(args, ws, rank, local):
             "cpu_baseline": cpu,
             "prefill": prefill,
             "decode_step": decode_step,
+            "sparse24": sparse24,
             "setup_s": round(setup_s, 1),
         }
         print(json.dumps(line), flush=True)
@@ -647,7 +763,19 @@ def main():
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the config-3 prefill GEMM measurement (profiling case) and print its JSON")
     ap.add_argument("--prefill-m", type=int, default=2048, help="tokens of the prefill GEMM measurement")
+    ap.add_argument("--no-sparse", action="store_true", help="skip the 2:4 sparse GEMV measurement")
+    ap.add_argument("--sparse-only", action="store_true",
+                    help="run only the 2:4 sparse GEMV measurement (profiling case) and print its JSON")
+    ap.add_argument("--sparse-layers", type=int, default=4, help="layers of the 2:4 measurement")
     args = ap.parse_args()
+    if args.sparse_only:
+        import torch
+        from bramha_b200 import CudaComputePlane
+        torch.cuda.set_device(0)
+        plane = CudaComputePlane(0)
+        print(json.dumps({"sparse24": sparse24_bench(plane, torch.device("cuda", 0), layers=args.sparse_layers)}))
+        plane.close()
+        return
     if args.prefill_only:
         import torch
         from bramha_b200 import CudaComputePlane

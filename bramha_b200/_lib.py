@@ -14,7 +14,7 @@ ROOT = os.path.dirname(HERE)
 LIB_PATH = os.path.join(HERE, "libbramha_cuda.so")
 HEADER = os.path.join(ROOT, "include", "bramha_cuda.h")
 
-FMT = {"f32": 0, "w8": 1, "w4zp8": 2, "log4": 3}
+FMT = {"f32": 0, "w8": 1, "w4zp8": 2, "log4": 3, "sp24_f32": 4, "sp24_w8": 5, "sp24_w4zp8": 6}
 DTYPE = {"f32": 0, "bf16": 1}
 STATUS = {
     0: "BRAMHA_OK", -1: "BRAMHA_ERR_INVALID", -2: "BRAMHA_ERR_SIZE", -3: "BRAMHA_ERR_CUDA",
@@ -57,6 +57,16 @@ _SIGNATURES = {
     "bramha_cuda_gemv_dev": [_vp, _vp, _vp, _i64, _vp, _vp],
     "bramha_cuda_gemv_multi_dev": [_vp, _int, _pp, _vp, _i64, _pp, _vp],
     "bramha_cuda_matvec": [_vp, _int, _vp, _i64, _vp, _sz, _vp, _sz, _i64, ctypes.c_char_p, ctypes.c_char_p, _vp],
+    "bramha_cuda_register_sparse24": [_vp, ctypes.c_char_p, _int, _i64, _i64, _vp, _sz, _vp, _sz,
+                                      ctypes.POINTER(_vp)],
+    "bramha_cuda_register_sparse24_dev": [_vp, ctypes.c_char_p, _int, _i64, _i64, _vp, _sz, _vp, _sz, _vp,
+                                          ctypes.POINTER(_vp)],
+    "bramha_cuda_register_sparse24_compressed": [_vp, ctypes.c_char_p, _i64, _i64, _vp, _sz, _vp, _sz,
+                                                 ctypes.POINTER(_vp)],
+    "bramha_cuda_sparse_matvec_2_4": [_vp, _int, _vp, _i64, _vp, _sz, _vp, _sz, _i64, ctypes.c_char_p,
+                                      ctypes.c_char_p, _vp],
+    "bramha_cuda_sparse_matvec_2_4_compressed": [_vp, _vp, _i64, _vp, _sz, _vp, _sz, _i64, ctypes.c_char_p,
+                                                 ctypes.c_char_p, _vp],
     "bramha_cuda_gemm": [_vp, _vp, _vp, _i64, _vp],
     "bramha_cuda_gemm_dev": [_vp, _vp, _vp, _int, _i64, _vp, _vp],
     "bramha_cuda_quantize_dev": [_vp, _int, _i64, _i64, _vp, _vp, _vp, _vp],

@@ -37,6 +37,7 @@ struct bramha_weight {
     bool keyed = false;
     bramha_ctx* ctx = nullptr;
     std::list<std::string>::iterator lru_it;
+    Sp24Weight sp{};  // 2:4 sparse layout inside q (is_sp24(fmt))
 };
 
 struct bramha_ctx {
@@ -102,6 +103,9 @@ const char* fmt_name(int fmt) {
         case BRAMHA_FMT_W8: return "INT8";
         case BRAMHA_FMT_W4ZP8: return "INT4";
         case BRAMHA_FMT_LOG4: return "LOG4";
+        case BRAMHA_FMT_SP24_F32: return "2:4 F32";
+        case BRAMHA_FMT_SP24_W8: return "2:4 INT8";
+        case BRAMHA_FMT_SP24_W4ZP8: return "2:4 INT4";
         default: return "?";
     }
 }
@@ -207,14 +211,13 @@ int upload(bramha_ctx* ctx, bramha_weight* w, const void* q, const float* scales
     return BRAMHA_OK;
 }
 
-int register_impl(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K, const void* q,
-                  size_t q_bytes, const float* scales, size_t n_scales, bool from_device, cudaStream_t st,
+// Registry insert shared by every registration path: returns the cached
+// weight for a known key (same shape and format required), otherwise evicts
+// down to the cap, creates the weight and lets `fill` allocate and upload it
+// (fill sets w->bytes and frees what it allocated on failure).
+template <class Fill>
+int register_with(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K, size_t need, Fill&& fill,
                   bramha_weight** out) {
-    if (!ctx || !out) return fail(BRAMHA_ERR_INVALID, "null context or output pointer");
-    if (!key) return fail(BRAMHA_ERR_INVALID, "null weight key");
-    int rc = check_sizes(fmt, N, K, q_bytes, n_scales, scales != nullptr);
-    if (rc) return rc;
-    if (!q && q_bytes > 0) return fail(BRAMHA_ERR_INVALID, "weight pointer is NULL");
     DeviceGuard g(ctx->device);
     std::lock_guard<std::mutex> lk(ctx->mu);
     auto it = ctx->reg.find(key);
@@ -226,9 +229,6 @@ int register_impl(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t 
         *out = w;
         return BRAMHA_OK;
     }
-    const size_t need = (is_tiled(fmt) ? (size_t)tiled_bytes(fmt, N, held_columns(fmt, K))
-                                       : (size_t)N * (size_t)pitch_of(row_bytes_of(fmt, K))) +
-                        (fmt == BRAMHA_FMT_F32 ? 0 : (size_t)N * sizeof(float));
     // enforce_limits (wgpu_backend.rs:65-81): evict least recently used first.
     while (ctx->cap > 0 && ctx->used + need > ctx->cap && !ctx->lru.empty()) evict_locked(ctx, ctx->lru.front());
     bramha_weight* w = new (std::nothrow) bramha_weight();
@@ -239,7 +239,7 @@ int register_impl(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t 
     w->K = K;
     w->keyed = true;
     w->ctx = ctx;
-    rc = upload(ctx, w, q, scales, from_device, st ? st : ctx->stream);
+    int rc = fill(w);
     if (rc) {
         delete w;
         return rc;
@@ -249,6 +249,183 @@ int register_impl(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t 
     w->lru_it = std::prev(ctx->lru.end());
     ctx->reg.emplace(w->key, w);
     *out = w;
+    return BRAMHA_OK;
+}
+
+int register_impl(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K, const void* q,
+                  size_t q_bytes, const float* scales, size_t n_scales, bool from_device, cudaStream_t st,
+                  bramha_weight** out) {
+    if (!ctx || !out) return fail(BRAMHA_ERR_INVALID, "null context or output pointer");
+    if (!key) return fail(BRAMHA_ERR_INVALID, "null weight key");
+    int rc = check_sizes(fmt, N, K, q_bytes, n_scales, scales != nullptr);
+    if (rc) return rc;
+    if (!q && q_bytes > 0) return fail(BRAMHA_ERR_INVALID, "weight pointer is NULL");
+    const size_t need = (is_tiled(fmt) ? (size_t)tiled_bytes(fmt, N, held_columns(fmt, K))
+                                       : (size_t)N * (size_t)pitch_of(row_bytes_of(fmt, K))) +
+                        (fmt == BRAMHA_FMT_F32 ? 0 : (size_t)N * sizeof(float));
+    return register_with(
+        ctx, key, fmt, N, K, need,
+        [&](bramha_weight* w) { return upload(ctx, w, q, scales, from_device, st ? st : ctx->stream); }, out);
+}
+
+// ---- 2:4 sparse weights ---------------------------------------------------
+
+// Device bytes of a 2:4 weight: code pairs, column pairs, tail, scales.
+size_t sp24_bytes(int base_fmt, int64_t N, int64_t K, size_t* idx_off, size_t* tail_off) {
+    const int64_t cp = sp24_groups_padded(K);
+    const size_t v = (size_t)N * (size_t)(cp * sp24_value_bytes(base_fmt));
+    const size_t i = (size_t)N * (size_t)(cp / 8) * 4;
+    const size_t t = (K % 4) ? (size_t)N * 4 * sizeof(float) : 0;
+    if (idx_off) *idx_off = v;
+    if (tail_off) *tail_off = v + i;
+    return v + i + t + (size_t)N * sizeof(float);
+}
+
+// Allocates the 2:4 layout of w (w->fmt, N, K set) and fills in w->sp.
+int sp24_alloc(bramha_weight* w, bool with_tail) {
+    const int base = sp24_base(w->fmt);
+    size_t idx_off = 0, tail_off = 0;
+    const size_t total = sp24_bytes(base, w->N, w->K, &idx_off, &tail_off);
+    const size_t qbytes = total - (size_t)w->N * sizeof(float);
+    w->bytes = total;
+    if (qbytes > 0) CK(cudaMalloc(&w->q, qbytes), "cudaMalloc(2:4 weight)");
+    if (w->N > 0) {
+        cudaError_t e = cudaMalloc(&w->scales, (size_t)w->N * sizeof(float));
+        if (e != cudaSuccess) {
+            free_weight_memory(w);
+            return cuda_fail(e, "cudaMalloc(scales)");
+        }
+    }
+    Sp24Weight& sp = w->sp;
+    sp.N = w->N;
+    sp.K = w->K;
+    sp.Cp = sp24_groups_padded(w->K);
+    sp.ldv = sp.Cp * sp24_value_bytes(base);
+    sp.ldi = sp.Cp / 8;
+    sp.vals = w->q;
+    sp.idx = reinterpret_cast<uint32_t*>(w->q + idx_off);
+    sp.tail = (with_tail && (w->K % 4)) ? reinterpret_cast<float*>(w->q + tail_off) : nullptr;
+    sp.scales = w->scales;
+    return BRAMHA_OK;
+}
+
+// The on-the-fly selection of sparse_matvec_mul_2_4_tensor_into
+// (cpu_engine.rs:1532-1640), made once: uploads the reference-layout weight
+// to a staging buffer and prunes it on the device.
+int sp24_fill_pruned(bramha_weight* w, const void* q, const float* scales, bool from_device,
+                     cudaStream_t st) {
+    int rc = sp24_alloc(w, true);
+    if (rc) return rc;
+    const int base = sp24_base(w->fmt);
+    const int64_t rb = row_bytes_of(base, w->K);
+    const size_t raw = (size_t)w->N * (size_t)rb;
+    const cudaMemcpyKind kind = from_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    cudaError_t e = cudaSuccess;
+    uint8_t* staging = nullptr;
+    const uint8_t* src = static_cast<const uint8_t*>(q);
+    if (!from_device && raw > 0) {
+        e = cudaMalloc(&staging, raw);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(staging, q, raw, cudaMemcpyHostToDevice, st);
+        src = staging;
+    }
+    if (e == cudaSuccess && raw > 0) e = launch_sp24_prune(base, src, rb, w->sp, st);
+    if (e == cudaSuccess && w->N > 0) {
+        if (base == BRAMHA_FMT_F32) {  // the reference's f32 arm has no scale
+            std::vector<float> ones((size_t)w->N, 1.0f);
+            e = cudaMemcpyAsync(w->scales, ones.data(), ones.size() * sizeof(float), cudaMemcpyHostToDevice, st);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        } else {
+            e = cudaMemcpyAsync(w->scales, scales, (size_t)w->N * sizeof(float), kind, st);
+        }
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (staging) cudaFree(staging);
+    if (e != cudaSuccess) {
+        free_weight_memory(w);
+        return cuda_fail(e, "2:4 weight upload");
+    }
+    return BRAMHA_OK;
+}
+
+int sp24_check_pruned(int fmt, int64_t N, int64_t K, size_t q_bytes, size_t n_scales, bool scales_given) {
+    if (fmt != BRAMHA_FMT_F32 && fmt != BRAMHA_FMT_W8 && fmt != BRAMHA_FMT_W4ZP8)
+        return fail(BRAMHA_ERR_INVALID, "2:4 selection takes F32, W8 or W4ZP8 weights, not format %d", fmt);
+    int rc = check_sizes(fmt, N, K, q_bytes, n_scales, scales_given);
+    if (rc) return rc;
+    // The reference's int4 arm reads byte (c + 2) / 2 of a K/2-byte row and
+    // panics for odd K (cpu_engine.rs:1604-1633).
+    if (fmt == BRAMHA_FMT_W4ZP8 && (K % 2) != 0)
+        return fail(BRAMHA_ERR_UNSUPPORTED, "2:4 INT4 selection needs an even in_features (got %lld)", (long long)K);
+    if (K > (int64_t)1 << 30 || N > 0x7fffffffLL) return fail(BRAMHA_ERR_UNSUPPORTED, "2:4 weight too large");
+    return BRAMHA_OK;
+}
+
+// sparse_matvec_2_4_compressed (spanda-engine/src/sparse.rs:100-138) reads,
+// for row r, masks[r*C + c] (C = cols / 4, low 4 bits, ascending bit order)
+// and consumes values from index 2*r*C onwards while any remain.  The walk is
+// restated here once and each group's (column, value) pairs are stored in
+// the 2:4 layout, in the order the reference consumes them.  A group that
+// consumes more than two values is not 2:4 and is refused.
+int sp24_canonicalise(int64_t rows, int64_t cols, const uint16_t* masks, const float* values, size_t n_values,
+                      std::vector<uint8_t>& vals, std::vector<uint32_t>& idx) {
+    const int64_t C = cols / 4, cp = sp24_groups_padded(cols);
+    vals.assign((size_t)(rows * cp * 8), 0);
+    idx.assign((size_t)(rows * (cp / 8)), 0);
+    for (int64_t r = 0; r < rows; ++r) {
+        size_t vi = (size_t)(r * C * 2);
+        for (int64_t c = 0; c < C; ++c) {
+            const unsigned m = masks[r * C + c] & 0xFu;
+            int n = 0, col[2] = {0, 1};
+            float val[2] = {0.f, 0.f};
+            for (int bit = 0; bit < 4; ++bit) {
+                if (!(m & (1u << bit)) || vi >= n_values) continue;
+                if (n == 2)
+                    return fail(BRAMHA_ERR_UNSUPPORTED,
+                                "2:4 mask of row %lld group %lld keeps more than two of four columns (mask 0x%x)",
+                                (long long)r, (long long)c, masks[r * C + c]);
+                col[n] = bit;
+                val[n] = values[vi++];
+                ++n;
+            }
+            if (n == 1) col[1] = col[0] == 0 ? 1 : 0;  // an empty slot: value 0, any other column
+            memcpy(&vals[(size_t)((r * cp + c) * 8)], val, 8);
+            idx[(size_t)(r * (cp / 8) + c / 8)] |= (uint32_t)(col[0] | (col[1] << 2)) << (4 * (c % 8));
+        }
+        for (int64_t c = C; c < cp; ++c)  // padding groups: zero values at columns (0, 1)
+            idx[(size_t)(r * (cp / 8) + c / 8)] |= 0x4u << (4 * (c % 8));
+    }
+    return BRAMHA_OK;
+}
+
+int sp24_fill_compressed(bramha_weight* w, const std::vector<uint8_t>& vals, const std::vector<uint32_t>& idx,
+                         cudaStream_t st) {
+    int rc = sp24_alloc(w, false);
+    if (rc) return rc;
+    cudaError_t e = cudaSuccess;
+    if (!vals.empty()) e = cudaMemcpyAsync(w->sp.vals, vals.data(), vals.size(), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess && !idx.empty())
+        e = cudaMemcpyAsync(w->sp.idx, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice, st);
+    std::vector<float> ones((size_t)w->N, 1.0f);
+    if (e == cudaSuccess && w->N > 0)
+        e = cudaMemcpyAsync(w->scales, ones.data(), ones.size() * sizeof(float), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        free_weight_memory(w);
+        return cuda_fail(e, "2:4 weight upload");
+    }
+    return BRAMHA_OK;
+}
+
+int sp24_check_compressed(int64_t rows, int64_t cols, size_t n_masks, const uint16_t* masks, const float* values,
+                          size_t n_values) {
+    if (rows < 0 || cols < 0) return fail(BRAMHA_ERR_INVALID, "negative shape");
+    if (cols > (int64_t)1 << 30 || rows > 0x7fffffffLL) return fail(BRAMHA_ERR_UNSUPPORTED, "2:4 weight too large");
+    // masks[r * C + c] must exist for every row (the reference would panic).
+    if ((uint64_t)n_masks < (uint64_t)rows * (uint64_t)(cols / 4))
+        return fail(BRAMHA_ERR_SIZE, "2:4 masks length is %zu, expected %lld x (%lld / 4) = %lld", n_masks,
+                    (long long)rows, (long long)cols, (long long)(rows * (cols / 4)));
+    if ((!masks && n_masks > 0) || (!values && n_values > 0))
+        return fail(BRAMHA_ERR_INVALID, "null masks or values pointer");
     return BRAMHA_OK;
 }
 
@@ -273,6 +450,14 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
         return BRAMHA_OK;
     }
     if (K > 0x7fffffffLL) return fail(BRAMHA_ERR_UNSUPPORTED, "K too large");
+    if (is_sp24(fmt)) {  // one launch per weight and activation row
+        for (int i = 0; i < n; ++i)
+            for (int64_t b = 0; b < batch; ++b)
+                CK(launch_sp24_gemv(sp24_base(fmt), ws[i]->sp, x + b * ldx, ys[i] + b * ws[i]->N, ctx->split_ws,
+                                    kSplitWsFloats, ctx->split_tickets, kSplitTickets, ctx->num_sms, st),
+                   "2:4 gemv launch");
+        return BRAMHA_OK;
+    }
     for (int64_t b0 = 0; b0 < batch; b0 += kMaxGemvBatch) {
         const int bc = (int)((batch - b0) < kMaxGemvBatch ? (batch - b0) : kMaxGemvBatch);
         GemvArgs a{};
@@ -340,8 +525,8 @@ int gemm_device(bramha_ctx* ctx, const bramha_weight* w, const void* x, int x_is
         CK(cudaMemsetAsync(y, 0, sizeof(float) * w->N * M, st), "memset(y)");
         return BRAMHA_OK;
     }
-    if (w->fmt == BRAMHA_FMT_F32) {
-        if (!x_is_f32) return fail(BRAMHA_ERR_UNSUPPORTED, "f32 weights take f32 activations");
+    if (w->fmt == BRAMHA_FMT_F32 || is_sp24(w->fmt)) {
+        if (!x_is_f32) return fail(BRAMHA_ERR_UNSUPPORTED, "%s weights take f32 activations", fmt_name(w->fmt));
         const bramha_weight* ws[1] = {w};
         float* ys[1] = {y};
         return gemv_device(ctx, 1, ws, static_cast<const float*>(x), ldx, M, ys, st);
@@ -626,6 +811,140 @@ int bramha_cuda_matvec(bramha_ctx* ctx, int fmt, const float* h, int64_t K, cons
     return rc;
 }
 
+// ---- 2:4 structured-sparse GEMV --------------------------------------------
+namespace {
+int register_sparse24_impl(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K, const void* q,
+                           size_t q_bytes, const float* scales, size_t n_scales, bool from_device, cudaStream_t st,
+                           bramha_weight** out) {
+    if (!ctx || !out) return fail(BRAMHA_ERR_INVALID, "null context or output pointer");
+    if (!key) return fail(BRAMHA_ERR_INVALID, "null weight key");
+    int rc = sp24_check_pruned(fmt, N, K, q_bytes, n_scales, scales != nullptr);
+    if (rc) return rc;
+    if (!q && q_bytes > 0) return fail(BRAMHA_ERR_INVALID, "weight pointer is NULL");
+    const int sfmt = fmt - BRAMHA_FMT_F32 + BRAMHA_FMT_SP24_F32;
+    return register_with(
+        ctx, key, sfmt, N, K, sp24_bytes(fmt, N, K, nullptr, nullptr),
+        [&](bramha_weight* w) { return sp24_fill_pruned(w, q, scales, from_device, st ? st : ctx->stream); }, out);
+}
+
+int register_sparse24_compressed_impl(bramha_ctx* ctx, const char* key, int64_t rows, int64_t cols,
+                                      const uint16_t* masks, size_t n_masks, const float* values, size_t n_values,
+                                      bramha_weight** out) {
+    if (!ctx || !out) return fail(BRAMHA_ERR_INVALID, "null context or output pointer");
+    if (!key) return fail(BRAMHA_ERR_INVALID, "null weight key");
+    int rc = sp24_check_compressed(rows, cols, n_masks, masks, values, n_values);
+    if (rc) return rc;
+    {  // a cached key skips the host walk
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        auto it = ctx->reg.find(key);
+        if (it != ctx->reg.end()) {
+            bramha_weight* w = it->second;
+            if (w->fmt != BRAMHA_FMT_SP24_F32 || w->N != rows || w->K != cols)
+                return fail(BRAMHA_ERR_SIZE, "key '%s' is registered with a different shape or format", key);
+            touch_locked(ctx, w);
+            *out = w;
+            return BRAMHA_OK;
+        }
+    }
+    std::vector<uint8_t> vals;
+    std::vector<uint32_t> idx;
+    rc = sp24_canonicalise(rows, cols, masks, values, n_values, vals, idx);
+    if (rc) return rc;
+    return register_with(
+        ctx, key, BRAMHA_FMT_SP24_F32, rows, cols, sp24_bytes(BRAMHA_FMT_F32, rows, cols, nullptr, nullptr),
+        [&](bramha_weight* w) { return sp24_fill_compressed(w, vals, idx, ctx->stream); }, out);
+}
+}  // namespace
+
+int bramha_cuda_register_sparse24(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K, const void* q,
+                                  size_t q_bytes, const float* scales, size_t n_scales, bramha_weight** out) {
+    return register_sparse24_impl(ctx, key, fmt, N, K, q, q_bytes, scales, n_scales, false, nullptr, out);
+}
+
+int bramha_cuda_register_sparse24_dev(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K,
+                                      const void* q_dev, size_t q_bytes, const float* scales_dev, size_t n_scales,
+                                      void* stream, bramha_weight** out) {
+    return register_sparse24_impl(ctx, key, fmt, N, K, q_dev, q_bytes, scales_dev, n_scales, true,
+                                  static_cast<cudaStream_t>(stream), out);
+}
+
+int bramha_cuda_register_sparse24_compressed(bramha_ctx* ctx, const char* key, int64_t rows, int64_t cols,
+                                             const uint16_t* masks, size_t n_masks, const float* values,
+                                             size_t n_values, bramha_weight** out) {
+    return register_sparse24_compressed_impl(ctx, key, rows, cols, masks, n_masks, values, n_values, out);
+}
+
+int bramha_cuda_sparse_matvec_2_4(bramha_ctx* ctx, int fmt, const float* h, int64_t K, const void* q_weight,
+                                  size_t q_bytes, const float* scales, size_t n_scales, int64_t N,
+                                  const char* model_name, const char* layer_name, float* out) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (N < 0 || K < 0) return fail(BRAMHA_ERR_INVALID, "negative shape");
+    if (N > 0 && !out) return fail(BRAMHA_ERR_INVALID, "null output pointer");
+    if (K == 0 || N == 0) {
+        if (N > 0) memset(out, 0, sizeof(float) * (size_t)N);
+        return BRAMHA_OK;
+    }
+    int rc = sp24_check_pruned(fmt, N, K, q_bytes, n_scales, scales != nullptr);
+    if (rc) return rc;
+    if (model_name && layer_name) {
+        std::string key = std::string(model_name) + ":" + layer_name;
+        bramha_weight* w = nullptr;
+        rc = register_sparse24_impl(ctx, key.c_str(), fmt, N, K, q_weight, q_bytes, scales, n_scales, false, nullptr,
+                                    &w);
+        if (rc) return rc;
+        return gemv_host(ctx, w, h, 1, out);
+    }
+    DeviceGuard g(ctx->device);
+    bramha_weight tmp;
+    tmp.fmt = fmt - BRAMHA_FMT_F32 + BRAMHA_FMT_SP24_F32;
+    tmp.N = N;
+    tmp.K = K;
+    tmp.ctx = ctx;
+    tmp.key = "<temporary>";
+    rc = sp24_fill_pruned(&tmp, q_weight, scales, false, ctx->stream);
+    if (rc) return rc;
+    rc = gemv_host(ctx, &tmp, h, 1, out);
+    free_weight_memory(&tmp);
+    return rc;
+}
+
+int bramha_cuda_sparse_matvec_2_4_compressed(bramha_ctx* ctx, const float* x, int64_t cols, const uint16_t* masks,
+                                             size_t n_masks, const float* values, size_t n_values, int64_t rows,
+                                             const char* model_name, const char* layer_name, float* out) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (rows < 0 || cols < 0) return fail(BRAMHA_ERR_INVALID, "negative shape");
+    if (rows > 0 && !out) return fail(BRAMHA_ERR_INVALID, "null output pointer");
+    if (rows == 0 || cols < 4) {  // no whole group: every output is 0 (sparse.rs:107-135)
+        if (rows > 0) memset(out, 0, sizeof(float) * (size_t)rows);
+        return BRAMHA_OK;
+    }
+    int rc = sp24_check_compressed(rows, cols, n_masks, masks, values, n_values);
+    if (rc) return rc;
+    if (model_name && layer_name) {
+        std::string key = std::string(model_name) + ":" + layer_name;
+        bramha_weight* w = nullptr;
+        rc = register_sparse24_compressed_impl(ctx, key.c_str(), rows, cols, masks, n_masks, values, n_values, &w);
+        if (rc) return rc;
+        return gemv_host(ctx, w, x, 1, out);
+    }
+    std::vector<uint8_t> vals;
+    std::vector<uint32_t> idx;
+    rc = sp24_canonicalise(rows, cols, masks, values, n_values, vals, idx);
+    if (rc) return rc;
+    DeviceGuard g(ctx->device);
+    bramha_weight tmp;
+    tmp.fmt = BRAMHA_FMT_SP24_F32;
+    tmp.N = rows;
+    tmp.K = cols;
+    tmp.ctx = ctx;
+    tmp.key = "<temporary>";
+    rc = sp24_fill_compressed(&tmp, vals, idx, ctx->stream);
+    if (rc) return rc;
+    rc = gemv_host(ctx, &tmp, x, 1, out);
+    free_weight_memory(&tmp);
+    return rc;
+}
+
 int bramha_cuda_gemm(bramha_ctx* ctx, const bramha_weight* w, const float* h_host, int64_t M, float* out_host) {
     int rc = check_weight(ctx, w);
     if (rc) return rc;
@@ -678,8 +997,8 @@ int bramha_cuda_gemm_noalloc_dev(bramha_ctx* ctx, const bramha_weight* w, const 
                     "gemm_noalloc_dev: M = %lld tokens exceeds the fixed scratch of this entry point "
                     "(%lld tokens); split the block or use bramha_cuda_gemm_dev",
                     (long long)M, (long long)kNoAllocMaxTokens);
-    if (w->fmt == BRAMHA_FMT_F32)
-        return fail(BRAMHA_ERR_UNSUPPORTED, "gemm_noalloc_dev: dense f32 weights are not supported");
+    if (w->fmt == BRAMHA_FMT_F32 || is_sp24(w->fmt))
+        return fail(BRAMHA_ERR_UNSUPPORTED, "gemm_noalloc_dev: %s weights are not supported", fmt_name(w->fmt));
     if (M == 0 || w->N == 0) return BRAMHA_OK;
     if (!x_dev || !y_dev) return fail(BRAMHA_ERR_INVALID, "null device pointer");
     const int64_t keff = (w->fmt == BRAMHA_FMT_W4ZP8 || w->fmt == BRAMHA_FMT_LOG4) ? (w->K / 2) * 2 : w->K;

@@ -8,6 +8,8 @@
 //    4-bit words are rearranged (even columns in bits 0-15, odd in 16-31).
 //    Rows past N and columns past K are zero.
 //  * dense f32: row-major, rows padded to a 16-byte pitch.
+//  * 2:4 sparse (BRAMHA_FMT_SP24_*): kept code pairs, 4-bit column pairs and
+//    the K % 4 tail, row-major (sparse24.cu).
 // Scales: f32 [N], one per output row.
 #pragma once
 
@@ -50,6 +52,22 @@ inline bool is_tiled(int fmt) { return tile_slice_bytes(fmt) > 0; }
 inline int64_t held_columns(int fmt, int64_t K) {
     return (fmt == BRAMHA_FMT_W4ZP8 || fmt == BRAMHA_FMT_LOG4) ? (K / 2) * 2 : K;
 }
+
+// 2:4 sparse formats: BRAMHA_FMT_SP24_X keeps the codes of BRAMHA_FMT_X.
+inline bool is_sp24(int fmt) { return fmt >= BRAMHA_FMT_SP24_F32 && fmt <= BRAMHA_FMT_SP24_W4ZP8; }
+inline int sp24_base(int fmt) { return fmt - BRAMHA_FMT_SP24_F32 + BRAMHA_FMT_F32; }
+
+// Device view of a 2:4 sparse weight (layout in sparse24.cu).
+struct Sp24Weight {
+    uint8_t* vals;    // [N][ldv] kept code pairs
+    int64_t ldv;      // bytes per row = Cp * sp24_value_bytes
+    uint32_t* idx;    // [N][ldi] 4-bit column pairs, 8 groups per word
+    int64_t ldi;      // words per row = Cp / 8
+    float* tail;      // [N][4] codes of the K % 4 trailing columns, or null
+    const float* scales;
+    int64_t N, K, Cp; // Cp = groups of 4 columns per row, rounded up to 8
+};
+inline int64_t sp24_groups_padded(int64_t K) { return (K / 4 + 7) / 8 * 8; }
 
 // One weight inside a (possibly fused) GEMV launch.
 struct GemvSeg {
@@ -135,6 +153,14 @@ cudaError_t launch_rope_attention(const float* q, const float* k, const float* v
 cudaError_t launch_silu_mul(const float* g, const float* u, int64_t n, float* out, cudaStream_t stream);
 cudaError_t launch_select(float* logits, int64_t vocab, int32_t* generated, int32_t* count, int64_t max_gen,
                           float penalty, int greedy, int32_t* token, int32_t* pos, cudaStream_t stream);
+
+// 2:4 sparse GEMV of one activation row x (16-byte aligned) into y, and the
+// registration-time selection from a reference-layout weight (sparse24.cu).
+int sp24_value_bytes(int base_fmt);
+cudaError_t launch_sp24_gemv(int base_fmt, const Sp24Weight& w, const float* x, float* y, float* ws,
+                             int64_t ws_floats, int* tickets, int n_tickets, int num_sms, cudaStream_t stream);
+cudaError_t launch_sp24_prune(int base_fmt, const uint8_t* src, int64_t row_bytes, const Sp24Weight& w,
+                              cudaStream_t stream);
 
 // GPU packers (quant.cu).
 cudaError_t launch_quantize(int fmt, int64_t N, int64_t K, const float* w, uint8_t* q, float* scales,

@@ -337,14 +337,19 @@ def write_manifest_dir(path: str, name: str, layers: Dict[str, object], *, archi
 
 
 def register_spanda(plane, path: str) -> Tuple[dict, Dict[str, object]]:
-    """Reads a .spanda file and registers its quantized tensors: Quant4Log ->
-    LOG4, Quant8Linear -> W8, with one scale per output row (N = len(scales));
-    the packed codes give K.  Dense and 2:4 tensors are returned as read."""
+    """Reads a .spanda file and registers its tensors on the device:
+    BlockSparse2_4 with a 2-D shape as a compressed 2:4 weight (rows =
+    shape[0], cols = shape[1], as the SPANDA forward loop reads it,
+    lib.rs:256-266); Quant4Log -> LOG4 and Quant8Linear -> W8 with one scale
+    per output row (N = len(scales), the packed codes give K).  Dense tensors
+    (and 2:4 tensors without a 2-D shape) are returned as read."""
     meta, tensors = read_spanda(path)
     model = meta["name"]
     out = {}
     for name, t in tensors.items():
-        if t.kind in ("log4", "int8"):
+        if t.kind == "sparse24" and len(t.shape) == 2:
+            out[name] = plane.register_sparse24_compressed(f"{model}:{name}", t.shape[0], t.shape[1], t.masks, t.data)
+        elif t.kind in ("log4", "int8"):
             n = int(t.scales.size)
             if n == 0 or t.data.size % n:
                 raise ValueError(f"{name}: {t.data.size} code bytes do not split into {n} rows")

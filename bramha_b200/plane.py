@@ -11,6 +11,12 @@ method, same argument meaning and error behaviour:
 * ``gemm(fmt, h_block, q, scales, block_size, in_features, out_features)``:
   the prefill GEMM that `gemm_cpu` (src/inference/cpu_engine.rs:565) computes
 * ``clear_persistent_buffers()`` (:725)
+* ``sparse_matvec_mul_2_4(x, w, cols)`` / ``sparse_matvec_2_4_compressed(x,
+  masks, nonzero_values, rows, cols)`` (spanda-engine/src/sparse.rs:19, 100)
+  and ``sparse_matvec_mul_2_4_tensor(h, fmt, q, scales, out_features, ...)``
+  (sparse_matvec_mul_2_4_tensor_into, src/inference/cpu_engine.rs:1532): the
+  2:4 structured-sparse GEMVs; ``register_sparse24`` /
+  ``register_sparse24_compressed`` register 2:4 weights for ``gemv``
 
 Where the reference returns ``Err(String)`` this raises :class:`BramhaError`;
 ``Ok(vec![0; N])`` for an empty input or output becomes a zero array.  When both
@@ -110,6 +116,70 @@ class CudaComputePlane:
             q.numel() * q.element_size(), None if scales is None else scales.data_ptr(),
             0 if scales is None else scales.numel(), _stream(stream), ctypes.byref(h)))
         return Weight(self, h.value, key, fmt, out_features, in_features)
+
+    def register_sparse24(self, key: str, fmt: str, out_features: int, in_features: int, q, scales=None) -> Weight:
+        """Registers a dense f32 / w8 / w4zp8 weight as 2:4 (the top two of every
+        group of four columns kept, selected once on the device)."""
+        qa = np.ascontiguousarray(q)
+        sa = None if scales is None else _f32(scales)
+        h = _vp()
+        check(lib().bramha_cuda_register_sparse24(
+            self._ctx, key.encode(), FMT[fmt], out_features, in_features, qa.ctypes.data, qa.nbytes,
+            None if sa is None else sa.ctypes.data, 0 if sa is None else sa.size, ctypes.byref(h)))
+        return Weight(self, h.value, key, "sp24_" + fmt, out_features, in_features)
+
+    def register_sparse24_dev(self, key: str, fmt: str, out_features: int, in_features: int, q, scales=None,
+                              stream=None) -> Weight:
+        h = _vp()
+        check(lib().bramha_cuda_register_sparse24_dev(
+            self._ctx, key.encode(), FMT[fmt], out_features, in_features, q.data_ptr(),
+            q.numel() * q.element_size(), None if scales is None else scales.data_ptr(),
+            0 if scales is None else scales.numel(), _stream(stream), ctypes.byref(h)))
+        return Weight(self, h.value, key, "sp24_" + fmt, out_features, in_features)
+
+    def register_sparse24_compressed(self, key: str, rows: int, cols: int, masks, nonzero_values) -> Weight:
+        """Registers a compressed 2:4 tensor (.spanda BlockSparse2_4: u16 masks
+        per group of four, kept values in column order)."""
+        m = np.ascontiguousarray(masks, dtype=np.uint16)
+        v = _f32(nonzero_values)
+        h = _vp()
+        check(lib().bramha_cuda_register_sparse24_compressed(self._ctx, key.encode(), rows, cols, m.ctypes.data,
+                                                             m.size, v.ctypes.data, v.size, ctypes.byref(h)))
+        return Weight(self, h.value, key, "sp24_f32", rows, cols)
+
+    def sparse_matvec_mul_2_4_tensor(self, h, fmt: str, q_weight, scales, out_features: int, model_name=None,
+                                     layer_name=None) -> np.ndarray:
+        h = _f32(h).reshape(-1)
+        qa = np.ascontiguousarray(q_weight)
+        sa = None if scales is None else _f32(scales)
+        out = np.zeros(out_features, np.float32)
+        check(lib().bramha_cuda_sparse_matvec_2_4(
+            self._ctx, FMT[fmt], h.ctypes.data, h.size, qa.ctypes.data, qa.nbytes,
+            None if sa is None else sa.ctypes.data, 0 if sa is None else sa.size, out_features,
+            None if model_name is None else model_name.encode(),
+            None if layer_name is None else layer_name.encode(), out.ctypes.data))
+        return out
+
+    def sparse_matvec_mul_2_4(self, x, w, cols: int, model_name=None, layer_name=None) -> np.ndarray:
+        """sparse.rs:19: rows = len(w) / cols, f32 weights."""
+        w = _f32(w).reshape(-1)
+        rows = w.size // cols if cols else 0
+        return self.sparse_matvec_mul_2_4_tensor(_f32(x)[:cols], "f32", w[:rows * cols], None, rows, model_name,
+                                                 layer_name)
+
+    def sparse_matvec_2_4_compressed(self, x, masks, nonzero_values, rows: int, cols: int, model_name=None,
+                                     layer_name=None) -> np.ndarray:
+        x = _f32(x).reshape(-1)
+        if x.size < cols:
+            raise BramhaError(-2, f"x has {x.size} elements, expected {cols}")
+        m = np.ascontiguousarray(masks, dtype=np.uint16)
+        v = _f32(nonzero_values)
+        out = np.zeros(rows, np.float32)
+        check(lib().bramha_cuda_sparse_matvec_2_4_compressed(
+            self._ctx, x.ctypes.data, cols, m.ctypes.data, m.size, v.ctypes.data, v.size, rows,
+            None if model_name is None else model_name.encode(),
+            None if layer_name is None else layer_name.encode(), out.ctypes.data))
+        return out
 
     def lookup(self, key: str) -> Weight:
         h = _vp()

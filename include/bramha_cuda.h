@@ -55,7 +55,13 @@ enum bramha_format {
     BRAMHA_FMT_F32 = 0,
     BRAMHA_FMT_W8 = 1,
     BRAMHA_FMT_W4ZP8 = 2,
-    BRAMHA_FMT_LOG4 = 3
+    BRAMHA_FMT_LOG4 = 3,
+    /* 2:4 structured-sparse weights (registered through the sparse24 calls
+     * below, never through bramha_cuda_register_weight): two kept codes of
+     * each group of four columns, of F32, W8 or W4ZP8. */
+    BRAMHA_FMT_SP24_F32 = 4,
+    BRAMHA_FMT_SP24_W8 = 5,
+    BRAMHA_FMT_SP24_W4ZP8 = 6
 };
 
 enum bramha_dtype { BRAMHA_DTYPE_F32 = 0, BRAMHA_DTYPE_BF16 = 1 };
@@ -167,6 +173,61 @@ BRAMHA_API int bramha_cuda_gemv_multi_dev(bramha_ctx* ctx, int n_weights, const 
 BRAMHA_API int bramha_cuda_matvec(bramha_ctx* ctx, int fmt, const float* h, int64_t K, const void* q_weight,
                        size_t q_bytes, const float* scales, size_t n_scales, int64_t N,
                        const char* model_name, const char* layer_name, float* out);
+
+/* ------------------------------------------------- 2:4 structured sparsity */
+
+/* The reference's 2:4 sparse GEMVs (spanda-engine/src/sparse.rs:19-138 and
+ * sparse_matvec_mul_2_4_tensor_into, cpu_engine.rs:1532-1640) keep, in every
+ * group of four consecutive columns of a row, two weights and sum their
+ * products with x.  Registered 2:4 weights (formats BRAMHA_FMT_SP24_*) run
+ * through bramha_cuda_gemv / _gemv_dev / _gemv_multi_dev / _gemm like any
+ * other weight (f32 activations; one launch per activation row), computing
+ *   y[j] = s_j * (sum over groups of the two kept products + the products of
+ *          the K % 4 trailing columns)
+ * in fp32 (s_j = 1 for F32 weights).  Device bytes per group of four
+ * columns: 8.5 (F32), 2.5 (W8), 1.5 (W4ZP8). */
+
+/* Registers a dense F32, W8 or W4ZP8 weight (the layouts and size rules of
+ * bramha_cuda_register_weight; W4ZP8 needs an even K, as the reference's int4
+ * arm panics otherwise) as 2:4: each group of four keeps the two codes of
+ * largest magnitude, ties to the lower column, the selection
+ * sparse_matvec_mul_2_4_tensor_into makes on every call (cpu_engine.rs:
+ * 1539-1552, 1568-1581, 1606-1623) made here once on the device.  The K % 4
+ * trailing columns stay dense (cpu_engine.rs:1558-1561).  Idempotent per key
+ * (a key registered with another format or shape is an error). */
+BRAMHA_API int bramha_cuda_register_sparse24(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K,
+                                             const void* q, size_t q_bytes, const float* scales, size_t n_scales,
+                                             bramha_weight** out);
+BRAMHA_API int bramha_cuda_register_sparse24_dev(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K,
+                                                 const void* q_dev, size_t q_bytes, const float* scales_dev,
+                                                 size_t n_scales, void* stream, bramha_weight** out);
+
+/* Registers a compressed 2:4 tensor (the .spanda BlockSparse2_4 variant,
+ * spanda-engine/src/lib.rs:89-93): masks [rows][cols / 4] u16, low 4 bits =
+ * kept columns of the group; values consumed in column order from index
+ * 2 * r * (cols / 4) for row r while any remain (sparse.rs:109-125).  Columns
+ * past the last whole group are ignored (sparse.rs:128-132).  Fails with
+ * BRAMHA_ERR_SIZE when masks holds fewer than rows * (cols / 4) entries and
+ * BRAMHA_ERR_UNSUPPORTED when a group would consume more than two values. */
+BRAMHA_API int bramha_cuda_register_sparse24_compressed(bramha_ctx* ctx, const char* key, int64_t rows,
+                                                        int64_t cols, const uint16_t* masks, size_t n_masks,
+                                                        const float* values, size_t n_values, bramha_weight** out);
+
+/* sparse_matvec_mul_2_4 (sparse.rs:19, F32) / sparse_matvec_mul_2_4_tensor_into
+ * (cpu_engine.rs:1532; F32, W8, W4ZP8) as a keyed one-shot call with the
+ * conventions of bramha_cuda_matvec: h [K] host, out [N] host, synchronous;
+ * cached under "model:layer" when both names are given. */
+BRAMHA_API int bramha_cuda_sparse_matvec_2_4(bramha_ctx* ctx, int fmt, const float* h, int64_t K,
+                                             const void* q_weight, size_t q_bytes, const float* scales,
+                                             size_t n_scales, int64_t N, const char* model_name,
+                                             const char* layer_name, float* out);
+
+/* sparse_matvec_2_4_compressed (sparse.rs:100): x [cols] host, out [rows]
+ * host, synchronous; cached under "model:layer" when both names are given. */
+BRAMHA_API int bramha_cuda_sparse_matvec_2_4_compressed(bramha_ctx* ctx, const float* x, int64_t cols,
+                                                        const uint16_t* masks, size_t n_masks, const float* values,
+                                                        size_t n_values, int64_t rows, const char* model_name,
+                                                        const char* layer_name, float* out);
 
 /* ------------------------------------------------------- prefill GEMM path */
 

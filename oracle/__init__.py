@@ -8,6 +8,8 @@ reference's CPU arithmetic (akshaybhlrp/bramha):
 * decode GEMV ``matvec_mul_into``: ``src/inference/cpu_engine.rs:1307-1444``
 * allocating GEMV ``matvec_mul``: ``src/inference/cpu_engine.rs:355-562``
 * prefill GEMM ``gemm_cpu``: ``src/inference/cpu_engine.rs:565-706``
+* 2:4 sparse GEMVs and compression: ``spanda-engine/src/sparse.rs:19-138``,
+  ``src/inference/cpu_engine.rs:1532-1640``, ``spanda-engine/src/bin/convert.rs:55-92``
 * decode-step operations (RMSNorm, RoPE, single-token attention, SwiGLU,
   repetition penalty + argmax): ``src/inference/cpu_engine.rs:1292-1302,
   1450-1530, 1682-1698, 2023-2026, 2985-3031``; the step itself is in
@@ -32,6 +34,7 @@ _lib = None
 _f32p = ctypes.POINTER(ctypes.c_float)
 _u8p = ctypes.POINTER(ctypes.c_uint8)
 _i8p = ctypes.POINTER(ctypes.c_int8)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
 _i64 = ctypes.c_int64
 
 
@@ -77,6 +80,10 @@ def lib():
             "bro_silu_mul": (None, [_f32p, _f32p, _i64, _f32p]),
             "bro_penalty_argmax": (ctypes.c_int64, [_f32p, _i64, ctypes.POINTER(ctypes.c_int32), _i64,
                                                     ctypes.c_float]),
+            "bro_sparse_matvec_2_4": (None, [ctypes.c_int, _f32p, _i64, ctypes.c_void_p, _f32p, _i64, _f32p,
+                                             ctypes.c_int]),
+            "bro_sparse_matvec_2_4_compressed": (None, [_f32p, _u16p, _f32p, _i64, _i64, _i64, _f32p, ctypes.c_int]),
+            "bro_compress_2_4": (_i64, [_f32p, _i64, _u16p, _f32p]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -303,3 +310,42 @@ def penalty_argmax(logits, generated, penalty: float = 1.15):
     gen = np.ascontiguousarray(np.asarray(generated, dtype=np.int32))
     return int(lib().bro_penalty_argmax(_p(logits, _f32p), logits.size,
                                         gen.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), gen.size, penalty))
+
+
+# ---- 2:4 structured sparsity (sparse.rs, cpu_engine.rs:1532-1640) ------------
+_SP_FMT = {"f32": 0, "w8": 1, "w4zp8": 2}
+
+
+def sparse_matvec_2_4(fmt: str, h, q, scales, out_features: int, threads: int = 0):
+    """sparse_matvec_mul_2_4_tensor_into: top-2-of-4 products per group, the
+    K % 4 trailing columns densely, times the row scale (i8 / int4)."""
+    h = _c(h, np.float32)
+    qa = np.ascontiguousarray(q)
+    sa = None if scales is None else _c(scales, np.float32)
+    out = np.empty(out_features, np.float32)
+    lib().bro_sparse_matvec_2_4(_SP_FMT[fmt], _p(h, _f32p), h.size, qa.ctypes.data,
+                                None if sa is None else _p(sa, _f32p), out_features, _p(out, _f32p), threads)
+    return out
+
+
+def sparse_matvec_2_4_compressed(x, masks, values, rows: int, cols: int, threads: int = 0):
+    x = _c(x, np.float32)
+    m = _c(masks, np.uint16)
+    v = _c(values, np.float32)
+    assert m.size >= rows * (cols // 4) and x.size >= (cols // 4) * 4
+    out = np.empty(rows, np.float32)
+    lib().bro_sparse_matvec_2_4_compressed(_p(x, _f32p), _p(m, _u16p), _p(v, _f32p), v.size, rows, cols,
+                                           _p(out, _f32p), threads)
+    return out
+
+
+def compress_2_4(w):
+    """convert.rs:55-92 over a flat f32 tensor (length a multiple of 4):
+    (masks u16 [n/4], values f32 [n/2])."""
+    w = _c(w, np.float32).reshape(-1)
+    assert w.size % 4 == 0
+    masks = np.empty(w.size // 4, np.uint16)
+    values = np.empty(w.size // 2, np.float32)
+    nv = lib().bro_compress_2_4(_p(w, _f32p), w.size, _p(masks, _u16p), _p(values, _f32p))
+    assert nv == values.size
+    return masks, values

@@ -522,3 +522,109 @@ BRO_API int64_t bro_penalty_argmax(float* logits, int64_t vocab, const int32_t* 
         }
     return max_idx;
 }
+
+/* ---- 2:4 structured sparsity ------------------------------------------------
+ * The two kept columns of a group of four.  The reference sorts the pairs
+ * (index, |w|) with Rust's stable slice::sort_by under
+ * `b.1.partial_cmp(&a.1).unwrap_or(Equal)` (spanda-engine/src/sparse.rs:35-47,
+ * cpu_engine.rs:1542-1552, bin/convert.rs:65-74); for four elements the
+ * standard library runs insertion sort (insertion_sort_shift_left), in which an
+ * element moves left only past strictly smaller magnitudes.  Restated here
+ * literally: descending magnitude, ties in column order, a NaN never moves. */
+static void top2_of4(const float m[4], int* i1, int* i2) {
+    int o[4] = {0, 1, 2, 3};
+    for (int i = 1; i < 4; ++i) {
+        const int t = o[i];
+        int j = i;
+        while (j > 0 && m[t] > m[o[j - 1]]) {
+            o[j] = o[j - 1];
+            --j;
+        }
+        o[j] = t;
+    }
+    *i1 = o[0];
+    *i2 = o[1];
+}
+
+/* Unscaled code of column c of row `row` for fmt 0 = f32, 1 = i8, 2 = int4
+ * (even column in the high nibble, value nibble - 8). */
+static float sp_code(int fmt, const void* row, int64_t c) {
+    if (fmt == 0) return ((const float*)row)[c];
+    if (fmt == 1) return (float)((const int8_t*)row)[c];
+    const uint8_t b = ((const uint8_t*)row)[c / 2];
+    return (float)((c % 2 == 0) ? ((b >> 4) & 0x0F) : (b & 0x0F)) - 8.0f;
+}
+
+/* sparse_matvec_mul_2_4_tensor_into, cpu_engine.rs:1532-1640 (its f32 arm is
+ * sparse_matvec_mul_2_4, sparse.rs:19-61): per row, the top two products of
+ * every whole group of four (largest magnitude first), then the K % 4
+ * trailing columns densely; times the row scale for i8 / int4.  Rows in
+ * parallel when threads > 1 (the reference's par_iter_mut). */
+BRO_API void bro_sparse_matvec_2_4(int fmt, const float* h, int64_t K, const void* q, const float* scales, int64_t N,
+                                   float* out, int threads) {
+    const int64_t rb = fmt == 0 ? K * 4 : fmt == 1 ? K : K / 2;
+#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1) if (threads > 1)
+    for (int64_t j = 0; j < N; ++j) {
+        const void* row = (const uint8_t*)q + j * rb;
+        float sum = 0.0f;
+        int64_t c = 0;
+        while (c + 4 <= K) {
+            float v[4], m[4];
+            for (int i = 0; i < 4; ++i) {
+                v[i] = sp_code(fmt, row, c + i);
+                m[i] = fabsf(v[i]);
+            }
+            int i1, i2;
+            top2_of4(m, &i1, &i2);
+            sum += v[i1] * h[c + i1];
+            sum += v[i2] * h[c + i2];
+            c += 4;
+        }
+        while (c < K) {
+            sum += sp_code(fmt, row, c) * h[c];
+            ++c;
+        }
+        out[j] = fmt == 0 ? sum : sum * scales[j];
+    }
+}
+
+/* sparse_matvec_2_4_compressed, sparse.rs:100-138: masks [rows][cols/4] (low 4
+ * bits), values consumed in column order from 2*r*(cols/4) while any remain;
+ * columns past the last whole group are ignored. */
+BRO_API void bro_sparse_matvec_2_4_compressed(const float* x, const uint16_t* masks, const float* values,
+                                              int64_t n_values, int64_t rows, int64_t cols, float* out,
+                                              int threads) {
+    const int64_t cpr = cols / 4;
+#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1) if (threads > 1)
+    for (int64_t r = 0; r < rows; ++r) {
+        int64_t vi = r * cpr * 2;
+        float sum = 0.0f;
+        for (int64_t c = 0; c < cpr; ++c) {
+            const uint16_t m = masks[r * cpr + c];
+            for (int bit = 0; bit < 4; ++bit)
+                if ((m & (1u << bit)) && vi < n_values) {
+                    sum += values[vi] * x[c * 4 + bit];
+                    ++vi;
+                }
+        }
+        out[r] = sum;
+    }
+}
+
+/* bin/convert.rs:55-92: 2:4 compression of a flat f32 tensor whose length is a
+ * multiple of 4: per group of four consecutive elements the mask of the top
+ * two and their values in index order.  Returns the number of values (n/2). */
+BRO_API int64_t bro_compress_2_4(const float* w, int64_t n, uint16_t* masks, float* values) {
+    int64_t nv = 0;
+    for (int64_t g = 0; g < n / 4; ++g) {
+        float m[4];
+        for (int i = 0; i < 4; ++i) m[i] = fabsf(w[4 * g + i]);
+        int i1, i2;
+        top2_of4(m, &i1, &i2);
+        const uint16_t mask = (uint16_t)((1u << i1) | (1u << i2));
+        masks[g] = mask;
+        for (int bit = 0; bit < 4; ++bit)
+            if (mask & (1u << bit)) values[nv++] = w[4 * g + bit];
+    }
+    return nv;
+}

@@ -159,6 +159,10 @@ class _FakePlane:
         self.calls.append((key, fmt, n, k, np.array(q), None if s is None else np.array(s)))
         return (key, fmt, n, k)
 
+    def register_sparse24_compressed(self, key, rows, cols, masks, values):
+        self.calls.append((key, "sp24_f32", rows, cols, np.array(masks), np.array(values)))
+        return (key, "sp24_f32", rows, cols)
+
 
 def test_register_manifest_dir_mapping(tmp_path):
     d = str(tmp_path / "m")
@@ -224,13 +228,18 @@ def test_register_spanda_mapping(tmp_path):
     meta = {k: 1 for k in L.META_FIELDS}
     meta.update(name="m", architecture="qwen2")
     p = str(tmp_path / "m.spanda")
+    masks, vals = oracle.compress_2_4(rng(3).normal(0, 1, 16 * 32).astype(np.float32))
     L.write_spanda(p, meta, {"x": L.SpandaTensor("log4", q4, scales=s4),
                              "y": L.SpandaTensor("int8", q8.view(np.int8), scales=s8),
-                             "z": L.SpandaTensor("dense", np.ones(3, np.float32))})
+                             "z": L.SpandaTensor("dense", np.ones(3, np.float32)),
+                             "s": L.SpandaTensor("sparse24", vals, shape=(16, 32), masks=masks),
+                             "s1": L.SpandaTensor("sparse24", vals, shape=(512,), masks=masks)})
     plane = _FakePlane()
     _, out = L.register_spanda(plane, p)
-    assert [(c[0], c[1], c[2], c[3]) for c in plane.calls] == [("m:x", "log4", 40, 64), ("m:y", "w8", 24, 32)]
-    assert out["z"].kind == "dense"
+    assert [(c[0], c[1], c[2], c[3]) for c in plane.calls] == [("m:x", "log4", 40, 64), ("m:y", "w8", 24, 32),
+                                                              ("m:s", "sp24_f32", 16, 32)]
+    assert np.array_equal(plane.calls[2][4], masks) and np.array_equal(plane.calls[2][5], vals)
+    assert out["z"].kind == "dense" and out["s1"].kind == "sparse24"
     L.write_spanda(p, meta, {"x": L.SpandaTensor("log4", q4[:-1], scales=s4)})
     with pytest.raises(ValueError, match="do not split into 40 rows"):
         L.register_spanda(_FakePlane(), p)
