@@ -283,7 +283,7 @@ def test_loaded_weights_compute_like_direct_registration(plane, tmp_path):
         direct = plane.register(f"direct:{w.key}", fmt, w.N, w.K, q, s)
         y = plane.gemv(w, x)
         assert np.array_equal(y, plane.gemv(direct, x)), w.key
-        ref = oracle.matvec_mul(fmt, x[0], q, s, w.N)
+        ref = oracle.matvec_mul_into(fmt, x[0], q, s, w.N)
         assert normwise_err(y, ref) <= GEMV_TOL, w.key
         plane.evict(direct.key)
         plane.evict(w.key)
