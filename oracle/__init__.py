@@ -10,6 +10,8 @@ reference's CPU arithmetic (akshaybhlrp/bramha):
 * prefill GEMM ``gemm_cpu``: ``src/inference/cpu_engine.rs:565-706``
 * 2:4 sparse GEMVs and compression: ``spanda-engine/src/sparse.rs:19-138``,
   ``src/inference/cpu_engine.rs:1532-1640``, ``spanda-engine/src/bin/convert.rs:55-92``
+* MoE expert MLP (router softmax, stable top-k, SwiGLU experts, weighted sum):
+  ``src/inference/cpu_engine.rs:1799-1989``
 * decode-step operations (RMSNorm, RoPE, single-token attention, SwiGLU,
   repetition penalty + argmax): ``src/inference/cpu_engine.rs:1292-1302,
   1450-1530, 1682-1698, 2023-2026, 2985-3031``; the step itself is in
@@ -84,6 +86,9 @@ def lib():
                                              ctypes.c_int]),
             "bro_sparse_matvec_2_4_compressed": (None, [_f32p, _u16p, _f32p, _i64, _i64, _i64, _f32p, ctypes.c_int]),
             "bro_compress_2_4": (_i64, [_f32p, _i64, _u16p, _f32p]),
+            "bro_moe_mlp": (None, [ctypes.c_int, _f32p, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int, _f32p,
+                                   ctypes.c_void_p, _f32p, ctypes.c_void_p, _f32p, ctypes.c_void_p, _f32p, _f32p,
+                                   ctypes.POINTER(ctypes.c_int32), _f32p, ctypes.c_int]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -349,3 +354,33 @@ def compress_2_4(w):
     nv = lib().bro_compress_2_4(_p(w, _f32p), w.size, _p(masks, _u16p), _p(values, _f32p))
     assert nv == values.size
     return masks, values
+
+
+# ---- MoE expert MLP (run_mlp_into's MoE branch, cpu_engine.rs:1799-1989) -----
+_MOE_FMT = {"f32": 0, "w8": 1, "w4zp8": 2, "log4": 3}
+
+
+def moe_mlp(fmt: str, h, logits, top_k: int, gate, up, down, threads: int = 0):
+    """h [T][H], logits [T][E]; gate / up = (codes of the E stacked [I][H]
+    weights, scales [E*I] or None for f32), down = (codes of [E][H][I], scales
+    [E*H]).  Returns (out [T][H], selected expert ids [T][k], their weights
+    [T][k]) -- the first k of the sorted order, including experts skipped for
+    a weight <= 0."""
+    h = _c(h, np.float32)
+    lg = _c(logits, np.float32)
+    T, H = h.shape
+    E = lg.shape[1]
+    gq, gs = gate
+    uq, us = up
+    dq, ds = down
+    gq, uq, dq = (np.ascontiguousarray(a) for a in (gq, uq, dq))
+    I = (gs.size if gs is not None else gq.size // (4 * H)) // E
+    k = min(top_k, E)
+    out = np.empty((T, H), np.float32)
+    ids = np.empty((T, k), np.int32)
+    w = np.empty((T, k), np.float32)
+    sp = lambda a: None if a is None else _p(_c(a, np.float32), _f32p)
+    lib().bro_moe_mlp(_MOE_FMT[fmt], _p(h, _f32p), T, H, I, E, top_k, _p(lg, _f32p), gq.ctypes.data, sp(gs),
+                      uq.ctypes.data, sp(us), dq.ctypes.data, sp(ds), _p(out, _f32p),
+                      ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), _p(w, _f32p), threads)
+    return out, ids, w

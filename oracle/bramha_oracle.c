@@ -628,3 +628,87 @@ BRO_API int64_t bro_compress_2_4(const float* w, int64_t n, uint16_t* masks, flo
     }
     return nv;
 }
+
+/* ---- MoE expert MLP (run_mlp_into's MoE branch, cpu_engine.rs:1799-1989) -----
+ * One decode token per row of h [T][H]; router logits [T][E] given (the router
+ * itself is a matvec_mul_into, :1801-1803, restated above).  Per token:
+ *  - softmax: max by f32::max fold, exps = exp(l - max), sequential sum, probs
+ *    = exps / sum when sum > 0 (:1805-1820);
+ *  - stable sort by probability, descending (slice::sort_by with
+ *    partial_cmp, :1822-1825): for finite values the order (-p, index);
+ *  - the first top_k, skipping weights <= 0 (:1826-1834);
+ *  - per expert: gate and up by matvec_mul_into, silu(g) = g / (1 + exp(-g))
+ *    times up (:1924-1936), down by matvec_mul_into (:1938-1942), then
+ *    out += down * weight in the sorted order (:1944-1946), from out = 0.
+ * fmt: 0 f32, 1 int8, 2 int4, 3 log4; expert weights stacked [E][I][.] for
+ * gate / up and [E][H][.] for down, scales [E][I] / [E][H].  Tokens in
+ * parallel when threads > 1; each token's arithmetic is sequential. */
+static void matvec_into_fmt(int fmt, const float* h, int64_t K, const void* q, const float* s, int64_t N, float* out) {
+    switch (fmt) {
+        case 0: bro_matvec_into_f32(h, K, (const float*)q, N, out, 1); break;
+        case 1: bro_matvec_into_i8(h, K, (const int8_t*)q, s, N, out, 1); break;
+        case 2: bro_matvec_into_u4(h, K, (const uint8_t*)q, s, N, out, 1); break;
+        default: bro_matvec_into_log4(h, K, (const uint8_t*)q, s, N, out, 1); break;
+    }
+}
+
+static int64_t fmt_row_bytes(int fmt, int64_t K) { return fmt == 0 ? 4 * K : fmt == 1 ? K : K / 2; }
+
+BRO_API void bro_moe_mlp(int fmt, const float* h, int64_t T, int64_t H, int64_t I, int E, int top_k,
+                         const float* logits, const void* gate_q, const float* gate_s, const void* up_q,
+                         const float* up_s, const void* down_q, const float* down_s, float* out,
+                         int32_t* sel_ids, float* sel_w, int threads) {
+    luts_init();
+    const int64_t gb = fmt_row_bytes(fmt, H) * I, db = fmt_row_bytes(fmt, I) * H;
+    const int k = top_k < E ? top_k : E;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(threads > 0 ? threads : 1) if (threads > 1)
+    for (int64_t t = 0; t < T; ++t) {
+        const float* lg = logits + t * E;
+        float* probs = (float*)malloc(sizeof(float) * (size_t)E);
+        int* order = (int*)malloc(sizeof(int) * (size_t)E);
+        float* g = (float*)malloc(sizeof(float) * (size_t)(3 * I + H));
+        float* u = g + I;
+        float* m = u + I;
+        float* dn = m + I;
+        float mx = -INFINITY;
+        for (int i = 0; i < E; ++i) mx = fmaxf(mx, lg[i]);
+        float sum = 0.0f;
+        for (int i = 0; i < E; ++i) {
+            probs[i] = expf(lg[i] - mx);
+            sum += probs[i];
+        }
+        for (int i = 0; i < E; ++i) probs[i] = sum > 0.0f ? probs[i] / sum : 0.0f;
+        for (int i = 0; i < E; ++i) order[i] = i;
+        for (int i = 1; i < E; ++i) {  /* stable insertion sort, descending */
+            const int o = order[i];
+            int j = i;
+            while (j > 0 && probs[o] > probs[order[j - 1]]) {
+                order[j] = order[j - 1];
+                --j;
+            }
+            order[j] = o;
+        }
+        float* y = out + t * H;
+        for (int64_t d = 0; d < H; ++d) y[d] = 0.0f;
+        for (int r = 0; r < k; ++r) {
+            const int e = order[r];
+            const float w = probs[e];
+            if (sel_ids) sel_ids[t * k + r] = e;
+            if (sel_w) sel_w[t * k + r] = w;
+            if (w <= 0.0f) continue;
+            const float* hh = h + t * H;
+            matvec_into_fmt(fmt, hh, H, (const uint8_t*)gate_q + e * gb, gate_s ? gate_s + (int64_t)e * I : NULL, I, g);
+            matvec_into_fmt(fmt, hh, H, (const uint8_t*)up_q + e * gb, up_s ? up_s + (int64_t)e * I : NULL, I, u);
+            for (int64_t d = 0; d < I; ++d) {
+                const float gd = g[d];
+                const float silu = gd / (1.0f + expf(-gd));
+                m[d] = silu * u[d];
+            }
+            matvec_into_fmt(fmt, m, I, (const uint8_t*)down_q + e * db, down_s ? down_s + (int64_t)e * H : NULL, H, dn);
+            for (int64_t d = 0; d < H; ++d) y[d] += dn[d] * w;
+        }
+        free(g);
+        free(order);
+        free(probs);
+    }
+}
