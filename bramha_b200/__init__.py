@@ -5,10 +5,10 @@ built by ``python -m bramha_b200.build``); this package is its Python host
 side, mirroring the reference's compute-plane interface.
 """
 from ._lib import FMT, BramhaError, header_symbols, last_error, lib
-from .plane import CudaComputePlane, Weight, get_cuda_plane, packed_nbytes
+from .plane import CudaComputePlane, Weight, get_cuda_plane, packed_nbytes, stack_gate_up
 from .decode import DecodeConfig, DecodeLayer, DecodeModel
 
 __all__ = [
     "FMT", "BramhaError", "CudaComputePlane", "DecodeConfig", "DecodeLayer", "DecodeModel", "Weight",
-    "get_cuda_plane", "header_symbols", "last_error", "lib", "packed_nbytes",
+    "get_cuda_plane", "header_symbols", "last_error", "lib", "packed_nbytes", "stack_gate_up",
 ]

@@ -15,6 +15,7 @@
 #include <cstdio>
 #include <cstring>
 #include <list>
+#include <utility>
 #include <mutex>
 #include <new>
 #include <string>
@@ -364,7 +365,8 @@ int sp24_check_pruned(int fmt, int64_t N, int64_t K, size_t q_bytes, size_t n_sc
 // for row r, masks[r*C + c] (C = cols / 4, low 4 bits, ascending bit order)
 // and consumes values from index 2*r*C onwards while any remain.  The walk is
 // restated here once and each group's (column, value) pairs are stored in
-// the 2:4 layout, in the order the reference consumes them.  A group that
+// the 2:4 layout (in column order, which is the order the reference consumes
+// them), with the id of their column pair.  A group that
 // consumes more than two values is not 2:4 and is refused.
 int sp24_canonicalise(int64_t rows, int64_t cols, const uint16_t* masks, const float* values, size_t n_values,
                       std::vector<uint8_t>& vals, std::vector<uint32_t>& idx) {
@@ -387,12 +389,17 @@ int sp24_canonicalise(int64_t rows, int64_t cols, const uint16_t* masks, const f
                 val[n] = values[vi++];
                 ++n;
             }
-            if (n == 1) col[1] = col[0] == 0 ? 1 : 0;  // an empty slot: value 0, any other column
+            if (n == 1) {  // an empty slot: value 0 at another column, slots in column order
+                col[1] = col[0] == 0 ? 1 : 0;
+                if (col[1] < col[0]) {
+                    std::swap(col[0], col[1]);
+                    std::swap(val[0], val[1]);
+                }
+            }
             memcpy(&vals[(size_t)((r * cp + c) * 8)], val, 8);
-            idx[(size_t)(r * (cp / 8) + c / 8)] |= (uint32_t)(col[0] | (col[1] << 2)) << (4 * (c % 8));
+            idx[(size_t)(r * (cp / 8) + c / 8)] |= (uint32_t)sp24_pair_id(col[0], col[1]) << (4 * (c % 8));
         }
-        for (int64_t c = C; c < cp; ++c)  // padding groups: zero values at columns (0, 1)
-            idx[(size_t)(r * (cp / 8) + c / 8)] |= 0x4u << (4 * (c % 8));
+        // padding groups: zero values at pair 0 (columns 0 and 1), id bits 0
     }
     return BRAMHA_OK;
 }
@@ -943,6 +950,83 @@ int bramha_cuda_sparse_matvec_2_4_compressed(bramha_ctx* ctx, const float* x, in
     rc = gemv_host(ctx, &tmp, x, 1, out);
     free_weight_memory(&tmp);
     return rc;
+}
+
+// ---- MoE expert MLP ----------------------------------------------------------
+namespace {
+int moe_check(bramha_ctx* ctx, const bramha_weight* gu, const bramha_weight* dn, int E, int top_k, int64_t T,
+              MoeWeights* mw) {
+    int rc = check_weight(ctx, gu);
+    if (rc) return rc;
+    rc = check_weight(ctx, dn);
+    if (rc) return rc;
+    if (gu->fmt != dn->fmt || (gu->fmt != BRAMHA_FMT_LOG4 && gu->fmt != BRAMHA_FMT_W4ZP8 && gu->fmt != BRAMHA_FMT_W8))
+        return fail(BRAMHA_ERR_UNSUPPORTED, "moe: gate_up and down must share one of LOG4, W4ZP8, W8");
+    if (E <= 0 || E > kMoeMaxExperts) return fail(BRAMHA_ERR_INVALID, "moe: num_experts must be in 1..%lld",
+                                                  (long long)kMoeMaxExperts);
+    if (top_k <= 0 || T < 0) return fail(BRAMHA_ERR_INVALID, "moe: top_k must be positive and T non-negative");
+    if (gu->N % E != 0 || dn->N % E != 0)
+        return fail(BRAMHA_ERR_SIZE, "moe: stacked weights must hold num_experts equal blocks of rows");
+    const int64_t two_i = gu->N / E, H = gu->K, I = two_i / 2;
+    if (two_i % 128 != 0 || H % 128 != 0)
+        return fail(BRAMHA_ERR_UNSUPPORTED, "moe: 2 * intermediate (%lld) and hidden (%lld) must be multiples of 128",
+                    (long long)two_i, (long long)H);
+    if (dn->N != E * H || dn->K != I)
+        return fail(BRAMHA_ERR_SIZE, "moe: down is %lld x %lld, expected %lld x %lld", (long long)dn->N,
+                    (long long)dn->K, (long long)(E * H), (long long)I);
+    const int64_t k = top_k < E ? top_k : E;
+    if (T * k > kMoeMaxAssignments)
+        return fail(BRAMHA_ERR_UNSUPPORTED, "moe: T * top_k = %lld exceeds %lld per call; split the batch",
+                    (long long)(T * k), (long long)kMoeMaxAssignments);
+    *mw = MoeWeights{gu->fmt, gu->q, gu->scales, dn->q, dn->scales, E, H, I};
+    return BRAMHA_OK;
+}
+}  // namespace
+
+int bramha_cuda_moe_mlp_dev(bramha_ctx* ctx, const bramha_weight* gate_up, const bramha_weight* down,
+                            int num_experts, int top_k, const float* x_dev, const float* logits_dev, int64_t T,
+                            float* out_dev, int32_t* selected_dev, void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    MoeWeights mw;
+    int rc = moe_check(ctx, gate_up, down, num_experts, top_k, T, &mw);
+    if (rc) return rc;
+    if (T == 0) return BRAMHA_OK;
+    if (!x_dev || !logits_dev || !out_dev) return fail(BRAMHA_ERR_INVALID, "null device pointer");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    CK(launch_moe_mlp(mw, top_k, x_dev, logits_dev, T, out_dev, selected_dev, ctx->d_err, st), "moe launch");
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_moe_mlp(bramha_ctx* ctx, const bramha_weight* gate_up, const bramha_weight* down, int num_experts,
+                        int top_k, const float* x_host, const float* logits_host, int64_t T, float* out_host,
+                        int32_t* selected_host) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    MoeWeights mw;
+    int rc = moe_check(ctx, gate_up, down, num_experts, top_k, T, &mw);
+    if (rc) return rc;
+    if (T == 0) return BRAMHA_OK;
+    if (!x_host || !logits_host || !out_host) return fail(BRAMHA_ERR_INVALID, "null host buffer");
+    DeviceGuard g(ctx->device);
+    std::lock_guard<std::mutex> lk(ctx->io_mu);
+    cudaStream_t st = ctx->stream;
+    const int64_t k = top_k < num_experts ? top_k : num_experts;
+    const size_t bx = (size_t)(T * mw.H) * 4, bl = (size_t)(T * num_experts) * 4, bs = (size_t)(T * k) * 4;
+    uint8_t* buf = nullptr;
+    CK(cudaMallocAsync(reinterpret_cast<void**>(&buf), 2 * bx + bl + bs, st), "moe staging");
+    float* xd = reinterpret_cast<float*>(buf);
+    float* od = reinterpret_cast<float*>(buf + bx);
+    float* ld = reinterpret_cast<float*>(buf + 2 * bx);
+    int32_t* sd = reinterpret_cast<int32_t*>(buf + 2 * bx + bl);
+    cudaError_t e = cudaMemcpyAsync(xd, x_host, bx, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(ld, logits_host, bl, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = launch_moe_mlp(mw, top_k, xd, ld, T, od, sd, ctx->d_err, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out_host, od, bx, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess && selected_host) e = cudaMemcpyAsync(selected_host, sd, bs, cudaMemcpyDeviceToHost, st);
+    cudaError_t e2 = cudaFreeAsync(buf, st);
+    if (e == cudaSuccess) e = e2;
+    if (e != cudaSuccess) return cuda_fail(e, "moe (host buffers)");
+    return check_device_error(ctx, st);
 }
 
 int bramha_cuda_gemm(bramha_ctx* ctx, const bramha_weight* w, const float* h_host, int64_t M, float* out_host) {

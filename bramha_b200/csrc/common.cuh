@@ -61,13 +61,18 @@ inline int sp24_base(int fmt) { return fmt - BRAMHA_FMT_SP24_F32 + BRAMHA_FMT_F3
 struct Sp24Weight {
     uint8_t* vals;    // [N][ldv] kept code pairs
     int64_t ldv;      // bytes per row = Cp * sp24_value_bytes
-    uint32_t* idx;    // [N][ldi] 4-bit column pairs, 8 groups per word
+    uint32_t* idx;    // [N][ldi] 4-bit column-pair ids, 8 groups per word
     int64_t ldi;      // words per row = Cp / 8
     float* tail;      // [N][4] codes of the K % 4 trailing columns, or null
     const float* scales;
     int64_t N, K, Cp; // Cp = groups of 4 columns per row, rounded up to 8
 };
 inline int64_t sp24_groups_padded(int64_t K) { return (K / 4 + 7) / 8 * 8; }
+// Column pairs (a < b) of a group of four and their ids 0..5:
+// (0,1) (0,2) (0,3) (1,2) (1,3) (2,3).
+__host__ __device__ constexpr int sp24_pair_a(int p) { return p < 3 ? 0 : p < 5 ? 1 : 2; }
+__host__ __device__ constexpr int sp24_pair_b(int p) { return p < 3 ? p + 1 : p < 5 ? p - 1 : 3; }
+__host__ __device__ constexpr int sp24_pair_id(int a, int b) { return a == 0 ? b - 1 : a == 1 ? b + 1 : 5; }
 
 // One weight inside a (possibly fused) GEMV launch.
 struct GemvSeg {
@@ -161,6 +166,31 @@ cudaError_t launch_sp24_gemv(int base_fmt, const Sp24Weight& w, const float* x, 
                              int64_t ws_floats, int* tickets, int n_tickets, int num_sms, cudaStream_t stream);
 cudaError_t launch_sp24_prune(int base_fmt, const uint8_t* src, int64_t row_bytes, const Sp24Weight& w,
                               cudaStream_t stream);
+
+// Grouped tcgen05 GEMM over a device tile table (gemm_tcgen05.cu); the MoE
+// path (moe.cu) builds the tables with kGemmGroupTok tokens per tile.
+constexpr int kGemmGroupTok = 64;
+cudaError_t launch_gemm_tcgen05_grouped(int fmt, const uint8_t* q, const float* scales, int64_t N_group, int64_t K,
+                                        const float* x, int64_t ldx, int64_t M, float* y, int64_t ldy,
+                                        const int4* tiles, const int* ntiles_dev, int64_t max_tiles, int* err,
+                                        cudaStream_t stream);
+
+// MoE expert MLP of T tokens (moe.cu): routing (softmax, stable top-k),
+// gather, grouped gate+up GEMM, SiLU * up, grouped down GEMM, weighted
+// combine.  gate_up: tile-major [E][2I][H] (gate rows then up rows per
+// expert), down: [E][H][I]; 2I and H multiples of 128.
+struct MoeWeights {
+    int fmt;
+    const uint8_t* gate_up;
+    const float* gate_up_scales;
+    const uint8_t* down;
+    const float* down_scales;
+    int64_t E, H, I;
+};
+cudaError_t launch_moe_mlp(const MoeWeights& w, int top_k, const float* x, const float* logits, int64_t T, float* out,
+                           int32_t* selected, int* err, cudaStream_t stream);
+constexpr int64_t kMoeMaxAssignments = 16384;  // T * top_k per call (routing state in shared memory)
+constexpr int64_t kMoeMaxExperts = 1024;
 
 // GPU packers (quant.cu).
 cudaError_t launch_quantize(int fmt, int64_t N, int64_t K, const float* w, uint8_t* q, float* scales,

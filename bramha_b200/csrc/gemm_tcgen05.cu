@@ -61,7 +61,28 @@ struct GemmArgs {
     int n_tiles, m_tiles;  // tiles along the weight rows and along the tokens
     int n_blocks;          // 128-row blocks of the repacked weight (ceil(N / 128))
     int* err;              // device error word (0 = ok)
+    // Grouped GEMM (MoE experts; 1-SM kernel only): when `tiles` is set the
+    // tile list comes from device memory -- *ntiles_dev entries of (128-row
+    // block of the stacked weight, first token row, tokens in the tile,
+    // first output column) -- and N is the row count of one group.
+    const int4* tiles;
+    const int* ntiles_dev;
 };
+
+// One output tile: 128-row block `wblk` of the (stacked) weight, token rows
+// [tok0, tok0 + mcount) of X and y, output columns [col0, col0 + 128).
+struct TileInfo {
+    int wblk, tok0, mcount, col0;
+};
+template <int BN>
+__device__ __forceinline__ TileInfo tile_info(const GemmArgs& a, int t) {
+    if (a.tiles) {
+        const int4 v = __ldg(a.tiles + t);
+        return {v.x, v.y, v.z, v.w};
+    }
+    const int nt = t % a.n_tiles, mt = t / a.n_tiles;
+    return {nt, mt * BN, min(BN, a.M - mt * BN), nt * BM};
+}
 
 // Packed weight bytes per row per stage.
 template <int FMT>
@@ -163,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::offAbort);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ntiles = a.n_tiles * a.m_tiles;
+    const int ntiles = a.tiles ? __ldg(a.ntiles_dev) : a.n_tiles * a.m_tiles;
     const int xs = a.x_steps;
 
     if (threadIdx.x == 0) {
@@ -196,8 +217,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             int g = 0;  // K steps issued by this CTA, over all its tiles
             bool ok = true;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-                const int nt = t % a.n_tiles, mt = t / a.n_tiles;
-                const uint8_t* wsrc = a.q + (int64_t)nt * a.k_steps * L::kP;
+                const TileInfo ti = tile_info<BN>(a, t);
+                const uint8_t* wsrc = a.q + (int64_t)ti.wblk * a.k_steps * L::kP;
                 for (int kx = 0; kx < xs; ++kx, ++g) {
                     const int s = g % S1;
                     if (g >= S1 && !mbar_wait(&empty_x[s], ((g / S1) & 1) ^ 1, abort_flag, a.err)) {
@@ -205,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     mbar_expect_tx(&full_tma[s], kTx);
-                    tma_load_2d(Xs + s * L::kX, &tmX, &full_tma[s], kx * BK, mt * BN);
+                    tma_load_2d(Xs + s * L::kX, &tmX, &full_tma[s], kx * BK, ti.tok0);
                     const int kw = kx < a.k_steps ? kx : kx - a.k_steps;
                     bulk_load(Ps + s * L::kP, wsrc + (int64_t)kw * L::kP, L::kP, &full_tma[s]);
                 }
@@ -300,25 +321,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) ok = mbar_wait(&acc_full[buf], (lt >> 1) & 1, abort_flag, a.err);
             if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
             tc_fence_after();
-            const int nt = t % a.n_tiles, mt = t / a.n_tiles;
-            const int grow = nt * BM + row;
-            const int m0 = mt * BN;
+            const TileInfo ti = tile_info<BN>(a, t);
+            const int grow = ti.col0 + row;
+            const int m0 = ti.tok0, mc = ti.mcount;
             const bool row_ok = grow < a.N;
             // a tile inside the matrix stores without per-element bounds checks
             // (a conditional store per element costs ~4x in issue)
-            const bool full = (int64_t)(nt + 1) * BM <= a.N && (int64_t)m0 + BN <= a.M;
-            const float sc = row_ok ? __ldg(a.scales + grow) : 0.f;
+            const bool full = ti.col0 + BM <= a.N && mc == BN;
+            const float sc = row_ok ? __ldg(a.scales + (int64_t)ti.wblk * BM + row) : 0.f;
             float* ycol = a.y + grow;
             const uint32_t taddr = tmem + (uint32_t)(buf * BN) + ((uint32_t)(q4 * 32) << 16);
             // log4: per-token sums, one chunk of 32 ahead of its use
             float rs_next = 0.f;
-            if constexpr (FMT == BRAMHA_FMT_LOG4) rs_next = m0 + lane < a.M ? __ldg(a.rowsum + m0 + lane) : 0.f;
+            if constexpr (FMT == BRAMHA_FMT_LOG4) rs_next = lane < mc ? __ldg(a.rowsum + m0 + lane) : 0.f;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 const float rs = rs_next;
                 if constexpr (FMT == BRAMHA_FMT_LOG4) {
-                    const int tl = m0 + c0 + 32 + lane;
-                    if (c0 + 32 < BN) rs_next = tl < a.M ? __ldg(a.rowsum + tl) : 0.f;
+                    const int tl = c0 + 32 + lane;
+                    if (c0 + 32 < BN) rs_next = tl < mc ? __ldg(a.rowsum + m0 + tl) : 0.f;
                 }
                 uint32_t v[32];
                 tmem_ld32(taddr + c0, v);
@@ -336,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else {
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
-                        if (row_ok && m0 + c0 + j < a.M) yc[(int64_t)j * a.ldy] = o[j];
+                        if (row_ok && c0 + j < mc) yc[(int64_t)j * a.ldy] = o[j];
                 }
             }
             tc_fence_before();
@@ -823,6 +844,8 @@ cudaError_t gemm_args(GemmArgs* g, const uint8_t* q, const float* scales, const 
     g->n_blocks = (int)((N + BM - 1) / BM);
     g->m_tiles = (int)m_tiles;
     g->err = err;
+    g->tiles = nullptr;
+    g->ntiles_dev = nullptr;
     return cudaSuccess;
 }
 }  // namespace
@@ -872,6 +895,50 @@ cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const fl
         if (e == cudaSuccess) e = e2;
     }
     return e;
+}
+
+// Grouped GEMM for MoE experts: the tiles of a device-side table (built by the
+// routing kernel, moe.cu), each a 128-row block of the group-stacked weight
+// against up to kGemmGroupTok token rows of x.  x is f32 [M][ldx] (split into
+// bf16 hi + lo, so results are within ~2^-16 of fp32), y [M][ldy]; N_group
+// is the row count of one group (rows past it are not stored); max_tiles
+// bounds the table (sizes the grid).  Scratch from the stream-ordered pool.
+cudaError_t launch_gemm_tcgen05_grouped(int fmt, const uint8_t* q, const float* scales, int64_t N_group, int64_t K,
+                                        const float* x, int64_t ldx, int64_t M, float* y, int64_t ldy,
+                                        const int4* tiles, const int* ntiles_dev, int64_t max_tiles, int* err,
+                                        cudaStream_t st) {
+    if (M <= 0 || N_group <= 0 || max_tiles <= 0) return cudaSuccess;
+    if (M > 0x7fffffff || N_group > 0x7fffffff || K > 0x7fffffff || K <= 0 || max_tiles > 0x7fffffff)
+        return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(q) & 15) != 0) return cudaErrorInvalidValue;
+    if (fmt != BRAMHA_FMT_LOG4 && fmt != BRAMHA_FMT_W4ZP8 && fmt != BRAMHA_FMT_W8) return cudaErrorInvalidValue;
+    if (!encode_fn()) return cudaErrorNotSupported;
+    const int64_t kp = (K + BK - 1) / BK * BK;
+    const bool log4 = fmt == BRAMHA_FMT_LOG4;
+    const int64_t cols = 2 * kp;
+    const size_t copy_bytes = (size_t)M * cols * sizeof(__nv_bfloat16);
+    const size_t bytes = copy_bytes + (log4 ? (size_t)M * sizeof(float) : 0);
+    uint8_t* scratch = nullptr;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), bytes, st);
+    if (e != cudaSuccess) return e;
+    __nv_bfloat16* xc = reinterpret_cast<__nv_bfloat16*>(scratch);
+    float* rs = log4 ? reinterpret_cast<float*>(scratch + copy_bytes) : nullptr;
+    const int wpb = 8;
+    prep_kernel<true><<<(unsigned)((M + wpb - 1) / wpb), 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
+    e = cudaGetLastError();
+    GemmArgs g;
+    CUtensorMap tmX;
+    if (e == cudaSuccess) e = gemm_args(&g, q, scales, rs, y, ldy, M, N_group, K, true, kGemmGroupTok, err);
+    if (e == cudaSuccess) {
+        g.tiles = tiles;
+        g.ntiles_dev = ntiles_dev;
+        g.n_tiles = (int)max_tiles;  // with a table, only the grid size reads these
+        g.m_tiles = 1;
+        e = make_x_map(&tmX, xc, cols, M, cols, kGemmGroupTok);
+    }
+    if (e == cudaSuccess) e = run_gemm(fmt, kGemmGroupTok, tmX, g, st);
+    cudaError_t e2 = cudaFreeAsync(scratch, st);
+    return e == cudaSuccess ? e2 : e;
 }
 
 cudaError_t launch_gemm_tcgen05_bf16_noalloc(int fmt, const uint8_t* q, int64_t ldq, const float* scales, int64_t N,

@@ -1,0 +1,251 @@
+// moe.cu -- the MoE expert MLP of a batch of decode tokens on one GPU.
+//
+// The reference runs, per token, the MoE branch of run_mlp_into
+// (src/inference/cpu_engine.rs:1799-1989): softmax of the router logits, a
+// stable descending sort, the first top_k experts (no renormalisation,
+// weights <= 0 skipped), per expert gate/up GEMVs, silu(g) * up, the down
+// GEMV, and out += down * weight in the sorted order.  Here the tokens of a
+// batch are grouped by expert so each expert's weights are streamed once for
+// all the tokens routed to it:
+//
+//   moe_route_kernel   one CTA: probabilities, top-k per token, per-expert
+//                      token lists (token order), row offsets, and the tile
+//                      tables of the two grouped GEMMs;
+//   moe_gather_kernel  activations of the routed (token, expert) pairs, in
+//                      expert order;
+//   grouped GEMM       gate and up of every expert in one launch (weights
+//                      stacked [E][2I][H]), tcgen05 (gemm_tcgen05.cu);
+//   moe_silu_kernel    silu(g) * up;
+//   grouped GEMM       down of every expert in one launch ([E][H][I]);
+//   moe_combine_kernel out[t] = sum over the token's kept experts, in the
+//                      sorted order, of down * weight.
+// Scratch (routing state and the intermediate activations) comes from the
+// stream-ordered pool and is released at the end of the call.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace bramha {
+namespace {
+
+constexpr int kRouteThreads = 1024;
+
+struct Route {
+    float* probs;   // [T][E]
+    int* sel_e;     // [T][k] r-th expert of the sorted order
+    float* sel_w;   // [T][k] its probability
+    int* slot;      // [T][k] row of the grouped activations, -1 when skipped (weight <= 0)
+    int* tok;       // [T*k] token of each grouped row
+    int* cnt;       // [E]
+    int* off;       // [E + 1] first grouped row of each expert; off[E] = rows in use
+    int4* tiles_gu; // tile table of the gate+up GEMM
+    int4* tiles_dn; // tile table of the down GEMM
+    int* ntiles;    // [2] entries of the two tables
+};
+
+// Probabilities and top-k of every token, then the per-expert grouping.
+__global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const float* __restrict__ logits, int T, int E,
+                                                                  int k, int nblk_gu, int nblk_dn, Route r,
+                                                                  int32_t* selected) {
+    extern __shared__ int sm[];
+    int* sel = sm;                // [T*k] expert of each choice, -1 when skipped
+    int* tg = sel + T * k;        // [E] first gate+up tile of each expert
+    int* td = tg + E;             // [E] first down tile of each expert
+    const int nk = T * k;
+
+    // softmax (sequential per token, as the reference) and the stable order
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const float* lg = logits + (int64_t)t * E;
+        float* p = r.probs + (int64_t)t * E;
+        float mx = -INFINITY;
+        for (int i = 0; i < E; ++i) mx = fmaxf(mx, lg[i]);
+        float sum = 0.f;
+        for (int i = 0; i < E; ++i) {
+            p[i] = expf(lg[i] - mx);
+            sum = __fadd_rn(sum, p[i]);
+        }
+        for (int i = 0; i < E; ++i) p[i] = sum > 0.f ? __fdiv_rn(p[i], sum) : 0.f;
+        // the r-th element of a stable descending sort: the largest probability
+        // after the previous pick in the order (probability desc, index asc)
+        float pp = INFINITY;
+        int pi = -1;
+        for (int j = 0; j < k; ++j) {
+            int best = -1;
+            float bp = -INFINITY;
+            for (int i = 0; i < E; ++i) {
+                const float v = p[i];
+                const bool after = v < pp || (v == pp && i > pi);
+                if (after && (best < 0 || v > bp)) {
+                    best = i;
+                    bp = v;
+                }
+            }
+            pp = bp;
+            pi = best;
+            r.sel_e[t * k + j] = best;
+            r.sel_w[t * k + j] = bp;
+            r.slot[t * k + j] = -1;
+            sel[t * k + j] = bp > 0.f ? best : -1;
+            if (selected) selected[t * k + j] = best;
+        }
+    }
+    __syncthreads();
+    // rows per expert
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int c = 0;
+        for (int i = 0; i < nk; ++i) c += sel[i] == e;
+        r.cnt[e] = c;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int o = 0, a = 0, b = 0;
+        for (int e = 0; e < E; ++e) {
+            r.off[e] = o;
+            tg[e] = a;
+            td[e] = b;
+            const int mt = (r.cnt[e] + kGemmGroupTok - 1) / kGemmGroupTok;
+            o += r.cnt[e];
+            a += mt * nblk_gu;
+            b += mt * nblk_dn;
+        }
+        r.off[E] = o;
+        r.ntiles[0] = a;
+        r.ntiles[1] = b;
+    }
+    __syncthreads();
+    // rows of each expert in token order, and its tiles
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const int o = r.off[e], c = r.cnt[e];
+        int s = o;
+        for (int i = 0; i < nk; ++i)
+            if (sel[i] == e) {
+                r.slot[i] = s;
+                r.tok[s] = i / k;
+                ++s;
+            }
+        const int mt = (c + kGemmGroupTok - 1) / kGemmGroupTok;
+        for (int m = 0; m < mt; ++m) {
+            const int tok0 = o + m * kGemmGroupTok, mc = min(kGemmGroupTok, c - m * kGemmGroupTok);
+            for (int nb = 0; nb < nblk_gu; ++nb)
+                r.tiles_gu[tg[e] + m * nblk_gu + nb] = make_int4(e * nblk_gu + nb, tok0, mc, nb * 128);
+            for (int nb = 0; nb < nblk_dn; ++nb)
+                r.tiles_dn[td[e] + m * nblk_dn + nb] = make_int4(e * nblk_dn + nb, tok0, mc, nb * 128);
+        }
+    }
+}
+
+// xg[s] = x[tok[s]] for the rows in use, zero for the rest.
+__global__ void moe_gather_kernel(const float* __restrict__ x, int64_t H, const int* __restrict__ tok,
+                                  const int* __restrict__ off_end, int64_t rows, float* __restrict__ xg) {
+    const int64_t s = blockIdx.y;
+    const int used = __ldg(off_end);
+    for (int64_t d = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; d < H; d += (int64_t)gridDim.x * blockDim.x)
+        xg[s * H + d] = s < used ? __ldg(x + (int64_t)__ldg(tok + s) * H + d) : 0.f;
+}
+
+// act[s][i] = silu(g) * up with silu(g) = g / (1 + exp(-g)) (cpu_engine.rs:1931-1935),
+// g = y[s][i], up = y[s][I + i].
+__global__ void moe_silu_kernel(const float* __restrict__ y, int64_t I, int64_t rows, float* __restrict__ act) {
+    const int64_t n = rows * I;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t s = i / I, c = i % I;
+        const float g = y[s * 2 * I + c], u = y[s * 2 * I + I + c];
+        const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+        act[i] = __fmul_rn(silu, u);
+    }
+}
+
+// out[t][d] = sum over r < k (kept choices, sorted order) of down[slot][d] * w,
+// starting from 0, one rounding per product and per sum (cpu_engine.rs:1944-1946).
+__global__ void moe_combine_kernel(const float* __restrict__ down, int64_t H, int k, const int* __restrict__ slot,
+                                   const float* __restrict__ w, float* __restrict__ out) {
+    const int64_t t = blockIdx.y;
+    for (int64_t d = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; d < H; d += (int64_t)gridDim.x * blockDim.x) {
+        float acc = 0.f;
+        for (int j = 0; j < k; ++j) {
+            const int s = __ldg(slot + t * k + j);
+            if (s >= 0) acc = __fadd_rn(acc, __fmul_rn(__ldg(down + (int64_t)s * H + d), __ldg(w + t * k + j)));
+        }
+        out[t * H + d] = acc;
+    }
+}
+
+template <class T>
+T* carve(uint8_t*& p, int64_t n) {
+    T* r = reinterpret_cast<T*>(p);
+    p += (n * (int64_t)sizeof(T) + 255) / 256 * 256;
+    return r;
+}
+
+}  // namespace
+
+cudaError_t launch_moe_mlp(const MoeWeights& w, int top_k, const float* x, const float* logits, int64_t T, float* out,
+                           int32_t* selected, int* err, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    const int64_t E = w.E, H = w.H, I = w.I;
+    const int k = (int)(top_k < E ? top_k : E);
+    if (E <= 0 || E > kMoeMaxExperts || k <= 0 || T * k > kMoeMaxAssignments || (2 * I) % 128 || H % 128)
+        return cudaErrorInvalidValue;
+    const int nblk_gu = (int)(2 * I / 128), nblk_dn = (int)(H / 128);
+    const int64_t rows = T * k;                                   // grouped rows, at most
+    const int64_t mtiles = rows / kGemmGroupTok + E;              // sum over experts of ceil(cnt / 64)
+    const int64_t max_gu = mtiles * nblk_gu, max_dn = mtiles * nblk_dn;
+    // scratch layout (256-byte aligned pieces)
+    auto pad = [](int64_t b) { return (b + 255) / 256 * 256; };
+    const int64_t bytes = pad(T * E * 4) + pad(rows * 4) * 4 + pad(E * 4) + pad((E + 1) * 4) +
+                          pad(max_gu * 16) + pad(max_dn * 16) + pad(8) + pad(rows * H * 4) +
+                          pad(rows * 2 * I * 4) + pad(rows * I * 4) + pad(rows * H * 4);
+    uint8_t* base = nullptr;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&base), (size_t)bytes, st);
+    if (e != cudaSuccess) return e;
+    uint8_t* p = base;
+    Route r;
+    r.probs = carve<float>(p, T * E);
+    r.sel_e = carve<int>(p, rows);
+    r.sel_w = carve<float>(p, rows);
+    r.slot = carve<int>(p, rows);
+    r.tok = carve<int>(p, rows);
+    r.cnt = carve<int>(p, E);
+    r.off = carve<int>(p, E + 1);
+    r.tiles_gu = carve<int4>(p, max_gu);
+    r.tiles_dn = carve<int4>(p, max_dn);
+    r.ntiles = carve<int>(p, 2);
+    float* xg = carve<float>(p, rows * H);
+    float* y1 = carve<float>(p, rows * 2 * I);
+    float* act = carve<float>(p, rows * I);
+    float* y2 = carve<float>(p, rows * H);
+
+    const size_t smem = (size_t)(rows + 2 * E) * sizeof(int);
+    if (smem > 48 * 1024) e = cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)smem);
+    if (e == cudaSuccess) {
+        moe_route_kernel<<<1, kRouteThreads, smem, st>>>(logits, (int)T, (int)E, k, nblk_gu, nblk_dn, r, selected);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) {
+        moe_gather_kernel<<<dim3((unsigned)((H + 255) / 256), (unsigned)rows), 256, 0, st>>>(x, H, r.tok, r.off + E,
+                                                                                           rows, xg);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess)
+        e = launch_gemm_tcgen05_grouped(w.fmt, w.gate_up, w.gate_up_scales, 2 * I, H, xg, H, rows, y1, 2 * I,
+                                        r.tiles_gu, r.ntiles, max_gu, err, st);
+    if (e == cudaSuccess) {
+        const int64_t n = rows * I;
+        moe_silu_kernel<<<(unsigned)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096), 256, 0, st>>>(y1, I, rows,
+                                                                                                   act);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess)
+        e = launch_gemm_tcgen05_grouped(w.fmt, w.down, w.down_scales, H, I, act, I, rows, y2, H, r.tiles_dn,
+                                        r.ntiles + 1, max_dn, err, st);
+    if (e == cudaSuccess) {
+        moe_combine_kernel<<<dim3((unsigned)((H + 255) / 256), (unsigned)T), 256, 0, st>>>(y2, H, k, r.slot, r.sel_w,
+                                                                                         out);
+        e = cudaGetLastError();
+    }
+    cudaError_t e2 = cudaFreeAsync(base, st);
+    return e == cudaSuccess ? e2 : e;
+}
+
+}  // namespace bramha

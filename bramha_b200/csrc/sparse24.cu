@@ -16,20 +16,26 @@
 //                  type -- f32 pair (8 B), int8 pair stored offset-binary
 //                  (q + 128, 2 B), or int4 pair (slot 0 low nibble, slot 1
 //                  high nibble, raw q, 1 B);
-//   idx  [N][Cp/8] u32 : 4 bits per group, bits 4j..4j+1 = column of slot 0
-//                  and 4j+2..4j+3 = column of slot 1 of group j of the word;
+//   idx  [N][Cp/8] u32 : 4 bits per group (group j of the word at bits
+//                  4j..4j+3): the id p of its column pair (a < b), p = 0..5
+//                  for (0,1) (0,2) (0,3) (1,2) (1,3) (2,3); slot 0 holds the
+//                  code of column a, slot 1 that of column b;
 //   tail [N][4] f32 : codes of the K % 4 columns after the last full group
 //                  (on-the-fly path only: the reference adds them densely);
 //   scales [N].
 // Cp = groups per row rounded up to 8 (padding groups hold zero codes).
 // Bytes per group of 4 weights: 8.5 (f32), 2.5 (int8), 1.5 (int4).
 //
-// GEMV: y[r] = s[r] * (sum over groups of v0 * x[4g + i0] + v1 * x[4g + i1]
-// + tail).  A block owns 64 rows and one K-slice; it stages the slice of x in
-// shared memory transposed so that the gather is free of bank conflicts:
-// lane l reads groups 8l..8l+7 of each 256-group segment (one vector load of
-// codes and one u32 of indices), and the x element (segment t, group 8l+j,
-// column i) sits at word ((t*8 + j)*128 + i*32 + l), i.e. always in bank l.
+// GEMV: y[r] = s[r] * (sum over groups of v0 * x[4g + a] + v1 * x[4g + b]
+// + tail).  A block (16 warps) owns 64 rows and one K-slice.  It stages the
+// slice of x in shared memory as all six column pairs of every group,
+// (x[4g+a], x[4g+b]) as one float2, so a group's two activations are ONE
+// 64-bit shared load picked by its pair id.  Lane l streams groups 8l..8l+7
+// of each 256-group segment (one vector load of codes and one u32 of pair
+// ids); the pair p of (segment t, group 8l+j) sits at float2 index
+// ((t*8 + j)*6 + p)*32 + l, so the 16 lanes of each half-warp always hit 16
+// distinct bank pairs.  Decoding and the two products of a group use
+// Blackwell's packed f32x2 add and fma (two fp32 accumulators per row).
 // K-slices are summed by the last block of each row tile (an atomic ticket,
 // no waiting), in slice order, so results are deterministic.
 #include "common.cuh"
@@ -37,11 +43,12 @@
 namespace bramha {
 namespace {
 
-constexpr int kSpThreads = 256;
+constexpr int kSpThreads = 512;
 constexpr int kSpWarps = kSpThreads / 32;
 constexpr int kSpTileRows = 64;
-constexpr int kSpSegChunks = 256;            // groups covered by one warp pass
-constexpr int kSpMaxSegs = 16;               // x slice <= 16 * 4 KB of shared memory
+constexpr int kSpSegChunks = 256;               // groups covered by one warp pass
+constexpr int kSpSegBytes = kSpSegChunks * 48;  // six float2 pairs per group
+constexpr int kSpMaxSegs = 8;                   // x slice <= 8 segments = 96 KB of shared memory
 constexpr int kSpMaxSplit = 16;
 
 template <int FMT>
@@ -98,7 +105,7 @@ __device__ __forceinline__ uint32_t ld_stream1(const void* p) {
     return r;
 }
 
-// Codes of one group of 8 chunks, as 32-bit words.
+// Codes of one group of 8 chunks, as 32-bit words, and their pair ids.
 template <int FMT>
 struct Group {
     static constexpr int kWords = SpFmt<FMT>::kVB * 8 / 4;
@@ -107,82 +114,92 @@ struct Group {
 };
 
 template <int FMT>
-__device__ __forceinline__ void load_group(const SpArgs& a, int row, int g, Group<FMT>& G) {
-    const uint8_t* p = a.vals + (int64_t)row * a.ldv + (int64_t)g * (SpFmt<FMT>::kVB * 8);
+__device__ __forceinline__ void load_at(const uint8_t* vp, const uint32_t* ip, Group<FMT>& G) {
     if constexpr (Group<FMT>::kWords >= 4) {
 #pragma unroll
         for (int v = 0; v < Group<FMT>::kWords / 4; ++v) {
-            const uint4 q = ld_stream4(p + 16 * v);
+            const uint4 q = ld_stream4(vp + 16 * v);
             G.w[4 * v] = q.x;
             G.w[4 * v + 1] = q.y;
             G.w[4 * v + 2] = q.z;
             G.w[4 * v + 3] = q.w;
         }
     } else {
-        const uint2 q = ld_stream2(p);
+        const uint2 q = ld_stream2(vp);
         G.w[0] = q.x;
         G.w[1] = q.y;
     }
-    G.idx = ld_stream1(a.idx + (int64_t)row * a.ldi + g);
+    G.idx = ld_stream1(ip);
 }
 
-// (column of the 2-bit field at bit s of idx) << 7: the byte offset of that
-// column's row of the transposed x segment.  s is a constant after unrolling.
-__device__ __forceinline__ uint32_t field_off(uint32_t idx, int s) {
-    return s >= 7 ? (idx >> (s - 7)) & 0x180u : (idx << (7 - s)) & 0x180u;
+// Byte offset of pair p's float2 row within a (segment, group) block: p * 256.
+__device__ __forceinline__ uint32_t pair_off(uint32_t idx, int j) {
+    const int s = 4 * j;  // field at bits s..s+2; wanted at bits 8..10
+    return s >= 8 ? (idx >> (s - 8)) & 0x700u : (idx << (8 - s)) & 0x700u;
 }
 
-// Exact float of byte b of `word`, minus `bias` (magic-number conversion:
-// 0x4B0000bb is 2^23 + bb).
-__device__ __forceinline__ float byte_val(uint32_t word, int b, float bias) {
-    return __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7540u | (uint32_t)b)) - (8388608.0f + bias);
+// Two fp32 lanes in one 64-bit register (packed f32x2 arithmetic, sm_100).
+__device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) { return (uint64_t)lo | ((uint64_t)hi << 32); }
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
 }
 
-// Adds the 16 kept products of one group of 8 chunks to acc.  lt: byte
-// offset of (segment t, chunk 0, column 0, this lane) in the staged x.
+// Byte b of `word` under the exponent of 2^23: the float 2^23 + byte, exactly.
+__device__ __forceinline__ uint32_t magic_byte(uint32_t word, int b) {
+    return __byte_perm(word, 0x4B000000u, 0x7540u | (uint32_t)b);
+}
+
+// Adds the 16 kept products of one group of 8 chunks to acc (slot-0 products
+// in the low lane, slot-1 products in the high lane).  lt: byte offset of
+// (segment, chunk 0, pair 0, this lane) in the staged pairs; its bits 8..10
+// are zero, so the pair offset is OR-ed in and j*1536 is a constant offset.
 template <int FMT>
-__device__ __forceinline__ float group_dot(const Group<FMT>& G, const float* xs, uint32_t lt, float acc) {
-    const char* xb = reinterpret_cast<const char*>(xs);
+__device__ __forceinline__ uint64_t group_dot(const Group<FMT>& G, const char* xb, uint32_t lt, uint64_t acc) {
     uint32_t lo4 = 0, hi4 = 0;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        const uint32_t base = lt + (uint32_t)j * 512u;  // bits 7..8 clear
-        const float x0 = *reinterpret_cast<const float*>(xb + (base | field_off(G.idx, 4 * j)));
-        const float x1 = *reinterpret_cast<const float*>(xb + (base | field_off(G.idx, 4 * j + 2)));
-        float v0, v1;
+        const uint64_t xp = *reinterpret_cast<const uint64_t*>(xb + (uint32_t)j * 1536u + (lt | pair_off(G.idx, j)));
+        uint64_t v;
         if constexpr (FMT == BRAMHA_FMT_F32) {
-            v0 = __uint_as_float(G.w[2 * j]);
-            v1 = __uint_as_float(G.w[2 * j + 1]);
-        } else if constexpr (FMT == BRAMHA_FMT_W8) {  // offset-binary int8 pair
+            v = pack2(G.w[2 * j], G.w[2 * j + 1]);
+        } else if constexpr (FMT == BRAMHA_FMT_W8) {  // (2^23 + q + 128) - (2^23 + 128)
             const uint32_t wd = G.w[j >> 1];
-            v0 = byte_val(wd, 2 * (j & 1), 128.0f);
-            v1 = byte_val(wd, 2 * (j & 1) + 1, 128.0f);
-        } else {  // int4 pair: slot 0 low nibble, slot 1 high nibble
+            v = add2(pack2(magic_byte(wd, 2 * (j & 1)), magic_byte(wd, 2 * (j & 1) + 1)),
+                     pack2(0xCB000080u, 0xCB000080u));
+        } else {  // int4 pair, slot 0 low nibble, slot 1 high nibble: (2^23 + q) - (2^23 + 8)
             if ((j & 3) == 0) {
                 lo4 = G.w[j >> 2] & 0x0F0F0F0Fu;
                 hi4 = (G.w[j >> 2] >> 4) & 0x0F0F0F0Fu;
             }
-            v0 = byte_val(lo4, j & 3, 8.0f);
-            v1 = byte_val(hi4, j & 3, 8.0f);
+            v = add2(pack2(magic_byte(lo4, j & 3), magic_byte(hi4, j & 3)), pack2(0xCB000008u, 0xCB000008u));
         }
-        acc = fmaf(v0, x0, acc);
-        acc = fmaf(v1, x1, acc);
+        acc = fma2(v, xp, acc);
     }
     return acc;
 }
 
 template <int FMT>
-__global__ void __launch_bounds__(kSpThreads) sp24_gemv_kernel(SpArgs a) {
+__global__ void __launch_bounds__(kSpThreads, 2) sp24_gemv_kernel(SpArgs a) {
     extern __shared__ float xs[];
     constexpr int U = SpFmt<FMT>::kU;
+    constexpr int GB = SpFmt<FMT>::kVB * 8;  // code bytes of a group of 8 chunks
     const int tile = blockIdx.x % a.row_tiles;
     const int ksl = blockIdx.x / a.row_tiles;
-    const int g0 = ksl * a.slice;                       // first group of the slice
-    const int S = min(a.slice, a.Cp - g0);              // groups in the slice (multiple of 8)
+    const int g0 = ksl * a.slice;           // first group of the slice
+    const int S = min(a.slice, a.Cp - g0);  // groups in the slice (multiple of 8)
     const int segs = (S + kSpSegChunks - 1) / kSpSegChunks;
+    const int full_segs = S / kSpSegChunks;
 
-    // Stage the slice of x, transposed; columns of padding groups (and of the
-    // tail, which has its own term) are zero.
+    // Stage the six column pairs of every group of the slice; columns of
+    // padding groups (and of the tail, which has its own term) are zero.
+    float2* xp = reinterpret_cast<float2*>(xs);
     for (int e = threadIdx.x; e < segs * kSpSegChunks; e += kSpThreads) {
         const int t = e >> 8, j = (e >> 5) & 7, l = e & 31;
         const int c = g0 + (t << 8) + (l << 3) + j;  // group index in the row
@@ -191,33 +208,50 @@ __global__ void __launch_bounds__(kSpThreads) sp24_gemv_kernel(SpArgs a) {
             const float4 q = __ldg(reinterpret_cast<const float4*>(a.x) + c);
             v[0] = q.x, v[1] = q.y, v[2] = q.z, v[3] = q.w;
         }
-        float* d = xs + ((t * 8 + j) * 128 + l);
+        float2* d = xp + (t * 8 + j) * 192 + l;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) d[i * 32] = v[i];
+        for (int p = 0; p < 6; ++p) d[p * 32] = make_float2(v[sp24_pair_a(p)], v[sp24_pair_b(p)]);
     }
     __syncthreads();
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const char* xb = reinterpret_cast<const char*>(xs);
     const bool last_slice = ksl == a.ks - 1;
-    for (int r0 = tile * kSpTileRows + warp * U; r0 < min(a.N, (tile + 1) * kSpTileRows); r0 += kSpWarps * U) {
-        float acc[U];
+    const int row_end = min(a.N, (tile + 1) * kSpTileRows);
+    for (int r0 = tile * kSpTileRows + warp * U; r0 < row_end; r0 += kSpWarps * U) {
+        // rows past N repeat row N-1 (in bounds) and are not written
+        const uint8_t* vp[U];
+        const uint32_t* ip[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) acc[u] = 0.f;
-        for (int t = 0; t < segs; ++t) {
-            const int gl = t * 32 + lane;  // group-of-8 index within the slice
-            if (8 * gl < S) {
-                Group<FMT> G[U];
+        for (int u = 0; u < U; ++u) {
+            const int row = min(r0 + u, a.N - 1);
+            vp[u] = a.vals + (int64_t)row * a.ldv + (int64_t)(g0 / 8 + lane) * GB;
+            ip[u] = a.idx + (int64_t)row * a.ldi + g0 / 8 + lane;
+        }
+        uint64_t acc[U];
 #pragma unroll
-                for (int u = 0; u < U; ++u)
-                    if (r0 + u < a.N) load_group<FMT>(a, r0 + u, g0 / 8 + gl, G[u]);
+        for (int u = 0; u < U; ++u) acc[u] = 0;
+        int t = 0;
+#pragma unroll 2
+        for (; t < full_segs; ++t) {
+            Group<FMT> G[U];
 #pragma unroll
-                for (int u = 0; u < U; ++u)
-                    if (r0 + u < a.N) acc[u] = group_dot<FMT>(G[u], xs, (uint32_t)t * 4096u + (uint32_t)lane * 4u, acc[u]);
-            }
+            for (int u = 0; u < U; ++u) load_at<FMT>(vp[u] + t * 32 * GB, ip[u] + t * 32, G[u]);
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                acc[u] = group_dot<FMT>(G[u], xb, (uint32_t)t * (uint32_t)kSpSegBytes + (uint32_t)lane * 8u, acc[u]);
+        }
+        if (t < segs && 8 * (t * 32 + lane) < S) {  // the partial last segment
+            Group<FMT> G[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) load_at<FMT>(vp[u] + t * 32 * GB, ip[u] + t * 32, G[u]);
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                acc[u] = group_dot<FMT>(G[u], xb, (uint32_t)t * (uint32_t)kSpSegBytes + (uint32_t)lane * 8u, acc[u]);
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            float s = acc[u];
+            float s = __uint_as_float((uint32_t)acc[u]) + __uint_as_float((uint32_t)(acc[u] >> 32));
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
             const int row = r0 + u;
@@ -247,7 +281,7 @@ __global__ void __launch_bounds__(kSpThreads) sp24_gemv_kernel(SpArgs a) {
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int row = tile * kSpTileRows + threadIdx.x; row < min(a.N, (tile + 1) * kSpTileRows); row += kSpThreads) {
+    for (int row = tile * kSpTileRows + threadIdx.x; row < row_end; row += kSpThreads) {
         float s = 0.f;
         for (int k = 0; k < a.ks; ++k) s += __ldcg(a.ws + (int64_t)k * a.N + row);
         a.y[row] = s * a.scales[row];
@@ -324,10 +358,15 @@ __global__ void sp24_prune_kernel(const uint8_t* src, int64_t row_bytes, int64_t
                 m[i] = fabsf(v[i]);
             }
             top2_of4(m, i1, i2);
+            if (i1 > i2) {  // slots in column order
+                const int t = i1;
+                i1 = i2;
+                i2 = t;
+            }
             v1 = v[i1];
             v2 = v[i2];
         }
-        iw |= (uint32_t)(i1 | (i2 << 2)) << (4 * j);
+        iw |= (uint32_t)sp24_pair_id(i1, i2) << (4 * j);
         if constexpr (FMT == BRAMHA_FMT_F32) {
             w[2 * j] = __float_as_uint(v1);
             w[2 * j + 1] = __float_as_uint(v2);
@@ -353,7 +392,7 @@ cudaError_t set_smem_attr() {
     if (e != cudaSuccess) return e;
     if (dev < 64 && done[dev]) return cudaSuccess;
     e = cudaFuncSetAttribute(sp24_gemv_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSpMaxSegs * kSpSegChunks * 16);
+                             kSpMaxSegs * kSpSegBytes + 512);
     if (e == cudaSuccess && dev < 64) done[dev] = 1;
     return e;
 }
@@ -398,7 +437,8 @@ cudaError_t launch_gemv_t(const Sp24Weight& w, const float* x, float* y, float* 
     }
     if (a.slice > kSpMaxSegs * kSpSegChunks) return cudaErrorInvalidValue;  // N too large for the workspace
     const int segs = a.Cp == 0 ? 0 : (a.slice + kSpSegChunks - 1) / kSpSegChunks;
-    const size_t smem = (size_t)segs * kSpSegChunks * 16;
+    // + 512 B: even a pair id of 6 or 7 (never written) stays inside the allocation
+    const size_t smem = segs ? (size_t)segs * kSpSegBytes + 512 : 0;
     sp24_gemv_kernel<FMT><<<a.row_tiles * a.ks, kSpThreads, smem, st>>>(a);
     return cudaGetLastError();
 }

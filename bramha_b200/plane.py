@@ -11,6 +11,9 @@ method, same argument meaning and error behaviour:
 * ``gemm(fmt, h_block, q, scales, block_size, in_features, out_features)``:
   the prefill GEMM that `gemm_cpu` (src/inference/cpu_engine.rs:565) computes
 * ``clear_persistent_buffers()`` (:725)
+* ``moe_mlp(gate_up, down, num_experts, top_k, x, logits)``: the MoE branch
+  of run_mlp_into (src/inference/cpu_engine.rs:1799-1989) for a batch of
+  tokens; ``stack_gate_up`` builds its stacked expert weight
 * ``sparse_matvec_mul_2_4(x, w, cols)`` / ``sparse_matvec_2_4_compressed(x,
   masks, nonzero_values, rows, cols)`` (spanda-engine/src/sparse.rs:19, 100)
   and ``sparse_matvec_mul_2_4_tensor(h, fmt, q, scales, out_features, ...)``
@@ -181,6 +184,25 @@ class CudaComputePlane:
             None if layer_name is None else layer_name.encode(), out.ctypes.data))
         return out
 
+    def moe_mlp(self, gate_up: Weight, down: Weight, num_experts: int, top_k: int, x, logits):
+        """MoE expert MLP of T tokens (run_mlp_into's MoE branch): x [T][H],
+        logits [T][E] -> (out [T][H], selected expert ids [T][min(k, E)])."""
+        x = _f32(x)
+        lg = _f32(logits)
+        T = x.shape[0]
+        k = min(top_k, num_experts)
+        out = np.empty_like(x)
+        sel = np.empty((T, k), np.int32)
+        check(lib().bramha_cuda_moe_mlp(self._ctx, gate_up.handle, down.handle, num_experts, top_k, x.ctypes.data,
+                                        lg.ctypes.data, T, out.ctypes.data, sel.ctypes.data))
+        return out, sel
+
+    def moe_mlp_dev(self, gate_up: Weight, down: Weight, num_experts: int, top_k: int, x, logits, out,
+                    selected=None, stream=None):
+        check(lib().bramha_cuda_moe_mlp_dev(self._ctx, gate_up.handle, down.handle, num_experts, top_k, x.data_ptr(),
+                                            logits.data_ptr(), x.shape[0], out.data_ptr(),
+                                            None if selected is None else selected.data_ptr(), _stream(stream)))
+
     def lookup(self, key: str) -> Weight:
         h = _vp()
         check(lib().bramha_cuda_lookup_weight(self._ctx, key.encode(), ctypes.byref(h)))
@@ -317,3 +339,13 @@ def get_cuda_plane(device: int = 0) -> Optional[CudaComputePlane]:
 
 def packed_nbytes(fmt: str, n: int, k: int) -> int:
     return {"f32": n * k * 4, "w8": n * k, "w4zp8": n * (k // 2), "log4": n * (k // 2)}[fmt]
+
+
+def stack_gate_up(gates, ups):
+    """Per-expert packed gate and up weights [(q, scales)] -> the stacked
+    gate_up layout of the MoE call: expert e's gate rows, then its up rows."""
+    qs, ss = [], []
+    for (gq, gs), (uq, us) in zip(gates, ups):
+        qs += [np.ascontiguousarray(gq).reshape(-1).view(np.uint8), np.ascontiguousarray(uq).reshape(-1).view(np.uint8)]
+        ss += [_f32(gs), _f32(us)]
+    return np.concatenate(qs), np.concatenate(ss)

@@ -229,6 +229,36 @@ BRAMHA_API int bramha_cuda_sparse_matvec_2_4_compressed(bramha_ctx* ctx, const f
                                                         size_t n_values, int64_t rows, const char* model_name,
                                                         const char* layer_name, float* out);
 
+/* ------------------------------------------------------- MoE expert MLP */
+
+/* The MoE branch of run_mlp_into (src/inference/cpu_engine.rs:1799-1989) for a
+ * batch of T decode tokens: per token, p = softmax(logits[t]) (sequential, as
+ * the reference), the first top_k experts of a stable descending sort (equal
+ * probabilities keep the lower expert first; no renormalisation; experts with
+ * p <= 0 skipped), and
+ *   out[t] = sum over the kept experts, in that order, of p_e * down_e(silu(gate_e x) * up_e x)
+ * with silu(g) = g / (1 + exp(-g)).  Tokens are grouped by expert so each
+ * expert's weights are read once per call (grouped tcgen05 GEMMs, f32
+ * activations split into bf16 hi + lo, fp32 accumulation: within ~1e-3
+ * normwise of the reference).
+ * Weights, registered with bramha_cuda_register_weight in one of LOG4, W4ZP8,
+ * W8 (both the same):
+ *   gate_up: [E * 2I][H], expert e's gate rows then its up rows at rows
+ *            [2I e, 2I e + I) and [2I e + I, 2I (e + 1));
+ *   down:    [E * H][I], expert e at rows [H e, H (e + 1)).
+ * 2I and H must be multiples of 128; T * min(top_k, E) <= 16384; E <= 1024.
+ * x [T][H], logits [T][E] (the router's output: a GEMV with the router weight,
+ * cpu_engine.rs:1801-1803, is a bramha_cuda_gemv call), out [T][H] f32;
+ * selected [T][min(top_k, E)] receives the sorted expert ids (skipped ones
+ * included), or pass NULL.  Scratch comes from the stream-ordered pool. */
+BRAMHA_API int bramha_cuda_moe_mlp_dev(bramha_ctx* ctx, const bramha_weight* gate_up, const bramha_weight* down,
+                                       int num_experts, int top_k, const float* x_dev, const float* logits_dev,
+                                       int64_t T, float* out_dev, int32_t* selected_dev, void* stream);
+/* Same with host buffers, synchronous. */
+BRAMHA_API int bramha_cuda_moe_mlp(bramha_ctx* ctx, const bramha_weight* gate_up, const bramha_weight* down,
+                                   int num_experts, int top_k, const float* x_host, const float* logits_host,
+                                   int64_t T, float* out_host, int32_t* selected_host);
+
 /* ------------------------------------------------------- prefill GEMM path */
 
 /* gemm_cpu (cpu_engine.rs:565-912): out[m][j] = sum_i h[m][i] * dq(w[j][i]),
