@@ -398,6 +398,90 @@ def sparse24_bench(plane, dev, layers=4, reps=5):
     return out
 
 
+# ------------------------------------------------------------------ MoE (config 5)
+def moe_bench(plane, dev, tokens=256, experts=64, top_k=8, hidden=3584, inter=2560, reps=10, cpu_tokens=8):
+    """the MoE expert MLP of `tokens` decode tokens, 64
+    SwiGLU experts (hidden 3584, intermediate 2560) in log4 from ~N(0,0.02),
+    top-8 routing from softmax of seeded N(0,1) logits, one GPU.  One call =
+    routing, gather, grouped gate+up GEMM, SiLU*up, grouped down GEMM,
+    combine (bramha_cuda_moe_mlp_dev), timed with CUDA events over `reps`
+    calls.  Algorithmic bytes = the distinct experts touched x 3*H*I/2 (+ their
+    scales) + x, logits and out."""
+    import torch
+    import oracle
+    hbm, kind = load_peaks()
+    E, H, I, T, k = experts, hidden, inter, tokens, top_k
+    gen = torch.Generator(device=dev).manual_seed(55)
+    gu_q = torch.empty(E * 2 * I * H // 2, dtype=torch.uint8, device=dev)
+    gu_s = torch.empty(E * 2 * I, dtype=torch.float32, device=dev)
+    dn_q = torch.empty(E * H * I // 2, dtype=torch.uint8, device=dev)
+    dn_s = torch.empty(E * H, dtype=torch.float32, device=dev)
+    for e in range(E):
+        wf = torch.randn((2 * I, H), generator=gen, device=dev) * 0.02
+        plane.quantize_dev("log4", wf, gu_q[e * I * H:(e + 1) * I * H], gu_s[e * 2 * I:(e + 1) * 2 * I])
+        wf = torch.randn((H, I), generator=gen, device=dev) * 0.02
+        plane.quantize_dev("log4", wf, dn_q[e * H * I // 2:(e + 1) * H * I // 2], dn_s[e * H:(e + 1) * H])
+    del wf
+    gu = plane.register_dev("moeb:gate_up", "log4", E * 2 * I, H, gu_q, gu_s)
+    dn = plane.register_dev("moeb:down", "log4", E * H, I, dn_q, dn_s)
+    x = torch.randn((T, H), generator=gen, device=dev)
+    lg = torch.randn((T, E), generator=gen, device=dev)
+    out = torch.empty((T, H), device=dev)
+    sel = torch.empty((T, k), dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            plane.moe_mlp_dev(gu, dn, E, k, x, lg, out, sel)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            plane.moe_mlp_dev(gu, dn, E, k, x, lg, out, sel)
+        e1.record()
+    torch.cuda.synchronize()
+    plane.stream_sync(stream)
+    ms = e0.elapsed_time(e1) / reps
+    touched = int(torch.unique(sel).numel())
+    per_expert = 3 * H * I // 2 + 4 * (2 * I + H)
+    nbytes = touched * per_expert + 4 * (2 * T * H + T * E)
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    # end to end through the host-buffer call
+    xh, lh = x.cpu().numpy(), lg.cpu().numpy()
+    plane.moe_mlp(gu, dn, E, k, xh, lh)
+    t0 = time.perf_counter()
+    n_e2e = 5
+    for _ in range(n_e2e):
+        plane.moe_mlp(gu, dn, E, k, xh, lh)
+    e2e_s = (time.perf_counter() - t0) / n_e2e
+    res = {"workload": f"moe mlp: {T} tokens, {E} experts top-{k}, hidden {H}, intermediate {I}, log4, 1 GPU",
+           "us_per_call": round(ms * 1e3, 1), "tokens_per_s": round(T / (ms * 1e-3), 1),
+           "experts_touched": touched, "bytes_per_call": nbytes, "achieved_gbs": round(gbs, 1),
+           "peak_gbs": hbm, "frac": round(gbs / hbm, 4),
+           "peak_source": f"{kind} hbm_gbs" + (" (MEASURED_PEAKS.json)" if kind == "measured" else " (6.65 TB/s)"),
+           "timing": f"CUDA events over {reps} calls of bramha_cuda_moe_mlp_dev (eager; scratch from the pool)",
+           "e2e": {"tokens_per_s": round(T / e2e_s, 1), "api": "bramha_cuda_moe_mlp (host buffers, synchronous)",
+                   "h2d_bytes": 4 * (T * H + T * E), "d2h_bytes": 4 * (T * H + T * k)}}
+    # CPU: the oracle's restatement on a bounded sample of tokens, all host threads
+    gq, gs, dq, ds = gu_q.cpu().numpy(), gu_s.cpu().numpy(), dn_q.cpu().numpy(), dn_s.cpu().numpy()
+    # the oracle takes gate and up as separate stacks
+    g4 = gq.reshape(E, 2, I * H // 2)
+    s4 = gs.reshape(E, 2, I)
+    gate = (np.ascontiguousarray(g4[:, 0]).reshape(-1), np.ascontiguousarray(s4[:, 0]).reshape(-1))
+    up = (np.ascontiguousarray(g4[:, 1]).reshape(-1), np.ascontiguousarray(s4[:, 1]).reshape(-1))
+    threads = oracle.max_threads()
+    t0 = time.perf_counter()
+    ref, _, _ = oracle.moe_mlp("log4", xh[:cpu_tokens], lh[:cpu_tokens], k, gate, up, (dq, ds), threads=threads)
+    dt = time.perf_counter() - t0
+    res["cpu_baseline"] = {"tokens_per_s": round(cpu_tokens / dt, 2), "cores": threads, "kind": "port",
+                           "sample": f"{cpu_tokens} of the {T} tokens through the C restatement of run_mlp_into's "
+                                     "MoE branch (cpu_engine.rs:1799-1989), OpenMP over tokens"}
+    gpu_out = out.cpu().numpy()[:cpu_tokens]
+    res["check_normwise_err_vs_cpu"] = float(np.max(np.abs(gpu_out - ref)) / np.max(np.abs(ref)))
+    plane.evict(gu.key)
+    plane.evict(dn.key)
+    return res
+
+
 # ------------------------------------------------------------------ decode step (config 2)
 def decode_step_bench(plane, dev, prompt_len=512, new_tokens=128):
     """a full Qwen2-0.5B-architecture decode step (24 layers,
@@ -700,6 +784,9 @@ def run_ours(args, ws, rank, local):
     decode_step = None
     if rank == 0 and ws == 1 and not args.no_decode_step:
         decode_step = decode_step_bench(plane, dev)
+    moe = None
+    if rank == 0 and ws == 1 and not args.no_moe:
+        moe = moe_bench(plane, dev, tokens=args.moe_tokens)
     sparse24 = None
     if rank == 0 and ws == 1 and not args.no_sparse:
         sparse24 = sparse24_bench(plane, dev, layers=args.sparse_layers)
@@ -739,6 +826,7 @@ def run_ours(args, ws, rank, local):
             "prefill": prefill,
             "decode_step": decode_step,
             "sparse24": sparse24,
+            "moe": moe,
             "setup_s": round(setup_s, 1),
         }
         print(json.dumps(line), flush=True)
@@ -767,7 +855,18 @@ def main():
     ap.add_argument("--sparse-only", action="store_true",
                     help="run only the 2:4 sparse GEMV measurement (profiling case) and print its JSON")
     ap.add_argument("--sparse-layers", type=int, default=4, help="layers of the 2:4 measurement")
+    ap.add_argument("--no-moe", action="store_true", help="skip the config-5 MoE measurement")
+    ap.add_argument("--moe-only", action="store_true", help="run only the config-5 MoE measurement and print its JSON")
+    ap.add_argument("--moe-tokens", type=int, default=256, help="tokens of the MoE measurement")
     args = ap.parse_args()
+    if args.moe_only:
+        import torch
+        from bramha_b200 import CudaComputePlane
+        torch.cuda.set_device(0)
+        plane = CudaComputePlane(0)
+        print(json.dumps({"moe": moe_bench(plane, torch.device("cuda", 0), tokens=args.moe_tokens)}))
+        plane.close()
+        return
     if args.sparse_only:
         import torch
         from bramha_b200 import CudaComputePlane

@@ -8,9 +8,10 @@
 // batch are grouped by expert so each expert's weights are streamed once for
 // all the tokens routed to it:
 //
-//   moe_route_kernel   one CTA: probabilities, top-k per token, per-expert
-//                      token lists (token order), row offsets, and the tile
-//                      tables of the two grouped GEMMs;
+//   moe_route_kernel   one warp per token: probabilities, top-k, per-expert
+//                      row counts;
+//   moe_place_kernel   one CTA per expert: its row offset, its rows in token
+//                      order, and its tiles of the two grouped GEMMs;
 //   moe_gather_kernel  activations of the routed (token, expert) pairs, in
 //                      expert order;
 //   grouped GEMM       gate and up of every expert in one launch (weights
@@ -28,8 +29,6 @@
 namespace bramha {
 namespace {
 
-constexpr int kRouteThreads = 1024;
-
 struct Route {
     float* probs;   // [T][E]
     int* sel_e;     // [T][k] r-th expert of the sorted order
@@ -43,94 +42,126 @@ struct Route {
     int* ntiles;    // [2] entries of the two tables
 };
 
-// Probabilities and top-k of every token, then the per-expert grouping.
-__global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const float* __restrict__ logits, int T, int E,
-                                                                  int k, int nblk_gu, int nblk_dn, Route r,
-                                                                  int32_t* selected) {
-    extern __shared__ int sm[];
-    int* sel = sm;                // [T*k] expert of each choice, -1 when skipped
-    int* tg = sel + T * k;        // [E] first gate+up tile of each expert
-    int* td = tg + E;             // [E] first down tile of each expert
-    const int nk = T * k;
-
-    // softmax (sequential per token, as the reference) and the stable order
-    for (int t = threadIdx.x; t < T; t += blockDim.x) {
-        const float* lg = logits + (int64_t)t * E;
-        float* p = r.probs + (int64_t)t * E;
-        float mx = -INFINITY;
-        for (int i = 0; i < E; ++i) mx = fmaxf(mx, lg[i]);
-        float sum = 0.f;
-        for (int i = 0; i < E; ++i) {
-            p[i] = expf(lg[i] - mx);
-            sum = __fadd_rn(sum, p[i]);
-        }
-        for (int i = 0; i < E; ++i) p[i] = sum > 0.f ? __fdiv_rn(p[i], sum) : 0.f;
-        // the r-th element of a stable descending sort: the largest probability
-        // after the previous pick in the order (probability desc, index asc)
-        float pp = INFINITY;
-        int pi = -1;
-        for (int j = 0; j < k; ++j) {
-            int best = -1;
-            float bp = -INFINITY;
-            for (int i = 0; i < E; ++i) {
-                const float v = p[i];
-                const bool after = v < pp || (v == pp && i > pi);
-                if (after && (best < 0 || v > bp)) {
-                    best = i;
-                    bp = v;
-                }
+// One warp per token: softmax of the router logits (max by a shuffle fold --
+// exact in any order -- and the sum of the exponentials added sequentially by
+// lane 0, as the reference does), then the first k of the stable descending
+// order, one warp argmax per rank (largest probability after the previous pick;
+// equal probabilities keep the lower expert first).  Counts the rows of each
+// expert (atomic increments: the totals do not depend on their order).
+__global__ void moe_route_kernel(const float* __restrict__ logits, int T, int E, int k, Route r,
+                                 int32_t* selected) {
+    extern __shared__ float sp[];  // [warps][E] probabilities
+    const int wpb = blockDim.x >> 5, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * wpb + w;
+    if (t >= T) return;
+    float* p = sp + w * E;
+    const float* lg = logits + (int64_t)t * E;
+    float mx = -INFINITY;
+    for (int i = lane; i < E; i += 32) mx = fmaxf(mx, lg[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int i = lane; i < E; i += 32) p[i] = expf(lg[i] - mx);
+    __syncwarp();
+    float sum = 0.f;
+    if (lane == 0)
+        for (int i = 0; i < E; ++i) sum = __fadd_rn(sum, p[i]);
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+    for (int i = lane; i < E; i += 32) p[i] = sum > 0.f ? __fdiv_rn(p[i], sum) : 0.f;
+    __syncwarp();
+    float pp = INFINITY;
+    int pi = -1;
+    for (int j = 0; j < k; ++j) {
+        float bp = -INFINITY;
+        int best = 0x7fffffff;
+        for (int i = lane; i < E; i += 32) {
+            const float v = p[i];
+            if ((v < pp || (v == pp && i > pi)) && (v > bp || (v == bp && i < best))) {
+                bp = v;
+                best = i;
             }
-            pp = bp;
-            pi = best;
-            r.sel_e[t * k + j] = best;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bp, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, best, o);
+            if (ov > bp || (ov == bp && oi < best)) {
+                bp = ov;
+                best = oi;
+            }
+        }
+        pp = bp;
+        pi = best;
+        if (lane == 0) {
+            r.sel_e[t * k + j] = bp > 0.f ? best : -1;
             r.sel_w[t * k + j] = bp;
             r.slot[t * k + j] = -1;
-            sel[t * k + j] = bp > 0.f ? best : -1;
             if (selected) selected[t * k + j] = best;
+            if (bp > 0.f) atomicAdd(r.cnt + best, 1);
         }
     }
-    __syncthreads();
-    // rows per expert
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        int c = 0;
-        for (int i = 0; i < nk; ++i) c += sel[i] == e;
-        r.cnt[e] = c;
+}
+
+// One block per expert: its first row (the counts of the experts before it),
+// its rows in token order (a block-wide ordered scan over the choices), and
+// its tiles of the two grouped GEMMs.  Block 0 also writes the totals.
+__global__ void moe_place_kernel(int T, int E, int k, int nblk_gu, int nblk_dn, Route r) {
+    __shared__ int warp_sum[32];
+    __shared__ int s_base;
+    const int e = blockIdx.x, nk = T * k;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int o = 0, tiles_before = 0;
+    for (int i = 0; i < e; ++i) {  // uniform over the block: counts are final
+        const int c = __ldg(r.cnt + i);
+        o += c;
+        tiles_before += (c + kGemmGroupTok - 1) / kGemmGroupTok;
     }
-    __syncthreads();
+    const int c = __ldg(r.cnt + e);
     if (threadIdx.x == 0) {
-        int o = 0, a = 0, b = 0;
-        for (int e = 0; e < E; ++e) {
-            r.off[e] = o;
-            tg[e] = a;
-            td[e] = b;
-            const int mt = (r.cnt[e] + kGemmGroupTok - 1) / kGemmGroupTok;
-            o += r.cnt[e];
-            a += mt * nblk_gu;
-            b += mt * nblk_dn;
+        r.off[e] = o;
+        s_base = o;
+        if (e == 0) {
+            int tot = 0, mt = 0;
+            for (int i = 0; i < E; ++i) {
+                const int ci = __ldg(r.cnt + i);
+                tot += ci;
+                mt += (ci + kGemmGroupTok - 1) / kGemmGroupTok;
+            }
+            r.off[E] = tot;
+            r.ntiles[0] = mt * nblk_gu;
+            r.ntiles[1] = mt * nblk_dn;
         }
-        r.off[E] = o;
-        r.ntiles[0] = a;
-        r.ntiles[1] = b;
     }
     __syncthreads();
-    // rows of each expert in token order, and its tiles
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        const int o = r.off[e], c = r.cnt[e];
-        int s = o;
-        for (int i = 0; i < nk; ++i)
-            if (sel[i] == e) {
-                r.slot[i] = s;
-                r.tok[s] = i / k;
-                ++s;
-            }
-        const int mt = (c + kGemmGroupTok - 1) / kGemmGroupTok;
-        for (int m = 0; m < mt; ++m) {
-            const int tok0 = o + m * kGemmGroupTok, mc = min(kGemmGroupTok, c - m * kGemmGroupTok);
-            for (int nb = 0; nb < nblk_gu; ++nb)
-                r.tiles_gu[tg[e] + m * nblk_gu + nb] = make_int4(e * nblk_gu + nb, tok0, mc, nb * 128);
-            for (int nb = 0; nb < nblk_dn; ++nb)
-                r.tiles_dn[td[e] + m * nblk_dn + nb] = make_int4(e * nblk_dn + nb, tok0, mc, nb * 128);
+    // ordered placement, one chunk of blockDim.x choices at a time
+    for (int i0 = 0; i0 < nk; i0 += blockDim.x) {
+        const int i = i0 + threadIdx.x;
+        const bool mine = i < nk && __ldg(r.sel_e + i) == e;
+        const unsigned bal = __ballot_sync(0xffffffffu, mine);
+        if (lane == 0) warp_sum[w] = __popc(bal);
+        __syncthreads();
+        int before = 0, total = 0;
+        for (int q = 0; q < nw; ++q) {
+            before += q < w ? warp_sum[q] : 0;
+            total += warp_sum[q];
         }
+        if (mine) {
+            const int s = s_base + before + __popc(bal & ((1u << lane) - 1u));
+            r.slot[i] = s;
+            r.tok[s] = i / k;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) s_base += total;
+        __syncthreads();
+    }
+    const int mt = (c + kGemmGroupTok - 1) / kGemmGroupTok;
+    for (int q = threadIdx.x; q < mt * (nblk_gu + nblk_dn); q += blockDim.x) {
+        const int m = q / (nblk_gu + nblk_dn), nb = q % (nblk_gu + nblk_dn);
+        const int tok0 = o + m * kGemmGroupTok, mc = min(kGemmGroupTok, c - m * kGemmGroupTok);
+        if (nb < nblk_gu)
+            r.tiles_gu[tiles_before * nblk_gu + m * nblk_gu + nb] = make_int4(e * nblk_gu + nb, tok0, mc, nb * 128);
+        else
+            r.tiles_dn[tiles_before * nblk_dn + m * nblk_dn + (nb - nblk_gu)] =
+                make_int4(e * nblk_dn + nb - nblk_gu, tok0, mc, (nb - nblk_gu) * 128);
     }
 }
 
@@ -215,11 +246,18 @@ cudaError_t launch_moe_mlp(const MoeWeights& w, int top_k, const float* x, const
     float* act = carve<float>(p, rows * I);
     float* y2 = carve<float>(p, rows * H);
 
-    const size_t smem = (size_t)(rows + 2 * E) * sizeof(int);
-    if (smem > 48 * 1024) e = cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   (int)smem);
+    const int wpb = 8;  // tokens per routing block
+    const size_t smem = (size_t)wpb * E * sizeof(float);
+    e = cudaMemsetAsync(r.cnt, 0, (size_t)E * sizeof(int), st);
+    if (e == cudaSuccess && smem > 48 * 1024)
+        e = cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess) {
-        moe_route_kernel<<<1, kRouteThreads, smem, st>>>(logits, (int)T, (int)E, k, nblk_gu, nblk_dn, r, selected);
+        moe_route_kernel<<<(unsigned)((T + wpb - 1) / wpb), 32 * wpb, smem, st>>>(logits, (int)T, (int)E, k, r,
+                                                                                 selected);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) {
+        moe_place_kernel<<<(unsigned)E, 256, 0, st>>>((int)T, (int)E, k, nblk_gu, nblk_dn, r);
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) {
