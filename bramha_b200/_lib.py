@@ -69,6 +69,8 @@ _SIGNATURES = {
                                                  ctypes.c_char_p, _vp],
     "bramha_cuda_moe_mlp_dev": [_vp, _vp, _vp, _int, _int, _vp, _vp, _i64, _vp, _vp, _vp],
     "bramha_cuda_moe_mlp": [_vp, _vp, _vp, _int, _int, _vp, _vp, _i64, _vp, _vp],
+    "bramha_cuda_moe_route_dev": [_vp, _vp, _i64, _int, _int, _vp, _vp, _vp],
+    "bramha_cuda_moe_experts_dev": [_vp, _vp, _vp, _int, _vp, _vp, _i64, _vp, _vp],
     "bramha_cuda_gemm": [_vp, _vp, _vp, _i64, _vp],
     "bramha_cuda_gemm_dev": [_vp, _vp, _vp, _int, _i64, _vp, _vp],
     "bramha_cuda_quantize_dev": [_vp, _int, _i64, _i64, _vp, _vp, _vp, _vp],

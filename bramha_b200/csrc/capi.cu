@@ -998,6 +998,34 @@ int bramha_cuda_moe_mlp_dev(bramha_ctx* ctx, const bramha_weight* gate_up, const
     return BRAMHA_OK;
 }
 
+int bramha_cuda_moe_route_dev(bramha_ctx* ctx, const float* logits_dev, int64_t T, int num_experts, int top_k,
+                              int32_t* ids_dev, float* weights_dev, void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (num_experts <= 0 || num_experts > kMoeMaxExperts || top_k <= 0 || T < 0)
+        return fail(BRAMHA_ERR_INVALID, "moe_route: bad num_experts, top_k or T");
+    if (T == 0) return BRAMHA_OK;
+    if (!logits_dev || !ids_dev || !weights_dev) return fail(BRAMHA_ERR_INVALID, "null device pointer");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    CK(launch_moe_route(logits_dev, T, num_experts, top_k, ids_dev, weights_dev, st), "moe route launch");
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_moe_experts_dev(bramha_ctx* ctx, const bramha_weight* gate_up, const bramha_weight* down,
+                                int num_experts, const float* x_dev, const int32_t* ids_dev, int64_t R, float* y_dev,
+                                void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    MoeWeights mw;
+    int rc = moe_check(ctx, gate_up, down, num_experts, 1, R, &mw);
+    if (rc) return rc;
+    if (R == 0) return BRAMHA_OK;
+    if (!x_dev || !ids_dev || !y_dev) return fail(BRAMHA_ERR_INVALID, "null device pointer");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    CK(launch_moe_experts(mw, x_dev, ids_dev, R, y_dev, ctx->d_err, st), "moe experts launch");
+    return BRAMHA_OK;
+}
+
 int bramha_cuda_moe_mlp(bramha_ctx* ctx, const bramha_weight* gate_up, const bramha_weight* down, int num_experts,
                         int top_k, const float* x_host, const float* logits_host, int64_t T, float* out_host,
                         int32_t* selected_host) {

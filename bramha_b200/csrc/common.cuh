@@ -189,6 +189,12 @@ struct MoeWeights {
 };
 cudaError_t launch_moe_mlp(const MoeWeights& w, int top_k, const float* x, const float* logits, int64_t T, float* out,
                            int32_t* selected, int* err, cudaStream_t stream);
+// Expert outputs of rows routed by the caller (ids[r] in [0, E); others give 0),
+// and the routing alone (sorted expert ids and probabilities, [T][min(k, E)]).
+cudaError_t launch_moe_experts(const MoeWeights& w, const float* x, const int32_t* ids, int64_t R, float* y, int* err,
+                               cudaStream_t stream);
+cudaError_t launch_moe_route(const float* logits, int64_t T, int64_t E, int top_k, int32_t* ids, float* weights,
+                             cudaStream_t stream);
 constexpr int64_t kMoeMaxAssignments = 16384;  // T * top_k per call (routing state in shared memory)
 constexpr int64_t kMoeMaxExperts = 1024;
 

@@ -101,6 +101,19 @@ __global__ void moe_route_kernel(const float* __restrict__ logits, int T, int E,
     }
 }
 
+// Routing given by the caller: row t goes to expert ids[t] (weight 1; an id
+// outside [0, E) drops the row, whose output is then 0).
+__global__ void moe_given_route_kernel(const int32_t* __restrict__ ids, int T, int E, Route r) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    const int e = ids[t];
+    const bool ok = e >= 0 && e < E;
+    r.sel_e[t] = ok ? e : -1;
+    r.sel_w[t] = ok ? 1.f : 0.f;
+    r.slot[t] = -1;
+    if (ok) atomicAdd(r.cnt + e, 1);
+}
+
 // One block per expert: its first row (the counts of the experts before it),
 // its rows in token order (a block-wide ordered scan over the choices), and
 // its tiles of the two grouped GEMMs.  Block 0 also writes the totals.
@@ -208,10 +221,54 @@ T* carve(uint8_t*& p, int64_t n) {
     return r;
 }
 
+cudaError_t launch_moe(const MoeWeights& w, int top_k, const float* x, const float* logits, const int32_t* given,
+                       int64_t T, float* out, int32_t* selected, int* err, cudaStream_t st);
+
 }  // namespace
 
 cudaError_t launch_moe_mlp(const MoeWeights& w, int top_k, const float* x, const float* logits, int64_t T, float* out,
                            int32_t* selected, int* err, cudaStream_t st) {
+    return launch_moe(w, top_k, x, logits, nullptr, T, out, selected, err, st);
+}
+
+cudaError_t launch_moe_experts(const MoeWeights& w, const float* x, const int32_t* ids, int64_t R, float* y, int* err,
+                               cudaStream_t st) {
+    return launch_moe(w, 1, x, nullptr, ids, R, y, nullptr, err, st);
+}
+
+cudaError_t launch_moe_route(const float* logits, int64_t T, int64_t E, int top_k, int32_t* ids, float* weights,
+                             cudaStream_t st) {
+    const int k = (int)(top_k < E ? top_k : E);
+    if (T <= 0) return cudaSuccess;
+    if (E <= 0 || E > kMoeMaxExperts || k <= 0) return cudaErrorInvalidValue;
+    uint8_t* base = nullptr;
+    const int64_t bytes = (T * k * 2 * 4 + 255) / 256 * 256 + (E * 4 + 255) / 256 * 256;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&base), (size_t)bytes, st);
+    if (e != cudaSuccess) return e;
+    uint8_t* p = base;
+    Route r{};
+    r.sel_e = carve<int>(p, T * k);
+    r.slot = carve<int>(p, T * k);
+    r.cnt = carve<int>(p, E);
+    r.sel_w = weights;
+    const int wpb = 8;
+    const size_t smem = (size_t)wpb * E * sizeof(float);
+    e = cudaMemsetAsync(r.cnt, 0, (size_t)E * sizeof(int), st);
+    if (e == cudaSuccess && smem > 48 * 1024)
+        e = cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) {
+        moe_route_kernel<<<(unsigned)((T + wpb - 1) / wpb), 32 * wpb, smem, st>>>(logits, (int)T, (int)E, k, r, ids);
+        e = cudaGetLastError();
+    }
+    cudaError_t e2 = cudaFreeAsync(base, st);
+    return e == cudaSuccess ? e2 : e;
+}
+
+namespace {
+// The whole layer; with `given` (one expert id per row, k = 1) the routing is
+// the caller's and out[t] is that expert's output.
+cudaError_t launch_moe(const MoeWeights& w, int top_k, const float* x, const float* logits, const int32_t* given,
+                       int64_t T, float* out, int32_t* selected, int* err, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     const int64_t E = w.E, H = w.H, I = w.I;
     const int k = (int)(top_k < E ? top_k : E);
@@ -252,8 +309,11 @@ cudaError_t launch_moe_mlp(const MoeWeights& w, int top_k, const float* x, const
     if (e == cudaSuccess && smem > 48 * 1024)
         e = cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess) {
-        moe_route_kernel<<<(unsigned)((T + wpb - 1) / wpb), 32 * wpb, smem, st>>>(logits, (int)T, (int)E, k, r,
-                                                                                 selected);
+        if (given)
+            moe_given_route_kernel<<<(unsigned)((T + 255) / 256), 256, 0, st>>>(given, (int)T, (int)E, r);
+        else
+            moe_route_kernel<<<(unsigned)((T + wpb - 1) / wpb), 32 * wpb, smem, st>>>(logits, (int)T, (int)E, k, r,
+                                                                                     selected);
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) {
@@ -285,5 +345,7 @@ cudaError_t launch_moe_mlp(const MoeWeights& w, int top_k, const float* x, const
     cudaError_t e2 = cudaFreeAsync(base, st);
     return e == cudaSuccess ? e2 : e;
 }
+
+}  // namespace
 
 }  // namespace bramha

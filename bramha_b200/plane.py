@@ -203,6 +203,17 @@ class CudaComputePlane:
                                             logits.data_ptr(), x.shape[0], out.data_ptr(),
                                             None if selected is None else selected.data_ptr(), _stream(stream)))
 
+    def moe_route_dev(self, logits, top_k: int, ids, weights, stream=None):
+        """Routing alone: logits [T][E] -> ids [T][k] int32, weights [T][k] f32 (CUDA tensors)."""
+        T, E = logits.shape
+        check(lib().bramha_cuda_moe_route_dev(self._ctx, logits.data_ptr(), T, E, top_k, ids.data_ptr(),
+                                              weights.data_ptr(), _stream(stream)))
+
+    def moe_experts_dev(self, gate_up: Weight, down: Weight, num_experts: int, x, ids, y, stream=None):
+        """y[r] = expert ids[r]'s SwiGLU MLP of x[r] (CUDA tensors, x/y [R][H], ids [R] int32)."""
+        check(lib().bramha_cuda_moe_experts_dev(self._ctx, gate_up.handle, down.handle, num_experts, x.data_ptr(),
+                                                ids.data_ptr(), x.shape[0], y.data_ptr(), _stream(stream)))
+
     def lookup(self, key: str) -> Weight:
         h = _vp()
         check(lib().bramha_cuda_lookup_weight(self._ctx, key.encode(), ctypes.byref(h)))

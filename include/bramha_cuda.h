@@ -254,6 +254,22 @@ BRAMHA_API int bramha_cuda_sparse_matvec_2_4_compressed(bramha_ctx* ctx, const f
 BRAMHA_API int bramha_cuda_moe_mlp_dev(bramha_ctx* ctx, const bramha_weight* gate_up, const bramha_weight* down,
                                        int num_experts, int top_k, const float* x_dev, const float* logits_dev,
                                        int64_t T, float* out_dev, int32_t* selected_dev, void* stream);
+/* The two halves of that layer for expert parallelism, where the experts of a
+ * layer are spread over several GPUs and each token's activation is sent to the
+ * GPUs holding its experts:
+ *  - moe_route_dev: the routing alone -- ids [T][min(top_k, E)] (int32) and
+ *    weights (the probabilities, f32) of the first top_k experts of the stable
+ *    descending order, as above; a weight <= 0 means the expert is skipped;
+ *  - moe_experts_dev: y[r] = down_e(silu(gate_e x[r]) * up_e x[r]) for e =
+ *    ids[r] (int32, an index into the E experts of the given weights; a row
+ *    with an id outside [0, E) gives 0), x and y [R][H], R <= 16384.
+ * Combining sum_j weight[t][j] * y(t, j) in j order (one rounding per product
+ * and per sum, starting from 0) reproduces bramha_cuda_moe_mlp_dev. */
+BRAMHA_API int bramha_cuda_moe_route_dev(bramha_ctx* ctx, const float* logits_dev, int64_t T, int num_experts,
+                                         int top_k, int32_t* ids_dev, float* weights_dev, void* stream);
+BRAMHA_API int bramha_cuda_moe_experts_dev(bramha_ctx* ctx, const bramha_weight* gate_up, const bramha_weight* down,
+                                           int num_experts, const float* x_dev, const int32_t* ids_dev, int64_t R,
+                                           float* y_dev, void* stream);
 /* Same with host buffers, synchronous. */
 BRAMHA_API int bramha_cuda_moe_mlp(bramha_ctx* ctx, const bramha_weight* gate_up, const bramha_weight* down,
                                    int num_experts, int top_k, const float* x_host, const float* logits_host,
