@@ -67,6 +67,12 @@ struct GemmArgs {
     // first output column) -- and N is the row count of one group.
     const int4* tiles;
     const int* ntiles_dev;
+    // Split in N (grouped mode): nonzero = the X copy holds the bf16 hi parts of
+    // the M token rows at rows [0, M) and the lo parts at rows [lo_row,
+    // lo_row + M); a tile carries BN/2 tokens, its hi rows in MMA columns
+    // [0, BN/2) and its lo rows in [BN/2, BN), and the epilogue adds the two.
+    // One pass over K: each weight block is loaded and dequantized once.
+    int lo_row;
 };
 
 // One output tile: 128-row block `wblk` of the (stacked) weight, token rows
@@ -226,7 +232,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     mbar_expect_tx(&full_tma[s], kTx);
-                    tma_load_2d(Xs + s * L::kX, &tmX, &full_tma[s], kx * BK, ti.tok0);
+                    if (a.lo_row) {  // hi and lo rows of the tile's tokens, one half slot each
+                        tma_load_2d(Xs + s * L::kX, &tmX, &full_tma[s], kx * BK, ti.tok0);
+                        tma_load_2d(Xs + s * L::kX + L::kX / 2, &tmX, &full_tma[s], kx * BK, a.lo_row + ti.tok0);
+                    } else {
+                        tma_load_2d(Xs + s * L::kX, &tmX, &full_tma[s], kx * BK, ti.tok0);
+                    }
                     const int kw = kx < a.k_steps ? kx : kx - a.k_steps;
                     bulk_load(Ps + s * L::kP, wsrc + (int64_t)kw * L::kP, L::kP, &full_tma[s]);
                 }
@@ -327,7 +338,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool row_ok = grow < a.N;
             // a tile inside the matrix stores without per-element bounds checks
             // (a conditional store per element costs ~4x in issue)
-            const bool full = ti.col0 + BM <= a.N && mc == BN;
+            const int ntok = a.lo_row ? BN / 2 : BN;  // tokens per tile
+            const bool full = ti.col0 + BM <= a.N && mc == ntok;
             const float sc = row_ok ? __ldg(a.scales + (int64_t)ti.wblk * BM + row) : 0.f;
             float* ycol = a.y + grow;
             const uint32_t taddr = tmem + (uint32_t)(buf * BN) + ((uint32_t)(q4 * 32) << 16);
@@ -335,18 +347,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             float rs_next = 0.f;
             if constexpr (FMT == BRAMHA_FMT_LOG4) rs_next = lane < mc ? __ldg(a.rowsum + m0 + lane) : 0.f;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+            for (int c0 = 0; c0 < ntok; c0 += 32) {
                 const float rs = rs_next;
                 if constexpr (FMT == BRAMHA_FMT_LOG4) {
                     const int tl = c0 + 32 + lane;
-                    if (c0 + 32 < BN) rs_next = tl < mc ? __ldg(a.rowsum + m0 + tl) : 0.f;
+                    if (c0 + 32 < ntok) rs_next = tl < mc ? __ldg(a.rowsum + m0 + tl) : 0.f;
                 }
                 uint32_t v[32];
                 tmem_ld32(taddr + c0, v);
                 float o[32];
 #pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] = __uint_as_float(v[j]);
+                if (a.lo_row) {  // + the lo parts' accumulator (warp-uniform)
+                    tmem_ld32(taddr + (uint32_t)(BN / 2) + c0, v);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) o[j] += __uint_as_float(v[j]);
+                }
+#pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    o[j] = __uint_as_float(v[j]);
                     if constexpr (FMT == BRAMHA_FMT_LOG4) o[j] = fmaf(o[j], 32768.0f, -__shfl_sync(0xffffffffu, rs, j));
                     o[j] *= sc;
                 }
@@ -650,12 +668,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<FMT>::kTh
 // exactly the values the MMA sees.  From f32 the activation is split
 // x = hi + lo (hi = bf16(x), lo = bf16(x - hi)); hi fills columns [0, kp) and
 // lo columns [kp, 2 kp) of the copy, so one pass over 2 kp reproduces x to ~2^-16.
-template <bool FROM_F32>
+// With ROWS (f32 only), lo goes to row M + r of a [2M][kp] copy instead.
+template <bool FROM_F32, bool ROWS = false>
 __global__ void prep_kernel(const void* __restrict__ x, int64_t ldx, int M, int K, int64_t kp,
                             __nv_bfloat16* __restrict__ xc, float* __restrict__ rs) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= M) return;
-    const int64_t ldc = FROM_F32 ? 2 * kp : kp;
+    const int64_t ldc = FROM_F32 && !ROWS ? 2 * kp : kp;
+    const int64_t lo_off = ROWS ? (int64_t)M * kp : kp;
     float sh = 0.f, sl = 0.f;
     for (int k = lane; k < (int)kp; k += 32) {
         float h = 0.f, l = 0.f;
@@ -670,7 +690,7 @@ __global__ void prep_kernel(const void* __restrict__ x, int64_t ldx, int M, int 
         }
         if (xc) {
             xc[(int64_t)warp * ldc + k] = __float2bfloat16_rn(h);
-            if constexpr (FROM_F32) xc[(int64_t)warp * ldc + kp + k] = __float2bfloat16_rn(l);
+            if constexpr (FROM_F32) xc[(int64_t)warp * ldc + lo_off + k] = __float2bfloat16_rn(l);
         }
         sh += h;
         sl += l;
@@ -846,6 +866,7 @@ cudaError_t gemm_args(GemmArgs* g, const uint8_t* q, const float* scales, const 
     g->err = err;
     g->tiles = nullptr;
     g->ntiles_dev = nullptr;
+    g->lo_row = 0;
     return cudaSuccess;
 }
 }  // namespace
@@ -915,8 +936,7 @@ cudaError_t launch_gemm_tcgen05_grouped(int fmt, const uint8_t* q, const float* 
     if (!encode_fn()) return cudaErrorNotSupported;
     const int64_t kp = (K + BK - 1) / BK * BK;
     const bool log4 = fmt == BRAMHA_FMT_LOG4;
-    const int64_t cols = 2 * kp;
-    const size_t copy_bytes = (size_t)M * cols * sizeof(__nv_bfloat16);
+    const size_t copy_bytes = (size_t)2 * M * kp * sizeof(__nv_bfloat16);  // hi rows, then lo rows
     const size_t bytes = copy_bytes + (log4 ? (size_t)M * sizeof(float) : 0);
     uint8_t* scratch = nullptr;
     cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), bytes, st);
@@ -924,19 +944,22 @@ cudaError_t launch_gemm_tcgen05_grouped(int fmt, const uint8_t* q, const float* 
     __nv_bfloat16* xc = reinterpret_cast<__nv_bfloat16*>(scratch);
     float* rs = log4 ? reinterpret_cast<float*>(scratch + copy_bytes) : nullptr;
     const int wpb = 8;
-    prep_kernel<true><<<(unsigned)((M + wpb - 1) / wpb), 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
+    prep_kernel<true, true><<<(unsigned)((M + wpb - 1) / wpb), 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc,
+                                                                                  rs);
     e = cudaGetLastError();
     GemmArgs g;
     CUtensorMap tmX;
-    if (e == cudaSuccess) e = gemm_args(&g, q, scales, rs, y, ldy, M, N_group, K, true, kGemmGroupTok, err);
+    constexpr int bn = 2 * kGemmGroupTok;  // MMA N: the tile's hi and lo rows
+    if (e == cudaSuccess) e = gemm_args(&g, q, scales, rs, y, ldy, M, N_group, K, false, bn, err);
     if (e == cudaSuccess) {
         g.tiles = tiles;
         g.ntiles_dev = ntiles_dev;
         g.n_tiles = (int)max_tiles;  // with a table, only the grid size reads these
         g.m_tiles = 1;
-        e = make_x_map(&tmX, xc, cols, M, cols, kGemmGroupTok);
+        g.lo_row = (int)M;
+        e = make_x_map(&tmX, xc, kp, 2 * M, kp, kGemmGroupTok);
     }
-    if (e == cudaSuccess) e = run_gemm(fmt, kGemmGroupTok, tmX, g, st);
+    if (e == cudaSuccess) e = run_gemm(fmt, bn, tmX, g, st);
     cudaError_t e2 = cudaFreeAsync(scratch, st);
     return e == cudaSuccess ? e2 : e;
 }
