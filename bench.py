@@ -542,7 +542,7 @@ def decode_step_bench(plane, dev, prompt_len=512, new_tokens=128):
             plane.gemv_multi_dev([lw.q, lw.k, lw.v], dm.h, [dm.q, dm.k, dm.v], stream=dm.stream)
             plane.gemv_multi_dev([lw.o], dm.attn, [dm.o], stream=dm.stream)
             plane.gemv_multi_dev([lw.gate, lw.up], dm.h, [dm.g, dm.u], stream=dm.stream)
-            plane.gemv_multi_dev([lw.down], dm.m, [dm.d], stream=dm.stream)
+            plane.gemv_swiglu_dev(lw.down, dm.g, dm.u, dm.d, stream=dm.stream)
         plane.gemv_multi_dev([dm.lm_head], dm.h, [dm.logits], stream=dm.stream)
     reps = 20
     with torch.cuda.stream(dm.stream):

@@ -446,8 +446,9 @@ int check_weight(const bramha_ctx* ctx, const bramha_weight* w) {
 
 // Core device GEMV over several weights sharing x.  x must be 16-byte aligned
 // with row pitch ldx (a multiple of 4 floats when batch > 1).
+// x_up (optional, tensor-core formats only): the activation is silu(x) * x_up.
 int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const float* x, int64_t ldx,
-                int64_t batch, float* const* ys, cudaStream_t st) {
+                int64_t batch, float* const* ys, cudaStream_t st, const float* x_up = nullptr) {
     const int fmt = ws[0]->fmt;
     const int64_t K = ws[0]->K;
     if (batch <= 0) return BRAMHA_OK;
@@ -469,6 +470,7 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
         const int bc = (int)((batch - b0) < kMaxGemvBatch ? (batch - b0) : kMaxGemvBatch);
         GemvArgs a{};
         a.x = x + b0 * ldx;
+        a.x_up = x_up ? x_up + b0 * ldx : nullptr;
         a.ldx = ldx;
         // Columns the packed rows actually hold: with odd K a nibble row has
         // K/2 bytes and the last activation is ignored (cpu_engine.rs:1364).
@@ -494,9 +496,9 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
         a.split_ws_floats = kSplitWsFloats;
         a.split_tickets = ctx->split_tickets;
         a.split_tickets_n = kSplitTickets;
-        const bool cc = ctx->gemv_kernel == BRAMHA_GEMV_CUDA_CORE
-                            ? is_tiled(fmt) && a.batch == 1
-                            : ctx->gemv_kernel == BRAMHA_GEMV_AUTO && gemv_cc_eligible(fmt, a);
+        const bool cc = !x_up && (ctx->gemv_kernel == BRAMHA_GEMV_CUDA_CORE
+                                      ? is_tiled(fmt) && a.batch == 1
+                                      : ctx->gemv_kernel == BRAMHA_GEMV_AUTO && gemv_cc_eligible(fmt, a));
         if (cc)
             CK(launch_gemv_cc(fmt, a, ctx->num_sms, st), "cuda-core gemv launch");
         else if (is_tiled(fmt))
@@ -780,6 +782,28 @@ int bramha_cuda_gemv_multi_dev(bramha_ctx* ctx, int n_weights, const bramha_weig
     DeviceGuard g(ctx->device);
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
     return gemv_device(ctx, n_weights, ws, x_dev, K, batch, y_devs, st);
+}
+
+int bramha_cuda_gemv_swiglu_dev(bramha_ctx* ctx, const bramha_weight* w, const float* gate_dev, const float* up_dev,
+                                int64_t batch, float* y_dev, void* stream) {
+    int rc = check_weight(ctx, w);
+    if (rc) return rc;
+    if (!is_tiled(w->fmt))
+        return fail(BRAMHA_ERR_UNSUPPORTED, "gemv_swiglu_dev: %s weights are not supported (LOG4, W4ZP8, W8 only)",
+                    fmt_name(w->fmt));
+    if (batch < 0) return fail(BRAMHA_ERR_INVALID, "negative batch");
+    if (batch > 0 && w->K > 0) {
+        if (!gate_dev || !up_dev) return fail(BRAMHA_ERR_INVALID, "null input pointer");
+        if (((reinterpret_cast<uintptr_t>(gate_dev) | reinterpret_cast<uintptr_t>(up_dev)) & 15) != 0 ||
+            (batch > 1 && (w->K & 3) != 0))
+            return fail(BRAMHA_ERR_INVALID, "gate_dev / up_dev must be 16-byte aligned (and K a multiple of 4 when batch > 1)");
+    }
+    if (!y_dev && w->N > 0 && batch > 0) return fail(BRAMHA_ERR_INVALID, "null output pointer");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    const bramha_weight* ws[1] = {w};
+    float* ys[1] = {y_dev};
+    return gemv_device(ctx, 1, ws, gate_dev, w->K, batch, ys, st, up_dev);
 }
 
 int bramha_cuda_matvec(bramha_ctx* ctx, int fmt, const float* h, int64_t K, const void* q_weight, size_t q_bytes,

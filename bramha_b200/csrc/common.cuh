@@ -89,6 +89,9 @@ struct GemvArgs {
     GemvSeg seg[kMaxSegments];
     const float* x;        // [batch][ldx]
     int64_t ldx;
+    // Non-null: the activation is silu(x) * x_up (x_up [batch][ldx]), formed
+    // while the tensor-core GEMV stages it (the SwiGLU before a down projection).
+    const float* x_up;
     int nseg;
     int K;                 // activation length (columns covered by the packed row)
     int batch;

@@ -129,6 +129,7 @@ struct TcGemvParams {
     TcSeg seg[kMaxSegments];
     const float* x;        // [B][ldx] f32
     int64_t ldx;
+    const float* x_up;     // non-null: the activation is silu(x) * x_up
     int* err;
     int nseg;
     int ntiles;
@@ -423,6 +424,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
                 for (int u = 0; u < kPerThread; ++u) {
                     const int k = ta + u * kActThreads;
                     v[u] = k < kv ? __ldg(xr + k) : 0.f;
+                }
+                if (p.x_up) {  // SwiGLU: silu(g) * up, rounded as the separate silu_mul kernel rounds it
+                    const float* ur = p.x_up + (int64_t)b * p.ldx + k0;
+#pragma unroll
+                    for (int u = 0; u < kPerThread; ++u) {
+                        const int k = ta + u * kActThreads;
+                        if (k < kv) {
+                            const float g = v[u];
+                            const float silu = __fmul_rn(g, 1.0f / __fadd_rn(1.0f, expf(-g)));
+                            v[u] = __fmul_rn(silu, __ldg(ur + k));
+                        }
+                    }
                 }
                 float am = 0.f, sm = 0.f;
 #pragma unroll
@@ -790,6 +803,7 @@ cudaError_t launch_gemv_tc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t
     if (ntiles <= 0) return cudaErrorInvalidValue;
     p.x = a.x;
     p.ldx = a.ldx;
+    p.x_up = a.x_up;
     p.err = a.err;
     p.nseg = a.nseg;
     p.ntiles = ntiles;

@@ -26,6 +26,10 @@ from ._lib import check, lib
 from .plane import CudaComputePlane, Weight
 
 
+# formats whose down GEMV forms silu(gate) * up itself (bramha_cuda_gemv_swiglu_dev)
+_FUSED_SWIGLU = ("log4", "w4zp8", "w8")
+
+
 @dataclass
 class DecodeConfig:
     layers: int = 24
@@ -147,9 +151,12 @@ class DecodeModel:
             check(L.bramha_cuda_op_rmsnorm(ctx, self.x.data_ptr(), self.o.data_ptr(), lw.ln2.data_ptr(), c.hidden,
                                            c.eps, self.h.data_ptr(), st))
             P.gemv_multi_dev([lw.gate, lw.up], self.h, [self.g, self.u], stream=self.stream)
-            check(L.bramha_cuda_op_silu_mul(ctx, self.g.data_ptr(), self.u.data_ptr(), c.intermediate,
-                                            self.m.data_ptr(), st))
-            P.gemv_multi_dev([lw.down], self.m, [self.d], stream=self.stream)
+            if lw.down.fmt in _FUSED_SWIGLU:  # silu(g) * u formed by the down GEMV itself
+                P.gemv_swiglu_dev(lw.down, self.g, self.u, self.d, stream=self.stream)
+            else:
+                check(L.bramha_cuda_op_silu_mul(ctx, self.g.data_ptr(), self.u.data_ptr(), c.intermediate,
+                                                self.m.data_ptr(), st))
+                P.gemv_multi_dev([lw.down], self.m, [self.d], stream=self.stream)
             delta = self.d
         check(L.bramha_cuda_op_rmsnorm(ctx, self.x.data_ptr(), _p(delta), self.norm.data_ptr(), c.hidden, c.eps,
                                        self.h.data_ptr(), st))
@@ -160,8 +167,9 @@ class DecodeModel:
 
     def kernel_launches_per_step(self) -> int:
         """Launches of this library's kernels in one step: the embedding, per layer
-        4 GEMVs and 4 other kernels, then the final norm, lm_head and selection."""
-        return 1 + 8 * self.cfg.layers + 3
+        4 GEMVs and 3 other kernels (4 when the down weight is f32: a separate
+        SiLU), then the final norm, lm_head and selection."""
+        return 1 + sum(7 if lw.down.fmt in _FUSED_SWIGLU else 8 for lw in self.layers) + 3
 
     def step(self, greedy: bool = True):
         """One token: eagerly launched, or replayed from the captured graph."""

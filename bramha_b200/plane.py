@@ -291,6 +291,12 @@ class CudaComputePlane:
         check(lib().bramha_cuda_gemm_dev(self._ctx, w.handle, x.data_ptr(), dt, x.shape[0], y.data_ptr(),
                                          _stream(stream)))
 
+    def gemv_swiglu_dev(self, w: Weight, gate, up, y, stream=None):
+        """y = W (silu(gate) * up), one launch (CUDA f32 tensors [batch][K])."""
+        batch = 1 if gate.dim() == 1 else gate.shape[0]
+        check(lib().bramha_cuda_gemv_swiglu_dev(self._ctx, w.handle, gate.data_ptr(), up.data_ptr(), batch,
+                                                y.data_ptr(), _stream(stream)))
+
     GEMV_KERNELS = {"auto": 0, "tensor_core": 1, "cuda_core": 2}
 
     def set_gemv_kernel(self, kind: str = "auto"):

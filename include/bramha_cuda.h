@@ -165,6 +165,15 @@ BRAMHA_API int bramha_cuda_gemv_dev(bramha_ctx* ctx, const bramha_weight* w, con
 BRAMHA_API int bramha_cuda_gemv_multi_dev(bramha_ctx* ctx, int n_weights, const bramha_weight* const* ws,
                                const float* x_dev, int64_t batch, float* const* y_devs, void* stream);
 
+/* The down projection of a SwiGLU MLP in one launch: y[b] = W (silu(gate[b]) *
+ * up[b]) with silu(g) = g * (1 / (1 + exp(-g))), the activation formed while the
+ * tensor-core GEMV stages it (run_mlp_into's dense branch, cpu_engine.rs:
+ * 2023-2029, as bramha_cuda_op_silu_mul followed by bramha_cuda_gemv_dev, with
+ * the same rounding).  LOG4, W4ZP8 and W8 weights; gate and up [batch][K] f32,
+ * 16-byte aligned; y [batch][N]; stream-ordered. */
+BRAMHA_API int bramha_cuda_gemv_swiglu_dev(bramha_ctx* ctx, const bramha_weight* w, const float* gate_dev,
+                                           const float* up_dev, int64_t batch, float* y_dev, void* stream);
+
 /* The reference's keyed one-shot call, e.g.
  * `matvec_mul_int4(h, q_weight, scales, out_features, model_name, layer_name)`
  * (wgpu_backend.rs:1083-1091): when both names are non-NULL the weight is

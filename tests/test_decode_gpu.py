@@ -172,3 +172,33 @@ def test_rope_attention_fused_equals_two_kernels(plane):
     kcache[pos], vcache[pos] = kn, (v + bv).cpu().numpy()
     ref = oracle.attention(qn, kcache, vcache, pos + 1, nq, nkv, hd)
     assert normwise_err(o2.cpu().numpy(), ref) <= 1e-5
+
+
+@pytest.mark.parametrize("fmt", ["log4", "w4zp8", "w8"])
+def test_gemv_swiglu_equals_silu_then_gemv(plane, fmt):
+    """bramha_cuda_gemv_swiglu_dev == bramha_cuda_op_silu_mul then the GEMV, bit
+    for bit (the same rounding of silu(g) * up), at the 0.5B down shape and at a
+    7B-sized one, batch 1 and 3."""
+    from bramha_b200 import lib
+    from bramha_b200._lib import check
+    from tests._util import make_weight
+    dev = torch.device("cuda", 0)
+    for n, k in [(896, 4864), (3584, 18944)]:
+        _, q, s = make_weight(fmt, n, k, seed=n)
+        w = plane.register(f"swiglu:{fmt}:{n}", fmt, n, k, q, s)
+        for batch in (1, 3):
+            r = rng(batch)
+            g = torch.from_numpy(r.normal(0, 2, (batch, k)).astype(np.float32)).to(dev)
+            u = torch.from_numpy(r.normal(0, 1, (batch, k)).astype(np.float32)).to(dev)
+            m = torch.empty_like(g)
+            from bramha_b200.plane import _stream
+            check(lib().bramha_cuda_op_silu_mul(plane.ctx, g.data_ptr(), u.data_ptr(), batch * k, m.data_ptr(),
+                                                _stream(None)))
+            y1 = torch.empty((batch, n), device=dev)
+            y2 = torch.empty((batch, n), device=dev)
+            plane.stream_sync()
+            plane.gemv_dev(w, m, y1)
+            plane.gemv_swiglu_dev(w, g, u, y2)
+            plane.stream_sync()
+            assert torch.equal(y1, y2), (n, batch)
+        plane.evict(w.key)
