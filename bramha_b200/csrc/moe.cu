@@ -242,7 +242,8 @@ cudaError_t launch_moe_route(const float* logits, int64_t T, int64_t E, int top_
     if (T <= 0) return cudaSuccess;
     if (E <= 0 || E > kMoeMaxExperts || k <= 0) return cudaErrorInvalidValue;
     uint8_t* base = nullptr;
-    const int64_t bytes = (T * k * 2 * 4 + 255) / 256 * 256 + (E * 4 + 255) / 256 * 256;
+    auto pad = [](int64_t b) { return (b + 255) / 256 * 256; };  // each carved piece is padded
+    const int64_t bytes = 2 * pad(T * k * 4) + pad(E * 4);
     cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&base), (size_t)bytes, st);
     if (e != cudaSuccess) return e;
     uint8_t* p = base;

@@ -139,3 +139,41 @@ def test_moe_device_call_and_errors(plane):
         plane.moe_mlp(gu, dn, E, k, np.zeros((9000, H), np.float32), np.zeros((9000, E), np.float32))
     plane.evict(gu.key)
     plane.evict(dn.key)
+
+
+def test_moe_route_and_experts_entry_points(plane):
+    """The two halves used for expert parallelism on one GPU: the routing alone
+    gives the layer's expert choice and the oracle's probabilities, and the
+    experts run on the routed rows, combined in the sorted order, reproduce the
+    whole layer bit for bit."""
+    E, H, I, T, k = 8, 256, 128, 24, 3
+    gates, ups, downs, cat = experts("log4", E, H, I, seed=11)
+    gu, dn = register(plane, "moe:halves", "log4", E, H, I, gates, ups, downs)
+    r = rng(12)
+    x = r.normal(0, 1, (T, H)).astype(np.float32)
+    lg = r.normal(0, 1, (T, E)).astype(np.float32)
+    lg[5] = np.array([0, -200, 50, -200, -200, -200, -200, -200], np.float32)  # weights that underflow
+    dev = torch.device("cuda", 0)
+    xd, ld = torch.from_numpy(x).to(dev), torch.from_numpy(lg).to(dev)
+    full = torch.empty((T, H), device=dev)
+    sel = torch.empty((T, k), dtype=torch.int32, device=dev)
+    plane.moe_mlp_dev(gu, dn, E, k, xd, ld, full, sel)
+    ids = torch.empty((T, k), dtype=torch.int32, device=dev)
+    w = torch.empty((T, k), device=dev)
+    plane.moe_route_dev(ld, k, ids, w)
+    plane.stream_sync()
+    assert torch.equal(ids, sel)
+    _, ref_ids, ref_w = oracle.moe_mlp("log4", x, lg, k, cat(gates), cat(ups), cat(downs))
+    check_selection(ids.cpu().numpy(), ref_ids, lg)
+    assert np.allclose(w.cpu().numpy(), ref_w, rtol=1e-6, atol=1e-12)
+    rows = xd.repeat_interleave(k, dim=0).contiguous()
+    y = torch.empty_like(rows)
+    plane.moe_experts_dev(gu, dn, E, rows, ids.reshape(-1).contiguous(), y)
+    plane.stream_sync()
+    y = y.view(T, k, H)
+    out = torch.zeros((T, H), device=dev)
+    for j in range(k):
+        out = torch.where((w[:, j:j + 1] > 0), out + y[:, j] * w[:, j:j + 1], out)
+    assert torch.equal(out, full)
+    plane.evict(gu.key)
+    plane.evict(dn.key)
