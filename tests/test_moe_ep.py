@@ -26,7 +26,7 @@ def free_port():
         return s.getsockname()[1]
 
 
-def make_model(fmt="log4", seed=3):
+def make_model(fmt="log4", seed=3, all_rank0=False):
     r = np.random.Generator(np.random.PCG64(seed))
     mk = lambda n, k: oracle.quantize(fmt, r.normal(0, 0.02, n * k).astype(np.float32), n, k)
     gates = [mk(I, H) for _ in range(E)]
@@ -36,6 +36,8 @@ def make_model(fmt="log4", seed=3):
     lg = r.normal(0, 1, (2 * T_RANK, E)).astype(np.float32)
     lg[3] = np.array([0, -200, 50, -200, -200, -200, -200, -200], np.float32)  # weights that underflow: skipped
     lg[T_RANK:, 0] += 8.0  # the second rank's tokens all go first to expert 0 (rank 0)
+    if all_rank0:  # every choice on rank 0's experts: rank 1 receives no rows at all
+        lg[:, E // 2:] -= 200.0
     return gates, ups, downs, x, lg
 
 
@@ -43,12 +45,12 @@ def cat(ws):
     return np.concatenate([q.view(np.uint8) for q, _ in ws]), np.concatenate([s for _, s in ws])
 
 
-def cpu_worker(rank, world, port, out_dir):
+def cpu_worker(rank, world, port, out_dir, all_rank0=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from bramha_b200.moe_ep import ExpertParallelMoE
-        gates, ups, downs, x, lg = make_model()
+        gates, ups, downs, x, lg = make_model(all_rank0=all_rank0)
         e_local = E // world
         xs, ls = x[rank * T_RANK:(rank + 1) * T_RANK], lg[rank * T_RANK:(rank + 1) * T_RANK]
         ref, ref_ids, ref_w = oracle.moe_mlp("log4", xs, ls, K, cat(gates), cat(ups), cat(downs))
@@ -75,9 +77,11 @@ def cpu_worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_expert_parallel_two_ranks_gloo(tmp_path):
+@pytest.mark.parametrize("all_rank0", [False, True])
+def test_expert_parallel_two_ranks_gloo(tmp_path, all_rank0):
     port = free_port()
-    mp.start_processes(cpu_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(cpu_worker, args=(2, port, str(tmp_path), all_rank0), nprocs=2, join=True,
+                       start_method="spawn")
     for rank in range(2):
         out, ref = np.load(tmp_path / f"out{rank}.npy"), np.load(tmp_path / f"ref{rank}.npy")
         assert np.max(np.abs(out - ref)) <= 1e-5 * np.max(np.abs(ref)), rank
