@@ -63,3 +63,18 @@ def test_moe_ties_and_top_k_beyond_experts():
     assert np.allclose(w[1], 0.25)
     out, ids, _ = oracle.moe_mlp("log4", h, lg, 9, g, u, d)  # top_k > E: every expert
     assert ids.shape == (T, E)
+
+
+def test_stack_gate_up_layout():
+    """Each expert's gate rows, then its up rows (the stacked layout of the MoE call)."""
+    from bramha_b200 import stack_gate_up
+    r = rng(23)
+    E, I, H = 3, 4, 8
+    gates = [(r.integers(0, 256, I * H // 2).astype(np.uint8), r.random(I).astype(np.float32)) for _ in range(E)]
+    ups = [(r.integers(0, 256, I * H // 2).astype(np.uint8), r.random(I).astype(np.float32)) for _ in range(E)]
+    q, s = stack_gate_up(gates, ups)
+    rows = q.reshape(E * 2 * I, H // 2)
+    for e in range(E):
+        assert np.array_equal(rows[2 * I * e:2 * I * e + I].reshape(-1), gates[e][0])
+        assert np.array_equal(rows[2 * I * e + I:2 * I * (e + 1)].reshape(-1), ups[e][0])
+        assert np.array_equal(s[2 * I * e:2 * I * (e + 1)], np.concatenate([gates[e][1], ups[e][1]]))
