@@ -9,8 +9,10 @@ Workload: the linears of one Qwen2-7B decode token --
 down 3584x18944) + lm_head 152064x3584 -- in the 4-bit log format, weights
 ~N(0, 0.02) packed on the device by this repo's packer, activations ~N(0, 1),
 batch 1.  One step = every linear once (q|k|v and gate|up share an input and
-run as one launch each: 113 GEMV launches per step).  Synthetic data; the
-3.55 GB of packed weights per step exceed the 126 MB L2, so no flush is needed.
+run as one launch each: 113 GEMV launches per step, issued as one GEMV chain in
+which each launch requests the next one's weights into L2).  Synthetic data;
+the 3.55 GB of packed weights per step exceed the 126 MB L2, so no flush is
+needed.  The same weights are then run at batch 8 and 64 (`batch_lines`).
 
 N > 1: every linear is column-sharded (output rows split across ranks) and
 each shard's output is all-gathered with NCCL (strong scaling: total work
@@ -18,9 +20,10 @@ fixed).  The linears' inputs are independent synthetic vectors.
 
 Prints ONE JSON line on rank 0.  `value` is algorithmic GB/s over the whole job
 (packed weights + scales + x + y per GEMV); `e2e` is the same metric through the
-public host-buffer C-ABI call (pinned host x in, host y out, every call
-synchronous).  `--impl reference` times the CPU restatement of the reference's
-GEMV loop on this host's cores (rank 0 only).
+public host-buffer C-ABI call for a whole step (bramha_cuda_gemv_chain: pinned
+host inputs in, every output back in host memory, synchronous).
+`--impl reference` times the CPU restatement of the reference's GEMV loop on
+this host's cores over the same whole step (rank 0 only).
 """
 from __future__ import annotations
 
@@ -30,6 +33,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -79,11 +83,10 @@ class ClockSampler:
     def __init__(self, device):
         self.device = device
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_dev{device}.csv")
+        self.path = os.path.join(tempfile.gettempdir(), f"bramha_bench_clocks_{os.getpid()}_dev{device}.csv")
 
     def __enter__(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -137,85 +140,179 @@ def dist_setup(args):
 
 
 # ------------------------------------------------------------- reference arm
+class CpuStep:
+    """The reference's CPU decode GEMV loop over a whole decode step: the C
+    restatement of `matvec_mul_into` (src/inference/cpu_engine.rs:1307-1444;
+    log4 through its tables) on every linear of `layers` Qwen2-7B layers + the
+    lm_head, OpenMP over rows on all host threads, built -march=native as the
+    reference builds with target-cpu=native.  The packed codes of the whole
+    step (3.55 GB at 4 bits for 28 layers) sit in host memory and are streamed
+    once per step, as the GPU arm streams them from HBM; they are drawn as
+    uniform random bytes (the CPU loop's time does not depend on code values).
+    Each linear has its own N(0, 1) input."""
+
+    def __init__(self, fmt, batch, layers=LAYERS, seed=2024):
+        import oracle
+        self.oracle = oracle
+        self.native = oracle.use_native_build()
+        self.threads = oracle.max_threads()
+        self.fmt, self.batch = fmt, batch
+        bits = BITS[fmt]
+        rng = np.random.Generator(np.random.PCG64(seed))
+        self.work = []
+        for _, n, k in token_linears(layers):
+            q = np.frombuffer(rng.bytes(n * k * bits // 8), dtype=np.uint8)
+            if fmt == "w8":
+                q = q.view(np.int8)
+            s = rng.uniform(1e-4, 1e-3, n).astype(np.float32)
+            x = rng.standard_normal((batch, k), dtype=np.float32)
+            self.work.append((n, k, q, s, x))
+        self.nbytes = sum(gemv_bytes(n, k, batch, bits) for n, k, _, _, _ in self.work)
+        self.layers = layers
+
+    def step(self):
+        o = self.oracle
+        for n, k, q, s, x in self.work:
+            for b in range(self.batch):
+                if self.fmt == "log4":
+                    o.matvec_fused_log4(x[b], q, s, n, threads=self.threads)
+                else:
+                    o.matvec_mul_into(self.fmt, x[b], q, s, n, threads=self.threads)
+
+    def timed(self, steps):
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            self.step()
+        return (time.perf_counter() - t0) / steps
+
+    def describe(self, steps, repeats):
+        return (f"{'whole step' if self.layers == LAYERS else f'{self.layers} layers'}: {self.layers} layers x 7 "
+                f"linears + lm_head ({self.nbytes / 1e9:.2f} GB packed, streamed from host memory), batch "
+                f"{self.batch}, {steps} steps x {repeats} timed regions; C restatement of matvec_mul_into "
+                f"(cpu_engine.rs:1307-1444), OpenMP over rows, "
+                + ("-march=native" if self.native else "-march=x86-64-v3 (native build unavailable)"))
+
+
 def run_reference(args, ws, rank):
-    """The reference's CPU GEMV loop (restated in C) on all host threads."""
+    """The reference's CPU GEMV loop (restated in C) on all host threads, over
+    the same workload as the GPU arm: every linear of the decode step."""
     if rank != 0:
         return
-    import oracle
-    threads = oracle.max_threads()
-    fmt = args.fmt
-    bits = BITS[fmt]
-    rng = np.random.Generator(np.random.PCG64(2024))
-    sample = []  # one layer's seven linears
-    for _, parts, k in GROUPS:
-        for p, n in parts:
-            w = rng.standard_normal(n * k, dtype=np.float32) * np.float32(0.02)
-            q, s = oracle.quantize(fmt, w, n, k)
-            x = rng.standard_normal((args.batch, k), dtype=np.float32)
-            sample.append((p, n, k, q, s, x))
-    sample_bytes = sum(gemv_bytes(n, k, args.batch, bits) for _, n, k, _, _, _ in sample)
-
-    def step():
-        for _, n, k, q, s, x in sample:
-            for b in range(args.batch):
-                if fmt == "log4":
-                    oracle.matvec_fused_log4(x[b], q, s, n, threads=threads)
-                else:
-                    oracle.matvec_mul_into(fmt, x[b], q, s, n, threads=threads)
-
+    cs = CpuStep(args.fmt, args.batch)
     for _ in range(args.warmup):
-        step()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
-    dt = (time.perf_counter() - t0) / args.steps
-    gbs = sample_bytes / dt / 1e9
-    tok_bytes = sum(gemv_bytes(n, k, args.batch, bits) for _, n, k in token_linears())
+        cs.step()
+    reps = [cs.timed(args.steps) for _ in range(max(1, args.repeats))]
+    dt = reps[0]
+    gbs = cs.nbytes / dt / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-        "config": {"workload": f"qwen2-7b linears, {fmt}, batch {args.batch} decode GEMV (CPU sample: one layer)",
-                   "batch": args.batch, "fmt": fmt, "hidden": H, "intermediate": I, "vocab": V, "layers": LAYERS},
-        "tokens_per_s": round(args.batch * gbs * 1e9 / tok_bytes, 3),
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"one layer's 7 linears ({sample_bytes / 1e6:.1f} MB packed), batch {args.batch}, "
-                                   f"{args.steps} steps; C restatement of matvec_mul_into "
-                                   "(cpu_engine.rs:1307-1444), OpenMP over rows"},
+        "data": "synthetic (seeded random packed codes and scales, N(0,1) activations)",
+        "config": {"workload": f"qwen2-7b linears ({LAYERS} layers + lm_head), {args.fmt}, batch {args.batch} "
+                               "decode GEMV",
+                   "batch": args.batch, "fmt": args.fmt, "hidden": H, "intermediate": I, "vocab": V,
+                   "layers": LAYERS, "parallelism": "host threads (CPU)",
+                   "l2": f"no flush: {cs.nbytes / 1e9:.2f} GB of packed weights per step >> host LLC"},
+        "tokens_per_s": round(args.batch / dt, 3),
+        "spread": {"repeats": len(reps), "steps_each": args.steps,
+                   "ms_per_step_median": round(statistics.median(reps) * 1e3, 3),
+                   "ms_per_step_min": round(min(reps) * 1e3, 3), "ms_per_step_max": round(max(reps) * 1e3, 3)},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cs.threads, "kind": "port",
+                         "sample": cs.describe(args.steps, len(reps))},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline_sample(fmt, batch, qs, seconds=8.0):
-    """Time the CPU restatement on layer 0's packed weights (copied from the GPU)."""
-    import oracle
-    threads = oracle.max_threads()
+def cpu_baseline_sample(fmt, batch, steps=3):
+    """The reference arm's CPU loop on the same whole-step workload, a few steps
+    (rank 0 at N = 1 only)."""
+    cs = CpuStep(fmt, batch)
+    cs.step()
+    dt = cs.timed(steps)
+    return {"value": round(cs.nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": cs.threads, "kind": "port",
+            "ms_per_step": round(dt * 1e3, 2), "sample": cs.describe(steps, 1)}
+
+
+# ------------------------------------------------------------------ batch 8 / 64 (config 4)
+def batch_lines(plane, dev, layers, fmt, batches=(8, 64), reps=5):
+    """BASELINE config 4 at batch 8 and 64 on the step's registered weights:
+    the step's 113 launches (q|k|v and gate|up fused) as one GEMV chain in a
+    CUDA graph, device time over `reps` replays.  Batch 8 runs on the tensor-core
+    GEMV (HBM-bound); batch 64 on the tcgen05 GEMM with the f32 rows split into
+    bf16 hi + lo halves of the MMA's N (twice the MMA work of 2*B*N*K, so it is
+    bound by the tensor pipe).  The roofline object covers the dominant linear
+    (per-group launches timed from their own graphs)."""
+    import torch
     bits = BITS[fmt]
-    rng = np.random.Generator(np.random.PCG64(99))
-    work = [(n, k, q, s, rng.standard_normal((batch, k), dtype=np.float32)) for (n, k, q, s) in qs]
-    nbytes = sum(gemv_bytes(n, k, batch, bits) for n, k, _, _, _ in work)
+    hbm, hbm_kind = load_peaks()
+    pk_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    tflops_peak = json.load(open(pk_path))["bf16_tflops"] if os.path.exists(pk_path) else 1590.0
+    stream = torch.cuda.Stream(device=dev)
+    gen = torch.Generator(device=dev).manual_seed(64)
+    out = {}
+    for B in batches:
+        ops, groups, nbytes, flops = [], {}, 0, 0
+        for entry in layers:
+            for gname, wts, x, _, _ in entry:
+                k = x.shape[1]
+                xb = torch.randn((B, k), generator=gen, device=dev)
+                yb = [torch.empty((B, w.N), device=dev) for w in wts]
+                ops.append((wts, xb, yb))
+                groups.setdefault(gname, []).append((wts, xb, yb))
+                nbytes += sum(gemv_bytes(w.N, k, B, bits) for w in wts)
+                flops += sum(2 * B * w.N * k for w in wts)
+        with torch.cuda.stream(stream):
+            plane.gemv_chain_dev(ops, B, stream)
+        torch.cuda.synchronize()
 
-    def once():
-        for n, k, q, s, x in work:
-            for b in range(batch):
-                if fmt == "log4":
-                    oracle.matvec_fused_log4(x[b], q, s, n, threads=threads)
-                else:
-                    oracle.matvec_mul_into(fmt, x[b], q, s, n, threads=threads)
+        def graph_ms(items, n_rep):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                plane.gemv_chain_dev(items, B, stream)
+            with torch.cuda.stream(stream):
+                g.replay()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                for _ in range(n_rep):
+                    g.replay()
+                b.record()
+            torch.cuda.synchronize()
+            del g
+            return a.elapsed_time(b) / n_rep
 
-    once()
-    reps, t0 = 0, time.perf_counter()
-    while True:
-        once()
-        reps += 1
-        if reps >= 3 and time.perf_counter() - t0 >= seconds:
-            break
-    dt = (time.perf_counter() - t0) / reps
-    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"layer 0's 7 linears ({nbytes / 1e6:.1f} MB packed) x {reps} reps; C restatement of "
-                      "matvec_mul_into (cpu_engine.rs:1307-1444) with log4 tables, OpenMP over rows"}
+        ms = graph_ms(ops, reps)
+        plane.stream_sync(stream)
+        per = {}
+        for gname, items in groups.items():
+            gms = graph_ms(items, 3)
+            gb = sum(sum(gemv_bytes(w.N, x.shape[1], B, bits) for w in wts) for wts, x, _ in items)
+            gf = sum(sum(2 * B * w.N * x.shape[1] for w in wts) for wts, x, _ in items)
+            per[gname] = {"launches": len(items), "us_mean": round(gms * 1e3 / len(items), 2),
+                          "gbs": round(gb / (gms * 1e-3) / 1e9, 1), "tflops": round(gf / (gms * 1e-3) / 1e12, 1),
+                          "ms": gms}
+        tot = sum(v["ms"] for v in per.values())
+        for v in per.values():
+            v["share"] = round(v.pop("ms") / tot, 3)
+        dom = max(per, key=lambda g_: per[g_]["share"])
+        if B <= 8:
+            ach = per[dom]["gbs"]
+            roof = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
+                    "kernel": f"tc_gemv_kernel<{fmt}, {B}> ({dom})", "peak_source": f"{hbm_kind} hbm_gbs"}
+        else:
+            ach = per[dom]["tflops"]
+            roof = {"bound": "tensor", "achieved": ach, "peak": tflops_peak, "unit": "TFLOP/s",
+                    "frac": round(ach / tflops_peak, 4), "kernel": f"gemm_kernel<{fmt}> ({dom}), bf16 hi+lo",
+                    "peak_source": "measured bf16_tflops (burst)" if os.path.exists(pk_path) else "fallback",
+                    "note": "achieved counts the GEMV's 2*B*N*K; the hi+lo split issues twice that on the tensor pipe"}
+        out[str(B)] = {"ms_per_step": round(ms, 4), "value": round(nbytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                       "tokens_per_s": round(B / (ms * 1e-3), 1), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+                       "frac_of_hbm_peak_step": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 4),
+                       "roofline": roof, "per_linear": per,
+                       "timing": f"CUDA graph of the step's chain, {reps} replays, device time"}
+        del ops, groups
+    return out
 
 
 # ------------------------------------------------------------------ prefill (config 3)
@@ -592,7 +689,6 @@ def run_ours(args, ws, rank, local):
     # ---- weights: generate full N(0,0.02) rows on device, keep this rank's shard, pack on device
     gen = torch.Generator(device=dev)
     layers = []  # per layer: list of (group, [Weight], x, [y_local], y_full)
-    layer0_host = []
     step_bytes = 0
     t_setup = time.time()
     for li in range(args.layers + 1):
@@ -611,8 +707,6 @@ def run_ours(args, ws, rank, local):
                 plane.quantize_dev(fmt, wf, qd, sd)
                 del wf
                 w = plane.register_dev(f"L{li}.{p}", fmt, hi - lo, k, qd, sd)
-                if li == 0:
-                    layer0_host.append((hi - lo, k, qd.cpu().numpy(), sd.cpu().numpy()))
                 del qd, sd
                 wts.append(w)
                 ys.append(hi - lo)
@@ -638,8 +732,14 @@ def run_ours(args, ws, rank, local):
     launches_per_step = sum(len(e) for e in layers)
 
     stream = torch.cuda.Stream(device=dev)
+    # one GPU: the step is one GEMV chain (bramha_cuda_gemv_chain_dev): each
+    # launch requests the next launch's weights into L2 while it runs
+    chain_ops = [(wts, x, ys) for entry in layers for _, wts, x, ys, _ in entry]
 
     def step():
+        if ws == 1:
+            plane.gemv_chain_dev(chain_ops, B, stream)
+            return
         for entry in layers:
             for gname, wts, x, ys, (ybuf, y_full) in entry:
                 plane.gemv_multi_dev(wts, x, ys)
@@ -696,6 +796,31 @@ def run_ours(args, ws, rank, local):
         ms = float(t.item())
     value = step_bytes / (ms * 1e-3) / 1e9
 
+    # ---- spread: the same K-step region timed `repeats` more times
+    rep_ms = []
+    for _ in range(args.repeats):
+        barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            r0.record()
+            for _ in range(args.steps):
+                run_step()
+            r1.record()
+        torch.cuda.synchronize()
+        v = r0.elapsed_time(r1) / args.steps
+        if ws > 1:
+            t = torch.tensor([v], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            v = float(t.item())
+        rep_ms.append(v)
+    spread = None
+    if rep_ms:
+        spread = {"repeats": len(rep_ms), "steps_each": args.steps,
+                  "ms_per_step_median": round(statistics.median(rep_ms), 4),
+                  "ms_per_step_min": round(min(rep_ms), 4), "ms_per_step_max": round(max(rep_ms), 4),
+                  "value_median": round(step_bytes / (statistics.median(rep_ms) * 1e-3) / 1e9, 2)}
+
     # ---- per-launch durations: each group's launches (e.g. the 28 gate|up GEMVs)
     # captured in their own CUDA graph and replayed, so host launch latency is
     # not part of the measurement; mean device time per launch
@@ -708,8 +833,7 @@ def run_ours(args, ws, rank, local):
     for gname, items in groups.items():
         gg = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gg, stream=stream):
-            for wts, x, ys in items:
-                plane.gemv_multi_dev(wts, x, ys)
+            plane.gemv_chain_dev(items, B, stream)
         gg.replay()
         torch.cuda.synchronize()
         with torch.cuda.stream(stream):
@@ -740,30 +864,24 @@ def run_ours(args, ws, rank, local):
         except Exception:
             traffic = None
 
-    # ---- e2e: the public host-buffer call (bramha_cuda_gemv) for every linear
-    import ctypes
-    from bramha_b200 import lib as blib, _lib
+    # ---- e2e: the public host-buffer call for the whole step: one
+    # bramha_cuda_gemv_chain call per step (pinned host inputs copied in, the
+    # 113 launches, every output copied back, one wait)
     h2d = d2h = 0
-    host_x, host_y = [], []
+    host_ops = []
     for entry in layers:
         for gname, wts, x, ys, _ in entry:
             xh = torch.empty((B, x.shape[1]), dtype=torch.float32, pin_memory=True)
             xh.copy_(x.cpu())
-            for w in wts:
-                yh = torch.empty((B, w.N), dtype=torch.float32, pin_memory=True)
-                host_x.append((w, xh))
-                host_y.append(yh)
-                h2d += xh.numel() * 4
-                d2h += yh.numel() * 4
-    L = blib()
+            yhs = [torch.empty((B, w.N), dtype=torch.float32, pin_memory=True) for w in wts]
+            host_ops.append((wts, xh, yhs))
+            h2d += xh.numel() * 4
+            d2h += sum(y.numel() * 4 for y in yhs)
 
     def e2e_step():
-        for (w, xh), yh in zip(host_x, host_y):
-            rc = L.bramha_cuda_gemv(plane.ctx, w.handle, xh.data_ptr(), B, yh.data_ptr())
-            if rc != 0:
-                raise RuntimeError(_lib.last_error())
-        if ws > 1:
-            pass  # host-side shards: a user of the host API gathers on the host; not timed here
+        plane.gemv_chain(host_ops, B)
+        # N > 1: each rank's host buffers hold its shard of every output (the
+        # gather of the shards is not part of this host-buffer figure)
 
     e2e_steps = max(2, min(args.steps, 10))
     e2e_step()
@@ -791,9 +909,13 @@ def run_ours(args, ws, rank, local):
     if rank == 0 and ws == 1 and not args.no_sparse:
         sparse24 = sparse24_bench(plane, dev, layers=args.sparse_layers)
 
+    batches = None
+    if rank == 0 and ws == 1 and B == 1 and not args.no_batch_lines:
+        batches = batch_lines(plane, dev, layers, fmt)
+
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_sample(fmt, B, layer0_host)
+        cpu = cpu_baseline_sample(fmt, B)
 
     if rank == 0:
         tok_bytes = step_bytes
@@ -820,9 +942,11 @@ def run_ours(args, ws, rank, local):
             "per_linear": per_linear,
             "clocks": clocks.summary(),
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "api": "bramha_cuda_gemv (host buffers, synchronous), one call per linear",
+                    "api": "bramha_cuda_gemv_chain (pinned host buffers, synchronous), one call per step",
                     "tokens_per_s": round(B / e2e_s, 2)},
+            "spread": spread,
             "cpu_baseline": cpu,
+            "batch_lines": batches,
             "prefill": prefill,
             "decode_step": decode_step,
             "sparse24": sparse24,
@@ -845,6 +969,8 @@ def main():
     ap.add_argument("--fmt", choices=list(BITS), default="log4")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--repeats", type=int, default=5, help="extra timed K-step regions for the spread")
+    ap.add_argument("--no-batch-lines", action="store_true", help="skip the batch 8 / 64 measurement")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill GEMM measurement")
     ap.add_argument("--no-decode-step", action="store_true", help="skip the config-2 decode-step measurement")
     ap.add_argument("--layers", type=int, default=LAYERS, help="decoder layers (smaller = profiling case)")

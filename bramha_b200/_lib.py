@@ -78,6 +78,11 @@ _SIGNATURES = {
     "bramha_cuda_stream_sync": [_vp, _vp],
     "bramha_cuda_gemm_noalloc_dev": [_vp, _vp, _vp, _i64, _vp, _vp],
     "bramha_cuda_set_gemv_kernel": [_vp, _int],
+    "bramha_cuda_set_wait_timeout": [_vp, ctypes.c_uint64],
+    "bramha_cuda_test_fault": [_vp, _int],
+    "bramha_cuda_set_prefetch": [_vp, _i64, _i64],
+    "bramha_cuda_gemv_chain_dev": [_vp, _int, _vp, _i64, _vp],
+    "bramha_cuda_gemv_chain": [_vp, _int, _vp, _i64],
     "bramha_cuda_op_embed": [_vp, _vp, _i64, _i64, _vp, _vp, _vp],
     "bramha_cuda_op_rmsnorm": [_vp, _vp, _vp, _vp, _i64, ctypes.c_float, _vp, _vp],
     "bramha_cuda_op_qkv_rope": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, ctypes.c_float, _vp, _i64,
@@ -88,6 +93,14 @@ _SIGNATURES = {
     "bramha_cuda_op_silu_mul": [_vp, _vp, _vp, _i64, _vp, _vp],
     "bramha_cuda_op_select": [_vp, _vp, _i64, _vp, _vp, _i64, ctypes.c_float, _int, _vp, _vp, _vp],
 }
+
+
+
+class GemvOp(ctypes.Structure):
+    """`bramha_gemv_op` of include/bramha_cuda.h (one launch of a GEMV chain)."""
+    _fields_ = [("n_weights", ctypes.c_int), ("weights", ctypes.POINTER(ctypes.c_void_p)),
+                ("x", ctypes.c_void_p), ("x_up", ctypes.c_void_p), ("y", ctypes.POINTER(ctypes.c_void_p))]
+
 
 _lib = None
 

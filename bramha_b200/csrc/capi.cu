@@ -54,10 +54,14 @@ struct bramha_ctx {
     float* dev_x = nullptr;
     float* dev_y = nullptr;
     size_t dev_x_cap = 0, dev_y_cap = 0;
-    int* d_err = nullptr;                // device error word written by bounded waits
+    DevStatus* d_status = nullptr;       // error word, wait bound, test fault switch (device)
+    int* d_err = nullptr;                // &d_status->err: what kernels are handed
+    int* h_err = nullptr;                // pinned host copy of the error word
     float* split_ws = nullptr;           // K-split partials of the tensor-core GEMV
     int* split_tickets = nullptr;        // per-tile arrival counters (kept zero between launches)
     int gemv_kernel = BRAMHA_GEMV_AUTO;  // kernel choice for the tiled formats
+    int64_t pf_lookahead = 128 << 10;    // GEMV L2 lookahead per CTA, bytes
+    int64_t pf_next = 24 << 20;          // GEMV chain: bytes of the next launch requested into L2
 };
 
 namespace {
@@ -154,7 +158,7 @@ void evict_locked(bramha_ctx* ctx, const std::string& key) {
     auto it = ctx->reg.find(key);
     if (it == ctx->reg.end()) return;
     bramha_weight* w = it->second;
-    cudaStreamSynchronize(ctx->stream);  // no launch may still read it
+    cudaDeviceSynchronize();  // no launch, on any stream, may still read it
     ctx->used -= w->bytes;
     ctx->lru.erase(w->lru_it);
     ctx->reg.erase(it);
@@ -447,8 +451,11 @@ int check_weight(const bramha_ctx* ctx, const bramha_weight* w) {
 // Core device GEMV over several weights sharing x.  x must be 16-byte aligned
 // with row pitch ldx (a multiple of 4 floats when batch > 1).
 // x_up (optional, tensor-core formats only): the activation is silu(x) * x_up.
+// next_ws (optional): the weights of the next launch of a chain, whose first
+// bytes the tensor-core GEMV requests into L2 at its tail.
 int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const float* x, int64_t ldx,
-                int64_t batch, float* const* ys, cudaStream_t st, const float* x_up = nullptr) {
+                int64_t batch, float* const* ys, cudaStream_t st, const float* x_up = nullptr, int next_n = 0,
+                const bramha_weight* const* next_ws = nullptr) {
     const int fmt = ws[0]->fmt;
     const int64_t K = ws[0]->K;
     if (batch <= 0) return BRAMHA_OK;
@@ -464,6 +471,38 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
                 CK(launch_sp24_gemv(sp24_base(fmt), ws[i]->sp, x + b * ldx, ys[i] + b * ws[i]->N, ctx->split_ws,
                                     kSplitWsFloats, ctx->split_tickets, kSplitTickets, ctx->num_sms, st),
                    "2:4 gemv launch");
+        return BRAMHA_OK;
+    }
+    if (is_tiled(fmt) && batch > kMaxGemvBatch) {
+        // More activation rows than the GEMV kernels take: the tcgen05 GEMM with
+        // the weights as the M operand and the rows as N (f32 rows split into
+        // bf16 hi + lo halves of the MMA's N, so each weight block is read once;
+        // K-split when the weight has fewer 128-row blocks than SMs), the
+        // reference's batched form being gemm_cpu (cpu_engine.rs:565-912).
+        const float* xin = x;
+        float* act = nullptr;
+        if (x_up) {  // SwiGLU: silu(x) * x_up first, rounded as bramha_cuda_op_silu_mul
+            CK(cudaMallocAsync(reinterpret_cast<void**>(&act), sizeof(float) * (size_t)(batch * ldx), st),
+               "cudaMallocAsync(swiglu activations)");
+            cudaError_t e = launch_silu_mul(x, x_up, batch * ldx, act, st);
+            if (e != cudaSuccess) {
+                cudaFreeAsync(act, st);
+                return cuda_fail(e, "silu_mul launch");
+            }
+            xin = act;
+        }
+        cudaError_t e = cudaSuccess;
+        for (int i = 0; i < n && e == cudaSuccess; ++i) {
+            if (ws[i]->N == 0) continue;
+            e = launch_gemm_tcgen05(fmt, ws[i]->q, ws[i]->ldq, ws[i]->scales, ws[i]->N, held_columns(fmt, K), xin, 1,
+                                    ldx, batch, ys[i], ws[i]->N, ctx->d_err, ctx->split_ws, kSplitWsFloats,
+                                    ctx->split_tickets, kSplitTickets, st);
+        }
+        if (act) {
+            cudaError_t e2 = cudaFreeAsync(act, st);
+            if (e == cudaSuccess) e = e2;
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "tcgen05 gemm launch (batched gemv)");
         return BRAMHA_OK;
     }
     for (int64_t b0 = 0; b0 < batch; b0 += kMaxGemvBatch) {
@@ -496,6 +535,19 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
         a.split_ws_floats = kSplitWsFloats;
         a.split_tickets = ctx->split_tickets;
         a.split_tickets_n = kSplitTickets;
+        a.pf_ahead = (int)(ctx->pf_lookahead / (2 * 8192));
+        a.pf_next_n = 0;
+        a.pf_next_total = 0;
+        if (b0 + kMaxGemvBatch >= batch) {  // the last chunk of this op hands over to the next op
+            for (int i = 0; i < next_n && i < kMaxSegments; ++i) {
+                const bramha_weight* nw = next_ws[i];
+                if (!nw || !is_tiled(nw->fmt) || nw->N == 0 || nw->K == 0) continue;
+                a.pf_next_ptr[a.pf_next_n] = nw->q;
+                a.pf_next_bytes[a.pf_next_n] = tiled_bytes(nw->fmt, nw->N, held_columns(nw->fmt, nw->K));
+                ++a.pf_next_n;
+            }
+            a.pf_next_total = a.pf_next_n ? ctx->pf_next : 0;
+        }
         const bool cc = !x_up && (ctx->gemv_kernel == BRAMHA_GEMV_CUDA_CORE
                                       ? is_tiled(fmt) && a.batch == 1
                                       : ctx->gemv_kernel == BRAMHA_GEMV_AUTO && gemv_cc_eligible(fmt, a));
@@ -509,11 +561,12 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
     return BRAMHA_OK;
 }
 
-// After the stream is idle: report (and clear) a device-side failure.
+// Waits for the stream, then reports (and clears) a device-side failure: the
+// error word is read back in the same stream, so one wait covers both.
 int check_device_error(bramha_ctx* ctx, cudaStream_t st) {
-    int h = 0;
-    CK(cudaMemcpyAsync(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, st), "read error word");
+    CK(cudaMemcpyAsync(ctx->h_err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, st), "read error word");
     CK(cudaStreamSynchronize(st), "stream sync");
+    const int h = *ctx->h_err;
     if (h != 0) {
         cudaMemsetAsync(ctx->d_err, 0, sizeof(int), st);
         // an aborted launch may leave K-split tickets taken
@@ -546,7 +599,7 @@ int gemm_device(bramha_ctx* ctx, const bramha_weight* w, const void* x, int x_is
         return BRAMHA_OK;
     }
     CK(launch_gemm_tcgen05(w->fmt, w->q, w->ldq, w->scales, w->N, keff, x, x_is_f32, ldx, M, y, w->N, ctx->d_err,
-                           st),
+                           ctx->split_ws, kSplitWsFloats, ctx->split_tickets, kSplitTickets, st),
        "tcgen05 gemm launch");
     return BRAMHA_OK;
 }
@@ -594,8 +647,7 @@ int gemv_host(bramha_ctx* ctx, const bramha_weight* w, const float* x_host, int6
     if (rc) return rc;
     CK(cudaMemcpyAsync(y_host, ctx->dev_y, sizeof(float) * (size_t)(w->N * batch), cudaMemcpyDeviceToHost, st),
        "D2H y");
-    CK(cudaStreamSynchronize(st), "stream sync");
-    return BRAMHA_OK;
+    return check_device_error(ctx, st);
 }
 
 }  // namespace
@@ -631,13 +683,19 @@ int bramha_cuda_init(int device, bramha_ctx** out) {
         delete ctx;
         return cuda_fail(e, "cudaStreamCreate");
     }
-    e = cudaMalloc(&ctx->d_err, sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, sizeof(int));
+    e = cudaMalloc(&ctx->d_status, sizeof(DevStatus));
+    if (e == cudaSuccess) {
+        const DevStatus init = {0, kFaultNone, kDefaultTimeoutNs};
+        e = cudaMemcpy(ctx->d_status, &init, sizeof init, cudaMemcpyHostToDevice);
+        ctx->d_err = &ctx->d_status->err;
+    }
+    if (e == cudaSuccess) e = cudaMallocHost(&ctx->h_err, sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(&ctx->split_ws, sizeof(float) * (size_t)kSplitWsFloats);
     if (e == cudaSuccess) e = cudaMalloc(&ctx->split_tickets, sizeof(int) * (size_t)kSplitTickets);
     if (e == cudaSuccess) e = cudaMemset(ctx->split_tickets, 0, sizeof(int) * (size_t)kSplitTickets);
     if (e != cudaSuccess) {
-        if (ctx->d_err) cudaFree(ctx->d_err);
+        if (ctx->d_status) cudaFree(ctx->d_status);
+        if (ctx->h_err) cudaFreeHost(ctx->h_err);
         if (ctx->split_ws) cudaFree(ctx->split_ws);
         if (ctx->split_tickets) cudaFree(ctx->split_tickets);
         cudaStreamDestroy(ctx->stream);
@@ -664,7 +722,8 @@ int bramha_cuda_destroy(bramha_ctx* ctx) {
     }
     if (ctx->dev_x) cudaFree(ctx->dev_x);
     if (ctx->dev_y) cudaFree(ctx->dev_y);
-    if (ctx->d_err) cudaFree(ctx->d_err);
+    if (ctx->d_status) cudaFree(ctx->d_status);
+    if (ctx->h_err) cudaFreeHost(ctx->h_err);
     if (ctx->split_ws) cudaFree(ctx->split_ws);
     if (ctx->split_tickets) cudaFree(ctx->split_tickets);
     cudaStreamDestroy(ctx->stream);
@@ -677,6 +736,33 @@ int bramha_cuda_set_gemv_kernel(bramha_ctx* ctx, int kind) {
     if (kind != BRAMHA_GEMV_AUTO && kind != BRAMHA_GEMV_TENSOR_CORE && kind != BRAMHA_GEMV_CUDA_CORE)
         return fail(BRAMHA_ERR_INVALID, "unknown GEMV kernel choice %d", kind);
     ctx->gemv_kernel = kind;
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_set_wait_timeout(bramha_ctx* ctx, uint64_t ns) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    const unsigned long long v = ns ? (unsigned long long)ns : kDefaultTimeoutNs;
+    DeviceGuard g(ctx->device);
+    CK(cudaMemcpy(&ctx->d_status->timeout_ns, &v, sizeof v, cudaMemcpyHostToDevice), "set wait timeout");
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_test_fault(bramha_ctx* ctx, int kind) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (kind != BRAMHA_TEST_FAULT_NONE && kind != BRAMHA_TEST_FAULT_GEMV && kind != BRAMHA_TEST_FAULT_GEMM)
+        return fail(BRAMHA_ERR_INVALID, "unknown test fault %d", kind);
+    static_assert(BRAMHA_TEST_FAULT_GEMV == kFaultGemvWithholdCopy && BRAMHA_TEST_FAULT_GEMM == kFaultGemmWithholdCopy,
+                  "test fault codes");
+    DeviceGuard g(ctx->device);
+    CK(cudaMemcpy(&ctx->d_status->fault, &kind, sizeof kind, cudaMemcpyHostToDevice), "set test fault");
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_set_prefetch(bramha_ctx* ctx, int64_t lookahead_bytes, int64_t next_launch_bytes) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (lookahead_bytes < 0 || next_launch_bytes < 0) return fail(BRAMHA_ERR_INVALID, "negative prefetch size");
+    ctx->pf_lookahead = lookahead_bytes;
+    ctx->pf_next = next_launch_bytes;
     return BRAMHA_OK;
 }
 
@@ -782,6 +868,134 @@ int bramha_cuda_gemv_multi_dev(bramha_ctx* ctx, int n_weights, const bramha_weig
     DeviceGuard g(ctx->device);
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
     return gemv_device(ctx, n_weights, ws, x_dev, K, batch, y_devs, st);
+}
+
+namespace {
+// Checks one op of a GEMV chain (the rules of gemv_multi_dev / gemv_swiglu_dev);
+// on the device path x and x_up must be 16-byte aligned.
+int check_chain_op(bramha_ctx* ctx, const bramha_gemv_op& op, int64_t batch, bool device_ptrs) {
+    if (op.n_weights < 1 || op.n_weights > kMaxSegments || !op.weights || !op.y)
+        return fail(BRAMHA_ERR_INVALID, "gemv chain: an op needs 1..%d weights and outputs", kMaxSegments);
+    for (int i = 0; i < op.n_weights; ++i) {
+        int rc = check_weight(ctx, op.weights[i]);
+        if (rc) return rc;
+        if (op.weights[i]->fmt != op.weights[0]->fmt || op.weights[i]->K != op.weights[0]->K)
+            return fail(BRAMHA_ERR_SIZE, "fused weights must share format and K");
+        if (!op.y[i] && op.weights[i]->N > 0 && batch > 0) return fail(BRAMHA_ERR_INVALID, "null output pointer");
+    }
+    const int64_t K = op.weights[0]->K;
+    if (op.x_up && !is_tiled(op.weights[0]->fmt))
+        return fail(BRAMHA_ERR_UNSUPPORTED, "gemv chain: SwiGLU ops take LOG4, W4ZP8 or W8 weights");
+    if (batch > 0 && K > 0) {
+        if (!op.x) return fail(BRAMHA_ERR_INVALID, "null input pointer");
+        if (device_ptrs && (((reinterpret_cast<uintptr_t>(op.x) | reinterpret_cast<uintptr_t>(op.x_up)) & 15) != 0 ||
+                            (batch > 1 && (K & 3) != 0)))
+            return fail(BRAMHA_ERR_INVALID,
+                        "gemv chain: x must be 16-byte aligned (and K a multiple of 4 when batch > 1); "
+                        "use bramha_cuda_gemv_chain for unaligned input");
+    }
+    return BRAMHA_OK;
+}
+
+// Launches the ops in order; op i also prefetches op i+1's weights.  xs / ups /
+// ldxs override the ops' input pointers (device staging of the host chain).
+int chain_device(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch, cudaStream_t st,
+                 const float* const* xs = nullptr, const float* const* ups = nullptr, const int64_t* ldxs = nullptr,
+                 float* const* const* ys = nullptr) {
+    for (int i = 0; i < n_ops; ++i) {
+        const bramha_gemv_op& op = ops[i];
+        const int nn = i + 1 < n_ops ? ops[i + 1].n_weights : 0;
+        const bramha_weight* const* nw = i + 1 < n_ops ? ops[i + 1].weights : nullptr;
+        const float* x = xs ? xs[i] : op.x;
+        const float* up = ups ? ups[i] : op.x_up;
+        const int64_t ldx = ldxs ? ldxs[i] : op.weights[0]->K;
+        int rc = gemv_device(ctx, op.n_weights, op.weights, x, ldx, batch, ys ? ys[i] : op.y, st, up, nn, nw);
+        if (rc) return rc;
+    }
+    return BRAMHA_OK;
+}
+}  // namespace
+
+int bramha_cuda_gemv_chain_dev(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch, void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (n_ops < 0 || (n_ops > 0 && !ops)) return fail(BRAMHA_ERR_INVALID, "gemv chain: bad op list");
+    if (batch < 0) return fail(BRAMHA_ERR_INVALID, "negative batch");
+    for (int i = 0; i < n_ops; ++i) {
+        int rc = check_chain_op(ctx, ops[i], batch, true);
+        if (rc) return rc;
+    }
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    return chain_device(ctx, n_ops, ops, batch, st);
+}
+
+int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (n_ops < 0 || (n_ops > 0 && !ops)) return fail(BRAMHA_ERR_INVALID, "gemv chain: bad op list");
+    if (batch < 0) return fail(BRAMHA_ERR_INVALID, "negative batch");
+    for (int i = 0; i < n_ops; ++i) {
+        int rc = check_chain_op(ctx, ops[i], batch, false);
+        if (rc) return rc;
+    }
+    if (n_ops == 0 || batch == 0) return BRAMHA_OK;
+    DeviceGuard g(ctx->device);
+    std::lock_guard<std::mutex> lk(ctx->io_mu);
+    // device staging: every op's x (and x_up) at a 16-byte aligned pitch, then
+    // every output, back to back
+    std::vector<int64_t> ldx((size_t)n_ops), xo((size_t)n_ops), uo((size_t)n_ops);
+    std::vector<int64_t> yo;
+    size_t xe = 0, ye = 0;
+    for (int i = 0; i < n_ops; ++i) {
+        const int64_t K = ops[i].weights[0]->K;
+        ldx[(size_t)i] = (K + 3) / 4 * 4;
+        xo[(size_t)i] = (int64_t)xe;
+        xe += (size_t)(ldx[(size_t)i] * batch);
+        uo[(size_t)i] = ops[i].x_up ? (int64_t)xe : -1;
+        if (ops[i].x_up) xe += (size_t)(ldx[(size_t)i] * batch);
+        for (int j = 0; j < ops[i].n_weights; ++j) {
+            yo.push_back((int64_t)ye);
+            ye += (size_t)(ops[i].weights[j]->N * batch);
+        }
+    }
+    int rc = ensure_staging(ctx, xe, ye > 0 ? ye : 1);
+    if (rc) return rc;
+    cudaStream_t st = ctx->stream;
+    std::vector<const float*> xs((size_t)n_ops), ups((size_t)n_ops, nullptr);
+    std::vector<std::vector<float*>> yv((size_t)n_ops);
+    std::vector<float* const*> ys((size_t)n_ops);
+    size_t yi = 0;
+    for (int i = 0; i < n_ops; ++i) {
+        const int64_t K = ops[i].weights[0]->K;
+        float* xd = ctx->dev_x + xo[(size_t)i];
+        xs[(size_t)i] = xd;
+        if (K > 0) {
+            CK(cudaMemcpy2DAsync(xd, (size_t)ldx[(size_t)i] * sizeof(float), ops[i].x, (size_t)K * sizeof(float),
+                                 (size_t)K * sizeof(float), (size_t)batch, cudaMemcpyHostToDevice, st),
+               "H2D x");
+            if (ops[i].x_up) {
+                float* ud = ctx->dev_x + uo[(size_t)i];
+                ups[(size_t)i] = ud;
+                CK(cudaMemcpy2DAsync(ud, (size_t)ldx[(size_t)i] * sizeof(float), ops[i].x_up,
+                                     (size_t)K * sizeof(float), (size_t)K * sizeof(float), (size_t)batch,
+                                     cudaMemcpyHostToDevice, st),
+                   "H2D x_up");
+            }
+        }
+        for (int j = 0; j < ops[i].n_weights; ++j) yv[(size_t)i].push_back(ctx->dev_y + yo[yi++]);
+        ys[(size_t)i] = yv[(size_t)i].data();
+    }
+    rc = chain_device(ctx, n_ops, ops, batch, st, xs.data(), ups.data(), ldx.data(), ys.data());
+    if (rc) return rc;
+    yi = 0;
+    for (int i = 0; i < n_ops; ++i)
+        for (int j = 0; j < ops[i].n_weights; ++j) {
+            const size_t n = (size_t)(ops[i].weights[j]->N * batch);
+            if (n > 0)
+                CK(cudaMemcpyAsync(ops[i].y[j], ctx->dev_y + yo[yi], n * sizeof(float), cudaMemcpyDeviceToHost, st),
+                   "D2H y");
+            ++yi;
+        }
+    return check_device_error(ctx, st);
 }
 
 int bramha_cuda_gemv_swiglu_dev(bramha_ctx* ctx, const bramha_weight* w, const float* gate_dev, const float* up_dev,
@@ -1143,6 +1357,10 @@ int bramha_cuda_gemm_noalloc_dev(bramha_ctx* ctx, const bramha_weight* w, const 
                     "gemm_noalloc_dev: x_dev must be 16-byte aligned bf16 [M][K] with K a multiple of 8");
     DeviceGuard g(ctx->device);
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    if (keff == 0) {  // an empty input gives zeros, as bramha_cuda_gemm_dev (a memset allocates nothing)
+        CK(cudaMemsetAsync(y_dev, 0, sizeof(float) * (size_t)(w->N * M), st), "memset(y)");
+        return BRAMHA_OK;
+    }
     float* scratch = nullptr;
     if (w->fmt == BRAMHA_FMT_LOG4) CK(noalloc_rowsum_scratch(ctx->device, &scratch), "cudaGetSymbolAddress(scratch)");
     CK(launch_gemm_tcgen05_bf16_noalloc(w->fmt, w->q, w->ldq, w->scales, w->N, keff, x_dev, w->K, M, y_dev, w->N,

@@ -23,6 +23,21 @@ namespace bramha {
 constexpr int kMaxGemvBatch = 8;     // GEMV kernels take batch 1..8 per launch
 constexpr int kMaxSegments = 8;      // weights fused into one GEMV launch
 
+// Device status block of a context.  Kernels are handed `int* err` = &err (the
+// first member); the tensor-core kernels also read the bound on their mbarrier
+// waits and the test-only fault switch from the same block.
+struct DevStatus {
+    int err;                        // 0 = ok, else the BRAMHA_ERR_* a kernel recorded
+    int fault;                      // kFault* (tests only; 0 in normal use)
+    unsigned long long timeout_ns;  // bound on every mbarrier wait
+};
+constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;  // 2 s
+// Test-only faults: CTA 0 of the next tensor-core GEMV (or GEMM) launches
+// withholds one weight copy, so the consumers' bounded waits run out.
+constexpr int kFaultNone = 0;
+constexpr int kFaultGemvWithholdCopy = 1;
+constexpr int kFaultGemmWithholdCopy = 2;
+
 // Bytes of one packed row (without padding) for a format.
 inline int64_t row_bytes_of(int fmt, int64_t K) {
     switch (fmt) {
@@ -106,10 +121,21 @@ struct GemvArgs {
     int64_t split_ws_floats;
     int* split_tickets;
     int split_tickets_n;
+    // L2 prefetch of the tensor-core GEMV: pf_ahead = slot pairs (even) that
+    // the bulk-copy producers request from HBM into L2 ahead of their copies
+    // (0 = none); pf_next_* = the weight buffers of the NEXT launch of a chain,
+    // whose first pf_next_total bytes the CTAs prefetch (a slice each) once
+    // their own copies are issued, so HBM keeps streaming across the launch
+    // boundary.
+    int pf_ahead;
+    int pf_next_n;
+    const uint8_t* pf_next_ptr[kMaxSegments];
+    int64_t pf_next_bytes[kMaxSegments];
+    int64_t pf_next_total;
 };
 
 constexpr int64_t kSplitWsFloats = 8 << 20;   // 32 MB of partial results per context
-constexpr int kSplitTickets = 1 << 18;         // tiles per launch that may be K-split
+constexpr int kSplitTickets = 1 << 18;         // K-split arrival counters (4 per tile of a launch)
 
 // CUDA-core GEMV for dense f32 weights (gemv_f32.cu).
 cudaError_t launch_gemv_f32(const GemvArgs& a, int num_sms, cudaStream_t stream);
@@ -120,10 +146,11 @@ cudaError_t launch_tile_weights(int fmt, const uint8_t* src, int64_t row_bytes, 
                                 cudaStream_t stream);
 
 // Prefill GEMM on tcgen05 (gemm_tcgen05.cu).  K = columns held by the packed
-// rows; x is bf16 (x_is_f32 = 0) or f32 (split into two bf16 passes).
+// rows; x is bf16 (x_is_f32 = 0) or f32 (split into bf16 hi + lo).  GEMMs with
+// fewer tiles than SMs are K-split through ws / tickets (NULL = never).
 cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const float* scales, int64_t N, int64_t K,
                                 const void* x, int x_is_f32, int64_t ldx, int64_t M, float* y, int64_t ldy, int* err,
-                                cudaStream_t stream);
+                                float* ws, int64_t ws_floats, int* tickets, int64_t n_tickets, cudaStream_t stream);
 
 // bf16-activation GEMM that allocates nothing: the log4 per-token sums go to
 // `rowsum_scratch` (at least M floats, caller-owned); x must be 16-byte

@@ -71,23 +71,38 @@ struct GemmArgs {
     // the M token rows at rows [0, M) and the lo parts at rows [lo_row,
     // lo_row + M); a tile carries BN/2 tokens, its hi rows in MMA columns
     // [0, BN/2) and its lo rows in [BN/2, BN), and the epilogue adds the two.
-    // One pass over K: each weight block is loaded and dequantized once.
+    // One pass over K: each weight block is loaded and dequantized once.  Also
+    // used without a table (a tile then carries BN/2 tokens).
     int lo_row;
+    // K split (single-CTA kernel, no tile table): each (weight block, token
+    // block) is cut into ksplit ranges of ks_steps K steps; a range writes its
+    // raw accumulators to `ws` and takes a ticket (one per TMEM lane quarter);
+    // the last range to arrive adds them in range order, applies the scale
+    // (and log4 correction) and stores y -- the result does not depend on
+    // which range finishes first.
+    int ksplit, ks_steps;
+    float* ws;
+    int* tickets;
 };
 
 // One output tile: 128-row block `wblk` of the (stacked) weight, token rows
-// [tok0, tok0 + mcount) of X and y, output columns [col0, col0 + 128).
+// [tok0, tok0 + mcount) of X and y, output columns [col0, col0 + 128), K steps
+// [kx0, kx1) (K split: range ks of the tile's nm-th (block, token block)).
 struct TileInfo {
     int wblk, tok0, mcount, col0;
+    int kx0, kx1, nm, ks;
 };
 template <int BN>
 __device__ __forceinline__ TileInfo tile_info(const GemmArgs& a, int t) {
     if (a.tiles) {
         const int4 v = __ldg(a.tiles + t);
-        return {v.x, v.y, v.z, v.w};
+        return {v.x, v.y, v.z, v.w, 0, a.x_steps, t, 0};
     }
-    const int nt = t % a.n_tiles, mt = t / a.n_tiles;
-    return {nt, mt * BN, min(BN, a.M - mt * BN), nt * BM};
+    const int tpt = a.lo_row ? BN / 2 : BN;  // tokens per tile
+    const int ks = t % a.ksplit, nm = t / a.ksplit;
+    const int nt = nm % a.n_tiles, mt = nm / a.n_tiles;
+    const int kx0 = ks * a.ks_steps;
+    return {nt, mt * tpt, min(tpt, a.M - mt * tpt), nt * BM, kx0, min(kx0 + a.ks_steps, a.x_steps), nm, ks};
 }
 
 // Packed weight bytes per row per stage.
@@ -190,8 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::offAbort);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ntiles = a.tiles ? __ldg(a.ntiles_dev) : a.n_tiles * a.m_tiles;
-    const int xs = a.x_steps;
+    const int ntiles = a.tiles ? __ldg(a.ntiles_dev) : a.n_tiles * a.m_tiles * a.ksplit;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S1; ++s) {
@@ -220,17 +234,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- producer
         if (lane == 0) {
             constexpr uint32_t kTx = L::kX + L::kP;
+            // test-only fault: CTA 0 withholds the copies of its second K step
+            const int withheld = blockIdx.x == 0 && injected_fault(a.err) == kFaultGemmWithholdCopy ? 1 : -1;
             int g = 0;  // K steps issued by this CTA, over all its tiles
             bool ok = true;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
                 const TileInfo ti = tile_info<BN>(a, t);
                 const uint8_t* wsrc = a.q + (int64_t)ti.wblk * a.k_steps * L::kP;
-                for (int kx = 0; kx < xs; ++kx, ++g) {
+                for (int kx = ti.kx0; kx < ti.kx1; ++kx, ++g) {
                     const int s = g % S1;
                     if (g >= S1 && !mbar_wait(&empty_x[s], ((g / S1) & 1) ^ 1, abort_flag, a.err)) {
                         ok = false;
                         break;
                     }
+                    if (g == withheld) continue;
                     mbar_expect_tx(&full_tma[s], kTx);
                     if (a.lo_row) {  // hi and lo rows of the tile's tokens, one half slot each
                         tma_load_2d(Xs + s * L::kX, &tmX, &full_tma[s], kx * BK, ti.tok0);
@@ -243,8 +260,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             // every issued copy lands before the CTA can exit
-            const uint64_t deadline = globaltimer() + kTimeoutNs;
-            for (int j = (g > S1 ? g - S1 : 0); j < g; ++j) mbar_wait_until(&full_tma[j % S1], (j / S1) & 1, deadline);
+            const uint64_t deadline = globaltimer() + wait_limit_ns(a.err);
+            for (int j = (g > S1 ? g - S1 : 0); j < g; ++j)
+                if (j != withheld) mbar_wait_until(&full_tma[j % S1], (j / S1) & 1, deadline);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer
@@ -257,7 +275,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lt >= 2 && !mbar_wait(&acc_empty[buf], ((lt >> 1) & 1) ^ 1, abort_flag, a.err)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(buf * BN);
-                for (int kx = 0; kx < xs; ++kx, ++g) {
+                const TileInfo ti = tile_info<BN>(a, t);
+                for (int kx = ti.kx0; kx < ti.kx1; ++kx, ++g) {
                     const int s1 = g % S1, s2 = g % S2;
                     if (!mbar_wait(&full_a[s2], (g / S2) & 1, abort_flag, a.err) ||
                         !mbar_wait(&full_tma[s1], (g / S1) & 1, abort_flag, a.err)) {
@@ -270,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk)
                         umma_bf16(d, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32), idesc,
-                                  (kx > 0 || kk > 0) ? 1u : 0u);
+                                  (kx > ti.kx0 || kk > 0) ? 1u : 0u);
                     umma_commit(&empty_x[s1]);
                     umma_commit(&empty_a[s2]);
                 }
@@ -278,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // every MMA issued above completes before TMEM is freed
             umma_commit(mma_done);
-            mbar_wait_until(mma_done, 0, globaltimer() + kTimeoutNs);
+            mbar_wait_until(mma_done, 0, globaltimer() + wait_limit_ns(a.err));
         }
     } else if (warp < 6) {
         // ---------------- dequantize (threads 64..191 -> tile rows)
@@ -286,7 +305,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         int g = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-            for (int kx = 0; kx < xs; ++kx, ++g) {
+            const TileInfo ti = tile_info<BN>(a, t);
+            for (int kx = ti.kx0; kx < ti.kx1; ++kx, ++g) {
                 const int s1 = g % S1, s2 = g % S2;
                 if (!mbar_wait(&full_tma[s1], (g / S1) & 1, abort_flag, a.err) ||
                     (g >= S2 && !mbar_wait(&empty_a[s2], ((g / S2) & 1) ^ 1, abort_flag, a.err))) {
@@ -343,6 +363,68 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float sc = row_ok ? __ldg(a.scales + (int64_t)ti.wblk * BM + row) : 0.f;
             float* ycol = a.y + grow;
             const uint32_t taddr = tmem + (uint32_t)(buf * BN) + ((uint32_t)(q4 * 32) << 16);
+            if (a.ksplit > 1) {
+                // K split: this range's raw accumulators -> workspace (token-major,
+                // a warp's 32 rows contiguous), then a ticket; the last range adds
+                // the ranges in order and stores the scaled result
+                float* part = a.ws + ((int64_t)ti.nm * a.ksplit + ti.ks) * (BM * ntok);
+#pragma unroll 1
+                for (int c0 = 0; c0 < ntok; c0 += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(taddr + c0, v);
+                    float o[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) o[j] = __uint_as_float(v[j]);
+                    if (a.lo_row) {
+                        tmem_ld32(taddr + (uint32_t)(BN / 2) + c0, v);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) o[j] += __uint_as_float(v[j]);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) part[(int64_t)(c0 + j) * BM + row] = o[j];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[buf]);  // TMEM no longer read
+                __threadfence();
+                __syncwarp();
+                int last = 0;
+                if (lane == 0) last = atomicAdd(&a.tickets[ti.nm * 4 + q4], 1) == a.ksplit - 1;
+                if (__shfl_sync(0xffffffffu, last, 0)) {
+                    __threadfence();
+                    const float* p0 = a.ws + (int64_t)ti.nm * a.ksplit * (BM * ntok);
+#pragma unroll 1
+                    for (int c0 = 0; c0 < ntok; c0 += 32) {
+                        float rs = 0.f;
+                        if constexpr (FMT == BRAMHA_FMT_LOG4) rs = c0 + lane < mc ? __ldg(a.rowsum + m0 + c0 + lane) : 0.f;
+                        float o[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) o[j] = __ldcg(p0 + (int64_t)(c0 + j) * BM + row);
+                        for (int r = 1; r < a.ksplit; ++r) {
+                            const float* pr = p0 + (int64_t)r * (BM * ntok);
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) o[j] += __ldcg(pr + (int64_t)(c0 + j) * BM + row);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if constexpr (FMT == BRAMHA_FMT_LOG4)
+                                o[j] = fmaf(o[j], 32768.0f, -__shfl_sync(0xffffffffu, rs, j));
+                            o[j] *= sc;
+                        }
+                        float* yc = ycol + (int64_t)(m0 + c0) * a.ldy;
+                        if (full) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) yc[(int64_t)j * a.ldy] = o[j];
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (row_ok && c0 + j < mc) yc[(int64_t)j * a.ldy] = o[j];
+                        }
+                    }
+                    if (lane == 0) a.tickets[ti.nm * 4 + q4] = 0;  // ready for the next launch
+                }
+                continue;
+            }
             // log4: per-token sums, one chunk of 32 ahead of its use
             float rs_next = 0.f;
             if constexpr (FMT == BRAMHA_FMT_LOG4) rs_next = lane < mc ? __ldg(a.rowsum + m0 + lane) : 0.f;
@@ -483,6 +565,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<FMT>::kTh
     if (warp == 0) {
         // ---------------- producer (both CTAs): this CTA's X half and weight block
         if (lane == 0) {
+            // test-only fault: CTA 0 of pair 0 withholds the copies of its second K step
+            const int withheld = blockIdx.x == 0 && injected_fault(a.err) == kFaultGemmWithholdCopy ? 1 : -1;
             int g = 0;
             bool ok = true;
             for (int t = pair; t < ntiles && ok; t += npairs) {
@@ -496,6 +580,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<FMT>::kTh
                         ok = false;
                         break;
                     }
+                    if (g == withheld) continue;
                     mbar_expect_tx(&full_x[s], L::kX);
                     tma_load_2d(Xs + s * L::kX, &tmX, &full_x[s], kx * BK, mt * BNP + (int)rank * (BNP / 2));
                     mbar_expect_tx(&full_p[s], has_w ? L::kP : 0);
@@ -504,8 +589,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<FMT>::kTh
                 }
             }
             // copies in flight land before the CTA can exit
-            const uint64_t deadline = globaltimer() + kTimeoutNs;
+            const uint64_t deadline = globaltimer() + wait_limit_ns(a.err);
             for (int j = (g > S ? g - S : 0); j < g; ++j) {
+                if (j == withheld) continue;
                 mbar_wait_until(&full_p[j % S], (j / S) & 1, deadline);
                 mbar_wait_until(&full_x[j % S], (j / S) & 1, deadline);
             }
@@ -542,7 +628,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<FMT>::kTh
             asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                              smem_u32(mma_done))
                          : "memory");
-            mbar_wait_until(mma_done, 0, globaltimer() + kTimeoutNs);
+            mbar_wait_until(mma_done, 0, globaltimer() + wait_limit_ns(a.err));
         }
     } else if (warp < 6) {
         // ---------------- dequantize (both CTAs, thread = weight row of this CTA's block)
@@ -744,7 +830,7 @@ cudaError_t launch_tiles(const CUtensorMap& tmX, const GemmArgs& g, cudaStream_t
         if (e != cudaSuccess) return e;
         attr_set.fetch_or(bit, std::memory_order_release);
     }
-    const int64_t ntiles = (int64_t)g.n_tiles * g.m_tiles;
+    const int64_t ntiles = (int64_t)g.n_tiles * g.m_tiles * g.ksplit;
     const int grid = (int)(ntiles < sm_count(dev) ? ntiles : sm_count(dev));
     kern<<<grid, kThreads, L::kAlloc, st>>>(tmX, g);
     return cudaGetLastError();
@@ -867,25 +953,53 @@ cudaError_t gemm_args(GemmArgs* g, const uint8_t* q, const float* scales, const 
     g->tiles = nullptr;
     g->ntiles_dev = nullptr;
     g->lo_row = 0;
+    g->ksplit = 1;
+    g->ks_steps = g->x_steps;
+    g->ws = nullptr;
+    g->tickets = nullptr;
     return cudaSuccess;
+}
+
+// K split of a single-CTA GEMM whose (weight block, token block) tiles do not
+// fill the GPU: ranges of at least 4 K steps, as many as bring the tile count
+// to about one per SM, within the workspace and ticket arrays.
+void plan_ksplit(GemmArgs* g, int bn, int sms, float* ws, int64_t ws_floats, int* tickets, int64_t n_tickets) {
+    const int64_t nm = (int64_t)g->n_tiles * g->m_tiles;
+    if (!ws || !tickets || nm >= sms || 4 * nm > n_tickets) return;
+    const int ntok = g->lo_row ? bn / 2 : bn;
+    int ks = (int)(sms / nm);
+    if (ks > g->x_steps / 4) ks = g->x_steps / 4;
+    while (ks > 1 && (int64_t)ks * nm * BM * ntok > ws_floats) --ks;
+    if (ks <= 1) return;
+    const int steps = (g->x_steps + ks - 1) / ks;
+    g->ksplit = (g->x_steps + steps - 1) / steps;  // no empty range
+    g->ks_steps = steps;
+    g->ws = ws;
+    g->tickets = tickets;
 }
 }  // namespace
 
 // y[M][ldy] = dequant(W)[N][K] applied to x[M][ldx] (bf16, or f32 split into
 // bf16 hi + lo).  K is the number of columns the packed rows hold.
+// f32 with M <= 128 tokens: the hi and lo parts are the two halves of the
+// MMA's N (each weight block loaded and dequantized once); larger M: side by
+// side along K.  GEMMs with fewer tiles than SMs are K-split through the
+// caller's workspace (ws / tickets; NULL = no split).
 // Scratch (bf16 copy, per-token sums) comes from the stream-ordered pool.
 cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const float* scales, int64_t N, int64_t K,
                                 const void* x, int x_is_f32, int64_t ldx, int64_t M, float* y, int64_t ldy, int* err,
-                                cudaStream_t st) {
+                                float* ws, int64_t ws_floats, int* tickets, int64_t n_tickets, cudaStream_t st) {
     if (M <= 0 || N <= 0) return cudaSuccess;
     if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff || K <= 0) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(q) & 15) != 0) return cudaErrorInvalidValue;
     if (!encode_fn()) return cudaErrorNotSupported;
     const int64_t kp = (K + BK - 1) / BK * BK;  // copy pitch per half: whole K steps
+    const bool nsplit = x_is_f32 && M <= 128;    // hi | lo as the halves of N
     const bool need_copy = x_is_f32 || (ldx % 8) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0;
     const bool log4 = fmt == BRAMHA_FMT_LOG4;
-    const int64_t cols = x_is_f32 ? 2 * kp : kp;  // columns of the bf16 copy
-    size_t copy_bytes = need_copy ? (size_t)M * cols * sizeof(__nv_bfloat16) : 0;
+    const int64_t cols = x_is_f32 && !nsplit ? 2 * kp : kp;  // columns of the bf16 copy
+    const int64_t crow = nsplit ? 2 * M : M;                  // rows of the bf16 copy
+    size_t copy_bytes = need_copy ? (size_t)crow * cols * sizeof(__nv_bfloat16) : 0;
     const size_t bytes = copy_bytes + (log4 ? (size_t)M * sizeof(float) : 0);
     uint8_t* scratch = nullptr;
     cudaError_t e = bytes ? cudaMallocAsync(reinterpret_cast<void**>(&scratch), bytes, st) : cudaSuccess;
@@ -895,7 +1009,9 @@ cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const fl
     if (need_copy || log4) {
         const int wpb = 8;
         const unsigned blocks = (unsigned)((M + wpb - 1) / wpb);
-        if (x_is_f32)
+        if (nsplit)
+            prep_kernel<true, true><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
+        else if (x_is_f32)
             prep_kernel<true><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
         else
             prep_kernel<false><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, need_copy ? kp : K, xc, rs);
@@ -903,13 +1019,23 @@ cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const fl
     }
     int dev = 0;
     if (e == cudaSuccess) e = cudaGetDevice(&dev);
-    const int bn = use_pair(M, N, sm_count(dev)) ? 0 : gemm_tile_n(M);
-    const int box = bn == 0 ? kPairTok / 2 : bn;  // X rows per TMA box (each CTA of a pair loads half a tile)
+    // N split: 2 x (32, 64 or 128) MMA columns (a 16-token half would not fill
+    // the epilogue's 32-column chunks)
+    const int bn = nsplit ? (M <= 32 ? 64 : M <= 64 ? 128 : 256) : use_pair(M, N, sm_count(dev)) ? 0 : gemm_tile_n(M);
+    // X rows per TMA box: a pair's CTA loads half a tile; an N-split tile loads hi and lo halves
+    const int box = bn == 0 ? kPairTok / 2 : nsplit ? bn / 2 : bn;
     GemmArgs g;
     CUtensorMap tmX;
-    if (e == cudaSuccess) e = gemm_args(&g, q, scales, rs, y, ldy, M, N, K, x_is_f32 != 0, bn, err);
+    if (e == cudaSuccess) e = gemm_args(&g, q, scales, rs, y, ldy, M, N, K, x_is_f32 != 0 && !nsplit, bn, err);
+    if (e == cudaSuccess && nsplit) {
+        g.lo_row = (int)M;
+        g.m_tiles = 1;
+    }
+    // (bf16 prefill keeps one range per tile: its results stay those of the
+    // allocation-free entry point, which has no workspace)
+    if (e == cudaSuccess && bn != 0 && x_is_f32) plan_ksplit(&g, bn, sm_count(dev), ws, ws_floats, tickets, n_tickets);
     if (e == cudaSuccess)
-        e = need_copy ? make_x_map(&tmX, xc, cols, M, cols, box) : make_x_map(&tmX, x, K, M, ldx, box);
+        e = need_copy ? make_x_map(&tmX, xc, cols, crow, cols, box) : make_x_map(&tmX, x, K, M, ldx, box);
     if (e == cudaSuccess) e = run_gemm(fmt, bn, tmX, g, st);
     if (scratch) {
         cudaError_t e2 = cudaFreeAsync(scratch, st);

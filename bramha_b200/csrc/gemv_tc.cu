@@ -139,7 +139,12 @@ struct TcGemvParams {
     int ctas_per_split;
     int ksplit;
     float* ws;             // [ntiles][ksplit][B][128] partials (ksplit > 1)
-    int* tickets;          // [ntiles] arrivals, zero between launches
+    int* tickets;          // [ntiles][4] arrivals per TMEM lane quarter, zero between launches
+    int pf_ahead;          // slot pairs (even) prefetched into L2 ahead of the copies
+    int pf_next_n;         // next launch's weight buffers (prefetched into L2 at our tail)
+    const uint8_t* pf_next_ptr[kMaxSegments];
+    int64_t pf_next_bytes[kMaxSegments];
+    int64_t pf_next_total;
 };
 
 struct alignas(1024) TcSmem {
@@ -152,7 +157,6 @@ struct alignas(1024) TcSmem {
     float sx_part[kActThreads / 32][8];  // per-warp partial sums, added in warp order
     uint32_t tmem;
     int abort_flag;
-    int last_split;
 };
 
 // Every lane polls; the warp proceeds only if all lanes saw the phase (so the
@@ -333,27 +337,47 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             if (c.i < nunit_tiles) c.base = tile_base(c.i);
         }
     };
-    // copies of slot pair d (slots 2d, 2d + 1; cursor c at slot 2d) into ring
-    // slots 2d % kSW, +1, completing on w_full[d % kSD]; one copy when the
-    // pair is contiguous
-    auto issue_pair = [&](int d, Cursor c) {
-        const int g = 2 * d, st = g % kSW;
-        const uint32_t b0 = (uint32_t)(min(Fm::kStepsPerSlot, nsteps - c.j * Fm::kStepsPerSlot) * Fm::kBlock);
-        const uint8_t* s0 = c.base + (int64_t)c.j * Fm::kStepsPerSlot * Fm::kBlock;
-        uint32_t b1 = 0;
-        const uint8_t* s1 = nullptr;
+    // source ranges of slot pair d (slots 2d, 2d + 1; cursor c at slot 2d)
+    auto pair_src = [&](int d, Cursor c, const uint8_t*& s0, uint32_t& b0, const uint8_t*& s1, uint32_t& b1) {
+        const int g = 2 * d;
+        b0 = (uint32_t)(min(Fm::kStepsPerSlot, nsteps - c.j * Fm::kStepsPerSlot) * Fm::kBlock);
+        s0 = c.base + (int64_t)c.j * Fm::kStepsPerSlot * Fm::kBlock;
+        b1 = 0;
+        s1 = nullptr;
         if (g + 1 < total) {
             advance(c, 1);
             b1 = (uint32_t)(min(Fm::kStepsPerSlot, nsteps - c.j * Fm::kStepsPerSlot) * Fm::kBlock);
             s1 = c.base + (int64_t)c.j * Fm::kStepsPerSlot * Fm::kBlock;
         }
+    };
+    // copies of slot pair d into ring slots 2d % kSW, +1, completing on
+    // w_full[d % kSD]; one copy when the pair is contiguous.  The weight lines
+    // are read once, so they are marked first to be evicted from L2.
+    const uint64_t pol = policy_evict_first();
+    auto issue_pair = [&](int d, Cursor c) {
+        const int st = (2 * d) % kSW;
+        const uint8_t *s0, *s1;
+        uint32_t b0, b1;
+        pair_src(d, c, s0, b0, s1, b1);
         uint64_t* bar = &S.w_full[d % kSD];
         mbar_expect_tx(bar, b0 + b1);
         if (s1 && b0 == (uint32_t)kSlotBytes && s1 == s0 + kSlotBytes) {
-            bulk_load(&S.w[st][0], s0, b0 + b1, bar);
+            bulk_load_hint(&S.w[st][0], s0, b0 + b1, bar, pol);
         } else {
-            bulk_load(&S.w[st][0], s0, b0, bar);
-            if (s1) bulk_load(&S.w[st + 1][0], s1, b1, bar);
+            bulk_load_hint(&S.w[st][0], s0, b0, bar, pol);
+            if (s1) bulk_load_hint(&S.w[st + 1][0], s1, b1, bar, pol);
+        }
+    };
+    // HBM -> L2 request of slot pair d, p.pf_ahead pairs before its copy
+    auto prefetch_pair = [&](int d, Cursor c) {
+        const uint8_t *s0, *s1;
+        uint32_t b0, b1;
+        pair_src(d, c, s0, b0, s1, b1);
+        if (s1 == s0 + b0) {
+            prefetch_l2(s0, b0 + b1);
+        } else {
+            prefetch_l2(s0, b0);
+            if (s1) prefetch_l2(s1, b1);
         }
     };
     const int npairs = (total + 1) / 2;
@@ -398,13 +422,26 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
     const bool producer = (warp == 0 || warp == kProdWarp1) && lane == 0;
     const int pid = warp == 0 ? 0 : 1;
     Cursor cur = {0, 0, nullptr};  // producer's cursor: slot 2 * (next pair of mine)
+    Cursor pcur = {0, 0, nullptr};  // its L2 prefetch cursor, pair pd
+    int pd = pid;
+    // keeps the prefetch front p.pf_ahead pairs past pair d (pairs of this producer)
+    auto prefetch_to = [&](int d) {
+        for (; pd < npairs && pd <= d + p.pf_ahead; pd += kNP) {
+            prefetch_pair(pd, pcur);
+            advance(pcur, 2 * kNP);
+        }
+    };
     if (producer) {
         cur.base = tile_base(0);
         advance(cur, 2 * pid);
+        pcur = cur;
         for (int d = pid; d < first; d += kNP) {
             issue_pair(d, cur);
             advance(cur, 2 * kNP);
         }
+        // pairs issued above need no prefetch; start the front past them
+        for (; pd < first; pd += kNP) advance(pcur, 2 * kNP);
+        if (p.pf_ahead > 0) prefetch_to(first - kNP);
     }
     const bool act = warp < kDeqWarp0 || warp >= kEpiWarp0;       // activation warps
     const int ta = (warp < kDeqWarp0 ? warp : warp - kEpiWarp0 + kDeqWarp0) * 32 + lane;  // 0..383
@@ -502,16 +539,46 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
     if (warp == 0 || warp == kProdWarp1) {
         // ---------------- bulk-copy producer `pid`: slot pairs d = pid, pid + 2, ...
         if (lane == 0) {
+            // test-only fault: producer 0 of CTA 0 withholds its first copy after the prologue
+            const bool withhold = pid == 0 && blockIdx.x == 0 && injected_fault(p.err) == kFaultGemvWithholdCopy;
+            int withheld = -1;
+            bool ok = true;
             int d = first + ((pid - first % kNP + kNP) % kNP);  // first pair of mine not yet requested
             for (; d < npairs; d += kNP) {
-                if (!mbar_wait(&S.w_empty[d % kSD], ((d / kSD) & 1) ^ 1, abort_flag, p.err)) break;
-                issue_pair(d, cur);
+                if (!mbar_wait(&S.w_empty[d % kSD], ((d / kSD) & 1) ^ 1, abort_flag, p.err)) {
+                    ok = false;
+                    break;
+                }
+                if (withhold && withheld < 0)
+                    withheld = d;
+                else
+                    issue_pair(d, cur);
                 advance(cur, 2 * kNP);
+                if (p.pf_ahead > 0) prefetch_to(d);
+            }
+            // the next launch of the chain: this producer's half of the CTA's
+            // slice of its first pf_next_total bytes, HBM -> L2
+            if (ok && p.pf_next_total > 0) {
+                const int64_t per = (p.pf_next_total / gridDim.x + 4095) & ~(int64_t)4095;
+                const int64_t half = (per / 2 + 4095) & ~(int64_t)4095;
+                int64_t lo = (int64_t)blockIdx.x * per + pid * half;
+                const int64_t hi = min(min((int64_t)blockIdx.x * per + per, lo + half), p.pf_next_total);
+                int64_t base = 0;
+                for (int r = 0; r < p.pf_next_n && lo < hi; ++r) {
+                    const int64_t end = base + p.pf_next_bytes[r];
+                    for (; lo < hi && lo < end;) {
+                        const int64_t n = min(min(hi, end) - lo, (int64_t)65536);
+                        prefetch_l2(p.pf_next_ptr[r] + (lo - base), (uint32_t)n);
+                        lo += n;
+                    }
+                    base = end;
+                }
             }
             // every copy this producer issued lands before the CTA exits
-            const uint64_t deadline = globaltimer() + kTimeoutNs;
+            const uint64_t deadline = globaltimer() + wait_limit_ns(p.err);
             for (int j = pid; j < d && j < npairs; j += kNP)
-                if (j + kSD >= d && !mbar_wait_until(&S.w_full[j % kSD], (j / kSD) & 1, deadline)) break;
+                if (j != withheld && j + kSD >= d && !mbar_wait_until(&S.w_full[j % kSD], (j / kSD) & 1, deadline))
+                    break;
         }
     } else if (warp >= kIssWarp0 && warp < kIssWarp0 + kNI) {
         // ---------------- MMA issuer `me`: slots g with g % kNI == me, into accumulator `me`
@@ -563,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             }
             // all MMAs issued have completed before TMEM and the ring are released
             umma_commit(&S.mma_done);
-            mbar_wait_until(&S.mma_done, 0, globaltimer() + kTimeoutNs);
+            mbar_wait_until(&S.mma_done, 0, globaltimer() + wait_limit_ns(p.err));
         }
     } else if (warp >= kDeqWarp0 && warp < kEpiWarp0) {
         if constexpr (Fm::kDeq) {
@@ -683,16 +750,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
                 continue;
             }
             // K split: publish this split's partial, take a ticket; the last
-            // split adds all partials in split order
+            // split adds all partials in split order.  Each warp (TMEM lane
+            // quarter) has its own ticket, so no barrier across the epilogue
+            // warps is needed (one that had given up a wait could not reach it).
             float* part = p.ws + (int64_t)tile * p.ksplit * B * TM;
             if (grow < sg.N)
 #pragma unroll
                 for (int b = 0; b < B; ++b) part[((int64_t)split * B + b) * TM + row] = res[b];
             __threadfence();
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            if (row == 0) S.last_split = atomicAdd(&p.tickets[tile], 1) == p.ksplit - 1;
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            if (S.last_split) {
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) last = atomicAdd(&p.tickets[tile * 4 + q4], 1) == p.ksplit - 1;
+            if (__shfl_sync(0xffffffffu, last, 0)) {
                 __threadfence();
                 if (grow < sg.N)
 #pragma unroll
@@ -701,7 +770,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
                         for (int s = 0; s < p.ksplit; ++s) acc += __ldcg(part + ((int64_t)s * B + b) * TM + row);
                         sg.y[(int64_t)b * sg.ldy + grow] = acc;
                     }
-                if (row == 0) p.tickets[tile] = 0;  // ready for the next launch
+                if (lane == 0) p.tickets[tile * 4 + q4] = 0;  // ready for the next launch
             }
         }
     }
@@ -813,8 +882,19 @@ cudaError_t launch_gemv_tc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t
     p.tickets = a.split_tickets;
     // splits need a workspace slot per (tile, split, batch row) and a ticket per tile
     int max_ksplit = 1;
-    if (a.split_ws && a.split_tickets && ntiles <= a.split_tickets_n)
+    if (a.split_ws && a.split_tickets && 4 * (int64_t)ntiles <= a.split_tickets_n)
         max_ksplit = (int)(a.split_ws_floats / ((int64_t)ntiles * a.batch * TM));
+    p.pf_ahead = a.pf_ahead < 0 ? 0 : (a.pf_ahead + 1) & ~1;
+    p.pf_next_n = a.pf_next_n < 0 ? 0 : (a.pf_next_n > kMaxSegments ? kMaxSegments : a.pf_next_n);
+    int64_t pf_avail = 0;
+    for (int i = 0; i < p.pf_next_n; ++i) {
+        if ((reinterpret_cast<uintptr_t>(a.pf_next_ptr[i]) & 15) != 0 || (a.pf_next_bytes[i] & 15) != 0)
+            return cudaErrorInvalidValue;
+        p.pf_next_ptr[i] = a.pf_next_ptr[i];
+        p.pf_next_bytes[i] = a.pf_next_bytes[i];
+        pf_avail += a.pf_next_bytes[i];
+    }
+    p.pf_next_total = (a.pf_next_total < pf_avail ? a.pf_next_total : pf_avail) & ~(int64_t)4095;
 #define BRAMHA_TC_B(n)                                                                                   \
     case n:                                                                                              \
         return fmt == BRAMHA_FMT_LOG4    ? launch_b<BRAMHA_FMT_LOG4, n>(p, max_ksplit, num_sms, st)      \

@@ -12,7 +12,14 @@
 namespace bramha {
 namespace {
 
-constexpr uint64_t kTimeoutNs = 2000000000ull;  // bound on every mbarrier wait (%globaltimer)
+// The bound on every mbarrier wait (%globaltimer nanoseconds) and the test-only
+// fault switch live in the context's DevStatus, whose first member is `err`.
+__device__ __forceinline__ uint64_t wait_limit_ns(const int* err) {
+    return err ? __ldcg(&reinterpret_cast<const DevStatus*>(err)->timeout_ns) : kDefaultTimeoutNs;
+}
+__device__ __forceinline__ int injected_fault(const int* err) {
+    return err ? __ldcg(&reinterpret_cast<const DevStatus*>(err)->fault) : kFaultNone;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -64,10 +71,11 @@ __device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
 __device__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err) {
     if (mbar_test(b, parity) || mbar_try_wait(b, parity)) return true;
     const uint64_t t0 = globaltimer();
+    const uint64_t limit = wait_limit_ns(err);
     for (;;) {
         if (mbar_try_wait(b, parity)) return true;
         if (*abort_flag) return false;
-        if (globaltimer() - t0 > kTimeoutNs) {
+        if (globaltimer() - t0 > limit) {
             *abort_flag = 1;
             atomicCAS(err, 0, (int)BRAMHA_ERR_TIMEOUT);
             return false;
@@ -92,6 +100,27 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                      smem_u32(dst)),
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
+}
+
+// Same, with an L2 eviction-priority policy (createpolicy) for the source lines.
+__device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                               uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+// L2 policy: lines read once (a weight stream) are the first to be evicted.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// Asynchronous prefetch of global memory into L2 (no completion, no data to
+// shared memory): 16-byte aligned address, size a multiple of 16 bytes.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {

@@ -40,7 +40,7 @@ from typing import Optional, Sequence
 
 import numpy as np
 
-from ._lib import DTYPE, FMT, BramhaError, check, lib
+from ._lib import DTYPE, FMT, BramhaError, GemvOp, check, lib
 
 _vp = ctypes.c_void_p
 
@@ -303,6 +303,58 @@ class CudaComputePlane:
         """'auto' (default), 'tensor_core' or 'cuda_core' for the quantized GEMVs."""
         check(lib().bramha_cuda_set_gemv_kernel(self._ctx, self.GEMV_KERNELS[kind]))
 
+    TEST_FAULTS = {"none": 0, "gemv": 1, "gemm": 2}
+
+    def set_wait_timeout(self, ns: int = 0):
+        """Bound on every device-side wait of the tensor-core kernels (0 = the 2 s default)."""
+        check(lib().bramha_cuda_set_wait_timeout(self._ctx, int(ns)))
+
+    def test_fault(self, kind: str = "none"):
+        """TEST ONLY: CTA 0 of later tensor-core GEMV ('gemv') or GEMM ('gemm')
+        launches withholds one weight copy, so a bounded wait runs out."""
+        check(lib().bramha_cuda_test_fault(self._ctx, self.TEST_FAULTS[kind]))
+
+    def set_prefetch(self, lookahead_bytes: int = 128 << 10, next_launch_bytes: int = 24 << 20):
+        """L2 prefetch of the tensor-core GEMV (tuning only; results do not change)."""
+        check(lib().bramha_cuda_set_prefetch(self._ctx, int(lookahead_bytes), int(next_launch_bytes)))
+
+    @staticmethod
+    def _chain_ops(ops):
+        """[(weights, x, ys[, x_up])] -> (GemvOp array, keep-alive list); x / ys / x_up
+        are torch tensors or numpy arrays (pointers taken as they are)."""
+        arr = (GemvOp * len(ops))()
+        keep = []
+        for i, op in enumerate(ops):
+            ws, x, ys = op[0], op[1], op[2]
+            up = op[3] if len(op) > 3 else None
+            wa = (ctypes.c_void_p * len(ws))(*[w.handle for w in ws])
+            ya = (ctypes.c_void_p * len(ys))(*[_ptr(y) for y in ys])
+            keep += [wa, ya]
+            arr[i].n_weights = len(ws)
+            arr[i].weights = ctypes.cast(wa, ctypes.POINTER(ctypes.c_void_p))
+            arr[i].x = _ptr(x)
+            arr[i].x_up = None if up is None else _ptr(up)
+            arr[i].y = ctypes.cast(ya, ctypes.POINTER(ctypes.c_void_p))
+        return arr, keep
+
+    def gemv_chain_dev(self, ops, batch: int = 1, stream=None):
+        """A chain of dependent GEMV launches on CUDA tensors: ops = [(weights, x, ys)
+        or (weights, x, ys, x_up)]; launch i prefetches launch i+1's weights into L2."""
+        arr, keep = self._chain_ops(ops)
+        check(lib().bramha_cuda_gemv_chain_dev(self._ctx, len(ops), arr, batch, _stream(stream)))
+        del keep
+
+    def gemv_chain(self, ops, batch: int = 1):
+        """The same chain on host buffers (numpy arrays or pinned torch CPU tensors):
+        inputs copied in, the chain run, outputs copied back; synchronous."""
+        for op in ops:
+            for a in (op[1],) + tuple(op[2]) + ((op[3],) if len(op) > 3 and op[3] is not None else ()):
+                if isinstance(a, np.ndarray) and (a.dtype != np.float32 or not a.flags.c_contiguous):
+                    raise BramhaError(-1, "gemv_chain: host buffers must be contiguous float32")
+        arr, keep = self._chain_ops(ops)
+        check(lib().bramha_cuda_gemv_chain(self._ctx, len(ops), arr, batch))
+        del keep
+
     def stream_sync(self, stream=None):
         """Wait for the stream and raise if a kernel reported a device-side failure."""
         check(lib().bramha_cuda_stream_sync(self._ctx, _stream(stream)))
@@ -311,6 +363,13 @@ class CudaComputePlane:
         n, k = w.shape
         check(lib().bramha_cuda_quantize_dev(self._ctx, FMT[fmt], n, k, w.data_ptr(), q.data_ptr(),
                                              scales.data_ptr(), _stream(stream)))
+
+
+def _ptr(a) -> int:
+    """Address of a torch tensor's or numpy array's data."""
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
 
 
 _STREAM_LEGACY = 0x1  # cudaStreamLegacy: the legacy default stream, valid in any CUDA runtime

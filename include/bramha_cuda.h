@@ -119,6 +119,35 @@ BRAMHA_API int bramha_cuda_memory_used(bramha_ctx* ctx, size_t* bytes);
 #define BRAMHA_GEMV_CUDA_CORE 2
 BRAMHA_API int bramha_cuda_set_gemv_kernel(bramha_ctx* ctx, int kind);
 
+/* Bound on every device-side wait of the tensor-core kernels, in nanoseconds
+ * of %globaltimer (default 2 s; 0 restores it).  A kernel whose wait runs out
+ * records BRAMHA_ERR_TIMEOUT, drains the copies and MMAs it issued, frees its
+ * TMEM and returns; the host-buffer calls and bramha_cuda_stream_sync then
+ * return BRAMHA_ERR_TIMEOUT (the reference reports a failed GPU call as
+ * `Err(String)`, wgpu_backend.rs:1096-1104, and falls back to the CPU).  Set it
+ * while no work of the context is in flight. */
+BRAMHA_API int bramha_cuda_set_wait_timeout(bramha_ctx* ctx, uint64_t ns);
+
+/* TEST ONLY (no counterpart in the reference): makes CTA 0 of every later
+ * tensor-core GEMV (kind BRAMHA_TEST_FAULT_GEMV) or tensor-core GEMM (kind
+ * BRAMHA_TEST_FAULT_GEMM) launch of this context withhold one weight copy, so
+ * the consumers' bounded waits run out and the call reports
+ * BRAMHA_ERR_TIMEOUT without hanging or faulting the GPU.  Kind 0 turns it off.
+ * Use a short bramha_cuda_set_wait_timeout with it. */
+#define BRAMHA_TEST_FAULT_NONE 0
+#define BRAMHA_TEST_FAULT_GEMV 1
+#define BRAMHA_TEST_FAULT_GEMM 2
+BRAMHA_API int bramha_cuda_test_fault(bramha_ctx* ctx, int kind);
+
+/* L2 prefetch of the tensor-core GEMV (tuning; no counterpart in the
+ * reference).  lookahead_bytes: how far ahead of its shared-memory copies each
+ * CTA asks HBM for its weight stream (default 128 KB; 0 = off).
+ * next_launch_bytes: in a GEMV chain, how many of the next launch's weight
+ * bytes the current launch requests into L2 once its own copies are issued
+ * (default 24 MB; 0 = off).  Prefetching reads no memory outside the weights
+ * and changes no result. */
+BRAMHA_API int bramha_cuda_set_prefetch(bramha_ctx* ctx, int64_t lookahead_bytes, int64_t next_launch_bytes);
+
 /* ---------------------------------------------------------------- weights */
 
 /* get_or_create_op (wgpu_backend.rs:603-722): copies the packed weight and
@@ -173,6 +202,34 @@ BRAMHA_API int bramha_cuda_gemv_multi_dev(bramha_ctx* ctx, int n_weights, const 
  * 16-byte aligned; y [batch][N]; stream-ordered. */
 BRAMHA_API int bramha_cuda_gemv_swiglu_dev(bramha_ctx* ctx, const bramha_weight* w, const float* gate_dev,
                                            const float* up_dev, int64_t batch, float* y_dev, void* stream);
+
+/* A chain of dependent GEMVs: the reference's decode loop calls
+ * matvec_mul_into back to back (fused_qkv_mul_into, o_proj, run_mlp_into's
+ * gate / up / down, lm_head; cpu_engine.rs:2873-2976), each GEMV reading what
+ * the previous steps wrote.  ops[i] is one launch of 1..8 weights sharing x
+ * (same format and K), run after ops[i-1] in stream order; while it runs it
+ * also requests the first weights of ops[i+1] from HBM into L2, so the
+ * weight stream does not pause at the launch boundary.  x_up non-NULL makes
+ * the activation silu(x) * x_up (the down projection of a SwiGLU MLP, as
+ * bramha_cuda_gemv_swiglu_dev).  Results equal one bramha_cuda_gemv_multi_dev
+ * (or _swiglu_dev) call per op. */
+typedef struct bramha_gemv_op {
+    int n_weights;                         /* 1..8 */
+    const bramha_weight* const* weights;   /* n_weights handles */
+    const float* x;                        /* [batch][K] */
+    const float* x_up;                     /* NULL, or [batch][K] (SwiGLU) */
+    float* const* y;                       /* y[i] is [batch][N_i] */
+} bramha_gemv_op;
+
+/* Device pointers, stream-ordered (x 16-byte aligned, as gemv_multi_dev). */
+BRAMHA_API int bramha_cuda_gemv_chain_dev(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch,
+                                          void* stream);
+
+/* Host buffers (any alignment), synchronous: every op's x is copied to the
+ * device, the chain runs, every y is copied back, and the call returns once
+ * they are in host memory (one wait for the whole chain, which also reports a
+ * device-side failure). */
+BRAMHA_API int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch);
 
 /* The reference's keyed one-shot call, e.g.
  * `matvec_mul_int4(h, q_weight, scales, out_features, model_name, layer_name)`
@@ -319,9 +376,10 @@ BRAMHA_API int bramha_cuda_gemm_noalloc_dev(bramha_ctx* ctx, const bramha_weight
                                             float* y_dev, void* stream);
 
 /* Waits for `stream` (NULL = the context stream) and reports a failure that a
- * kernel recorded on the device: the tensor-core GEMM bounds every wait and
- * returns BRAMHA_ERR_TIMEOUT here instead of hanging.  Host-buffer calls
- * already check this before returning. */
+ * kernel recorded on the device: the tensor-core GEMV and GEMM bound every
+ * wait and return BRAMHA_ERR_TIMEOUT here instead of hanging.  Host-buffer
+ * calls (bramha_cuda_gemv, _matvec, _gemm, _gemv_chain, _moe_mlp, ...) check
+ * this before returning. */
 BRAMHA_API int bramha_cuda_stream_sync(bramha_ctx* ctx, void* stream);
 
 /* ------------------------------------------------------------ packers (GPU) */

@@ -42,11 +42,29 @@ _i64 = ctypes.c_int64
 
 def build(force: bool = False) -> str:
     """Compile liboracle.so with its Makefile (gcc, no fast-math, no FMA contraction)."""
+    target = os.path.basename(_LIB_PATH)
     if force or not os.path.exists(_LIB_PATH) or (
         os.path.getmtime(_LIB_PATH) < os.path.getmtime(os.path.join(_HERE, "bramha_oracle.c"))
     ):
-        subprocess.run(["make", "-s", "-C", _HERE, "-B" if force else "liboracle.so"], check=True)
+        subprocess.run(["make", "-s", "-C", _HERE] + (["-B"] if force else []) + [target], check=True)
     return _LIB_PATH
+
+
+def use_native_build() -> bool:
+    """Switch this process to a ``-march=native`` build of the same source, for
+    the timed CPU legs of bench.py only: the reference compiles with
+    ``target-cpu=native`` (.cargo/config.toml:2).  The build is redone on the
+    host that runs it (a native binary does not travel); on failure the
+    portable build stays in use and False is returned."""
+    global _lib, _LIB_PATH
+    native = os.path.join(_HERE, "liboracle_native.so")
+    try:
+        subprocess.run(["make", "-s", "-B", "-C", _HERE, "liboracle_native.so"], check=True, capture_output=True)
+    except Exception:
+        return False
+    _lib = None
+    _LIB_PATH = native
+    return True
 
 
 def lib():
