@@ -14,9 +14,11 @@ which each launch requests the next one's weights into L2).  Synthetic data;
 the 3.55 GB of packed weights per step exceed the 126 MB L2, so no flush is
 needed.  The same weights are then run at batch 8 and 64 (`batch_lines`).
 
-N > 1: every linear is column-sharded (output rows split across ranks) and
-each shard's output is all-gathered with NCCL (strong scaling: total work
-fixed).  The linears' inputs are independent synthetic vectors.
+N > 1: every linear is column-sharded (output rows split across ranks); each
+GEMV's epilogue stores its rows into every rank's copy of the output over
+NVLink and publishes the launch, and the next GEMV waits for every rank's
+publication (strong scaling: total work fixed).  The linears' inputs are
+independent synthetic vectors, the same on every rank.
 
 Prints ONE JSON line on rank 0.  `value` is algorithmic GB/s over the whole job
 (packed weights + scales + x + y per GEMV); `e2e` is the same metric through the
@@ -680,15 +682,17 @@ def run_ours(args, ws, rank, local):
         dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
     plane = CudaComputePlane(local)
     fmt, B, bits = args.fmt, args.batch, BITS[args.fmt]
+    sp = None
+    if ws > 1:
+        # column-shard group: every linear's output rows split across the ranks; the
+        # GEMV epilogue stores each rank's rows into every rank's copy over NVLink
+        from bramha_b200 import ShardedPlane
+        sp = ShardedPlane(plane, arena_bytes=64 << 20)
 
-    def shard(n):
-        lo = n * rank // ws
-        hi = n * (rank + 1) // ws
-        return lo, hi
-
-    # ---- weights: generate full N(0,0.02) rows on device, keep this rank's shard, pack on device
+    # ---- weights: each linear generated whole (N(0,0.02), the same seed on every
+    # rank), packed on the device; with N > 1 each rank keeps its rows
     gen = torch.Generator(device=dev)
-    layers = []  # per layer: list of (group, [Weight], x, [y_local], y_full)
+    layers = []  # per layer: list of (group, [Weight], x, [y], None)
     step_bytes = 0
     t_setup = time.time()
     for li in range(args.layers + 1):
@@ -697,58 +701,38 @@ def run_ours(args, ws, rank, local):
         for gname, parts, k in groups:
             wts, ys = [], []
             for p, n in parts:
-                lo, hi = shard(n)
-                gen.manual_seed(1_000_003 * li + sum(map(ord, p)) + 7919 * rank)
-                # rows lo..hi of the full matrix: draw the full-row stream for this shard only
-                wf = torch.randn((hi - lo, k), generator=gen, device=dev, dtype=torch.float32).mul_(0.02)
-                qb = (hi - lo) * k * bits // 8
-                qd = torch.empty(qb, dtype=torch.uint8, device=dev)
-                sd = torch.empty(hi - lo, dtype=torch.float32, device=dev)
+                gen.manual_seed(1_000_003 * li + sum(map(ord, p)))
+                wf = torch.randn((n, k), generator=gen, device=dev, dtype=torch.float32).mul_(0.02)
+                qd = torch.empty(n * k * bits // 8, dtype=torch.uint8, device=dev)
+                sd = torch.empty(n, dtype=torch.float32, device=dev)
                 plane.quantize_dev(fmt, wf, qd, sd)
                 del wf
-                w = plane.register_dev(f"L{li}.{p}", fmt, hi - lo, k, qd, sd)
+                if sp is None:
+                    w = plane.register_dev(f"L{li}.{p}", fmt, n, k, qd, sd)
+                    ys.append(torch.empty((B, n), dtype=torch.float32, device=dev))
+                else:
+                    w = sp.register_dev(f"L{li}.{p}", fmt, n, k, qd, sd)
+                    ys.append(sp.empty((B, n)))  # the full output, in the symmetric arena
                 del qd, sd
                 wts.append(w)
-                ys.append(hi - lo)
                 step_bytes += gemv_bytes(n, k, B, bits)  # whole-job algorithmic bytes
             gen.manual_seed(7 + li * 13 + len(entry))
             x = torch.randn((B, k), generator=gen, device=dev, dtype=torch.float32)
-            ntot = sum(w.N for w in wts)
-            # batch 1: the parts' outputs are consecutive views of one buffer, which is
-            # also the all-gather send buffer (no concatenation copy)
-            ybuf = torch.empty((B * ntot,), dtype=torch.float32, device=dev)
-            if B == 1:
-                offs = [0]
-                for nloc in ys:
-                    offs.append(offs[-1] + nloc)
-                ys = [ybuf[offs[i]:offs[i + 1]].view(1, -1) for i in range(len(ys))]
-            else:
-                ys = [torch.empty((B, nloc), dtype=torch.float32, device=dev) for nloc in ys]
-            y_full = torch.empty((ws, B * ntot), dtype=torch.float32, device=dev) if ws > 1 else None
-            entry.append((gname, wts, x, ys, (ybuf, y_full)))
+            entry.append((gname, wts, x, ys, None))
         layers.append(entry)
     torch.cuda.synchronize()
     setup_s = time.time() - t_setup
     launches_per_step = sum(len(e) for e in layers)
 
     stream = torch.cuda.Stream(device=dev)
-    # one GPU: the step is one GEMV chain (bramha_cuda_gemv_chain_dev): each
-    # launch requests the next launch's weights into L2 while it runs
+    # the step is one GEMV chain (bramha_cuda_gemv_chain_dev); with N > 1 the
+    # GEMVs are sharded and the step ends when every rank's rows have landed
     chain_ops = [(wts, x, ys) for entry in layers for _, wts, x, ys, _ in entry]
 
     def step():
-        if ws == 1:
-            plane.gemv_chain_dev(chain_ops, B, stream)
-            return
-        for entry in layers:
-            for gname, wts, x, ys, (ybuf, y_full) in entry:
-                plane.gemv_multi_dev(wts, x, ys)
-                if ws > 1:
-                    if B == 1:
-                        local_y = ybuf
-                    else:
-                        local_y = torch.cat([y.reshape(-1) for y in ys]) if len(ys) > 1 else ys[0].reshape(-1)
-                    dist.all_gather_into_tensor(y_full.view(-1), local_y)
+        plane.gemv_chain_dev(chain_ops, B, stream)
+        if sp is not None:
+            sp.sync(stream)
 
     # ---- capture one step (GEMVs and, on several GPUs, the NCCL all-gathers) in a
     # CUDA graph; replay it K times
@@ -834,6 +818,8 @@ def run_ours(args, ws, rank, local):
         gg = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gg, stream=stream):
             plane.gemv_chain_dev(items, B, stream)
+            if sp is not None:
+                sp.sync(stream)
         gg.replay()
         torch.cuda.synchronize()
         with torch.cuda.stream(stream):
@@ -845,6 +831,9 @@ def run_ours(args, ws, rank, local):
         torch.cuda.synchronize()
         per[gname] = [a_.elapsed_time(b_) * 1e3 / (reps * len(items))] * len(items)
         del gg
+    def shard(n):  # this rank's rows [lo, hi) of an n-row linear
+        return n * rank // ws, n * (rank + 1) // ws
+
     group_bytes = {}
     for gname, parts, k in GROUPS + [("lm_head", [("lm_head", V)], H)]:
         nloc = sum(shard(n)[1] - shard(n)[0] for _, n in parts)
@@ -873,15 +862,13 @@ def run_ours(args, ws, rank, local):
         for gname, wts, x, ys, _ in entry:
             xh = torch.empty((B, x.shape[1]), dtype=torch.float32, pin_memory=True)
             xh.copy_(x.cpu())
-            yhs = [torch.empty((B, w.N), dtype=torch.float32, pin_memory=True) for w in wts]
+            yhs = [torch.empty((B, w.n_full), dtype=torch.float32, pin_memory=True) for w in wts]
             host_ops.append((wts, xh, yhs))
             h2d += xh.numel() * 4
             d2h += sum(y.numel() * 4 for y in yhs)
 
     def e2e_step():
-        plane.gemv_chain(host_ops, B)
-        # N > 1: each rank's host buffers hold its shard of every output (the
-        # gather of the shards is not part of this host-buffer figure)
+        plane.gemv_chain(host_ops, B)  # N > 1: every rank's host buffers receive the full outputs
 
     e2e_steps = max(2, min(args.steps, 10))
     e2e_step()
@@ -927,7 +914,8 @@ def run_ours(args, ws, rank, local):
             "data": "synthetic (seeded N(0,0.02) weights packed on device, N(0,1) activations)",
             "config": {"workload": f"qwen2-7b linears ({args.layers} layers + lm_head), {fmt}, batch {B} decode GEMV",
                        "batch": B, "fmt": fmt, "hidden": H, "intermediate": I, "vocab": V, "layers": args.layers,
-                       "parallelism": f"column-shard x{ws} + NCCL all-gather" if ws > 1 else "single GPU",
+                       "parallelism": f"column-shard x{ws}: each GEMV's epilogue stores its rows into every rank's "
+                                      "output over NVLink (no collective library)" if ws > 1 else "single GPU",
                        "l2": f"no flush: {step_bytes / 1e9:.2f} GB of packed weights per step >> 126 MB L2",
                        "cuda_graph": graph is not None,
                        "gemv_kernel": "tc_gemv_kernel: tile-major weights streamed by 2 bulk-copy producers, "
@@ -956,6 +944,9 @@ def run_ours(args, ws, rank, local):
         print(json.dumps(line), flush=True)
     del graph
     if ws > 1:
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[local])  # no rank reads or writes a peer's arena any more
+        plane.close()
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
 

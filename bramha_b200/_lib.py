@@ -81,6 +81,16 @@ _SIGNATURES = {
     "bramha_cuda_set_wait_timeout": [_vp, ctypes.c_uint64],
     "bramha_cuda_test_fault": [_vp, _int],
     "bramha_cuda_set_prefetch": [_vp, _i64, _i64],
+    "bramha_cuda_set_gemv_tuning": [_vp, _int, _i64],
+    "bramha_cuda_shard_handle": [_vp, _sz, _vp],
+    "bramha_cuda_shard_init": [_vp, _int, _int, _vp],
+    "bramha_cuda_shard_malloc": [_vp, _sz, ctypes.POINTER(_vp)],
+    "bramha_cuda_register_weight_shard": [_vp, ctypes.c_char_p, _int, _i64, _i64, _vp, _sz, _vp, _sz,
+                                          ctypes.POINTER(_vp)],
+    "bramha_cuda_register_weight_shard_dev": [_vp, ctypes.c_char_p, _int, _i64, _i64, _vp, _sz, _vp, _sz, _vp,
+                                              ctypes.POINTER(_vp)],
+    "bramha_cuda_shard_rows": [_vp, _i64, ctypes.POINTER(_i64), ctypes.POINTER(_i64)],
+    "bramha_cuda_shard_sync_dev": [_vp, _vp],
     "bramha_cuda_gemv_chain_dev": [_vp, _int, _vp, _i64, _vp],
     "bramha_cuda_gemv_chain": [_vp, _int, _vp, _i64],
     "bramha_cuda_op_embed": [_vp, _vp, _i64, _i64, _vp, _vp, _vp],

@@ -39,6 +39,8 @@ struct bramha_weight {
     bramha_ctx* ctx = nullptr;
     std::list<std::string>::iterator lru_it;
     Sp24Weight sp{};  // 2:4 sparse layout inside q (is_sp24(fmt))
+    bool shard = false;    // rows [row0, row0 + N) of an n_full-row weight (column-shard group)
+    int64_t row0 = 0, n_full = 0;
 };
 
 struct bramha_ctx {
@@ -60,9 +62,29 @@ struct bramha_ctx {
     float* split_ws = nullptr;           // K-split partials of the tensor-core GEMV
     int* split_tickets = nullptr;        // per-tile arrival counters (kept zero between launches)
     int gemv_kernel = BRAMHA_GEMV_AUTO;  // kernel choice for the tiled formats
-    int64_t pf_lookahead = 128 << 10;    // GEMV L2 lookahead per CTA, bytes
-    int64_t pf_next = 24 << 20;          // GEMV chain: bytes of the next launch requested into L2
+    // GEMV tuning (measured on the Qwen2-7B step: L2 lookahead slowed the large
+    // launches, next-launch prefetch of 8 MB was neutral to slightly positive,
+    // and a K-split whose tiles are short makes the epilogue the bottleneck)
+    int64_t pf_lookahead = 0;            // GEMV L2 lookahead per CTA, bytes
+    int64_t pf_next = 8 << 20;           // GEMV chain: bytes of the next launch requested into L2
+    int evict_first = 0;                 // GEMV weight copies marked first to be evicted from L2
+    int split_cost = 240;                // GEMV K-split plan: cost of splitting, eighths of a block
+    // column-shard group (bramha_cuda_shard_*): this rank's symmetric arena
+    // (control block, then allocations from the bottom and host-chain staging
+    // from the top) and the peers' arenas opened through CUDA IPC
+    int shard_world = 0, shard_rank = 0;
+    uint8_t* arena = nullptr;
+    size_t arena_bytes = 0, arena_used = 0, arena_top = 0;
+    uint8_t* peer_arena[kMaxShardWorld] = {};
 };
+
+namespace {
+// Control block at the start of every arena.
+constexpr size_t kArenaFlags = 0;     // u32 flags[world]: epochs ranks published here
+constexpr size_t kArenaEpoch = 64;    // u32: sharded launches this rank completed
+constexpr size_t kArenaDone = 128;    // u32: CTAs of the running launch that finished
+constexpr size_t kArenaHeader = 4096; // allocations start here
+}  // namespace
 
 namespace {
 
@@ -453,11 +475,19 @@ int check_weight(const bramha_ctx* ctx, const bramha_weight* w) {
 // x_up (optional, tensor-core formats only): the activation is silu(x) * x_up.
 // next_ws (optional): the weights of the next launch of a chain, whose first
 // bytes the tensor-core GEMV requests into L2 at its tail.
+int gemv_device_sharded(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const float* x, int64_t ldx,
+                        int64_t batch, float* const* ys, cudaStream_t st, const float* x_up, int next_n,
+                        const bramha_weight* const* next_ws);
+
 int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const float* x, int64_t ldx,
                 int64_t batch, float* const* ys, cudaStream_t st, const float* x_up = nullptr, int next_n = 0,
                 const bramha_weight* const* next_ws = nullptr) {
     const int fmt = ws[0]->fmt;
     const int64_t K = ws[0]->K;
+    for (int i = 1; i < n; ++i)
+        if (ws[i]->shard != ws[0]->shard)
+            return fail(BRAMHA_ERR_INVALID, "one launch cannot mix sharded and unsharded weights");
+    if (ws[0]->shard) return gemv_device_sharded(ctx, n, ws, x, ldx, batch, ys, st, x_up, next_n, next_ws);
     if (batch <= 0) return BRAMHA_OK;
     if (K == 0) {
         for (int i = 0; i < n; ++i)
@@ -491,13 +521,10 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
             }
             xin = act;
         }
-        cudaError_t e = cudaSuccess;
-        for (int i = 0; i < n && e == cudaSuccess; ++i) {
-            if (ws[i]->N == 0) continue;
-            e = launch_gemm_tcgen05(fmt, ws[i]->q, ws[i]->ldq, ws[i]->scales, ws[i]->N, held_columns(fmt, K), xin, 1,
-                                    ldx, batch, ys[i], ws[i]->N, ctx->d_err, ctx->split_ws, kSplitWsFloats,
-                                    ctx->split_tickets, kSplitTickets, st);
-        }
+        GemmOut outs[kMaxSegments];
+        for (int i = 0; i < n; ++i) outs[i] = GemmOut{ws[i]->q, ws[i]->scales, ws[i]->N, ys[i], ws[i]->N};
+        cudaError_t e = launch_gemm_tcgen05_multi(fmt, n, outs, held_columns(fmt, K), xin, 1, ldx, batch, ctx->d_err,
+                                                  ctx->split_ws, kSplitWsFloats, ctx->split_tickets, kSplitTickets, st);
         if (act) {
             cudaError_t e2 = cudaFreeAsync(act, st);
             if (e == cudaSuccess) e = e2;
@@ -536,6 +563,8 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
         a.split_tickets = ctx->split_tickets;
         a.split_tickets_n = kSplitTickets;
         a.pf_ahead = (int)(ctx->pf_lookahead / (2 * 8192));
+        a.evict_first = ctx->evict_first;
+        a.split_cost = ctx->split_cost;
         a.pf_next_n = 0;
         a.pf_next_total = 0;
         if (b0 + kMaxGemvBatch >= batch) {  // the last chunk of this op hands over to the next op
@@ -558,6 +587,94 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
         else
             CK(launch_gemv_f32(a, ctx->num_sms, st), "gemv launch");
     }
+    return BRAMHA_OK;
+}
+
+// Shard-group view of the context for the kernels.
+ShardArgs shard_args(bramha_ctx* ctx) {
+    ShardArgs sa{};
+    sa.world = ctx->shard_world;
+    sa.rank = ctx->shard_rank;
+    sa.flags = reinterpret_cast<unsigned*>(ctx->arena + kArenaFlags);
+    sa.epoch = reinterpret_cast<unsigned*>(ctx->arena + kArenaEpoch);
+    sa.done = reinterpret_cast<unsigned*>(ctx->arena + kArenaDone);
+    for (int r = 0; r < ctx->shard_world; ++r)
+        sa.peer_flags[r] = reinterpret_cast<unsigned*>(ctx->peer_arena[r] + kArenaFlags);
+    return sa;
+}
+
+bool in_arena(const bramha_ctx* ctx, const void* p, size_t bytes) {
+    const uint8_t* b = static_cast<const uint8_t*>(p);
+    return b >= ctx->arena + kArenaHeader && b + bytes <= ctx->arena + ctx->arena_bytes;
+}
+
+// GEMV of sharded weights: this rank's rows of every output, stored into every
+// rank's copy of it by the tensor-core GEMV's epilogue (see ShardArgs).
+int gemv_device_sharded(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const float* x, int64_t ldx,
+                        int64_t batch, float* const* ys, cudaStream_t st, const float* x_up, int next_n,
+                        const bramha_weight* const* next_ws) {
+    if (ctx->shard_world < 2) return fail(BRAMHA_ERR_INVALID, "sharded weights need a shard group (bramha_cuda_shard_init)");
+    if (batch < 1 || batch > kMaxGemvBatch)
+        return fail(BRAMHA_ERR_UNSUPPORTED, "a sharded GEMV takes batch 1..%d (got %lld)", kMaxGemvBatch, (long long)batch);
+    const int fmt = ws[0]->fmt;
+    const int64_t K = ws[0]->K;
+    for (int i = 0; i < n; ++i)
+        if (!ys[i] || !in_arena(ctx, ys[i], sizeof(float) * (size_t)(batch * ws[i]->n_full)))
+            return fail(BRAMHA_ERR_INVALID,
+                        "the output of a sharded GEMV must lie in the shard arena (bramha_cuda_shard_malloc), "
+                        "[batch][N] for the full N");
+    ShardArgs sa = shard_args(ctx);
+    if (held_columns(fmt, K) == 0) {  // an empty input: every rank zeroes its own copies
+        for (int i = 0; i < n; ++i)
+            CK(cudaMemsetAsync(ys[i], 0, sizeof(float) * (size_t)(batch * ws[i]->n_full), st), "memset(y)");
+        CK(launch_shard_signal(sa, ctx->d_err, 1, st), "shard signal launch");
+        return BRAMHA_OK;
+    }
+    if (K > 0x7fffffffLL) return fail(BRAMHA_ERR_UNSUPPORTED, "K too large");
+    GemvArgs a{};
+    a.x = x;
+    a.x_up = x_up;
+    a.ldx = ldx;
+    a.K = (int)held_columns(fmt, K);
+    a.batch = (int)batch;
+    a.ldq_min = 0x7fffffff;
+    for (int i = 0; i < n; ++i) {
+        if (ws[i]->N == 0) continue;
+        const int si = a.nseg++;
+        GemvSeg& g = a.seg[si];
+        g.q = ws[i]->q;
+        g.scales = ws[i]->scales;
+        g.ldq = ws[i]->ldq;
+        g.ldy = ws[i]->n_full;
+        g.y = ys[i];
+        g.N = (int)ws[i]->N;
+        sa.row0[si] = ws[i]->row0;
+        for (int r = 0; r < ctx->shard_world; ++r)
+            sa.peer_y[si][r] = reinterpret_cast<float*>(ctx->peer_arena[r] +
+                                                        (reinterpret_cast<uint8_t*>(ys[i]) - ctx->arena));
+    }
+    if (a.nseg == 0) {  // no rows here: take part in the launch order only
+        CK(launch_shard_signal(sa, ctx->d_err, 1, st), "shard signal launch");
+        return BRAMHA_OK;
+    }
+    a.err = ctx->d_err;
+    a.split_ws = ctx->split_ws;
+    a.split_ws_floats = kSplitWsFloats;
+    a.split_tickets = ctx->split_tickets;
+    a.split_tickets_n = kSplitTickets;
+    a.pf_ahead = (int)(ctx->pf_lookahead / (2 * 8192));
+    a.evict_first = ctx->evict_first;
+    a.split_cost = ctx->split_cost;
+    for (int i = 0; i < next_n && i < kMaxSegments; ++i) {
+        const bramha_weight* nw = next_ws[i];
+        if (!nw || !is_tiled(nw->fmt) || nw->N == 0 || nw->K == 0) continue;
+        a.pf_next_ptr[a.pf_next_n] = nw->q;
+        a.pf_next_bytes[a.pf_next_n] = tiled_bytes(nw->fmt, nw->N, held_columns(nw->fmt, nw->K));
+        ++a.pf_next_n;
+    }
+    a.pf_next_total = a.pf_next_n ? ctx->pf_next : 0;
+    a.shard = sa;
+    CK(launch_gemv_tc(fmt, a, ctx->num_sms, st), "sharded tensor-core gemv launch");
     return BRAMHA_OK;
 }
 
@@ -625,6 +742,12 @@ int ensure_staging(bramha_ctx* ctx, size_t x_elems, size_t y_elems) {
 // Host-buffer GEMV/GEMM: H2D x, launch, D2H y, wait.
 int gemv_host(bramha_ctx* ctx, const bramha_weight* w, const float* x_host, int64_t batch, float* y_host) {
     if (batch < 0) return fail(BRAMHA_ERR_INVALID, "negative batch");
+    if (w->shard) {  // every rank's rows, through the host-buffer chain (y_host is [batch][full N])
+        const bramha_weight* ws[1] = {w};
+        float* ys[1] = {y_host};
+        const bramha_gemv_op op = {1, ws, x_host, nullptr, ys};
+        return bramha_cuda_gemv_chain(ctx, 1, &op, batch);
+    }
     if (batch > 0 && ((!x_host && w->K > 0) || (!y_host && w->N > 0)))
         return fail(BRAMHA_ERR_INVALID, "null host buffer");
     if (batch == 0 || w->N == 0) return BRAMHA_OK;
@@ -726,6 +849,9 @@ int bramha_cuda_destroy(bramha_ctx* ctx) {
     if (ctx->h_err) cudaFreeHost(ctx->h_err);
     if (ctx->split_ws) cudaFree(ctx->split_ws);
     if (ctx->split_tickets) cudaFree(ctx->split_tickets);
+    for (int r = 0; r < ctx->shard_world; ++r)
+        if (r != ctx->shard_rank && ctx->peer_arena[r]) cudaIpcCloseMemHandle(ctx->peer_arena[r]);
+    if (ctx->arena) cudaFree(ctx->arena);
     cudaStreamDestroy(ctx->stream);
     delete ctx;
     return BRAMHA_OK;
@@ -763,6 +889,22 @@ int bramha_cuda_set_prefetch(bramha_ctx* ctx, int64_t lookahead_bytes, int64_t n
     if (lookahead_bytes < 0 || next_launch_bytes < 0) return fail(BRAMHA_ERR_INVALID, "negative prefetch size");
     ctx->pf_lookahead = lookahead_bytes;
     ctx->pf_next = next_launch_bytes;
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_set_gemv_tuning(bramha_ctx* ctx, int what, int64_t value) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (value < 0) return fail(BRAMHA_ERR_INVALID, "negative tuning value");
+    switch (what) {
+        case BRAMHA_TUNE_LOOKAHEAD_BYTES: ctx->pf_lookahead = value; break;
+        case BRAMHA_TUNE_NEXT_LAUNCH_BYTES: ctx->pf_next = value; break;
+        case BRAMHA_TUNE_EVICT_FIRST: ctx->evict_first = value ? 1 : 0; break;
+        case BRAMHA_TUNE_SPLIT_COST:
+            if (value > 1 << 20) return fail(BRAMHA_ERR_INVALID, "split cost out of range");
+            ctx->split_cost = (int)value;
+            break;
+        default: return fail(BRAMHA_ERR_INVALID, "unknown tuning key %d", what);
+    }
     return BRAMHA_OK;
 }
 
@@ -942,9 +1084,13 @@ int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops
     std::lock_guard<std::mutex> lk(ctx->io_mu);
     // device staging: every op's x (and x_up) at a 16-byte aligned pitch, then
     // every output, back to back
+    // (outputs of sharded ops -- every rank's rows -- are staged at the top of
+    // the shard arena, where the other ranks' GEMVs can store theirs)
     std::vector<int64_t> ldx((size_t)n_ops), xo((size_t)n_ops), uo((size_t)n_ops);
     std::vector<int64_t> yo;
-    size_t xe = 0, ye = 0;
+    std::vector<char> in_arena_y;
+    size_t xe = 0, ye = 0, ya = 0;
+    bool any_shard = false;
     for (int i = 0; i < n_ops; ++i) {
         const int64_t K = ops[i].weights[0]->K;
         ldx[(size_t)i] = (K + 3) / 4 * 4;
@@ -953,12 +1099,29 @@ int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops
         uo[(size_t)i] = ops[i].x_up ? (int64_t)xe : -1;
         if (ops[i].x_up) xe += (size_t)(ldx[(size_t)i] * batch);
         for (int j = 0; j < ops[i].n_weights; ++j) {
-            yo.push_back((int64_t)ye);
-            ye += (size_t)(ops[i].weights[j]->N * batch);
+            const bramha_weight* w = ops[i].weights[j];
+            if (w->shard) {
+                any_shard = true;
+                yo.push_back((int64_t)ya);
+                ya += (size_t)(w->n_full * batch);
+            } else {
+                yo.push_back((int64_t)ye);
+                ye += (size_t)(w->N * batch);
+            }
+            in_arena_y.push_back(w->shard ? 1 : 0);
         }
     }
     int rc = ensure_staging(ctx, xe, ye > 0 ? ye : 1);
     if (rc) return rc;
+    float* arena_y = nullptr;
+    if (any_shard) {
+        if (!ctx->arena || ctx->shard_world < 2) return fail(BRAMHA_ERR_INVALID, "sharded weights need a shard group");
+        const size_t need = (ya * sizeof(float) + 255) / 256 * 256;
+        if (need > ctx->arena_bytes - ctx->arena_used)
+            return fail(BRAMHA_ERR_OOM, "shard arena too small to stage this chain's outputs (%zu bytes)", need);
+        if (ctx->arena_bytes - need < ctx->arena_top) ctx->arena_top = ctx->arena_bytes - need;
+        arena_y = reinterpret_cast<float*>(ctx->arena + (ctx->arena_bytes - need));
+    }
     cudaStream_t st = ctx->stream;
     std::vector<const float*> xs((size_t)n_ops), ups((size_t)n_ops, nullptr);
     std::vector<std::vector<float*>> yv((size_t)n_ops);
@@ -981,19 +1144,22 @@ int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops
                    "H2D x_up");
             }
         }
-        for (int j = 0; j < ops[i].n_weights; ++j) yv[(size_t)i].push_back(ctx->dev_y + yo[yi++]);
+        for (int j = 0; j < ops[i].n_weights; ++j, ++yi)
+            yv[(size_t)i].push_back((in_arena_y[yi] ? arena_y : ctx->dev_y) + yo[yi]);
         ys[(size_t)i] = yv[(size_t)i].data();
     }
     rc = chain_device(ctx, n_ops, ops, batch, st, xs.data(), ups.data(), ldx.data(), ys.data());
     if (rc) return rc;
+    if (any_shard) CK(launch_shard_signal(shard_args(ctx), ctx->d_err, 0, st), "shard sync launch");
     yi = 0;
     for (int i = 0; i < n_ops; ++i)
-        for (int j = 0; j < ops[i].n_weights; ++j) {
-            const size_t n = (size_t)(ops[i].weights[j]->N * batch);
+        for (int j = 0; j < ops[i].n_weights; ++j, ++yi) {
+            const bramha_weight* w = ops[i].weights[j];
+            const size_t n = (size_t)((w->shard ? w->n_full : w->N) * batch);
             if (n > 0)
-                CK(cudaMemcpyAsync(ops[i].y[j], ctx->dev_y + yo[yi], n * sizeof(float), cudaMemcpyDeviceToHost, st),
+                CK(cudaMemcpyAsync(ops[i].y[j], (in_arena_y[yi] ? arena_y : ctx->dev_y) + yo[yi], n * sizeof(float),
+                                   cudaMemcpyDeviceToHost, st),
                    "D2H y");
-            ++yi;
         }
     return check_device_error(ctx, st);
 }
@@ -1366,6 +1532,133 @@ int bramha_cuda_gemm_noalloc_dev(bramha_ctx* ctx, const bramha_weight* w, const 
     CK(launch_gemm_tcgen05_bf16_noalloc(w->fmt, w->q, w->ldq, w->scales, w->N, keff, x_dev, w->K, M, y_dev, w->N,
                                         ctx->d_err, scratch, st),
        "tcgen05 gemm (no-alloc) launch");
+    return BRAMHA_OK;
+}
+
+// ---- column-shard group ----------------------------------------------------
+int bramha_cuda_shard_handle(bramha_ctx* ctx, size_t arena_bytes, bramha_ipc_handle* out) {
+    if (!ctx || !out) return fail(BRAMHA_ERR_INVALID, "null argument");
+    if (ctx->arena) return fail(BRAMHA_ERR_INVALID, "this context already has a shard arena");
+    if (arena_bytes < 2 * kArenaHeader) return fail(BRAMHA_ERR_INVALID, "shard arena of %zu bytes is too small", arena_bytes);
+    static_assert(sizeof(cudaIpcMemHandle_t) == sizeof(bramha_ipc_handle), "IPC handle size");
+    DeviceGuard g(ctx->device);
+    arena_bytes = (arena_bytes + 255) / 256 * 256;
+    CK(cudaMalloc(&ctx->arena, arena_bytes), "cudaMalloc(shard arena)");
+    cudaError_t e = cudaMemset(ctx->arena, 0, kArenaHeader);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, ctx->arena);
+    if (e != cudaSuccess) {
+        cudaFree(ctx->arena);
+        ctx->arena = nullptr;
+        return cuda_fail(e, "shard arena IPC handle");
+    }
+    memcpy(out->bytes, &h, sizeof h);
+    ctx->arena_bytes = arena_bytes;
+    ctx->arena_used = kArenaHeader;
+    ctx->arena_top = arena_bytes;
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_shard_init(bramha_ctx* ctx, int world, int rank, const bramha_ipc_handle* handles) {
+    if (!ctx || !handles) return fail(BRAMHA_ERR_INVALID, "null argument");
+    if (world < 2 || world > kMaxShardWorld || rank < 0 || rank >= world)
+        return fail(BRAMHA_ERR_INVALID, "shard group of %d ranks (rank %d): 2..%d ranks", world, rank, kMaxShardWorld);
+    if (!ctx->arena) return fail(BRAMHA_ERR_INVALID, "call bramha_cuda_shard_handle first");
+    if (ctx->shard_world) return fail(BRAMHA_ERR_INVALID, "this context is already in a shard group");
+    DeviceGuard g(ctx->device);
+    for (int r = 0; r < world; ++r) {
+        if (r == rank) {
+            ctx->peer_arena[r] = ctx->arena;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, handles[r].bytes, sizeof h);
+        void* p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < r; ++q)
+                if (q != rank && ctx->peer_arena[q]) cudaIpcCloseMemHandle(ctx->peer_arena[q]);
+            for (int q = 0; q < world; ++q) ctx->peer_arena[q] = nullptr;
+            return cuda_fail(e, "open a peer's shard arena (cudaIpcOpenMemHandle)");
+        }
+        ctx->peer_arena[r] = static_cast<uint8_t*>(p);
+    }
+    ctx->shard_world = world;
+    ctx->shard_rank = rank;
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_shard_malloc(bramha_ctx* ctx, size_t bytes, void** out) {
+    if (!ctx || !out) return fail(BRAMHA_ERR_INVALID, "null argument");
+    if (!ctx->arena) return fail(BRAMHA_ERR_INVALID, "no shard arena");
+    const size_t b = (bytes + 255) / 256 * 256;
+    if (ctx->arena_used + b > ctx->arena_top)
+        return fail(BRAMHA_ERR_OOM, "shard arena exhausted (%zu of %zu bytes in use, %zu asked)", ctx->arena_used,
+                    ctx->arena_bytes, bytes);
+    *out = ctx->arena + ctx->arena_used;
+    ctx->arena_used += b;
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_shard_rows(bramha_ctx* ctx, int64_t N, int64_t* row0, int64_t* rows) {
+    if (!ctx || !row0 || !rows) return fail(BRAMHA_ERR_INVALID, "null argument");
+    if (N < 0) return fail(BRAMHA_ERR_INVALID, "negative N");
+    const int w = ctx->shard_world ? ctx->shard_world : 1, r = ctx->shard_rank;
+    *row0 = N * r / w;
+    *rows = N * (r + 1) / w - *row0;
+    return BRAMHA_OK;
+}
+
+namespace {
+int register_shard_impl(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K, const void* q,
+                        size_t q_bytes, const float* scales, size_t n_scales, bool from_device, cudaStream_t st,
+                        bramha_weight** out) {
+    if (!ctx || !out || !key) return fail(BRAMHA_ERR_INVALID, "null argument");
+    if (ctx->shard_world < 2) return fail(BRAMHA_ERR_INVALID, "no shard group (bramha_cuda_shard_init)");
+    int rc = check_sizes(fmt, N, K, q_bytes, n_scales, scales != nullptr);
+    if (rc) return rc;
+    if (!is_tiled(fmt)) return fail(BRAMHA_ERR_UNSUPPORTED, "sharded weights take LOG4, W4ZP8 or W8");
+    int64_t row0 = 0, rows = 0;
+    bramha_cuda_shard_rows(ctx, N, &row0, &rows);
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        auto it = ctx->reg.find(key);
+        if (it != ctx->reg.end() && (!it->second->shard || it->second->n_full != N || it->second->row0 != row0))
+            return fail(BRAMHA_ERR_SIZE, "key '%s' is registered with a different shape or sharding", key);
+    }
+    const int64_t rb = row_bytes_of(fmt, K);
+    const uint8_t* qs = static_cast<const uint8_t*>(q) + (q ? row0 * rb : 0);
+    const float* ss = scales ? scales + row0 : nullptr;
+    bramha_weight* w = nullptr;
+    rc = register_impl(ctx, key, fmt, rows, K, rows ? qs : nullptr, (size_t)(rows * rb), ss, (size_t)rows, from_device,
+                       st, &w);
+    if (rc) return rc;
+    w->shard = true;
+    w->row0 = row0;
+    w->n_full = N;
+    *out = w;
+    return BRAMHA_OK;
+}
+}  // namespace
+
+int bramha_cuda_register_weight_shard(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K, const void* q,
+                                      size_t q_bytes, const float* scales, size_t n_scales, bramha_weight** out) {
+    return register_shard_impl(ctx, key, fmt, N, K, q, q_bytes, scales, n_scales, false, nullptr, out);
+}
+
+int bramha_cuda_register_weight_shard_dev(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K,
+                                          const void* q_dev, size_t q_bytes, const float* scales_dev, size_t n_scales,
+                                          void* stream, bramha_weight** out) {
+    return register_shard_impl(ctx, key, fmt, N, K, q_dev, q_bytes, scales_dev, n_scales, true,
+                               static_cast<cudaStream_t>(stream), out);
+}
+
+int bramha_cuda_shard_sync_dev(bramha_ctx* ctx, void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (ctx->shard_world < 2) return fail(BRAMHA_ERR_INVALID, "no shard group");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    CK(launch_shard_signal(shard_args(ctx), ctx->d_err, 0, st), "shard sync launch");
     return BRAMHA_OK;
 }
 

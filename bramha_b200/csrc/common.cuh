@@ -89,6 +89,24 @@ __host__ __device__ constexpr int sp24_pair_a(int p) { return p < 3 ? 0 : p < 5 
 __host__ __device__ constexpr int sp24_pair_b(int p) { return p < 3 ? p + 1 : p < 5 ? p - 1 : 3; }
 __host__ __device__ constexpr int sp24_pair_id(int a, int b) { return a == 0 ? b - 1 : a == 1 ? b + 1 : 5; }
 
+// Column-shard group of a tensor-core GEMV launch (world > 1; one process per
+// GPU).  The launch computes rows [row0, row0 + N) of each segment's output
+// and stores them in every rank's copy of that output (peer pointers into the
+// ranks' symmetric arenas, plain stores over NVLink).  Before it reads its
+// activations it waits (bounded) until every rank has published the previous
+// sharded launch; when all its CTAs are done it publishes this one.
+constexpr int kMaxShardWorld = 8;
+struct ShardArgs {
+    int world;                                    // 0 or 1: not sharded
+    int rank;
+    float* peer_y[kMaxSegments][kMaxShardWorld];  // segment s: rank p's copy of the full output
+    int64_t row0[kMaxSegments];                   // first output row of this rank's shard
+    unsigned* flags;                              // this rank's flags[world]: epochs ranks published here
+    unsigned* peer_flags[kMaxShardWorld];         // rank p's flags array
+    unsigned* epoch;                              // sharded launches this rank has completed
+    unsigned* done;                               // CTAs of the running launch that have finished
+};
+
 // One weight inside a (possibly fused) GEMV launch.
 struct GemvSeg {
     const uint8_t* q;      // device weight: tile-major (quantized) or rows of pitch ldq (f32)
@@ -132,6 +150,9 @@ struct GemvArgs {
     const uint8_t* pf_next_ptr[kMaxSegments];
     int64_t pf_next_bytes[kMaxSegments];
     int64_t pf_next_total;
+    int evict_first;       // weight copies marked first to be evicted from L2
+    int split_cost;        // K-split plan: cost of a split launch, in eighths of a 64-column block
+    ShardArgs shard;       // column-shard group (shard.world > 1), tensor-core GEMV only
 };
 
 constexpr int64_t kSplitWsFloats = 8 << 20;   // 32 MB of partial results per context
@@ -152,6 +173,19 @@ cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const fl
                                 const void* x, int x_is_f32, int64_t ldx, int64_t M, float* y, int64_t ldy, int* err,
                                 float* ws, int64_t ws_floats, int* tickets, int64_t n_tickets, cudaStream_t stream);
 
+// Several weights (same format, same K) applied to one x: the activation
+// copy and per-token sums are prepared once for all of them.
+struct GemmOut {
+    const uint8_t* q;      // tile-major weight
+    const float* scales;
+    int64_t N;
+    float* y;              // [M][ldy]
+    int64_t ldy;
+};
+cudaError_t launch_gemm_tcgen05_multi(int fmt, int n, const GemmOut* outs, int64_t K, const void* x, int x_is_f32,
+                                      int64_t ldx, int64_t M, int* err, float* ws, int64_t ws_floats, int* tickets,
+                                      int64_t n_tickets, cudaStream_t stream);
+
 // bf16-activation GEMM that allocates nothing: the log4 per-token sums go to
 // `rowsum_scratch` (at least M floats, caller-owned); x must be 16-byte
 // aligned with a row pitch that is a multiple of 8 elements.
@@ -170,6 +204,11 @@ cudaError_t launch_gemv_cc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t
 
 // Tensor-core GEMV for the quantized formats, batch 1..8 (gemv_tc.cu).
 cudaError_t launch_gemv_tc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t stream);
+// Shard-group bookkeeping without a GEMV (gemv_tc.cu): publish = 1 takes part
+// in a sharded launch in which this rank has no rows (waits for the previous
+// launch, publishes this one); publish = 0 waits until every rank has
+// published this rank's latest launch, so later work sees every shard.
+cudaError_t launch_shard_signal(const ShardArgs& s, int* err, int publish, cudaStream_t stream);
 
 // Decode-step operations (decode.cu); token and position live in device memory.
 cudaError_t launch_embed(const float* table, int64_t vocab, int64_t hidden, const int32_t* token, float* x,

@@ -755,28 +755,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<FMT>::kTh
 // x = hi + lo (hi = bf16(x), lo = bf16(x - hi)); hi fills columns [0, kp) and
 // lo columns [kp, 2 kp) of the copy, so one pass over 2 kp reproduces x to ~2^-16.
 // With ROWS (f32 only), lo goes to row M + r of a [2M][kp] copy instead.
+// One block of kPrepThreads per token row (a few rows of long K would leave a
+// warp-per-row kernel latency-bound); the row sum is reduced in a fixed order.
+constexpr int kPrepThreads = 1024;
 template <bool FROM_F32, bool ROWS = false>
-__global__ void prep_kernel(const void* __restrict__ x, int64_t ldx, int M, int K, int64_t kp,
-                            __nv_bfloat16* __restrict__ xc, float* __restrict__ rs) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (warp >= M) return;
+__global__ void __launch_bounds__(kPrepThreads) prep_kernel(const void* __restrict__ x, int64_t ldx, int M, int K,
+                                                            int64_t kp, __nv_bfloat16* __restrict__ xc,
+                                                            float* __restrict__ rs) {
+    __shared__ float part[kPrepThreads / 32][2];
+    const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t ldc = FROM_F32 && !ROWS ? 2 * kp : kp;
     const int64_t lo_off = ROWS ? (int64_t)M * kp : kp;
     float sh = 0.f, sl = 0.f;
-    for (int k = lane; k < (int)kp; k += 32) {
+#pragma unroll 4
+    for (int k = threadIdx.x; k < (int)kp; k += kPrepThreads) {
         float h = 0.f, l = 0.f;
         if (k < K) {
             if constexpr (FROM_F32) {
-                const float v = static_cast<const float*>(x)[(int64_t)warp * ldx + k];
+                const float v = static_cast<const float*>(x)[(int64_t)row * ldx + k];
                 h = __bfloat162float(__float2bfloat16_rn(v));
                 l = __bfloat162float(__float2bfloat16_rn(v - h));
             } else {
-                h = __bfloat162float(static_cast<const __nv_bfloat16*>(x)[(int64_t)warp * ldx + k]);
+                h = __bfloat162float(static_cast<const __nv_bfloat16*>(x)[(int64_t)row * ldx + k]);
             }
         }
         if (xc) {
-            xc[(int64_t)warp * ldc + k] = __float2bfloat16_rn(h);
-            if constexpr (FROM_F32) xc[(int64_t)warp * ldc + lo_off + k] = __float2bfloat16_rn(l);
+            xc[(int64_t)row * ldc + k] = __float2bfloat16_rn(h);
+            if constexpr (FROM_F32) xc[(int64_t)row * ldc + lo_off + k] = __float2bfloat16_rn(l);
         }
         sh += h;
         sl += l;
@@ -786,7 +791,19 @@ __global__ void prep_kernel(const void* __restrict__ x, int64_t ldx, int M, int 
         sh += __shfl_xor_sync(0xffffffffu, sh, o);
         sl += __shfl_xor_sync(0xffffffffu, sl, o);
     }
-    if (lane == 0 && rs) rs[warp] = sh + sl;
+    if (lane == 0) {
+        part[warp][0] = sh;
+        part[warp][1] = sl;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && rs) {
+        float a = 0.f, b = 0.f;
+        for (int w = 0; w < kPrepThreads / 32; ++w) {
+            a += part[w][0];
+            b += part[w][1];
+        }
+        rs[row] = a + b;
+    }
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -986,12 +1003,13 @@ void plan_ksplit(GemmArgs* g, int bn, int sms, float* ws, int64_t ws_floats, int
 // side along K.  GEMMs with fewer tiles than SMs are K-split through the
 // caller's workspace (ws / tickets; NULL = no split).
 // Scratch (bf16 copy, per-token sums) comes from the stream-ordered pool.
-cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const float* scales, int64_t N, int64_t K,
-                                const void* x, int x_is_f32, int64_t ldx, int64_t M, float* y, int64_t ldy, int* err,
-                                float* ws, int64_t ws_floats, int* tickets, int64_t n_tickets, cudaStream_t st) {
-    if (M <= 0 || N <= 0) return cudaSuccess;
-    if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff || K <= 0) return cudaErrorInvalidValue;
-    if ((reinterpret_cast<uintptr_t>(q) & 15) != 0) return cudaErrorInvalidValue;
+cudaError_t launch_gemm_tcgen05_multi(int fmt, int n, const GemmOut* outs, int64_t K, const void* x, int x_is_f32,
+                                      int64_t ldx, int64_t M, int* err, float* ws, int64_t ws_floats, int* tickets,
+                                      int64_t n_tickets, cudaStream_t st) {
+    if (M <= 0 || n <= 0) return cudaSuccess;
+    if (M > 0x7fffffff || K > 0x7fffffff || K <= 0) return cudaErrorInvalidValue;
+    for (int i = 0; i < n; ++i)
+        if (outs[i].N > 0x7fffffff || (reinterpret_cast<uintptr_t>(outs[i].q) & 15) != 0) return cudaErrorInvalidValue;
     if (!encode_fn()) return cudaErrorNotSupported;
     const int64_t kp = (K + BK - 1) / BK * BK;  // copy pitch per half: whole K steps
     const bool nsplit = x_is_f32 && M <= 128;    // hi | lo as the halves of N
@@ -1006,42 +1024,57 @@ cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const fl
     if (e != cudaSuccess) return e;
     __nv_bfloat16* xc = need_copy ? reinterpret_cast<__nv_bfloat16*>(scratch) : nullptr;
     float* rs = log4 ? reinterpret_cast<float*>(scratch + copy_bytes) : nullptr;
-    if (need_copy || log4) {
-        const int wpb = 8;
-        const unsigned blocks = (unsigned)((M + wpb - 1) / wpb);
+    if (need_copy || log4) {  // once for every weight that shares x
+        const unsigned blocks = (unsigned)M;
         if (nsplit)
-            prep_kernel<true, true><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
+            prep_kernel<true, true><<<blocks, kPrepThreads, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
         else if (x_is_f32)
-            prep_kernel<true><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
+            prep_kernel<true><<<blocks, kPrepThreads, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
         else
-            prep_kernel<false><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, need_copy ? kp : K, xc, rs);
+            prep_kernel<false><<<blocks, kPrepThreads, 0, st>>>(x, ldx, (int)M, (int)K, need_copy ? kp : K, xc, rs);
         e = cudaGetLastError();
     }
     int dev = 0;
     if (e == cudaSuccess) e = cudaGetDevice(&dev);
-    // N split: 2 x (32, 64 or 128) MMA columns (a 16-token half would not fill
-    // the epilogue's 32-column chunks)
-    const int bn = nsplit ? (M <= 32 ? 64 : M <= 64 ? 128 : 256) : use_pair(M, N, sm_count(dev)) ? 0 : gemm_tile_n(M);
-    // X rows per TMA box: a pair's CTA loads half a tile; an N-split tile loads hi and lo halves
-    const int box = bn == 0 ? kPairTok / 2 : nsplit ? bn / 2 : bn;
-    GemmArgs g;
-    CUtensorMap tmX;
-    if (e == cudaSuccess) e = gemm_args(&g, q, scales, rs, y, ldy, M, N, K, x_is_f32 != 0 && !nsplit, bn, err);
-    if (e == cudaSuccess && nsplit) {
-        g.lo_row = (int)M;
-        g.m_tiles = 1;
+    for (int i = 0; i < n && e == cudaSuccess; ++i) {
+        const int64_t N = outs[i].N;
+        if (N <= 0) continue;
+        // N split: 2 x (32, 64 or 128) MMA columns (a 16-token half would not fill
+        // the epilogue's 32-column chunks)
+        const int bn =
+            nsplit ? (M <= 32 ? 64 : M <= 64 ? 128 : 256) : use_pair(M, N, sm_count(dev)) ? 0 : gemm_tile_n(M);
+        // X rows per TMA box: a pair's CTA loads half a tile; an N-split tile loads hi and lo halves
+        const int box = bn == 0 ? kPairTok / 2 : nsplit ? bn / 2 : bn;
+        GemmArgs g;
+        CUtensorMap tmX;
+        e = gemm_args(&g, outs[i].q, outs[i].scales, rs, outs[i].y, outs[i].ldy, M, N, K, x_is_f32 != 0 && !nsplit, bn,
+                      err);
+        if (e == cudaSuccess && nsplit) {
+            g.lo_row = (int)M;
+            g.m_tiles = 1;
+        }
+        // (bf16 prefill keeps one range per tile: its results stay those of the
+        // allocation-free entry point, which has no workspace)
+        if (e == cudaSuccess && bn != 0 && x_is_f32)
+            plan_ksplit(&g, bn, sm_count(dev), ws, ws_floats, tickets, n_tickets);
+        if (e == cudaSuccess)
+            e = need_copy ? make_x_map(&tmX, xc, cols, crow, cols, box) : make_x_map(&tmX, x, K, M, ldx, box);
+        if (e == cudaSuccess) e = run_gemm(fmt, bn, tmX, g, st);
     }
-    // (bf16 prefill keeps one range per tile: its results stay those of the
-    // allocation-free entry point, which has no workspace)
-    if (e == cudaSuccess && bn != 0 && x_is_f32) plan_ksplit(&g, bn, sm_count(dev), ws, ws_floats, tickets, n_tickets);
-    if (e == cudaSuccess)
-        e = need_copy ? make_x_map(&tmX, xc, cols, crow, cols, box) : make_x_map(&tmX, x, K, M, ldx, box);
-    if (e == cudaSuccess) e = run_gemm(fmt, bn, tmX, g, st);
     if (scratch) {
         cudaError_t e2 = cudaFreeAsync(scratch, st);
         if (e == cudaSuccess) e = e2;
     }
     return e;
+}
+
+cudaError_t launch_gemm_tcgen05(int fmt, const uint8_t* q, int64_t ldq, const float* scales, int64_t N, int64_t K,
+                                const void* x, int x_is_f32, int64_t ldx, int64_t M, float* y, int64_t ldy, int* err,
+                                float* ws, int64_t ws_floats, int* tickets, int64_t n_tickets, cudaStream_t st) {
+    (void)ldq;
+    if (N <= 0) return cudaSuccess;
+    const GemmOut o = {q, scales, N, y, ldy};
+    return launch_gemm_tcgen05_multi(fmt, 1, &o, K, x, x_is_f32, ldx, M, err, ws, ws_floats, tickets, n_tickets, st);
 }
 
 // Grouped GEMM for MoE experts: the tiles of a device-side table (built by the
@@ -1069,9 +1102,7 @@ cudaError_t launch_gemm_tcgen05_grouped(int fmt, const uint8_t* q, const float* 
     if (e != cudaSuccess) return e;
     __nv_bfloat16* xc = reinterpret_cast<__nv_bfloat16*>(scratch);
     float* rs = log4 ? reinterpret_cast<float*>(scratch + copy_bytes) : nullptr;
-    const int wpb = 8;
-    prep_kernel<true, true><<<(unsigned)((M + wpb - 1) / wpb), 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc,
-                                                                                  rs);
+    prep_kernel<true, true><<<(unsigned)M, kPrepThreads, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
     e = cudaGetLastError();
     GemmArgs g;
     CUtensorMap tmX;
@@ -1103,10 +1134,8 @@ cudaError_t launch_gemm_tcgen05_bf16_noalloc(int fmt, const uint8_t* q, int64_t 
     if (fmt == BRAMHA_FMT_LOG4) {
         if (!rowsum_scratch) return cudaErrorInvalidValue;
         rs = rowsum_scratch;
-        const int wpb = 8;
-        const unsigned blocks = (unsigned)((M + wpb - 1) / wpb);
         // every one of the M sums is written here before the GEMM reads it
-        prep_kernel<false><<<blocks, 32 * wpb, 0, st>>>(x, ldx, (int)M, (int)K, K, nullptr, rs);
+        prep_kernel<false><<<(unsigned)M, kPrepThreads, 0, st>>>(x, ldx, (int)M, (int)K, K, nullptr, rs);
         e = cudaGetLastError();
     }
     int dev = 0;

@@ -178,8 +178,14 @@ __global__ void __launch_bounds__(kCcThreads) cc_gemv_kernel(const __grid_consta
     if (!last) return;
     __threadfence();
     if (half == 0) {
+        // partials added in split order, 16 loads in flight (at most 16 splits)
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] = k < p.ksplit ? __ldcg(part + k * kTileRows + row) : 0.f;
         float s = 0.f;
-        for (int k = 0; k < p.ksplit; ++k) s += __ldcg(part + k * kTileRows + row);
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+            if (k < p.ksplit) s += v[k];
         if (grow < sg.N) sg.y[grow] = s * sc;
     }
     if (threadIdx.x == 0) p.tickets[tile] = 0;  // ready for the next launch
@@ -208,7 +214,8 @@ cudaError_t launch_fmt(const CcParams& p, cudaStream_t st) {
 // 5.8) and at 7B sizes (q 9.7 vs 7.3) the tensor-core GEMV is faster.
 constexpr int64_t kCcMaxBytes = 8ll << 20;
 constexpr int kCcMaxK = 1024;
-constexpr int kCcMaxSplit = 16;  // the last CTA of a tile adds the partials one by one
+constexpr int kCcMaxSplit = 16;  // the last CTA of a tile adds the partials (16 loads in flight)
+static_assert(kCcMaxSplit <= 16, "the combine loads at most 16 partials at once");
 
 bool gemv_cc_eligible(int fmt, const GemvArgs& a) {
     if (!is_tiled(fmt) || a.batch != 1 || a.nseg < 1 || a.K > kCcMaxK) return false;

@@ -72,6 +72,7 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "shard.cuh"
 #include "tc_common.cuh"
 
 namespace bramha {
@@ -145,6 +146,8 @@ struct TcGemvParams {
     const uint8_t* pf_next_ptr[kMaxSegments];
     int64_t pf_next_bytes[kMaxSegments];
     int64_t pf_next_total;
+    int evict_first;       // weight copies marked first to be evicted from L2
+    ShardArgs shard;       // column-shard group (shard.world > 1)
 };
 
 struct alignas(1024) TcSmem {
@@ -352,7 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
     };
     // copies of slot pair d into ring slots 2d % kSW, +1, completing on
     // w_full[d % kSD]; one copy when the pair is contiguous.  The weight lines
-    // are read once, so they are marked first to be evicted from L2.
+    // are read once: with p.evict_first they are marked first to be evicted
+    // from L2, ahead of the lines prefetched for later copies.
     const uint64_t pol = policy_evict_first();
     auto issue_pair = [&](int d, Cursor c) {
         const int st = (2 * d) % kSW;
@@ -361,11 +365,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
         pair_src(d, c, s0, b0, s1, b1);
         uint64_t* bar = &S.w_full[d % kSD];
         mbar_expect_tx(bar, b0 + b1);
+        auto copy = [&](void* dst, const uint8_t* src, uint32_t bytes) {
+            if (p.evict_first)
+                bulk_load_hint(dst, src, bytes, bar, pol);
+            else
+                bulk_load(dst, src, bytes, bar);
+        };
         if (s1 && b0 == (uint32_t)kSlotBytes && s1 == s0 + kSlotBytes) {
-            bulk_load_hint(&S.w[st][0], s0, b0 + b1, bar, pol);
+            copy(&S.w[st][0], s0, b0 + b1);
         } else {
-            bulk_load_hint(&S.w[st][0], s0, b0, bar, pol);
-            if (s1) bulk_load_hint(&S.w[st + 1][0], s1, b1, bar, pol);
+            copy(&S.w[st][0], s0, b0);
+            if (s1) copy(&S.w[st + 1][0], s1, b1);
         }
     };
     // HBM -> L2 request of slot pair d, p.pf_ahead pairs before its copy
@@ -446,9 +456,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
     const bool act = warp < kDeqWarp0 || warp >= kEpiWarp0;       // activation warps
     const int ta = (warp < kDeqWarp0 ? warp : warp - kEpiWarp0 + kDeqWarp0) * 32 + lane;  // 0..383
 
+    const bool sharded = p.shard.world > 1;
     if (act) {
         // activations, outputs and the K-split workspace belong to the stream order
         asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (sharded) {
+            // every rank's rows of the previous sharded launch have landed here
+            // (the activations may be that launch's output)
+            if (ta == 0) shard_wait(p.shard, *reinterpret_cast<volatile unsigned*>(p.shard.epoch), p.err);
+            asm volatile("bar.sync 2, %0;" ::"n"(kActThreads) : "memory");
+        }
 
         // ---------------- activations -> staging, max|x|, sum(x)
         {
@@ -460,7 +477,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
 #pragma unroll
                 for (int u = 0; u < kPerThread; ++u) {
                     const int k = ta + u * kActThreads;
-                    v[u] = k < kv ? __ldg(xr + k) : 0.f;
+                    // (written by other GPUs during this kernel when sharded: L2, not the read-only path)
+                    v[u] = k < kv ? (sharded ? __ldcg(xr + k) : __ldg(xr + k)) : 0.f;
                 }
                 if (p.x_up) {  // SwiGLU: silu(g) * up, rounded as the separate silu_mul kernel rounds it
                     const float* ur = p.x_up + (int64_t)b * p.ldx + k0;
@@ -470,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
                         if (k < kv) {
                             const float g = v[u];
                             const float silu = __fmul_rn(g, 1.0f / __fadd_rn(1.0f, expf(-g)));
-                            v[u] = __fmul_rn(silu, __ldg(ur + k));
+                            v[u] = __fmul_rn(silu, sharded ? __ldcg(ur + k) : __ldg(ur + k));
                         }
                     }
                 }
@@ -719,9 +737,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.d_empty[buf]);
             const int tile = ci + i * p.ctas_per_split;
-            const TcSeg& sg = p.seg[seg_of(p, tile)];
+            const int si = seg_of(p, tile);
+            const TcSeg& sg = p.seg[si];
             const int row = q4 * 32 + lane;
             const int grow = (tile - sg.tile_begin) * TM + row;
+            // output row grow of batch row b: this GPU's y, or (sharded) row
+            // row0 + grow of every rank's copy of the full output
+            auto store_y = [&](int b, float v) {
+                if (!sharded) {
+                    sg.y[(int64_t)b * sg.ldy + grow] = v;
+                    return;
+                }
+                const int64_t off = (int64_t)b * sg.ldy + p.shard.row0[si] + grow;
+                for (int r = 0; r < p.shard.world; ++r) p.shard.peer_y[si][r][off] = v;
+            };
             float res[B];
             if (grow < sg.N) {
                 const float sc = __ldg(sg.scales + grow);
@@ -746,7 +775,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             if (p.ksplit == 1) {
                 if (grow < sg.N)
 #pragma unroll
-                    for (int b = 0; b < B; ++b) sg.y[(int64_t)b * sg.ldy + grow] = res[b];
+                    for (int b = 0; b < B; ++b) store_y(b, res[b]);
                 continue;
             }
             // K split: publish this split's partial, take a ticket; the last
@@ -763,23 +792,57 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             if (lane == 0) last = atomicAdd(&p.tickets[tile * 4 + q4], 1) == p.ksplit - 1;
             if (__shfl_sync(0xffffffffu, last, 0)) {
                 __threadfence();
-                if (grow < sg.N)
+                if (grow < sg.N) {
+                    // the partials are added in split order; up to 32 loads are in
+                    // flight per lane (a load per split in turn would cost one L2
+                    // round trip per split and batch row)
+                    constexpr int U = B >= 8 ? 4 : B >= 4 ? 8 : 16;
+                    float acc[B];
 #pragma unroll
-                    for (int b = 0; b < B; ++b) {
-                        float acc = 0.f;
-                        for (int s = 0; s < p.ksplit; ++s) acc += __ldcg(part + ((int64_t)s * B + b) * TM + row);
-                        sg.y[(int64_t)b * sg.ldy + grow] = acc;
+                    for (int b = 0; b < B; ++b) acc[b] = 0.f;
+                    for (int s0 = 0; s0 < p.ksplit; s0 += U) {
+                        float v[U][B];
+#pragma unroll
+                        for (int u = 0; u < U; ++u)
+#pragma unroll
+                            for (int b = 0; b < B; ++b)
+                                v[u][b] = s0 + u < p.ksplit ? __ldcg(part + ((int64_t)(s0 + u) * B + b) * TM + row) : 0.f;
+#pragma unroll
+                        for (int u = 0; u < U; ++u)
+                            if (s0 + u < p.ksplit)
+#pragma unroll
+                                for (int b = 0; b < B; ++b) acc[b] += v[u][b];
                     }
+#pragma unroll
+                    for (int b = 0; b < B; ++b) store_y(b, acc[b]);
+                }
                 if (lane == 0) p.tickets[tile * 4 + q4] = 0;  // ready for the next launch
             }
         }
     }
+    if (sharded) __threadfence_system();  // this thread's stores to other GPUs, before the publication
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }
+    if (sharded && threadIdx.x == 0) shard_complete(p.shard, p.err);
+}
+
+// A sharded launch in which this rank has no rows (publish = 1), or a wait for
+// every rank to publish this rank's latest launch (publish = 0).
+__global__ void shard_signal_kernel(const __grid_constant__ ShardArgs s, int* err, int publish) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (threadIdx.x != 0) return;
+    volatile unsigned* ep = s.epoch;
+    const unsigned e = *ep;
+    const bool ok = shard_wait(s, e, err);
+    if (!publish) return;
+    __threadfence_system();
+    *ep = e + 1;
+    if (ok && *reinterpret_cast<volatile int*>(err) == 0)
+        for (int r = 0; r < s.world; ++r) st_release_sys(s.peer_flags[r] + s.rank, e + 1);
 }
 
 // Largest K range (64-column blocks) one CTA takes: its B terms fit the B
@@ -799,7 +862,7 @@ int max_split_steps(int fmt, int batch) {
 // SM), counted in 64-column blocks: its blocks, ~1 per tile for the
 // epilogue, and for a split ~2 + ksplit/8 for the combine.  Splits start on
 // even blocks so 4-bit slots stay whole.  False when no split fits.
-bool plan_gemv_tc(int ntiles, int ksteps, int max_steps, int max_ksplit, int num_sms, int* ksplit_out,
+bool plan_gemv_tc(int ntiles, int ksteps, int max_steps, int max_ksplit, int num_sms, int split_cost, int* ksplit_out,
                   int* steps_per_split_out, int* ctas_per_split_out) {
     int64_t best = INT64_MAX;
     int bk = 1, bspp = ksteps, bcps = 1;
@@ -812,7 +875,7 @@ bool plan_gemv_tc(int ntiles, int ksteps, int max_steps, int max_ksplit, int num
         const int cps = ntiles < num_sms / ks ? ntiles : num_sms / ks;
         if (cps < 1) continue;
         const int64_t tpc = (ntiles + cps - 1) / cps;
-        const int64_t cost = 8 * (tpc * (spp + 1)) + (ks > 1 ? 16 + ks : 0);  // eighths of a block
+        const int64_t cost = 8 * (tpc * (spp + 1)) + (ks > 1 ? split_cost + ks : 0);  // eighths of a block
         if (cost < best) {
             best = cost;
             bk = ks;
@@ -827,11 +890,11 @@ bool plan_gemv_tc(int ntiles, int ksteps, int max_steps, int max_ksplit, int num
 }
 
 template <int FMT, int B>
-cudaError_t launch_b(TcGemvParams& p, int max_ksplit, int num_sms, cudaStream_t st) {
+cudaError_t launch_b(TcGemvParams& p, int max_ksplit, int num_sms, int split_cost, cudaStream_t st) {
     auto kern = tc_gemv_kernel<FMT, B>;
     constexpr int smem = (int)sizeof(TcSmem) + 1024;
     static_assert(smem <= 227 * 1024, "shared memory per CTA exceeds 227 KB");
-    if (!plan_gemv_tc(p.ntiles, p.ksteps, max_split_steps(FMT, B), max_ksplit, num_sms, &p.ksplit,
+    if (!plan_gemv_tc(p.ntiles, p.ksteps, max_split_steps(FMT, B), max_ksplit, num_sms, split_cost, &p.ksplit,
                       &p.steps_per_split, &p.ctas_per_split))
         return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -895,11 +958,15 @@ cudaError_t launch_gemv_tc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t
         pf_avail += a.pf_next_bytes[i];
     }
     p.pf_next_total = (a.pf_next_total < pf_avail ? a.pf_next_total : pf_avail) & ~(int64_t)4095;
+    p.shard = a.shard;
+    p.evict_first = a.evict_first;
+    if (p.shard.world > 1 && (p.shard.world > kMaxShardWorld || !p.shard.flags || !p.shard.epoch || !p.shard.done))
+        return cudaErrorInvalidValue;
 #define BRAMHA_TC_B(n)                                                                                   \
     case n:                                                                                              \
-        return fmt == BRAMHA_FMT_LOG4    ? launch_b<BRAMHA_FMT_LOG4, n>(p, max_ksplit, num_sms, st)      \
-               : fmt == BRAMHA_FMT_W4ZP8 ? launch_b<BRAMHA_FMT_W4ZP8, n>(p, max_ksplit, num_sms, st)     \
-                                         : launch_b<BRAMHA_FMT_W8, n>(p, max_ksplit, num_sms, st);
+        return fmt == BRAMHA_FMT_LOG4    ? launch_b<BRAMHA_FMT_LOG4, n>(p, max_ksplit, num_sms, a.split_cost, st)      \
+               : fmt == BRAMHA_FMT_W4ZP8 ? launch_b<BRAMHA_FMT_W4ZP8, n>(p, max_ksplit, num_sms, a.split_cost, st)     \
+                                         : launch_b<BRAMHA_FMT_W8, n>(p, max_ksplit, num_sms, a.split_cost, st);
     switch (a.batch) {
         BRAMHA_TC_B(1)
         BRAMHA_TC_B(2)
@@ -912,6 +979,12 @@ cudaError_t launch_gemv_tc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t
         default: return cudaErrorInvalidValue;
     }
 #undef BRAMHA_TC_B
+}
+
+cudaError_t launch_shard_signal(const ShardArgs& s, int* err, int publish, cudaStream_t st) {
+    if (s.world < 2 || s.world > kMaxShardWorld || !s.flags || !s.epoch) return cudaErrorInvalidValue;
+    shard_signal_kernel<<<1, 32, 0, st>>>(s, err, publish);
+    return cudaGetLastError();
 }
 
 }  // namespace bramha

@@ -54,6 +54,7 @@ class Weight:
 
     def __init__(self, plane: "CudaComputePlane", handle: int, key: str, fmt: str, n: int, k: int):
         self.plane, self.handle, self.key, self.fmt, self.N, self.K = plane, handle, key, fmt, n, k
+        self.n_full, self.row0 = n, 0  # a column shard holds rows [row0, row0 + N) of n_full
 
     @property
     def device_bytes(self) -> int:
@@ -314,9 +315,17 @@ class CudaComputePlane:
         launches withholds one weight copy, so a bounded wait runs out."""
         check(lib().bramha_cuda_test_fault(self._ctx, self.TEST_FAULTS[kind]))
 
-    def set_prefetch(self, lookahead_bytes: int = 128 << 10, next_launch_bytes: int = 24 << 20):
+    def set_prefetch(self, lookahead_bytes: int = 0, next_launch_bytes: int = 8 << 20):
         """L2 prefetch of the tensor-core GEMV (tuning only; results do not change)."""
         check(lib().bramha_cuda_set_prefetch(self._ctx, int(lookahead_bytes), int(next_launch_bytes)))
+
+    TUNING = {"lookahead_bytes": 1, "next_launch_bytes": 2, "evict_first": 3, "split_cost": 4}
+
+    def set_gemv_tuning(self, **kw):
+        """Tensor-core GEMV tuning (results do not change): lookahead_bytes,
+        next_launch_bytes, evict_first (0/1), split_cost."""
+        for k, v in kw.items():
+            check(lib().bramha_cuda_set_gemv_tuning(self._ctx, self.TUNING[k], int(v)))
 
     @staticmethod
     def _chain_ops(ops):

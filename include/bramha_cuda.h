@@ -141,12 +141,22 @@ BRAMHA_API int bramha_cuda_test_fault(bramha_ctx* ctx, int kind);
 
 /* L2 prefetch of the tensor-core GEMV (tuning; no counterpart in the
  * reference).  lookahead_bytes: how far ahead of its shared-memory copies each
- * CTA asks HBM for its weight stream (default 128 KB; 0 = off).
- * next_launch_bytes: in a GEMV chain, how many of the next launch's weight
- * bytes the current launch requests into L2 once its own copies are issued
- * (default 24 MB; 0 = off).  Prefetching reads no memory outside the weights
- * and changes no result. */
+ * CTA asks HBM for its weight stream (default 0 = off).  next_launch_bytes: in
+ * a GEMV chain, how many of the next launch's weight bytes the current launch
+ * requests into L2 once its own copies are issued (default 8 MB; 0 = off).
+ * Prefetching reads no memory outside the weights and changes no result. */
 BRAMHA_API int bramha_cuda_set_prefetch(bramha_ctx* ctx, int64_t lookahead_bytes, int64_t next_launch_bytes);
+
+/* Tensor-core GEMV tuning (no counterpart in the reference; results do not
+ * change): LOOKAHEAD_BYTES / NEXT_LAUNCH_BYTES as bramha_cuda_set_prefetch;
+ * EVICT_FIRST (default 0): weight copies are marked first to be evicted from
+ * L2; SPLIT_COST (default 240): what the K-split plan charges for splitting a
+ * launch's K range, in eighths of one 64-column weight block. */
+#define BRAMHA_TUNE_LOOKAHEAD_BYTES 1
+#define BRAMHA_TUNE_NEXT_LAUNCH_BYTES 2
+#define BRAMHA_TUNE_EVICT_FIRST 3
+#define BRAMHA_TUNE_SPLIT_COST 4
+BRAMHA_API int bramha_cuda_set_gemv_tuning(bramha_ctx* ctx, int what, int64_t value);
 
 /* ---------------------------------------------------------------- weights */
 
@@ -381,6 +391,62 @@ BRAMHA_API int bramha_cuda_gemm_noalloc_dev(bramha_ctx* ctx, const bramha_weight
  * calls (bramha_cuda_gemv, _matvec, _gemm, _gemv_chain, _moe_mlp, ...) check
  * this before returning. */
 BRAMHA_API int bramha_cuda_stream_sync(bramha_ctx* ctx, void* stream);
+
+/* ------------------------------------------- column sharding over several GPUs
+ *
+ * The reference runs every linear on one device (matvec_mul_into,
+ * cpu_engine.rs:1307-1444); here a linear's output rows (its out_features)
+ * can be split across the GPUs of one node, one process and one context per
+ * GPU.  Each rank holds rows [N*rank/world, N*(rank+1)/world) of a sharded
+ * weight; a GEMV on sharded weights (bramha_cuda_gemv_dev, _gemv_multi_dev,
+ * _gemv_chain_dev, _gemv_chain; tensor-core formats LOG4, W4ZP8, W8, batch
+ * 1..8) computes this rank's rows and stores them, over NVLink, straight into
+ * every rank's copy of the full output -- the all-gather is part of the GEMV's
+ * epilogue -- and then publishes the launch to every rank.  Before a sharded
+ * GEMV reads its input it waits until every rank has published the previous
+ * sharded GEMV, so a sharded GEMV may read the output of the one before it.
+ * Outputs of sharded GEMVs live in a symmetric arena: every rank allocates the
+ * same sizes in the same order (bramha_cuda_shard_malloc), so an output has
+ * the same offset on every rank.  All ranks must issue the same sequence of
+ * sharded GEMVs.  Waits are bounded (bramha_cuda_set_wait_timeout); after a
+ * BRAMHA_ERR_TIMEOUT the group is unusable and must be re-created.  An output
+ * buffer may be written again only after every rank has finished reading it,
+ * which the ordering above guarantees for reads by the next sharded GEMV.
+ * No multicast and no collective library: plain peer loads and stores.
+ *
+ * Set-up: each rank calls bramha_cuda_shard_handle (allocates its arena and
+ * returns an IPC handle), the caller exchanges the handles between the ranks
+ * (for example with torch.distributed), and each rank calls
+ * bramha_cuda_shard_init with all of them. */
+typedef struct bramha_ipc_handle {
+    unsigned char bytes[64];
+} bramha_ipc_handle;
+
+BRAMHA_API int bramha_cuda_shard_handle(bramha_ctx* ctx, size_t arena_bytes, bramha_ipc_handle* out);
+
+/* handles[r] is rank r's handle (world <= 8); opens the peers' arenas. */
+BRAMHA_API int bramha_cuda_shard_init(bramha_ctx* ctx, int world, int rank, const bramha_ipc_handle* handles);
+
+/* Symmetric allocation from the arena (256-byte aligned; same sizes and
+ * order on every rank); *out is this rank's device pointer. */
+BRAMHA_API int bramha_cuda_shard_malloc(bramha_ctx* ctx, size_t bytes, void** out);
+
+/* Registers this rank's rows of the full packed weight (the layout and size
+ * rules of bramha_cuda_register_weight, for the whole N x K weight).  A rank
+ * may hold no rows (N < world). */
+BRAMHA_API int bramha_cuda_register_weight_shard(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K,
+                                                 const void* q, size_t q_bytes, const float* scales, size_t n_scales,
+                                                 bramha_weight** out);
+BRAMHA_API int bramha_cuda_register_weight_shard_dev(bramha_ctx* ctx, const char* key, int fmt, int64_t N, int64_t K,
+                                                     const void* q_dev, size_t q_bytes, const float* scales_dev,
+                                                     size_t n_scales, void* stream, bramha_weight** out);
+
+/* First row and row count of this rank's shard of an N-row weight. */
+BRAMHA_API int bramha_cuda_shard_rows(bramha_ctx* ctx, int64_t N, int64_t* row0, int64_t* rows);
+
+/* Stream-ordered: work after it sees every rank's rows of every sharded GEMV
+ * this rank has issued (a bounded wait on the ranks' publications). */
+BRAMHA_API int bramha_cuda_shard_sync_dev(bramha_ctx* ctx, void* stream);
 
 /* ------------------------------------------------------------ packers (GPU) */
 
