@@ -93,6 +93,11 @@ _SIGNATURES = {
     "bramha_cuda_shard_sync_dev": [_vp, _vp],
     "bramha_cuda_gemv_chain_dev": [_vp, _int, _vp, _i64, _vp],
     "bramha_cuda_gemv_chain": [_vp, _int, _vp, _i64],
+    "bramha_cuda_gemv_program_create": [_vp, _int, _vp, _i64, ctypes.POINTER(_vp)],
+    "bramha_cuda_gemv_program_run_dev": [_vp, _vp, _vp],
+    "bramha_cuda_gemv_program_destroy": [_vp, _vp],
+    "bramha_cuda_gemv_program_trace": [_vp, _vp, _int],
+    "bramha_cuda_gemv_program_read_trace": [_vp, _vp, _vp, _sz, ctypes.POINTER(_int)],
     "bramha_cuda_op_embed": [_vp, _vp, _i64, _i64, _vp, _vp, _vp],
     "bramha_cuda_op_rmsnorm": [_vp, _vp, _vp, _vp, _i64, ctypes.c_float, _vp, _vp],
     "bramha_cuda_op_qkv_rope": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, ctypes.c_float, _vp, _i64,

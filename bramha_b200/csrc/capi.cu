@@ -80,10 +80,10 @@ struct bramha_ctx {
 
 namespace {
 // Control block at the start of every arena.
-constexpr size_t kArenaFlags = 0;     // u32 flags[world]: epochs ranks published here
-constexpr size_t kArenaEpoch = 64;    // u32: sharded launches this rank completed
-constexpr size_t kArenaDone = 128;    // u32: CTAs of the running launch that finished
-constexpr size_t kArenaHeader = 4096; // allocations start here
+constexpr size_t kArenaArrive = 0;     // u32 arrive[world]: CTAs of rank r whose rows are here
+constexpr size_t kArenaExpected = 64;  // u32 expected[world]: arrivals through the last launch
+constexpr size_t kArenaDone = 128;     // u32: CTAs of the running launch that finished
+constexpr size_t kArenaHeader = 4096;  // allocations start here
 }  // namespace
 
 namespace {
@@ -595,11 +595,13 @@ ShardArgs shard_args(bramha_ctx* ctx) {
     ShardArgs sa{};
     sa.world = ctx->shard_world;
     sa.rank = ctx->shard_rank;
-    sa.flags = reinterpret_cast<unsigned*>(ctx->arena + kArenaFlags);
-    sa.epoch = reinterpret_cast<unsigned*>(ctx->arena + kArenaEpoch);
+    sa.arrive = reinterpret_cast<unsigned*>(ctx->arena + kArenaArrive);
+    sa.expected = reinterpret_cast<unsigned*>(ctx->arena + kArenaExpected);
     sa.done = reinterpret_cast<unsigned*>(ctx->arena + kArenaDone);
-    for (int r = 0; r < ctx->shard_world; ++r)
-        sa.peer_flags[r] = reinterpret_cast<unsigned*>(ctx->peer_arena[r] + kArenaFlags);
+    for (int r = 0; r < ctx->shard_world; ++r) {
+        sa.peer_arrive[r] = reinterpret_cast<unsigned*>(ctx->peer_arena[r] + kArenaArrive);
+        sa.grid_of[r] = 1;
+    }
     return sa;
 }
 
@@ -624,6 +626,21 @@ int gemv_device_sharded(bramha_ctx* ctx, int n, const bramha_weight* const* ws, 
                         "the output of a sharded GEMV must lie in the shard arena (bramha_cuda_shard_malloc), "
                         "[batch][N] for the full N");
     ShardArgs sa = shard_args(ctx);
+    // every rank's grid for this launch (each rank's rows of each weight, the
+    // same plan as the launch): what the ranks' arrivals must add up to
+    if (held_columns(fmt, K) > 0 && K <= 0x7fffffffLL)
+        for (int r = 0; r < ctx->shard_world; ++r) {
+            int64_t nt = 0;
+            for (int i = 0; i < n; ++i) {
+                const int64_t n_full = ws[i]->n_full;
+                nt += row_tiles(n_full * (r + 1) / ctx->shard_world - n_full * r / ctx->shard_world);
+            }
+            const int gr = nt == 0 ? 1
+                                   : gemv_tc_grid(fmt, (int)batch, (int)nt, (int)held_columns(fmt, K), ctx->num_sms,
+                                                  ctx->split_cost, kSplitWsFloats, kSplitTickets);
+            if (gr <= 0) return fail(BRAMHA_ERR_UNSUPPORTED, "sharded GEMV: no launch plan for rank %d", r);
+            sa.grid_of[r] = gr;
+        }
     if (held_columns(fmt, K) == 0) {  // an empty input: every rank zeroes its own copies
         for (int i = 0; i < n; ++i)
             CK(cudaMemsetAsync(ys[i], 0, sizeof(float) * (size_t)(batch * ws[i]->n_full), st), "memset(y)");
@@ -1162,6 +1179,96 @@ int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops
                    "D2H y");
         }
     return check_device_error(ctx, st);
+}
+
+struct bramha_gemv_program {
+    bramha_ctx* ctx = nullptr;
+    ChainProgram* prog = nullptr;
+};
+
+int bramha_cuda_gemv_program_create(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch,
+                                    bramha_gemv_program** out) {
+    if (!ctx || !out) return fail(BRAMHA_ERR_INVALID, "null argument");
+    *out = nullptr;
+    if (n_ops < 1 || !ops) return fail(BRAMHA_ERR_INVALID, "gemv program: needs at least one op");
+    if (batch < 1 || batch > kMaxGemvBatch)
+        return fail(BRAMHA_ERR_UNSUPPORTED, "gemv program: batch must be in 1..%d", kMaxGemvBatch);
+    const int fmt = ops[0].n_weights > 0 && ops[0].weights && ops[0].weights[0] ? ops[0].weights[0]->fmt : -1;
+    std::vector<GemvArgs> args((size_t)n_ops);
+    for (int i = 0; i < n_ops; ++i) {
+        const bramha_gemv_op& op = ops[i];
+        int rc = check_chain_op(ctx, op, batch, true);
+        if (rc) return rc;
+        const int64_t K = op.weights[0]->K;
+        if (op.weights[0]->fmt != fmt || !is_tiled(fmt))
+            return fail(BRAMHA_ERR_UNSUPPORTED, "gemv program: every op must use the same one of LOG4, W4ZP8, W8");
+        if (held_columns(fmt, K) <= 0 || K > 0x7fffffffLL)
+            return fail(BRAMHA_ERR_UNSUPPORTED, "gemv program: op %d has no input columns", i);
+        GemvArgs& a = args[(size_t)i];
+        a = GemvArgs{};
+        a.x = op.x;
+        a.x_up = op.x_up;
+        a.ldx = K;
+        a.K = (int)held_columns(fmt, K);
+        a.batch = (int)batch;
+        for (int j = 0; j < op.n_weights; ++j) {
+            const bramha_weight* w = op.weights[j];
+            if (w->shard) return fail(BRAMHA_ERR_UNSUPPORTED, "gemv program: sharded weights are not supported");
+            if (w->N <= 0 || w->N > 0x7fffffffLL)
+                return fail(BRAMHA_ERR_UNSUPPORTED, "gemv program: op %d weight %d has no rows", i, j);
+            GemvSeg& g = a.seg[a.nseg++];
+            g.q = w->q;
+            g.scales = w->scales;
+            g.y = op.y[j];
+            g.ldy = w->N;
+            g.N = (int)w->N;
+        }
+    }
+    bramha_gemv_program* p = new (std::nothrow) bramha_gemv_program();
+    if (!p) return fail(BRAMHA_ERR_OOM, "host allocation failed");
+    DeviceGuard g(ctx->device);
+    cudaError_t e = chain_program_create(fmt, (int)batch, n_ops, args.data(), ctx->num_sms, ctx->split_cost,
+                                         ctx->split_ws, kSplitWsFloats, ctx->split_tickets, kSplitTickets, &p->prog);
+    if (e != cudaSuccess) {
+        delete p;
+        return cuda_fail(e, "gemv program create");
+    }
+    p->ctx = ctx;
+    *out = p;
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_gemv_program_run_dev(bramha_ctx* ctx, bramha_gemv_program* prog, void* stream) {
+    if (!ctx || !prog || prog->ctx != ctx) return fail(BRAMHA_ERR_INVALID, "null program or another context's");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    CK(chain_program_run(prog->prog, ctx->d_err, st), "gemv program launch");
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_gemv_program_trace(bramha_ctx* ctx, bramha_gemv_program* prog, int on) {
+    if (!ctx || !prog || prog->ctx != ctx) return fail(BRAMHA_ERR_INVALID, "null program or another context's");
+    DeviceGuard g(ctx->device);
+    CK(chain_program_trace(prog->prog, on), "gemv program trace");
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_gemv_program_read_trace(bramha_ctx* ctx, bramha_gemv_program* prog, uint64_t* out, size_t n,
+                                        int* grid) {
+    if (!ctx || !prog || prog->ctx != ctx || !out || !grid) return fail(BRAMHA_ERR_INVALID, "null argument");
+    DeviceGuard g(ctx->device);
+    CK(chain_program_read_trace(prog->prog, reinterpret_cast<unsigned long long*>(out), n, grid),
+       "gemv program trace (is tracing on?)");
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_gemv_program_destroy(bramha_ctx* ctx, bramha_gemv_program* prog) {
+    if (!ctx || !prog || prog->ctx != ctx) return fail(BRAMHA_ERR_INVALID, "null program or another context's");
+    DeviceGuard g(ctx->device);
+    cudaDeviceSynchronize();  // no run may still use its tables
+    chain_program_destroy(prog->prog);
+    delete prog;
+    return BRAMHA_OK;
 }
 
 int bramha_cuda_gemv_swiglu_dev(bramha_ctx* ctx, const bramha_weight* w, const float* gate_dev, const float* up_dev,

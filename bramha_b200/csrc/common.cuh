@@ -92,18 +92,22 @@ __host__ __device__ constexpr int sp24_pair_id(int a, int b) { return a == 0 ? b
 // Column-shard group of a tensor-core GEMV launch (world > 1; one process per
 // GPU).  The launch computes rows [row0, row0 + N) of each segment's output
 // and stores them in every rank's copy of that output (peer pointers into the
-// ranks' symmetric arenas, plain stores over NVLink).  Before it reads its
-// activations it waits (bounded) until every rank has published the previous
-// sharded launch; when all its CTAs are done it publishes this one.
+// ranks' symmetric arenas, plain stores over NVLink).  Every CTA, once its
+// stores are done, makes them visible system-wide (one fence) and adds 1 to
+// its rank's arrival counter in every rank's arena.  Before a launch reads its
+// activations it waits (bounded) until each rank's counter here has reached
+// the total CTA count of that rank's sharded launches so far (`expected`,
+// advanced by each launch's last CTA with every rank's grid size).
 constexpr int kMaxShardWorld = 8;
 struct ShardArgs {
     int world;                                    // 0 or 1: not sharded
     int rank;
     float* peer_y[kMaxSegments][kMaxShardWorld];  // segment s: rank p's copy of the full output
     int64_t row0[kMaxSegments];                   // first output row of this rank's shard
-    unsigned* flags;                              // this rank's flags[world]: epochs ranks published here
-    unsigned* peer_flags[kMaxShardWorld];         // rank p's flags array
-    unsigned* epoch;                              // sharded launches this rank has completed
+    int grid_of[kMaxShardWorld];                  // CTAs of this launch on rank p
+    unsigned* arrive;                             // this rank's arrive[world]: CTAs of rank p done here
+    unsigned* peer_arrive[kMaxShardWorld];        // rank p's arrive array
+    unsigned* expected;                           // this rank's expected[world] (through the last launch)
     unsigned* done;                               // CTAs of the running launch that have finished
 };
 
@@ -202,13 +206,31 @@ cudaError_t noalloc_rowsum_scratch(int device, float** out);
 bool gemv_cc_eligible(int fmt, const GemvArgs& a);
 cudaError_t launch_gemv_cc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t stream);
 
+// A chain of dependent tensor-core GEMVs in one persistent cooperative launch
+// (gemv_chain.cu): ops[j] describes launch j as launch_gemv_tc would take it
+// (one format and batch for the whole chain); the program owns its device op
+// table and per-op completion counters and uses the caller's K-split
+// workspace and tickets.
+struct ChainProgram;
+cudaError_t chain_program_create(int fmt, int batch, int nops, const GemvArgs* ops, int num_sms, int split_cost,
+                                 float* ws, int64_t ws_floats, int* tickets, int n_tickets, ChainProgram** out);
+cudaError_t chain_program_run(ChainProgram* prog, int* err, cudaStream_t stream);
+void chain_program_destroy(ChainProgram* prog);
+// Per-op, per-CTA %globaltimer stamps of the next runs ([nops][grid][4]).
+cudaError_t chain_program_trace(ChainProgram* prog, int on);
+cudaError_t chain_program_read_trace(ChainProgram* prog, unsigned long long* out, size_t n, int* grid);
+
 // Tensor-core GEMV for the quantized formats, batch 1..8 (gemv_tc.cu).
 cudaError_t launch_gemv_tc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t stream);
 // Shard-group bookkeeping without a GEMV (gemv_tc.cu): publish = 1 takes part
-// in a sharded launch in which this rank has no rows (waits for the previous
-// launch, publishes this one); publish = 0 waits until every rank has
-// published this rank's latest launch, so later work sees every shard.
+// in a sharded launch in which this rank has no rows (one CTA: waits for the
+// previous launch, then arrives); publish = 0 waits until every rank's CTAs of
+// every sharded launch so far have arrived, so later work sees every shard.
 cudaError_t launch_shard_signal(const ShardArgs& s, int* err, int publish, cudaStream_t stream);
+// CTAs a tensor-core GEMV launch of `ntiles` 128-row tiles over K columns uses
+// (the grid a rank's sharded launch will have; gemv_tc.cu).
+int gemv_tc_grid(int fmt, int batch, int ntiles, int K, int num_sms, int split_cost, int64_t split_ws_floats,
+                 int split_tickets_n);
 
 // Decode-step operations (decode.cu); token and position live in device memory.
 cudaError_t launch_embed(const float* table, int64_t vocab, int64_t hidden, const int32_t* token, float* x,

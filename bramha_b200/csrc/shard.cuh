@@ -1,8 +1,8 @@
 #pragma once
 // shard.cuh -- device side of the column-shard group (ShardArgs, common.cuh):
-// bounded waits on the epochs that ranks publish into each other's flag
-// arrays, and the publication itself.  Plain loads and stores to peer memory
-// (IPC mappings over NVLink); no multicast of any kind.
+// the bounded wait on the ranks' arrival counters and a CTA's arrival.  Plain
+// loads, stores and reductions on peer memory (IPC mappings over NVLink); no
+// multicast of any kind.
 #include <cstdint>
 
 #include "common.cuh"
@@ -16,43 +16,44 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void red_add_sys(unsigned* p, unsigned v) {
+    asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void fence_sc_sys() { asm volatile("fence.sc.sys;" ::: "memory"); }
 
-// Waits until every rank has published at least epoch e here (bounded by the
-// context's wait limit; records BRAMHA_ERR_TIMEOUT and returns false when it
-// runs out).
-__device__ bool shard_wait(const ShardArgs& s, unsigned e, int* err) {
+// Waits until every rank's arrivals here have reached what this rank expects
+// (all CTAs of every sharded launch before the running one); bounded by the
+// context's wait limit: records BRAMHA_ERR_TIMEOUT and returns false when it
+// runs out.
+__device__ bool shard_wait(const ShardArgs& s, int* err) {
     const uint64_t t0 = globaltimer();
     const uint64_t limit = wait_limit_ns(err);
     for (int r = 0; r < s.world; ++r) {
-        while ((int)(ld_acquire_sys(s.flags + r) - e) < 0) {
+        const unsigned want = *reinterpret_cast<volatile unsigned*>(s.expected + r);
+        while ((int)(ld_acquire_sys(s.arrive + r) - want) < 0) {
             if (globaltimer() - t0 > limit) {
                 atomicCAS(err, 0, (int)BRAMHA_ERR_TIMEOUT);
                 return false;
             }
-            __nanosleep(64);
+            __nanosleep(32);
         }
     }
     return true;
 }
 
-// Called by thread 0 of every CTA once the CTA's stores are done (after a
-// system-scope fence by every storing thread and a CTA barrier): the last CTA
-// of the launch advances this rank's epoch and, unless a failure was recorded,
-// publishes it in every rank's flag array.
-__device__ void shard_complete(const ShardArgs& s, int* err) {
-    __threadfence_system();
+// Thread 0 of a CTA whose stores are done (every storing thread passed a CTA
+// barrier after its stores): one system-scope fence makes them visible, then
+// the CTA arrives in every rank's arena (unless a failure was recorded, so the
+// other ranks' waits run out rather than read incomplete rows).  The launch's
+// last CTA advances `expected` by every rank's grid for the next launch.
+__device__ void shard_arrive(const ShardArgs& s, int* err) {
+    fence_sc_sys();
+    if (*reinterpret_cast<volatile int*>(err) == 0)
+        for (int r = 0; r < s.world; ++r) red_add_sys(s.peer_arrive[r] + s.rank, 1u);
     const unsigned t = atomicAdd(s.done, 1u);
     if (t == gridDim.x - 1) {
-        __threadfence_system();
         *s.done = 0;
-        volatile unsigned* ep = s.epoch;
-        const unsigned e = *ep + 1;
-        *ep = e;
-        if (*reinterpret_cast<volatile int*>(err) == 0)
-            for (int r = 0; r < s.world; ++r) st_release_sys(s.peer_flags[r] + s.rank, e);
+        for (int r = 0; r < s.world; ++r) s.expected[r] += (unsigned)s.grid_of[r];
     }
 }
 

@@ -353,6 +353,11 @@ class CudaComputePlane:
         check(lib().bramha_cuda_gemv_chain_dev(self._ctx, len(ops), arr, batch, _stream(stream)))
         del keep
 
+    def gemv_program(self, ops, batch: int = 1) -> "GemvProgram":
+        """The chain `ops` (as gemv_chain_dev takes it) as one persistent launch;
+        the ops' tensors are bound now and must outlive the program."""
+        return GemvProgram(self, ops, batch)
+
     def gemv_chain(self, ops, batch: int = 1):
         """The same chain on host buffers (numpy arrays or pinned torch CPU tensors):
         inputs copied in, the chain run, outputs copied back; synchronous."""
@@ -372,6 +377,45 @@ class CudaComputePlane:
         n, k = w.shape
         check(lib().bramha_cuda_quantize_dev(self._ctx, FMT[fmt], n, k, w.data_ptr(), q.data_ptr(),
                                              scales.data_ptr(), _stream(stream)))
+
+
+class GemvProgram:
+    """A chain of GEMVs run as one persistent launch (bramha_cuda_gemv_program_*)."""
+
+    def __init__(self, plane: "CudaComputePlane", ops, batch: int = 1):
+        arr, keep = CudaComputePlane._chain_ops(ops)
+        h = ctypes.c_void_p()
+        check(lib().bramha_cuda_gemv_program_create(plane.ctx, len(ops), arr, batch, ctypes.byref(h)))
+        self.plane, self.handle, self._ops = plane, h.value, ops
+
+    def run(self, stream=None):
+        check(lib().bramha_cuda_gemv_program_run_dev(self.plane.ctx, self.handle, _stream(stream)))
+
+    def trace(self, on: bool = True):
+        """Record per-op, per-CTA timestamps in the next runs."""
+        check(lib().bramha_cuda_gemv_program_trace(self.plane.ctx, self.handle, int(on)))
+
+    def read_trace(self) -> np.ndarray:
+        """[n_ops][grid][8] %globaltimer stamps (ns) of the last traced run: op
+        reached, previous op finished everywhere, B area free, activations loaded,
+        terms built, last accumulator ready, outputs stored, completion published."""
+        n = len(self._ops) * 1024 * 8
+        buf = np.zeros(n, np.uint64)
+        g = ctypes.c_int()
+        check(lib().bramha_cuda_gemv_program_read_trace(self.plane.ctx, self.handle, buf.ctypes.data, n,
+                                                        ctypes.byref(g)))
+        return buf[:len(self._ops) * g.value * 8].reshape(len(self._ops), g.value, 8)
+
+    def close(self):
+        if self.handle:
+            lib().bramha_cuda_gemv_program_destroy(self.plane.ctx, self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def _ptr(a) -> int:

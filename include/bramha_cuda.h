@@ -241,6 +241,39 @@ BRAMHA_API int bramha_cuda_gemv_chain_dev(bramha_ctx* ctx, int n_ops, const bram
  * device-side failure). */
 BRAMHA_API int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch);
 
+/* The same chain as ONE persistent launch (no counterpart in the reference,
+ * which runs one GEMV at a time).  One CTA per SM runs every op: the weight
+ * stream and its decoding continue across op boundaries, and op i+1 reads its
+ * input only after every CTA has finished op i (a bounded wait on a per-op
+ * counter), so op i+1 may read op i's output.  A program binds its ops --
+ * weights, x, x_up and y pointers -- at creation and can be run any number of
+ * times (also from a CUDA graph); the weights must stay registered while it
+ * exists.  Requirements: every op LOG4, or every op W4ZP8, or every op W8;
+ * batch 1..8; every weight with N > 0 and K > 0; device pointers as for
+ * bramha_cuda_gemv_chain_dev; no sharded weights.  Results: W8 and W4ZP8
+ * equal the op-by-op chain within fp32 rounding of sum(x); LOG4 within fp32
+ * rounding (the chain's slots are grouped differently among the four MMA
+ * accumulators); all within the path's 1e-3 of the reference.  A program
+ * shares its context's K-split workspace: run one program or GEMV of a
+ * context at a time. */
+typedef struct bramha_gemv_program bramha_gemv_program;
+BRAMHA_API int bramha_cuda_gemv_program_create(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch,
+                                               bramha_gemv_program** out);
+BRAMHA_API int bramha_cuda_gemv_program_run_dev(bramha_ctx* ctx, bramha_gemv_program* prog, void* stream);
+BRAMHA_API int bramha_cuda_gemv_program_destroy(bramha_ctx* ctx, bramha_gemv_program* prog);
+
+/* Tracing of a program (the GPU counterpart of the reference's scoped
+ * profiler, src/inference/profiler.rs:57-153): with `on`, each later run
+ * records, per op and CTA, eight %globaltimer stamps in nanoseconds -- the op
+ * is reached, every CTA has finished the previous op, this CTA's MMAs of it
+ * are done, the activations are loaded, the activation terms are built, the
+ * last accumulator is ready, the outputs are stored, the completion is
+ * published.  read_trace copies [n_ops][grid][8] stamps (at most `n`) into
+ * host memory after a run; *grid receives the CTA count. */
+BRAMHA_API int bramha_cuda_gemv_program_trace(bramha_ctx* ctx, bramha_gemv_program* prog, int on);
+BRAMHA_API int bramha_cuda_gemv_program_read_trace(bramha_ctx* ctx, bramha_gemv_program* prog, uint64_t* out,
+                                                   size_t n, int* grid);
+
 /* The reference's keyed one-shot call, e.g.
  * `matvec_mul_int4(h, q_weight, scales, out_features, model_name, layer_name)`
  * (wgpu_backend.rs:1083-1091): when both names are non-NULL the weight is
