@@ -1,10 +1,11 @@
-"""Build libbramha_cuda.so in-tree with nvcc for sm_100a.
+"""Build libbramha_cuda.so and libbramha_cuda.a in-tree with nvcc for sm_100a.
 
     python -m bramha_b200.build [--force] [-v]
 
 Every .cu file under csrc/ is compiled with
 ``-gencode arch=compute_100a,code=sm_100a -lineinfo -O3`` and linked into one
-shared library next to this file (the C ABI of include/bramha_cuda.h).  No
+shared library next to this file (the C ABI of include/bramha_cuda.h), and
+archived into a static library of the same objects.  No
 fast-math: the packers must round exactly like the reference, and the GEMV's
 int4/int8 decode relies on subnormal floats (no flush-to-zero).
 """
@@ -22,6 +23,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libbramha_cuda.so")
+STATIC_LIB = os.path.join(HERE, "libbramha_cuda.a")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -76,6 +78,16 @@ def build(force: bool = False, verbose: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    if force or _stale(STATIC_LIB, objs):
+        # the same objects as a static archive, for a host program (e.g. a Rust
+        # crate's build step) that links the plane into its own binary; the
+        # final link adds -lcudart_static (or -lcudart) -lrt -ldl -lpthread -lstdc++
+        if os.path.exists(STATIC_LIB):
+            os.remove(STATIC_LIB)
+        cmd = [NVCC] + ARCH + ["-lib", "-o", STATIC_LIB] + objs
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"archive failed:\n{r.stdout}\n{r.stderr}")
     return LIB
 
 

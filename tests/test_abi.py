@@ -55,3 +55,36 @@ def test_get_cuda_plane_respects_bramha_cpu(monkeypatch):
     from bramha_b200 import plane
     monkeypatch.setenv("BRAMHA_CPU", "1")
     assert plane.get_cuda_plane(0) is None
+
+
+def test_static_archive_links_into_a_host_program(tmp_path):
+    """libbramha_cuda.a (the static form a Rust build step links) holds the
+    whole ABI: a C program that names every header symbol links against it
+    alone (plus the CUDA runtime) and runs; without a GPU, init reports an
+    error status."""
+    import os
+    from bramha_b200 import build as b
+    if not os.path.exists(b.STATIC_LIB):
+        b.build()
+    syms = bb.header_symbols()
+    src = tmp_path / "prog.c"
+    refs = "\n".join(f"    (void*)&{s}," for s in syms)
+    src.write_text(
+        '#include <stdio.h>\n#include "bramha_cuda.h"\n'
+        f"static void* all[] = {{\n{refs}\n}};\n"
+        "int main(void) {\n"
+        "    bramha_ctx* ctx = 0;\n"
+        "    int v = bramha_cuda_abi_version();\n"
+        "    int rc = bramha_cuda_init(0, 0);\n"
+        '    printf("%d %d %d\\n", v, rc, (int)(sizeof(all) / sizeof(all[0])));\n'
+        "    (void)ctx;\n    return 0;\n}\n")
+    exe = tmp_path / "prog"
+    cuda = "/usr/local/cuda"
+    r = subprocess.run(["g++", "-x", "c", str(src), "-x", "none", "-I", os.path.join(b.ROOT, "include"),
+                        b.STATIC_LIB, f"-L{cuda}/lib64", "-lcudart_static", "-lrt", "-ldl", "-lpthread",
+                        "-lstdc++", "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0, out.stderr
+    v, rc, n = map(int, out.stdout.split())
+    assert v == 1 and rc == -1 and n == len(syms)
