@@ -549,9 +549,24 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
         const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
         constexpr int kCols = B * T;  // accumulator columns in use
         constexpr int kHalves = kCols > 16 ? 2 : 1;
+        // output row `grow` of batch row b: this GPU's y, or (sharded) row
+        // row0 + grow of every rank's copy of the full output
+        auto store_y = [&](const TcSeg& sg, int si, int grow, int b, float v) {
+            if (!sharded) {
+                sg.y[(int64_t)b * sg.ldy + grow] = v;
+                return;
+            }
+            const int64_t off = (int64_t)b * sg.ldy + p.shard.row0[si] + grow;
+            for (int r = 0; r < p.shard.world; ++r) p.shard.peer_y[si][r][off] = v;
+        };
+        const int row = q4 * 32 + lane;
+        bool ok = true;
         for (int i = 0; i < ntile_cta; ++i) {
             const int buf = i & 1;
-            if (!warp_wait(&S.acc_full[buf], (i >> 1) & 1, abort_flag, p.err)) break;
+            if (!warp_wait(&S.acc_full[buf], (i >> 1) & 1, abort_flag, p.err)) {
+                ok = false;
+                break;
+            }
             tc_fence_after();
             // add the accumulators of the issuers that had a slot in this tile, in issuer order
             const int g0 = i * nslots;
@@ -580,18 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             const int tile = ci + i * p.ctas_per_split;
             const int si = seg_of(p, tile);
             const TcSeg& sg = p.seg[si];
-            const int row = q4 * 32 + lane;
             const int grow = (tile - sg.tile_begin) * TM + row;
-            // output row grow of batch row b: this GPU's y, or (sharded) row
-            // row0 + grow of every rank's copy of the full output
-            auto store_y = [&](int b, float v) {
-                if (!sharded) {
-                    sg.y[(int64_t)b * sg.ldy + grow] = v;
-                    return;
-                }
-                const int64_t off = (int64_t)b * sg.ldy + p.shard.row0[si] + grow;
-                for (int r = 0; r < p.shard.world; ++r) p.shard.peer_y[si][r][off] = v;
-            };
             float res[B];
             if (grow < sg.N) {
                 const float sc = __ldg(sg.scales + grow);
@@ -616,48 +620,68 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             if (p.ksplit == 1) {
                 if (grow < sg.N)
 #pragma unroll
-                    for (int b = 0; b < B; ++b) store_y(b, res[b]);
+                    for (int b = 0; b < B; ++b) store_y(sg, si, grow, b, res[b]);
                 continue;
             }
-            // K split: publish this split's partial, take a ticket; the last
-            // split adds all partials in split order.  Each warp (TMEM lane
-            // quarter) has its own ticket, so no barrier across the epilogue
-            // warps is needed (one that had given up a wait could not reach it).
+            // K split: this split's partial of the tile; its ticket is taken
+            // after the CTA's last tile (below), so the ticket round trips do not
+            // hold up the accumulators of the next tiles
             float* part = p.ws + (int64_t)tile * p.ksplit * B * TM;
             if (grow < sg.N)
 #pragma unroll
                 for (int b = 0; b < B; ++b) part[((int64_t)split * B + b) * TM + row] = res[b];
+        }
+        if (ok && p.ksplit > 1) {
+            // One fence for every partial of the CTA, then the tickets of all its
+            // tiles at once (lane t takes tile c + t); the split that arrives last
+            // at a tile adds all partials in split order.  Each warp (TMEM lane
+            // quarter) has its own tickets, so no barrier across the epilogue
+            // warps is needed (one that had given up a wait could not reach it).
             __threadfence();
             __syncwarp();
-            int last = 0;
-            if (lane == 0) last = atomicAdd(&p.tickets[tile * 4 + q4], 1) == p.ksplit - 1;
-            if (__shfl_sync(0xffffffffu, last, 0)) {
-                __threadfence();
-                if (grow < sg.N) {
-                    // the partials are added in split order; up to 32 loads are in
-                    // flight per lane (a load per split in turn would cost one L2
-                    // round trip per split and batch row)
-                    constexpr int U = B >= 8 ? 4 : B >= 4 ? 8 : 16;
-                    float acc[B];
-#pragma unroll
-                    for (int b = 0; b < B; ++b) acc[b] = 0.f;
-                    for (int s0 = 0; s0 < p.ksplit; s0 += U) {
-                        float v[U][B];
-#pragma unroll
-                        for (int u = 0; u < U; ++u)
-#pragma unroll
-                            for (int b = 0; b < B; ++b)
-                                v[u][b] = s0 + u < p.ksplit ? __ldcg(part + ((int64_t)(s0 + u) * B + b) * TM + row) : 0.f;
-#pragma unroll
-                        for (int u = 0; u < U; ++u)
-                            if (s0 + u < p.ksplit)
-#pragma unroll
-                                for (int b = 0; b < B; ++b) acc[b] += v[u][b];
-                    }
-#pragma unroll
-                    for (int b = 0; b < B; ++b) store_y(b, acc[b]);
+            for (int c = 0; c < ntile_cta; c += 32) {
+                int last = 0;
+                if (c + lane < ntile_cta) {
+                    const int tile = ci + (c + lane) * p.ctas_per_split;
+                    last = atomicAdd(&p.tickets[tile * 4 + q4], 1) == p.ksplit - 1;
                 }
-                if (lane == 0) p.tickets[tile * 4 + q4] = 0;  // ready for the next launch
+                unsigned mask = __ballot_sync(0xffffffffu, last);
+                if (mask) __threadfence();
+                while (mask) {
+                    const int l = __ffs(mask) - 1;
+                    mask &= mask - 1;
+                    const int tile = ci + (c + l) * p.ctas_per_split;
+                    const int si = seg_of(p, tile);
+                    const TcSeg& sg = p.seg[si];
+                    const int grow = (tile - sg.tile_begin) * TM + row;
+                    const float* part = p.ws + (int64_t)tile * p.ksplit * B * TM;
+                    if (grow < sg.N) {
+                        // the partials are added in split order; up to 32 loads are in
+                        // flight per lane (a load per split in turn would cost one L2
+                        // round trip per split and batch row)
+                        constexpr int U = B >= 8 ? 4 : B >= 4 ? 8 : 16;
+                        float acc[B];
+#pragma unroll
+                        for (int b = 0; b < B; ++b) acc[b] = 0.f;
+                        for (int s0 = 0; s0 < p.ksplit; s0 += U) {
+                            float v[U][B];
+#pragma unroll
+                            for (int u = 0; u < U; ++u)
+#pragma unroll
+                                for (int b = 0; b < B; ++b)
+                                    v[u][b] =
+                                        s0 + u < p.ksplit ? __ldcg(part + ((int64_t)(s0 + u) * B + b) * TM + row) : 0.f;
+#pragma unroll
+                            for (int u = 0; u < U; ++u)
+                                if (s0 + u < p.ksplit)
+#pragma unroll
+                                    for (int b = 0; b < B; ++b) acc[b] += v[u][b];
+                        }
+#pragma unroll
+                        for (int b = 0; b < B; ++b) store_y(sg, si, grow, b, acc[b]);
+                    }
+                    if (lane == 0) p.tickets[tile * 4 + q4] = 0;  // ready for the next launch
+                }
             }
         }
     }
