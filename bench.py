@@ -14,10 +14,13 @@ which each launch requests the next one's weights into L2).  Synthetic data;
 the 3.55 GB of packed weights per step exceed the 126 MB L2, so no flush is
 needed.  The same weights are then run at batch 8 and 64 (`batch_lines`).
 
-N > 1: every linear is column-sharded (output rows split across ranks); each
-GEMV's epilogue stores its rows into every rank's copy of the output over
-NVLink and publishes the launch, and the next GEMV waits for every rank's
-publication (strong scaling: total work fixed).  The linears' inputs are
+N > 1: the linears of at least --shard-min-mb MB of packed weights are
+column-sharded (output rows split across ranks): each such GEMV's epilogue
+stores its rows into every rank's copy of the output over NVLink and publishes
+the launch, and whatever reads that output waits for every rank's publication.
+Smaller linears run whole on every rank (a column shard of a launch-latency-bound
+GEMV costs more in cross-GPU waits than it saves in weight bytes).  Strong
+scaling: total work fixed, each linear counted once.  The linears' inputs are
 independent synthetic vectors, the same on every rank.
 
 Prints ONE JSON line on rank 0.  `value` is algorithmic GB/s over the whole job
@@ -582,7 +585,7 @@ def moe_bench(plane, dev, tokens=256, experts=64, top_k=8, hidden=3584, inter=25
 
 
 # ------------------------------------------------------------------ decode step (config 2)
-def decode_step_bench(plane, dev, prompt_len=512, new_tokens=128):
+def decode_step_bench(plane, dev, prompt_len=512, new_tokens=128, fuse_norm=False):
     """a full Qwen2-0.5B-architecture decode step (24 layers,
     hidden 896, 14/2 heads of 64, SwiGLU 4864, RMSNorm 1e-6, RoPE 1e6, vocab
     151936) with random weights in log4, KV cache prefilled to `prompt_len` from
@@ -614,7 +617,7 @@ def decode_step_bench(plane, dev, prompt_len=512, new_tokens=128):
                           lin(f"{i}.g", I, H), lin(f"{i}.u", I, H), lin(f"{i}.d", H, I)) for i in range(cfg.layers)]
     embed = torch.randn((V, H), generator=gen, device=dev)
     dm = DecodeModel(plane, cfg, layers, embed, vec(H, 1, 0.1), lin("lm", V, H),
-                     max_ctx=prompt_len + new_tokens, max_generated=new_tokens)
+                     max_ctx=prompt_len + new_tokens, max_generated=new_tokens, fuse_norm=fuse_norm)
     dm.capture()
     prompt = torch.randint(0, V, (prompt_len,), generator=torch.Generator().manual_seed(7)).tolist()
     dm.reset()
@@ -684,10 +687,11 @@ def run_ours(args, ws, rank, local):
     fmt, B, bits = args.fmt, args.batch, BITS[args.fmt]
     sp = None
     if ws > 1:
-        # column-shard group: every linear's output rows split across the ranks; the
+        # column-shard group: a large linear's output rows split across the ranks; the
         # GEMV epilogue stores each rank's rows into every rank's copy over NVLink
         from bramha_b200 import ShardedPlane
         sp = ShardedPlane(plane, arena_bytes=64 << 20)
+    shard_min = int(args.shard_min_mb * (1 << 20))
 
     # ---- weights: each linear generated whole (N(0,0.02), the same seed on every
     # rank), packed on the device; with N > 1 each rank keeps its rows
@@ -700,6 +704,7 @@ def run_ours(args, ws, rank, local):
         entry = []
         for gname, parts, k in groups:
             wts, ys = [], []
+            sharded = sp is not None and sum(n * k * bits // 8 for _, n in parts) >= shard_min
             for p, n in parts:
                 gen.manual_seed(1_000_003 * li + sum(map(ord, p)))
                 wf = torch.randn((n, k), generator=gen, device=dev, dtype=torch.float32).mul_(0.02)
@@ -707,7 +712,7 @@ def run_ours(args, ws, rank, local):
                 sd = torch.empty(n, dtype=torch.float32, device=dev)
                 plane.quantize_dev(fmt, wf, qd, sd)
                 del wf
-                if sp is None:
+                if not sharded:
                     w = plane.register_dev(f"L{li}.{p}", fmt, n, k, qd, sd)
                     ys.append(torch.empty((B, n), dtype=torch.float32, device=dev))
                 else:
@@ -718,21 +723,30 @@ def run_ours(args, ws, rank, local):
                 step_bytes += gemv_bytes(n, k, B, bits)  # whole-job algorithmic bytes
             gen.manual_seed(7 + li * 13 + len(entry))
             x = torch.randn((B, k), generator=gen, device=dev, dtype=torch.float32)
-            entry.append((gname, wts, x, ys, None))
+            entry.append((gname, wts, x, ys, sharded))
         layers.append(entry)
     torch.cuda.synchronize()
     setup_s = time.time() - t_setup
     launches_per_step = sum(len(e) for e in layers)
 
     stream = torch.cuda.Stream(device=dev)
-    # the step is one GEMV chain (bramha_cuda_gemv_chain_dev); with N > 1 the
-    # GEMVs are sharded and the step ends when every rank's rows have landed
-    chain_ops = [(wts, x, ys) for entry in layers for _, wts, x, ys, _ in entry]
+    # the step is one GEMV chain (bramha_cuda_gemv_chain_dev); with N > 1 a run of
+    # sharded GEMVs is followed by a wait for every rank's rows before an unsharded
+    # GEMV (its input may be their output), and the step ends when all have landed
+    flat = [(wts, x, ys, shd) for entry in layers for _, wts, x, ys, shd in entry]
+    segments = []  # [(ops, ends with a sharded op)]
+    for wts, x, ys, shd in flat:
+        if not segments or (segments[-1][1] and not shd):
+            segments.append(([], shd))
+        segments[-1][0].append((wts, x, ys))
+        segments[-1] = (segments[-1][0], shd)
+    n_sharded = sum(1 for *_, shd in flat if shd)
 
     def step():
-        plane.gemv_chain_dev(chain_ops, B, stream)
-        if sp is not None:
-            sp.sync(stream)
+        for ops, ends_sharded in segments:
+            plane.gemv_chain_dev(ops, B, stream)
+            if ends_sharded:
+                sp.sync(stream)
 
     # ---- capture one step (GEMVs and, on several GPUs, the NCCL all-gathers) in a
     # CUDA graph; replay it K times
@@ -808,17 +822,18 @@ def run_ours(args, ws, rank, local):
     # ---- per-launch durations: each group's launches (e.g. the 28 gate|up GEMVs)
     # captured in their own CUDA graph and replayed, so host launch latency is
     # not part of the measurement; mean device time per launch
-    groups = {}
+    groups, group_sharded = {}, {}
     for entry in layers:
-        for gname, wts, x, ys, _ in entry:
+        for gname, wts, x, ys, shd in entry:
             groups.setdefault(gname, []).append((wts, x, ys))
+            group_sharded[gname] = shd
     per = {}
     reps = 5
     for gname, items in groups.items():
         gg = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gg, stream=stream):
             plane.gemv_chain_dev(items, B, stream)
-            if sp is not None:
+            if group_sharded[gname]:
                 sp.sync(stream)
         gg.replay()
         torch.cuda.synchronize()
@@ -831,14 +846,12 @@ def run_ours(args, ws, rank, local):
         torch.cuda.synchronize()
         per[gname] = [a_.elapsed_time(b_) * 1e3 / (reps * len(items))] * len(items)
         del gg
-    def shard(n):  # this rank's rows [lo, hi) of an n-row linear
-        return n * rank // ws, n * (rank + 1) // ws
+    def shard(n, g):  # this rank's rows [lo, hi) of an n-row linear of group g
+        return (n * rank // ws, n * (rank + 1) // ws) if group_sharded[g] else (0, n)
 
-    group_bytes = {}
+    group_bytes = {}  # this rank's algorithmic bytes per launch of each group
     for gname, parts, k in GROUPS + [("lm_head", [("lm_head", V)], H)]:
-        nloc = sum(shard(n)[1] - shard(n)[0] for _, n in parts)
-        group_bytes[gname] = gemv_bytes(nloc, k, B, bits) if len(parts) == 1 else sum(
-            gemv_bytes(shard(n)[1] - shard(n)[0], k, B, bits) for _, n in parts)
+        group_bytes[gname] = sum(gemv_bytes(shard(n, gname)[1] - shard(n, gname)[0], k, B, bits) for _, n in parts)
     per_linear = {g: {"launches_per_step": len(v), "us_mean": round(sum(v) / len(v), 2),
                       "gbs": round(group_bytes[g] / (sum(v) / len(v) * 1e-6) / 1e9, 1),
                       "share": round(sum(v) / sum(sum(u) for u in per.values()), 3)} for g, v in per.items()}
@@ -914,8 +927,10 @@ def run_ours(args, ws, rank, local):
             "data": "synthetic (seeded N(0,0.02) weights packed on device, N(0,1) activations)",
             "config": {"workload": f"qwen2-7b linears ({args.layers} layers + lm_head), {fmt}, batch {B} decode GEMV",
                        "batch": B, "fmt": fmt, "hidden": H, "intermediate": I, "vocab": V, "layers": args.layers,
-                       "parallelism": f"column-shard x{ws}: each GEMV's epilogue stores its rows into every rank's "
-                                      "output over NVLink (no collective library)" if ws > 1 else "single GPU",
+                       "parallelism": f"column-shard x{ws} of the linears >= {args.shard_min_mb:g} MB "
+                                      f"({n_sharded} of {len(flat)} launches; the rest whole on every rank): each "
+                                      "sharded GEMV's epilogue stores its rows into every rank's output over NVLink "
+                                      "(no collective library)" if ws > 1 else "single GPU",
                        "l2": f"no flush: {step_bytes / 1e9:.2f} GB of packed weights per step >> 126 MB L2",
                        "cuda_graph": graph is not None,
                        "gemv_kernel": "tc_gemv_kernel: tile-major weights streamed by 2 bulk-copy producers, "
@@ -959,6 +974,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--fmt", choices=list(BITS), default="log4")
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--shard-min-mb", type=float, default=128.0,
+                    help="N > 1: column-shard the linears with at least this many MB of packed weights")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--repeats", type=int, default=5, help="extra timed K-step regions for the spread")
     ap.add_argument("--no-batch-lines", action="store_true", help="skip the batch 8 / 64 measurement")

@@ -68,6 +68,7 @@ _SIGNATURES = {
     "bramha_cuda_sparse_matvec_2_4_compressed": [_vp, _vp, _i64, _vp, _sz, _vp, _sz, _i64, ctypes.c_char_p,
                                                  ctypes.c_char_p, _vp],
     "bramha_cuda_gemv_swiglu_dev": [_vp, _vp, _vp, _vp, _i64, _vp, _vp],
+    "bramha_cuda_gemv_rmsnorm_dev": [_vp, _int, _vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp],
     "bramha_cuda_moe_mlp_dev": [_vp, _vp, _vp, _int, _int, _vp, _vp, _i64, _vp, _vp, _vp],
     "bramha_cuda_moe_mlp": [_vp, _vp, _vp, _int, _int, _vp, _vp, _i64, _vp, _vp],
     "bramha_cuda_moe_route_dev": [_vp, _vp, _i64, _int, _int, _vp, _vp, _vp],

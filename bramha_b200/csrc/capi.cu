@@ -69,6 +69,9 @@ struct bramha_ctx {
     int64_t pf_next = 8 << 20;           // GEMV chain: bytes of the next launch requested into L2
     int evict_first = 0;                 // GEMV weight copies marked first to be evicted from L2
     int split_cost = 240;                // GEMV K-split plan: cost of splitting, eighths of a block
+    // GEMV programs: L2 lookahead per CTA, bytes (measured on the Qwen2-7B step:
+    // 0 -> 1.48 ms, 128 KiB -> 1.52, 256 KiB -> 1.72; off by default)
+    int64_t prog_lookahead = 0;
     // column-shard group (bramha_cuda_shard_*): this rank's symmetric arena
     // (control block, then allocations from the bottom and host-chain staging
     // from the top) and the peers' arenas opened through CUDA IPC
@@ -479,9 +482,17 @@ int gemv_device_sharded(bramha_ctx* ctx, int n, const bramha_weight* const* ws, 
                         int64_t batch, float* const* ys, cudaStream_t st, const float* x_up, int next_n,
                         const bramha_weight* const* next_ws);
 
+// RMSNorm folded into a batch-1 GEMV's activation staging (GemvArgs::norm_w).
+struct NormIn {
+    const float* w;      // norm weight [K]
+    const float* delta;  // residual added to x first (may be null)
+    float* x_out;        // receives x + delta (may be null)
+    float eps;
+};
+
 int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const float* x, int64_t ldx,
                 int64_t batch, float* const* ys, cudaStream_t st, const float* x_up = nullptr, int next_n = 0,
-                const bramha_weight* const* next_ws = nullptr) {
+                const bramha_weight* const* next_ws = nullptr, const NormIn* norm = nullptr) {
     const int fmt = ws[0]->fmt;
     const int64_t K = ws[0]->K;
     for (int i = 1; i < n; ++i)
@@ -580,6 +591,13 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
         const bool cc = !x_up && (ctx->gemv_kernel == BRAMHA_GEMV_CUDA_CORE
                                       ? is_tiled(fmt) && a.batch == 1
                                       : ctx->gemv_kernel == BRAMHA_GEMV_AUTO && gemv_cc_eligible(fmt, a));
+        if (norm) {  // only the CUDA-core kernel forms the RMSNorm (the caller checked cc)
+            if (!cc || a.batch != 1 || a.K != K) return fail(BRAMHA_ERR_INVALID, "internal: fused RMSNorm without the CUDA-core GEMV");
+            a.norm_w = norm->w;
+            a.delta = norm->delta;
+            a.x_out = norm->x_out;
+            a.eps = norm->eps;
+        }
         if (cc)
             CK(launch_gemv_cc(fmt, a, ctx->num_sms, st), "cuda-core gemv launch");
         else if (is_tiled(fmt))
@@ -916,6 +934,7 @@ int bramha_cuda_set_gemv_tuning(bramha_ctx* ctx, int what, int64_t value) {
         case BRAMHA_TUNE_LOOKAHEAD_BYTES: ctx->pf_lookahead = value; break;
         case BRAMHA_TUNE_NEXT_LAUNCH_BYTES: ctx->pf_next = value; break;
         case BRAMHA_TUNE_EVICT_FIRST: ctx->evict_first = value ? 1 : 0; break;
+        case BRAMHA_TUNE_PROGRAM_LOOKAHEAD_BYTES: ctx->prog_lookahead = value; break;
         case BRAMHA_TUNE_SPLIT_COST:
             if (value > 1 << 20) return fail(BRAMHA_ERR_INVALID, "split cost out of range");
             ctx->split_cost = (int)value;
@@ -1242,7 +1261,7 @@ int bramha_cuda_gemv_program_run_dev(bramha_ctx* ctx, bramha_gemv_program* prog,
     if (!ctx || !prog || prog->ctx != ctx) return fail(BRAMHA_ERR_INVALID, "null program or another context's");
     DeviceGuard g(ctx->device);
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-    CK(chain_program_run(prog->prog, ctx->d_err, st), "gemv program launch");
+    CK(chain_program_run(prog->prog, ctx->d_err, ctx->prog_lookahead, st), "gemv program launch");
     return BRAMHA_OK;
 }
 
@@ -1291,6 +1310,76 @@ int bramha_cuda_gemv_swiglu_dev(bramha_ctx* ctx, const bramha_weight* w, const f
     const bramha_weight* ws[1] = {w};
     float* ys[1] = {y_dev};
     return gemv_device(ctx, 1, ws, gate_dev, w->K, batch, ys, st, up_dev);
+}
+
+namespace {
+bool overlaps(const float* a, const float* b, int64_t n) {
+    return a && b && a < b + n && b < a + n;
+}
+// The CUDA-core GEMV takes this launch (so it can form the RMSNorm itself).
+bool norm_fusable(bramha_ctx* ctx, int n, const bramha_weight* const* ws) {
+    const int fmt = ws[0]->fmt;
+    const int64_t K = ws[0]->K;
+    if (!is_tiled(fmt) || ctx->gemv_kernel == BRAMHA_GEMV_TENSOR_CORE || held_columns(fmt, K) != K || K > 1024)
+        return false;  // (the fused kernel keeps the whole residual, <= 1024 columns, in shared memory)
+    GemvArgs a{};
+    a.batch = 1;
+    a.K = (int)K;
+    for (int i = 0; i < n; ++i)
+        if (ws[i]->N > 0) {
+            if (ws[i]->N > 0x7fffffffLL) return false;
+            a.seg[a.nseg++].N = (int)ws[i]->N;
+        }
+    if (a.nseg == 0) return false;
+    if (ctx->gemv_kernel == BRAMHA_GEMV_CUDA_CORE) return true;
+    a.split_ws = ctx->split_ws;
+    a.split_ws_floats = kSplitWsFloats;
+    a.split_tickets = ctx->split_tickets;
+    a.split_tickets_n = kSplitTickets;
+    return gemv_cc_eligible(fmt, a);
+}
+}  // namespace
+
+int bramha_cuda_gemv_rmsnorm_dev(bramha_ctx* ctx, int n_weights, const bramha_weight* const* ws, const float* x_dev,
+                                 const float* delta_dev, const float* norm_w_dev, float eps, float* x_out_dev,
+                                 float* const* y_devs, void* stream) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (n_weights < 1 || n_weights > kMaxSegments)
+        return fail(BRAMHA_ERR_INVALID, "gemv_rmsnorm_dev: 1..%d weights (got %d)", kMaxSegments, n_weights);
+    if (!ws || !y_devs) return fail(BRAMHA_ERR_INVALID, "null argument");
+    for (int i = 0; i < n_weights; ++i) {
+        int rc = check_weight(ctx, ws[i]);
+        if (rc) return rc;
+        if (ws[i]->fmt != ws[0]->fmt || ws[i]->K != ws[0]->K)
+            return fail(BRAMHA_ERR_INVALID, "gemv_rmsnorm_dev: every weight must have the same format and K");
+        if (ws[i]->shard) return fail(BRAMHA_ERR_UNSUPPORTED, "gemv_rmsnorm_dev: sharded weights are not supported");
+        if (ws[i]->N > 0 && !y_devs[i]) return fail(BRAMHA_ERR_INVALID, "null output pointer");
+    }
+    const int64_t K = ws[0]->K;
+    if (K <= 0 || K > (1 << 24)) return fail(BRAMHA_ERR_INVALID, "gemv_rmsnorm_dev: K = %lld out of range", (long long)K);
+    if (!x_dev || !norm_w_dev) return fail(BRAMHA_ERR_INVALID, "null device pointer");
+    if (overlaps(x_out_dev, x_dev, K) || overlaps(x_out_dev, delta_dev, K))
+        return fail(BRAMHA_ERR_INVALID, "gemv_rmsnorm_dev: x_out_dev must not overlap x_dev or delta_dev");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    if (norm_fusable(ctx, n_weights, ws)) {
+        const NormIn nin = {norm_w_dev, delta_dev, x_out_dev, eps};
+        return gemv_device(ctx, n_weights, ws, x_dev, K, 1, y_devs, st, nullptr, 0, nullptr, &nin);
+    }
+    // Otherwise the RMSNorm kernel, then the GEMV (the same values, two launches):
+    // r and the normalised activations in stream-ordered scratch.
+    const int64_t kp = (K + 3) & ~int64_t(3);
+    float* tmp = nullptr;
+    CK(cudaMallocAsync(reinterpret_cast<void**>(&tmp), sizeof(float) * (size_t)(2 * kp), st),
+       "cudaMallocAsync(rmsnorm scratch)");
+    float* h = tmp;
+    float* r = x_out_dev ? x_out_dev : tmp + kp;
+    cudaError_t e = cudaMemcpyAsync(r, x_dev, sizeof(float) * (size_t)K, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess) e = launch_rmsnorm(r, delta_dev, norm_w_dev, K, eps, h, st);
+    int rc = e == cudaSuccess ? gemv_device(ctx, n_weights, ws, h, K, 1, y_devs, st) : cuda_fail(e, "rmsnorm launch");
+    cudaError_t e2 = cudaFreeAsync(tmp, st);
+    if (rc == BRAMHA_OK && e2 != cudaSuccess) rc = cuda_fail(e2, "cudaFreeAsync(rmsnorm scratch)");
+    return rc;
 }
 
 int bramha_cuda_matvec(bramha_ctx* ctx, int fmt, const float* h, int64_t K, const void* q_weight, size_t q_bytes,

@@ -150,6 +150,14 @@ struct GemvArgs {
     // their own copies are issued, so HBM keeps streaming across the launch
     // boundary.
     int pf_ahead;
+    // Non-null norm_w (CUDA-core GEMV, batch 1): the activation is the RMSNorm
+    // of r = x + delta (delta may be null) with weight norm_w and epsilon eps,
+    // computed exactly as launch_rmsnorm does; r is also stored to x_out (when
+    // non-null; it must not overlap x or delta).
+    const float* norm_w;
+    const float* delta;
+    float* x_out;
+    float eps;
     int pf_next_n;
     const uint8_t* pf_next_ptr[kMaxSegments];
     int64_t pf_next_bytes[kMaxSegments];
@@ -214,7 +222,7 @@ cudaError_t launch_gemv_cc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t
 struct ChainProgram;
 cudaError_t chain_program_create(int fmt, int batch, int nops, const GemvArgs* ops, int num_sms, int split_cost,
                                  float* ws, int64_t ws_floats, int* tickets, int n_tickets, ChainProgram** out);
-cudaError_t chain_program_run(ChainProgram* prog, int* err, cudaStream_t stream);
+cudaError_t chain_program_run(ChainProgram* prog, int* err, int64_t lookahead_bytes, cudaStream_t stream);
 void chain_program_destroy(ChainProgram* prog);
 // Per-op, per-CTA %globaltimer stamps of the next runs ([nops][grid][4]).
 cudaError_t chain_program_trace(ChainProgram* prog, int on);

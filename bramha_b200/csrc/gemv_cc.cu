@@ -28,6 +28,7 @@ namespace bramha {
 namespace {
 
 constexpr int kCcThreads = 256;  // 2 threads per row of a 128-row tile
+constexpr int kCcNormMaxK = 1024;  // a fused RMSNorm keeps the whole residual in shared memory
 constexpr int kCcMaxBlocks = 16;  // 64-column blocks per CTA (registers: 4-bit 4 words/block, int8 8)
 
 struct CcParams {
@@ -41,6 +42,11 @@ struct CcParams {
     int bps;       // blocks per split
     float* ws;     // [ntiles][ksplit][128] partials (ksplit > 1)
     int* tickets;  // [ntiles], zero between launches
+    // RMSNorm of r = x + delta as the activation (GemvArgs::norm_w); r -> x_out
+    const float* norm_w;
+    const float* delta;
+    float* x_out;
+    float eps;
 };
 
 template <int FMT>
@@ -102,6 +108,36 @@ __device__ __forceinline__ float block_dot(const uint32_t (&w)[CcFmt<FMT>::kWord
     return acc;
 }
 
+// 1 / sqrt(mean(r^2) + eps) of r = x + delta over the K (<= 1024) columns,
+// with the additions in exactly the order of the RMSNorm kernel (launch_rmsnorm,
+// 1024 threads: thread t sums columns t, t + 1024, ..., warp trees, then a tree
+// over the 32 warp sums): thread t of this CTA stands for threads t + 256j of
+// that kernel.  r is left in rs[] for the staging.  Every thread returns the
+// same value.
+__device__ float rms_inv(const CcParams& p, float* red, float* rs) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 0; j < 1024 / kCcThreads; ++j) {
+        const int vt = threadIdx.x + kCcThreads * j;
+        float ss = 0.f;
+        if (vt < p.K) {
+            float v = __ldcg(p.x + vt);
+            if (p.delta) v = __fadd_rn(v, __ldcg(p.delta + vt));
+            rs[vt] = v;
+            ss = __fadd_rn(ss, __fmul_rn(v, v));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) red[vt >> 5] = ss;
+    }
+    __syncthreads();
+    float v = red[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const float var = v / (float)p.K;
+    return 1.0f / sqrtf(__fadd_rn(var, p.eps));
+}
+
 template <int FMT>
 __device__ __forceinline__ void load_block(const uint8_t* blk, int row, int half, uint32_t (&w)[CcFmt<FMT>::kWords]) {
     if constexpr (FMT == BRAMHA_FMT_W8) {
@@ -118,10 +154,12 @@ __device__ __forceinline__ void load_block(const uint8_t* blk, int row, int half
     }
 }
 
-template <int FMT>
+template <int FMT, bool NORM>
 __global__ void __launch_bounds__(kCcThreads) cc_gemv_kernel(const __grid_constant__ CcParams p) {
     using Fm = CcFmt<FMT>;
     __shared__ float xs[kCcMaxBlocks * kTileK];
+    __shared__ float red[32];
+    __shared__ float rs[NORM ? kCcNormMaxK : 1];  // fused RMSNorm: the residual r = x + delta
     __shared__ int last;
     const int tile = blockIdx.x / p.ksplit, split = blockIdx.x - tile * p.ksplit;
     const int row = threadIdx.x >> 1, half = threadIdx.x & 1;
@@ -142,7 +180,18 @@ __global__ void __launch_bounds__(kCcThreads) cc_gemv_kernel(const __grid_consta
     for (int i = 0; i < kCcMaxBlocks; ++i)
         if (i < n0) load_block<FMT>(base + (int64_t)i * kBlockBytes, row, half, w[i]);
     const float sc = grow < sg.N ? __ldg(sg.scales + grow) : 0.f;
+    // fused RMSNorm: this thread's norm weights of the staging loop below (one
+    // chunk: K <= 1024), also immutable
+    constexpr int kNw = NORM ? kCcNormMaxK / kCcThreads : 1;
+    float nwr[kNw];
+#pragma unroll
+    for (int u = 0; u < kNw; ++u) {
+        const int j = threadIdx.x + u * kCcThreads, col = b0 * kTileK + j;
+        nwr[u] = NORM && j < n0 * kTileK && col < p.K ? __ldg(p.norm_w + col) : 0.f;
+    }
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    float rinv = 0.f;
+    if constexpr (NORM) rinv = rms_inv(p, red, rs);  // (its barrier also publishes rs)
 
     float acc = 0.f;
     for (int c0 = 0; c0 < nb; c0 += kCcMaxBlocks) {
@@ -154,9 +203,24 @@ __global__ void __launch_bounds__(kCcThreads) cc_gemv_kernel(const __grid_consta
             for (int i = 0; i < kCcMaxBlocks; ++i)
                 if (i < cn) load_block<FMT>(base + (int64_t)(c0 + i) * kBlockBytes, row, half, w[i]);
         }
-        for (int j = threadIdx.x; j < cn * kTileK; j += kCcThreads) {
+#pragma unroll 4
+        for (int u = 0, j = threadIdx.x; j < cn * kTileK; ++u, j += kCcThreads) {
             const int col = col0 + j;
-            xs[j] = col < p.K ? __ldcg(p.x + col) : 0.f;  // written by the previous kernel: L2, not L1
+            float v = 0.f;
+            if (col < p.K) {
+                if constexpr (NORM) {  // r = x + delta, then r * rinv * w as the RMSNorm kernel rounds it
+                    v = rs[col];   // (one chunk: u < kNw)
+                    if (p.x_out && tile == 0) p.x_out[col] = v;  // each column once: the splits of tile 0
+                    float w = 0.f;
+#pragma unroll
+                    for (int q = 0; q < kNw; ++q)
+                        if (q == u) w = nwr[q];
+                    v = __fmul_rn(__fmul_rn(v, rinv), w);
+                } else {
+                    v = __ldcg(p.x + col);  // written by the previous kernel: L2, not L1
+                }
+            }
+            xs[j] = v;
         }
         __syncthreads();
 #pragma unroll
@@ -202,7 +266,8 @@ cudaError_t launch_fmt(const CcParams& p, cudaStream_t st) {
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, cc_gemv_kernel<FMT>, p);
+    if (p.norm_w) return cudaLaunchKernelEx(&cfg, cc_gemv_kernel<FMT, true>, p);
+    return cudaLaunchKernelEx(&cfg, cc_gemv_kernel<FMT, false>, p);
 }
 
 }  // namespace
@@ -254,6 +319,11 @@ cudaError_t launch_gemv_cc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t
     p.ksplit = (p.ksteps + p.bps - 1) / p.bps;
     p.ws = a.split_ws;
     p.tickets = a.split_tickets;
+    if (a.norm_w && a.K > kCcNormMaxK) return cudaErrorInvalidValue;
+    p.norm_w = a.norm_w;
+    p.delta = a.delta;
+    p.x_out = a.x_out;
+    p.eps = a.eps;
     switch (fmt) {
         case BRAMHA_FMT_LOG4: return launch_fmt<BRAMHA_FMT_LOG4>(p, st);
         case BRAMHA_FMT_W4ZP8: return launch_fmt<BRAMHA_FMT_W4ZP8>(p, st);

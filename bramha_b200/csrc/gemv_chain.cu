@@ -76,6 +76,10 @@ struct ChainParams {
     // optional trace, [nops][gridDim.x][kTraceStamps] %globaltimer stamps per op
     // and CTA (kTraceStamps, below)
     unsigned long long* trace;
+    // L2 lookahead: each producer requests its slot pairs this many of its own
+    // pairs ahead of its copies (HBM -> L2), so the weight stream keeps going
+    // while an op waits for the previous one (0 = off)
+    int pf_ahead;
 };
 
 struct alignas(1024) ChSmem {
@@ -300,7 +304,38 @@ __global__ void __launch_bounds__(kThreads, 1) chain_gemv_kernel(const __grid_co
             const int withheld =
                 pid == 0 && blockIdx.x == 0 && injected_fault(p.err) == kFaultGemvWithholdCopy ? 6 : -1;
             int d = pid;
+            // L2 prefetch front: pair pd of this producer, at cursor pc
+            Cur pc = cur;
+            int pd = d;
+            auto prefetch_to = [&](int upto) {
+                for (; pc.op < p.nops && pd <= upto; pd += kNP) {
+                    const uint32_t b0 = (uint32_t)(min(Fm::kStepsPerSlot, pc.nsteps - pc.j * Fm::kStepsPerSlot) * Fm::kBlock);
+                    const uint8_t* s0 = pc.base + (int64_t)pc.j * Fm::kStepsPerSlot * Fm::kBlock;
+                    Cur c1 = pc;
+                    cur_advance<FMT>(p, c1, 1);
+                    if (c1.op < p.nops) {
+                        const uint32_t b1 =
+                            (uint32_t)(min(Fm::kStepsPerSlot, c1.nsteps - c1.j * Fm::kStepsPerSlot) * Fm::kBlock);
+                        const uint8_t* s1 = c1.base + (int64_t)c1.j * Fm::kStepsPerSlot * Fm::kBlock;
+                        if (s1 == s0 + b0) {
+                            prefetch_l2(s0, b0 + b1);
+                        } else {
+                            prefetch_l2(s0, b0);
+                            prefetch_l2(s1, b1);
+                        }
+                    } else {
+                        prefetch_l2(s0, b0);
+                    }
+                    cur_advance<FMT>(p, pc, 2 * kNP);
+                }
+            };
+            // the first kSD pairs go straight to shared memory; the front starts past them
+            if (p.pf_ahead > 0) {
+                for (int i = 0; i < kSD / kNP && pc.op < p.nops; ++i, pd += kNP) cur_advance<FMT>(p, pc, 2 * kNP);
+                prefetch_to(pid + kSD + (p.pf_ahead - 1) * kNP);
+            }
             for (; cur.op < p.nops; d += kNP) {
+                if (p.pf_ahead > 0) prefetch_to(d + kSD + (p.pf_ahead - 1) * kNP);
                 if (!mbar_wait(&S.w_empty[d % kSD], ((d / kSD) & 1) ^ 1, abort_flag, p.err)) break;
                 if (d == withheld) {
                     cur_advance<FMT>(p, cur, 2 * kNP);
@@ -870,8 +905,9 @@ cudaError_t chain_program_create(int fmt, int batch, int nops, const GemvArgs* o
     return cudaSuccess;
 }
 
-cudaError_t chain_program_run(ChainProgram* prog, int* err, cudaStream_t st) {
+cudaError_t chain_program_run(ChainProgram* prog, int* err, int64_t lookahead_bytes, cudaStream_t st) {
     ChainParams p;
+    p.pf_ahead = (int)std::min<int64_t>(lookahead_bytes / (2 * kSlotBytes * kNP), 1 << 16);  // pairs per producer
     p.ops = prog->ops;
     p.nops = prog->nops;
     p.slots_total = prog->slots;

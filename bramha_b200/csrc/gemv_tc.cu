@@ -309,8 +309,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
         }
 
         // ---------------- activations -> staging, max|x|, sum(x)
+        // (a split whose rows do not fit the staging area reads them again from
+        // global memory when it builds the terms, computing the same values)
+        const int kv = min(nk, p.K - k0);
+        // (at batch 1 and 2 every K range a plan gives fits: no second path)
+        const bool staged = B <= 2 || B * nk <= kStageFloats;
         {
-            const int kv = min(nk, p.K - k0);
 #pragma unroll
             for (int b = 0; b < B; ++b) {
                 const float* xr = p.x + (int64_t)b * p.ldx + k0;
@@ -337,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
 #pragma unroll
                 for (int u = 0; u < kPerThread; ++u) {
                     const int k = ta + u * kActThreads;
-                    if (k < nk) stage[b * nk + k] = v[u];
+                    if (staged && k < nk) stage[b * nk + k] = v[u];
                     am = fmaxf(am, fabsf(v[u]));
                     sm += v[u];
                 }
@@ -377,7 +381,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const int col = (kb << 7) + pos_to_col<FMT>(pin + e);
-                    v[e] = col < nk ? stage[b * nk + col] * s : 0.f;
+                    float a = 0.f;
+                    if (staged) {
+                        if (col < nk) a = stage[b * nk + col];
+                    } else if (col < kv) {
+                        const int64_t off = (int64_t)b * p.ldx + k0 + col;
+                        a = sharded ? __ldcg(p.x + off) : __ldg(p.x + off);
+                        if (p.x_up) {  // as in the first pass
+                            const float silu = __fmul_rn(a, 1.0f / __fadd_rn(1.0f, expf(-a)));
+                            a = __fmul_rn(silu, sharded ? __ldcg(p.x_up + off) : __ldg(p.x_up + off));
+                        }
+                    }
+                    v[e] = a * s;
                 }
                 uint32_t word[T];
                 make_terms<FMT, T>(v[0], v[1], v[2], v[3], word);
@@ -548,7 +563,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
         const int q4 = warp & 3;
         const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
         constexpr int kCols = B * T;  // accumulator columns in use
-        constexpr int kHalves = kCols > 16 ? 2 : 1;
         // output row `grow` of batch row b: this GPU's y, or (sharded) row
         // row0 + grow of every rank's copy of the full output
         auto store_y = [&](const TcSeg& sg, int si, int grow, int b, float v) {
@@ -560,6 +574,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
             for (int r = 0; r < p.shard.world; ++r) p.shard.peer_y[si][r][off] = v;
         };
         const int row = q4 * 32 + lane;
+        // accumulator columns per TMEM load, issuers per wait (at most 32
+        // registers of loads in flight)
+        // (32 columns: two 16-column loads per issuer, a wait after each)
+        constexpr int kNC = kCols <= 4 ? 4 : kCols <= 8 ? 8 : kCols <= 16 ? 16 : 32;
+        constexpr int kLd = kNC == 32 ? 16 : kNC;  // columns per load
+        constexpr int kPer = kNC <= 8 ? 4 : kNC == 16 ? 2 : 1;
+        static_assert(kNC <= N && kNI % kPer == 0, "accumulator columns");
         bool ok = true;
         for (int i = 0; i < ntile_cta; ++i) {
             const int buf = i & 1;
@@ -568,24 +589,32 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
                 break;
             }
             tc_fence_after();
-            // add the accumulators of the issuers that had a slot in this tile, in issuer order
+            // add the accumulators of the issuers that had a slot in this tile, in
+            // issuer order; the loads of kPer issuers are in flight before one wait
             const int g0 = i * nslots;
-            uint32_t d[16 * kHalves];
+            uint32_t d[kNC];
 #pragma unroll
-            for (int c = 0; c < 16 * kHalves; ++c) d[c] = 0;
+            for (int c = 0; c < kNC; ++c) d[c] = 0;
 #pragma unroll
-            for (int me = 0; me < kNI; ++me) {
-                if ((me - g0 % kNI + kNI) % kNI >= nslots) continue;  // no slot of this tile
+            for (int m0 = 0; m0 < kNI; m0 += kPer) {
 #pragma unroll
-                for (int h = 0; h < kHalves; ++h) {
-                    uint32_t t[16];
-                    tmem_ld16(tmem + lane_base + (me * 2 + buf) * N + h * 16, t);
+                for (int h = 0; h < kNC / kLd; ++h) {
+                    uint32_t t[kPer][kLd];
 #pragma unroll
-                    for (int c = 0; c < 16; ++c) {
-                        if constexpr (FMT == BRAMHA_FMT_LOG4)
-                            d[h * 16 + c] = __float_as_uint(__uint_as_float(d[h * 16 + c]) + __uint_as_float(t[c]));
-                        else
-                            d[h * 16 + c] += t[c];  // s32
+                    for (int u = 0; u < kPer; ++u)
+                        if ((m0 + u - g0 % kNI + kNI) % kNI < nslots)  // this issuer had a slot here
+                            tmem_ld_nw<kLd>(tmem + lane_base + ((m0 + u) * 2 + buf) * N + h * kLd, t[u]);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int u = 0; u < kPer; ++u) {
+                        if ((m0 + u - g0 % kNI + kNI) % kNI >= nslots) continue;
+#pragma unroll
+                        for (int c = 0; c < kLd; ++c) {
+                            if constexpr (FMT == BRAMHA_FMT_LOG4)
+                                d[h * kLd + c] = __float_as_uint(__uint_as_float(d[h * kLd + c]) + __uint_as_float(t[u][c]));
+                            else
+                                d[h * kLd + c] += t[u][c];  // s32
+                        }
                     }
                 }
             }
@@ -609,10 +638,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemv_kernel(const __grid_const
 #pragma unroll
                         for (int j = T - 1; j >= 0; --j) acc = acc * 0.0078125f + (float)(int)d[b * T + j];
                     }
-                    const float xq = acc / act_scale<FMT>(S.amax[b]);  // sum(a * x), a as held in A
+                    // sum(a * x), a as held in A: acc / s with s = 2^k (normal, as is
+                    // 1/s), so the product with 1/s (bits 254 - exponent) is exact
+                    const float xq = acc * __int_as_float(0x7F000000 - __float_as_int(act_scale<FMT>(S.amax[b])));
+                    const float sx = S.sx[b];
                     float dot;
-                    if constexpr (FMT == BRAMHA_FMT_LOG4) dot = fmaf(xq, 16384.0f, -S.sx[b]);  // sum((2^c - 1) x)
-                    else if constexpr (FMT == BRAMHA_FMT_W4ZP8) dot = fmaf(-8.0f, S.sx[b], xq);  // sum((q - 8) x)
+                    if constexpr (FMT == BRAMHA_FMT_LOG4) dot = fmaf(xq, 16384.0f, -sx);  // sum((2^c - 1) x)
+                    else if constexpr (FMT == BRAMHA_FMT_W4ZP8) dot = fmaf(-8.0f, sx, xq);  // sum((q - 8) x)
                     else dot = xq;
                     res[b] = dot * sc;
                 }

@@ -177,14 +177,13 @@ __device__ __forceinline__ void make_terms(float v0, float v1, float v2, float v
 }
 
 // Largest K range (64-column blocks) one CTA takes: its B terms fit the B
-// area and its raw activations the staging area and the threads' loads.
+// area and its activation columns the threads' loads (rows that do not fit
+// the staging area are read twice instead).
 int max_split_steps(int fmt, int batch) {
     const int terms = fmt == BRAMHA_FMT_LOG4 ? 4 : 3;
     const int n = batch * terms <= 16 ? 16 : 32;
     int m = 2 * (kXBytes / (n * 128));
-    const int by_stage = kStageFloats / (batch * kTileK);
     const int by_threads = kPerThread * kActThreads / kTileK;
-    if (by_stage < m) m = by_stage;
     if (by_threads < m) m = by_threads;
     return m;
 }

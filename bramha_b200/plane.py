@@ -292,6 +292,17 @@ class CudaComputePlane:
         check(lib().bramha_cuda_gemm_dev(self._ctx, w.handle, x.data_ptr(), dt, x.shape[0], y.data_ptr(),
                                          _stream(stream)))
 
+    def gemv_rmsnorm_dev(self, ws: Sequence[Weight], x, delta, norm_w, eps: float, x_out, ys, stream=None):
+        """ys[i] = W_i rms_norm(x + delta) * norm_w at batch 1, with x + delta stored
+        to x_out (None: not stored; it must not overlap x or delta); delta may be
+        None.  One launch when the CUDA-core GEMV takes the weights."""
+        n = len(ws)
+        harr = (ctypes.c_void_p * n)(*[w.handle for w in ws])
+        yarr = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+        check(lib().bramha_cuda_gemv_rmsnorm_dev(self._ctx, n, harr, x.data_ptr(), _ptr_or_none(delta),
+                                                 norm_w.data_ptr(), float(eps), _ptr_or_none(x_out), yarr,
+                                                 _stream(stream)))
+
     def gemv_swiglu_dev(self, w: Weight, gate, up, y, stream=None):
         """y = W (silu(gate) * up), one launch (CUDA f32 tensors [batch][K])."""
         batch = 1 if gate.dim() == 1 else gate.shape[0]
@@ -319,11 +330,12 @@ class CudaComputePlane:
         """L2 prefetch of the tensor-core GEMV (tuning only; results do not change)."""
         check(lib().bramha_cuda_set_prefetch(self._ctx, int(lookahead_bytes), int(next_launch_bytes)))
 
-    TUNING = {"lookahead_bytes": 1, "next_launch_bytes": 2, "evict_first": 3, "split_cost": 4}
+    TUNING = {"lookahead_bytes": 1, "next_launch_bytes": 2, "evict_first": 3, "split_cost": 4,
+              "program_lookahead_bytes": 5}
 
     def set_gemv_tuning(self, **kw):
         """Tensor-core GEMV tuning (results do not change): lookahead_bytes,
-        next_launch_bytes, evict_first (0/1), split_cost."""
+        next_launch_bytes, evict_first (0/1), split_cost, program_lookahead_bytes."""
         for k, v in kw.items():
             check(lib().bramha_cuda_set_gemv_tuning(self._ctx, self.TUNING[k], int(v)))
 
@@ -423,6 +435,10 @@ def _ptr(a) -> int:
     if hasattr(a, "data_ptr"):
         return a.data_ptr()
     return a.ctypes.data
+
+
+def _ptr_or_none(a) -> Optional[int]:
+    return None if a is None else _ptr(a)
 
 
 _STREAM_LEGACY = 0x1  # cudaStreamLegacy: the legacy default stream, valid in any CUDA runtime

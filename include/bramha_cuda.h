@@ -151,11 +151,15 @@ BRAMHA_API int bramha_cuda_set_prefetch(bramha_ctx* ctx, int64_t lookahead_bytes
  * change): LOOKAHEAD_BYTES / NEXT_LAUNCH_BYTES as bramha_cuda_set_prefetch;
  * EVICT_FIRST (default 0): weight copies are marked first to be evicted from
  * L2; SPLIT_COST (default 240): what the K-split plan charges for splitting a
- * launch's K range, in eighths of one 64-column weight block. */
+ * launch's K range, in eighths of one 64-column weight block;
+ * PROGRAM_LOOKAHEAD_BYTES (default 0 = off): how far ahead of its shared-memory
+ * copies each CTA of a GEMV program requests its weight stream into L2, so the
+ * stream continues while an op waits for the previous op's output. */
 #define BRAMHA_TUNE_LOOKAHEAD_BYTES 1
 #define BRAMHA_TUNE_NEXT_LAUNCH_BYTES 2
 #define BRAMHA_TUNE_EVICT_FIRST 3
 #define BRAMHA_TUNE_SPLIT_COST 4
+#define BRAMHA_TUNE_PROGRAM_LOOKAHEAD_BYTES 5
 BRAMHA_API int bramha_cuda_set_gemv_tuning(bramha_ctx* ctx, int what, int64_t value);
 
 /* ---------------------------------------------------------------- weights */
@@ -212,6 +216,23 @@ BRAMHA_API int bramha_cuda_gemv_multi_dev(bramha_ctx* ctx, int n_weights, const 
  * 16-byte aligned; y [batch][N]; stream-ordered. */
 BRAMHA_API int bramha_cuda_gemv_swiglu_dev(bramha_ctx* ctx, const bramha_weight* w, const float* gate_dev,
                                            const float* up_dev, int64_t batch, float* y_dev, void* stream);
+
+/* A pre-norm block's RMSNorm and the GEMVs that read it, batch 1: with
+ * r = x + delta (delta may be NULL: r = x), h = rms_norm(r) * norm_w exactly as
+ * bramha_cuda_op_rmsnorm computes it (rms_norm, cpu_engine.rs:1292-1302, with
+ * the residual add of the decode loop, :2819-3064), then y_i = W_i h for each
+ * weight (fused_qkv_mul_into / the gate and up projections, :3342-3354).  r is
+ * stored to x_out_dev when it is non-NULL (x_out_dev must not overlap x_dev or
+ * delta_dev: the residual stream is double-buffered); h is not stored.  When
+ * the CUDA-core GEMV takes the weights (batch-1 launches of short rows, see
+ * bramha_cuda_set_gemv_kernel) the RMSNorm is formed inside that one launch,
+ * every CTA reducing the whole r in the RMSNorm kernel's order; otherwise the
+ * RMSNorm kernel runs first (stream-ordered scratch).  Either way the outputs
+ * equal bramha_cuda_op_rmsnorm followed by bramha_cuda_gemv_multi_dev bit for
+ * bit.  1..8 weights of one tiled format and K; device pointers; stream-ordered. */
+BRAMHA_API int bramha_cuda_gemv_rmsnorm_dev(bramha_ctx* ctx, int n_weights, const bramha_weight* const* ws,
+                                            const float* x_dev, const float* delta_dev, const float* norm_w_dev,
+                                            float eps, float* x_out_dev, float* const* y_devs, void* stream);
 
 /* A chain of dependent GEMVs: the reference's decode loop calls
  * matvec_mul_into back to back (fused_qkv_mul_into, o_proj, run_mlp_into's

@@ -54,7 +54,7 @@ def oracle_model(fmt, layers=2, vocab=4096, seed=31):
     return m
 
 
-def gpu_model(plane, m, tag, max_ctx=64):
+def gpu_model(plane, m, tag, max_ctx=64, fuse_norm=True):
     from bramha_b200 import DecodeConfig, DecodeLayer, DecodeModel
     c = m.cfg
     dev = torch.device("cuda", 0)
@@ -65,7 +65,8 @@ def gpu_model(plane, m, tag, max_ctx=64):
                           reg(f"{i}.d", L.down)) for i, L in enumerate(m.layers)]
     cfg = DecodeConfig(layers=c.layers, hidden=c.hidden, heads=c.heads, kv_heads=c.kv_heads, head_dim=c.head_dim,
                        intermediate=c.intermediate, vocab=c.vocab, eps=c.eps, rope_theta=c.rope_theta)
-    return DecodeModel(plane, cfg, layers, t(m.embed), t(m.norm), reg("lm", m.lm_head), max_ctx=max_ctx)
+    return DecodeModel(plane, cfg, layers, t(m.embed), t(m.norm), reg("lm", m.lm_head), max_ctx=max_ctx,
+                       fuse_norm=fuse_norm)
 
 
 @pytest.mark.parametrize("fmt", ["log4", "w4zp8", "w8"])
@@ -201,4 +202,88 @@ def test_gemv_swiglu_equals_silu_then_gemv(plane, fmt):
             plane.gemv_swiglu_dev(w, g, u, y2)
             plane.stream_sync()
             assert torch.equal(y1, y2), (n, batch)
+        plane.evict(w.key)
+
+
+@pytest.mark.parametrize("fmt,fuse", [("log4", True), ("w4zp8", True), ("w8", True), ("log4", "mlp")])
+def test_decode_fused_norms_equal_separate_kernels(plane, fmt, fuse):
+    """The step with residual adds + RMSNorms formed by the GEMV that reads them
+    (bramha_cuda_gemv_rmsnorm_dev, double-buffered residual) equals the step with
+    the RMSNorm kernel and the plain GEMV, bit for bit: logits and greedy tokens."""
+    m = oracle_model(fmt, layers=3, vocab=2048, seed=13)
+    fused = gpu_model(plane, m, f"fnf:{fmt}:{fuse}", fuse_norm=fuse)
+    plain = gpu_model(plane, m, f"fnp:{fmt}:{fuse}", fuse_norm=False)
+    # log4 / w4zp8: the norms inside the GEMVs; w8 gate|up (8.7 MB) keeps its norm kernel
+    per_layer = (1 if fmt == "w8" else 2) if fuse is True else 1
+    assert fused.kernel_launches_per_step() == plain.kernel_launches_per_step() - per_layer * m.cfg.layers
+    toks = [5, 700, 1999, 12]
+    outs = []
+    for dm in (fused, plain):
+        dm.reset()
+        logits = []
+        for tok in toks:
+            dm.set_token(tok)
+            dm.step(greedy=False)
+            dm.sync()
+            logits.append(dm.logits.clone())
+        dm.set_token(toks[-1])
+        for _ in range(3):
+            dm.step(greedy=True)
+        dm.sync()
+        outs.append((logits, dm.generated_tokens(), dm.residual.clone()))
+    for a, b in zip(outs[0][0], outs[1][0]):
+        assert torch.equal(a, b)
+    assert outs[0][1] == outs[1][1]
+    assert torch.equal(outs[0][2], outs[1][2])  # the residual stream ends in the same buffer
+    for dm in (fused, plain):
+        for L in dm.layers:
+            for w in (L.q, L.k, L.v, L.o, L.gate, L.up, L.down):
+                plane.evict(w.key)
+        plane.evict(dm.lm_head.key)
+
+
+@pytest.mark.parametrize("fmt,n_list,k", [("log4", [896, 128, 128], 896), ("w8", [896, 128, 128], 896),
+                                          ("log4", [4864, 4864], 896), ("w8", [4864, 4864], 896),
+                                          ("w4zp8", [3584], 3584)],
+                         ids=["log4_qkv_one_launch", "w8_qkv_one_launch", "log4_gate_up_one_launch",
+                              "w8_gate_up_two_kernels", "w4zp8_7b_two_kernels"])
+def test_gemv_rmsnorm_dev_equals_rmsnorm_then_gemv(plane, fmt, n_list, k):
+    """bramha_cuda_gemv_rmsnorm_dev == bramha_cuda_op_rmsnorm (residual add in
+    place) then bramha_cuda_gemv_multi_dev, bit for bit, with and without the
+    residual and with and without x_out; the 7B-sized case takes the path that
+    runs the RMSNorm kernel first."""
+    from bramha_b200 import lib
+    from bramha_b200._lib import check
+    from bramha_b200.plane import _stream
+    from tests._util import make_weight
+    dev = torch.device("cuda", 0)
+    ws = []
+    for i, n in enumerate(n_list):
+        _, q, s = make_weight(fmt, n, k, seed=100 + i)
+        ws.append(plane.register(f"rmsg:{fmt}:{i}:{n}:{k}", fmt, n, k, q, s))
+    r = rng(k)
+    x = torch.from_numpy(r.normal(0, 3, k).astype(np.float32)).to(dev)
+    delta = torch.from_numpy(r.normal(0, 1, k).astype(np.float32)).to(dev)
+    nw = torch.from_numpy(r.normal(1, 0.1, k).astype(np.float32)).to(dev)
+    for d in (delta, None):
+        for want_out in (True, False):
+            xr = x.clone()
+            h = torch.empty(k, device=dev)
+            check(lib().bramha_cuda_op_rmsnorm(plane.ctx, xr.data_ptr(), None if d is None else d.data_ptr(),
+                                               nw.data_ptr(), k, 1e-6, h.data_ptr(), _stream(None)))
+            y1 = [torch.empty(n, device=dev) for n in n_list]
+            plane.gemv_multi_dev(ws, h, y1)
+            y2 = [torch.full((n,), float("nan"), device=dev) for n in n_list]
+            xo = torch.full((k,), float("nan"), device=dev) if want_out else None
+            plane.gemv_rmsnorm_dev(ws, x, d, nw, 1e-6, xo, y2)
+            plane.stream_sync()
+            for a, b in zip(y1, y2):
+                assert torch.equal(a, b), (d is None, want_out)
+            if want_out:
+                assert torch.equal(xo, xr)
+    # the inputs are untouched; x_out may not alias them
+    from bramha_b200 import BramhaError
+    with pytest.raises(BramhaError):
+        plane.gemv_rmsnorm_dev(ws, x, delta, nw, 1e-6, x, [torch.empty(n, device=dev) for n in n_list])
+    for w in ws:
         plane.evict(w.key)
