@@ -755,9 +755,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<FMT>::kTh
 // x = hi + lo (hi = bf16(x), lo = bf16(x - hi)); hi fills columns [0, kp) and
 // lo columns [kp, 2 kp) of the copy, so one pass over 2 kp reproduces x to ~2^-16.
 // With ROWS (f32 only), lo goes to row M + r of a [2M][kp] copy instead.
-// One block of kPrepThreads per token row (a few rows of long K would leave a
-// warp-per-row kernel latency-bound); the row sum is reduced in a fixed order.
+// One block per token row, of prep_threads(M, K) threads: 1024 when a few long
+// rows would leave the GPU idle (a batched GEMV), about 8 columns per thread when
+// hundreds of rows fill it (a 2048 x 896 prefill lost ~5 us to 1024-thread
+// blocks).  The row sum is reduced in a fixed order for a given block size, so
+// results are reproducible for a given (M, K).
 constexpr int kPrepThreads = 1024;
+inline unsigned prep_threads(int64_t M, int64_t K) {
+    if (M < 256) return kPrepThreads;
+    const int64_t t = ((K + 7) / 8 + 31) / 32 * 32;
+    return (unsigned)(t < 32 ? 32 : t > kPrepThreads ? kPrepThreads : t);
+}
 template <bool FROM_F32, bool ROWS = false>
 __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const void* __restrict__ x, int64_t ldx, int M, int K,
                                                             int64_t kp, __nv_bfloat16* __restrict__ xc,
@@ -768,7 +776,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const void* __restri
     const int64_t lo_off = ROWS ? (int64_t)M * kp : kp;
     float sh = 0.f, sl = 0.f;
 #pragma unroll 4
-    for (int k = threadIdx.x; k < (int)kp; k += kPrepThreads) {
+    for (int k = threadIdx.x; k < (int)kp; k += blockDim.x) {
         float h = 0.f, l = 0.f;
         if (k < K) {
             if constexpr (FROM_F32) {
@@ -798,7 +806,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const void* __restri
     __syncthreads();
     if (threadIdx.x == 0 && rs) {
         float a = 0.f, b = 0.f;
-        for (int w = 0; w < kPrepThreads / 32; ++w) {
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
             a += part[w][0];
             b += part[w][1];
         }
@@ -1027,11 +1035,11 @@ cudaError_t launch_gemm_tcgen05_multi(int fmt, int n, const GemmOut* outs, int64
     if (need_copy || log4) {  // once for every weight that shares x
         const unsigned blocks = (unsigned)M;
         if (nsplit)
-            prep_kernel<true, true><<<blocks, kPrepThreads, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
+            prep_kernel<true, true><<<blocks, prep_threads(M, K), 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
         else if (x_is_f32)
-            prep_kernel<true><<<blocks, kPrepThreads, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
+            prep_kernel<true><<<blocks, prep_threads(M, K), 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
         else
-            prep_kernel<false><<<blocks, kPrepThreads, 0, st>>>(x, ldx, (int)M, (int)K, need_copy ? kp : K, xc, rs);
+            prep_kernel<false><<<blocks, prep_threads(M, K), 0, st>>>(x, ldx, (int)M, (int)K, need_copy ? kp : K, xc, rs);
         e = cudaGetLastError();
     }
     int dev = 0;
@@ -1102,7 +1110,7 @@ cudaError_t launch_gemm_tcgen05_grouped(int fmt, const uint8_t* q, const float* 
     if (e != cudaSuccess) return e;
     __nv_bfloat16* xc = reinterpret_cast<__nv_bfloat16*>(scratch);
     float* rs = log4 ? reinterpret_cast<float*>(scratch + copy_bytes) : nullptr;
-    prep_kernel<true, true><<<(unsigned)M, kPrepThreads, 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
+    prep_kernel<true, true><<<(unsigned)M, prep_threads(M, K), 0, st>>>(x, ldx, (int)M, (int)K, kp, xc, rs);
     e = cudaGetLastError();
     GemmArgs g;
     CUtensorMap tmX;
@@ -1135,7 +1143,7 @@ cudaError_t launch_gemm_tcgen05_bf16_noalloc(int fmt, const uint8_t* q, int64_t 
         if (!rowsum_scratch) return cudaErrorInvalidValue;
         rs = rowsum_scratch;
         // every one of the M sums is written here before the GEMM reads it
-        prep_kernel<false><<<(unsigned)M, kPrepThreads, 0, st>>>(x, ldx, (int)M, (int)K, K, nullptr, rs);
+        prep_kernel<false><<<(unsigned)M, prep_threads(M, K), 0, st>>>(x, ldx, (int)M, (int)K, K, nullptr, rs);
         e = cudaGetLastError();
     }
     int dev = 0;
