@@ -1936,7 +1936,8 @@ int bramha_cuda_op_attention(bramha_ctx* ctx, const float* q_dev, const float* k
     if (!q_dev || !k_cache_dev || !v_cache_dev || !pos_dev || !out_dev)
         return fail(BRAMHA_ERR_INVALID, "null device pointer");
     DeviceGuard g(ctx->device);
-    CK(launch_attention(q_dev, k_cache_dev, v_cache_dev, pos_dev, num_q_heads, num_kv_heads, head_dim, max_ctx, out_dev,
+    CK(launch_attention(q_dev, k_cache_dev, v_cache_dev, pos_dev, num_q_heads, num_kv_heads, head_dim, max_ctx,
+                        ctx->split_ws, kSplitWsFloats, ctx->split_tickets, kSplitTickets, out_dev,
                         op_stream(ctx, stream)),
        "attention launch");
     return BRAMHA_OK;
@@ -1955,7 +1956,8 @@ int bramha_cuda_op_rope_attention(bramha_ctx* ctx, const float* q_dev, const flo
         return fail(BRAMHA_ERR_INVALID, "null device pointer");
     DeviceGuard g(ctx->device);
     CK(launch_rope_attention(q_dev, k_dev, v_dev, bq_dev, bk_dev, bv_dev, rope_theta, pos_dev, max_ctx, k_cache_dev,
-                             v_cache_dev, num_q_heads, num_kv_heads, head_dim, out_dev, op_stream(ctx, stream)),
+                             v_cache_dev, num_q_heads, num_kv_heads, head_dim, ctx->split_ws, kSplitWsFloats,
+                             ctx->split_tickets, kSplitTickets, out_dev, op_stream(ctx, stream)),
        "rope_attention launch");
     return BRAMHA_OK;
 }

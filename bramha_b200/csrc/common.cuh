@@ -248,11 +248,15 @@ cudaError_t launch_rmsnorm(float* x, const float* delta, const float* w, int64_t
 cudaError_t launch_qkv_rope(float* q, const float* k, const float* v, const float* bq, const float* bk,
                             const float* bv, int nq, int nkv, int hd, float rope_theta, const int32_t* pos,
                             int64_t max_ctx, float* k_cache, float* v_cache, cudaStream_t stream);
+// (ws / tickets: the context's K-split workspace and tickets, for the per-head
+// combine of the attention's token splits; tickets are left at zero)
 cudaError_t launch_attention(const float* q, const float* k_cache, const float* v_cache, const int32_t* pos, int nq,
-                             int nkv, int hd, int64_t max_ctx, float* out, cudaStream_t stream);
+                             int nkv, int hd, int64_t max_ctx, float* ws, int64_t ws_floats, int* tickets,
+                             int64_t n_tickets, float* out, cudaStream_t stream);
 cudaError_t launch_rope_attention(const float* q, const float* k, const float* v, const float* bq, const float* bk,
                                   const float* bv, float rope_theta, const int32_t* pos, int64_t max_ctx,
-                                  float* k_cache, float* v_cache, int nq, int nkv, int hd, float* out,
+                                  float* k_cache, float* v_cache, int nq, int nkv, int hd, float* ws,
+                                  int64_t ws_floats, int* tickets, int64_t n_tickets, float* out,
                                   cudaStream_t stream);
 cudaError_t launch_silu_mul(const float* g, const float* u, int64_t n, float* out, cudaStream_t stream);
 cudaError_t launch_select(float* logits, int64_t vocab, int32_t* generated, int32_t* count, int64_t max_gen,

@@ -147,39 +147,46 @@ __global__ void qkv_rope_kernel(float* __restrict__ q, const float* __restrict__
     }
 }
 
-// Single-token attention, one CTA per query head: scores of the *pos + 1
-// cached tokens, softmax, weighted sum of the values (grouped-query: query
-// head h reads kv head h / (nq / nkv)).  Scores are kept in shared memory
-// (max_ctx floats; the token count is clamped to it).
+// Single-token attention (grouped-query: query head h reads kv head
+// h / (nq / nkv)), split over the cached tokens: a grid of nq x kAttnSplits CTAs,
+// CTA (h, s) takes the s-th contiguous range of the *pos + 1 tokens.  It computes
+// the scores of its range (a warp per token, lanes across the head dims: the key
+// rows are read whole), its own softmax statistics m_s = max score and
+// l_s = sum exp(score - m_s), and o_s = sum exp(score - m_s) v; the last CTA of a
+// head to finish (a ticket) combines the splits in split order:
+// out = sum_s o_s exp(m_s - M) / sum_s l_s exp(m_s - M), M = max_s m_s.  The same
+// softmax as the reference's single pass up to rounding, in a fixed order (bit-
+// reproducible); 14 heads became 112 CTAs on 148 SMs (one CTA per head read
+// 512 key rows with one thread per row before).
 constexpr int kAttnThreads = 128;
 constexpr int kAttnMaxHd = 128;
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __restrict__ q,
-                                                                 const float* __restrict__ k_cache,
-                                                                 const float* __restrict__ v_cache,
-                                                                 const int32_t* __restrict__ pos_ptr, int64_t max_ctx,
-                                                                 int nq, int nkv, int hd, float* __restrict__ out) {
-    extern __shared__ float sc[];  // [kv_len] scores, then probabilities
-    __shared__ float qs[kAttnMaxHd];
-    __shared__ float red[32];
-    __shared__ float part[kAttnThreads / 32][kAttnMaxHd];
-    pdl_entry();
-    const int head = blockIdx.x;
-    const int kvh = head / (nq / nkv);
-    const int kv_len = (int)min((int64_t)max(*pos_ptr + 1, 1), max_ctx);
-    const int ld = nkv * hd;
+constexpr int kAttnSplits = 8;
+constexpr int kAttnPart = 2 + kAttnMaxHd;  // workspace floats per (head, split): m, l, o[hd]
+
+// The attention core of one CTA (see above).  qs: the query head (shared
+// memory); kn / vn: the newest token's key / value row (shared memory) used for
+// token kv_len - 1 instead of the cache, or null; sc: shared scores of the
+// CTA's range.
+__device__ void attend_split(const float* qs, const float* kn, const float* vn, const float* __restrict__ k_cache,
+                             const float* __restrict__ v_cache, int kvh, int ld, int hd, int kv_len, int head,
+                             float* sc, float* red, float (*part)[kAttnMaxHd], float* __restrict__ ws,
+                             int* __restrict__ tickets, float* __restrict__ out) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int d = threadIdx.x; d < hd; d += kAttnThreads) qs[d] = q[head * hd + d];
-    __syncthreads();
+    const int S = gridDim.y, split = blockIdx.y;
+    const int per = (kv_len + S - 1) / S;
+    const int t0 = min(kv_len, split * per), n = min(kv_len, t0 + per) - t0;
     const float scale = 1.0f / sqrtf((float)hd);
-    // scores: thread per token, dot product in d order
+    // scores: warp w takes tokens t0 + w, t0 + w + 4, ...; lane sums dims lane, lane + 32, ...
     float mx = -INFINITY;
-    for (int t = threadIdx.x; t < kv_len; t += kAttnThreads) {
-        const float* kr = k_cache + (int64_t)t * ld + kvh * hd;
+    for (int i = warp; i < n; i += kAttnThreads / 32) {
+        const int t = t0 + i;
+        const float* kr = (kn && t == kv_len - 1) ? kn : k_cache + (int64_t)t * ld + kvh * hd;
         float dot = 0.f;
-        for (int d = 0; d < hd; ++d) dot = __fadd_rn(dot, __fmul_rn(qs[d], kr[d]));
-        const float s = __fmul_rn(dot, scale);
-        sc[t] = s;
-        mx = fmaxf(mx, s);
+        for (int d = lane; d < hd; d += 32) dot = __fadd_rn(dot, __fmul_rn(qs[d], kr[d]));
+        dot = warp_sum(dot);
+        const float sv = __fmul_rn(dot, scale);
+        if (lane == 0) sc[i] = sv;
+        mx = fmaxf(mx, sv);
     }
     mx = warp_max(mx);
     if (lane == 0) red[warp] = mx;
@@ -188,9 +195,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __
     mx = warp_max(mx);
     __syncthreads();
     float sum = 0.f;
-    for (int t = threadIdx.x; t < kv_len; t += kAttnThreads) {
-        const float p = expf(sc[t] - mx);
-        sc[t] = p;
+    for (int i = threadIdx.x; i < n; i += kAttnThreads) {
+        const float p = expf(sc[i] - mx);
+        sc[i] = p;
         sum = __fadd_rn(sum, p);
     }
     sum = block_sum<kAttnThreads>(sum, red);
@@ -198,9 +205,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __
     float acc[kAttnMaxHd / 32];
 #pragma unroll
     for (int j = 0; j < kAttnMaxHd / 32; ++j) acc[j] = 0.f;
-    for (int t = warp; t < kv_len; t += kAttnThreads / 32) {
-        const float p = sc[t];
-        const float* vr = v_cache + (int64_t)t * ld + kvh * hd;
+    for (int i = warp; i < n; i += kAttnThreads / 32) {
+        const int t = t0 + i;
+        const float p = sc[i];
+        const float* vr = (vn && t == kv_len - 1) ? vn : v_cache + (int64_t)t * ld + kvh * hd;
 #pragma unroll
         for (int j = 0; j < kAttnMaxHd / 32; ++j) {
             const int d = lane + 32 * j;
@@ -213,27 +221,80 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __
         if (d < hd) part[warp][d] = acc[j];
     }
     __syncthreads();
-    const float inv = 1.0f / sum;
+    // this split's statistics and weighted sum -> workspace, then the head's ticket
+    float* wp = ws + ((int64_t)head * S + split) * kAttnPart;
     for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
         float o = 0.f;
 #pragma unroll
         for (int w = 0; w < kAttnThreads / 32; ++w) o = __fadd_rn(o, part[w][d]);
+        wp[2 + d] = o;
+    }
+    if (threadIdx.x == 0) {
+        wp[0] = mx;   // -inf for an empty range
+        wp[1] = sum;  // 0 for an empty range
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int last;
+    if (threadIdx.x == 0) last = atomicAdd(&tickets[head], 1) == S - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // the head's last CTA: combine the splits in split order
+    const float* hp = ws + (int64_t)head * S * kAttnPart;
+    float M = -INFINITY;
+    for (int q = 0; q < S; ++q)
+        if (__ldcg(hp + q * kAttnPart + 1) > 0.f) M = fmaxf(M, __ldcg(hp + q * kAttnPart));
+    float L = 0.f;
+    for (int q = 0; q < S; ++q) {
+        const float l = __ldcg(hp + q * kAttnPart + 1);
+        if (l > 0.f) L = __fadd_rn(L, __fmul_rn(l, expf(__ldcg(hp + q * kAttnPart) - M)));
+    }
+    const float inv = 1.0f / L;
+    for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
+        float o = 0.f;
+        for (int q = 0; q < S; ++q) {
+            const float l = __ldcg(hp + q * kAttnPart + 1);
+            if (l > 0.f) o = __fadd_rn(o, __fmul_rn(__ldcg(hp + q * kAttnPart + 2 + d), expf(__ldcg(hp + q * kAttnPart) - M)));
+        }
         out[head * hd + d] = __fmul_rn(o, inv);
     }
+    if (threadIdx.x == 0) tickets[head] = 0;  // ready for the next launch
 }
 
-// Fused form of qkv_rope_kernel + attention_kernel, one CTA per query head:
-// the CTA adds the biases and rotates its query head and the current token's
-// key (of its kv head) itself, attends over cache rows 0 .. pos-1 plus that
-// new row (held in shared memory), and the first query head of each kv group
-// appends the new key / value row to the caches (rows the other CTAs of the
-// group do not read).  Same arithmetic as the two kernels.
+// Attention over the caches (the new row already appended by qkv_rope_kernel).
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __restrict__ q,
+                                                                 const float* __restrict__ k_cache,
+                                                                 const float* __restrict__ v_cache,
+                                                                 const int32_t* __restrict__ pos_ptr, int64_t max_ctx,
+                                                                 int nq, int nkv, int hd, float* __restrict__ ws,
+                                                                 int* __restrict__ tickets, float* __restrict__ out) {
+    extern __shared__ float sc[];  // the CTA's scores, then probabilities
+    __shared__ float qs[kAttnMaxHd];
+    __shared__ float red[32];
+    __shared__ float part[kAttnThreads / 32][kAttnMaxHd];
+    pdl_entry();
+    const int head = blockIdx.x;
+    const int kvh = head / (nq / nkv);
+    const int kv_len = (int)min((int64_t)max(*pos_ptr + 1, 1), max_ctx);
+    for (int d = threadIdx.x; d < hd; d += kAttnThreads) qs[d] = q[head * hd + d];
+    __syncthreads();
+    attend_split(qs, nullptr, nullptr, k_cache, v_cache, kvh, nkv * hd, hd, kv_len, head, sc, red, part, ws, tickets,
+                 out);
+}
+
+// Fused form of qkv_rope_kernel + attention_kernel: every CTA of a query head
+// adds the biases and rotates its query head and the current token's key (of
+// its kv head) itself and attends over its range of cache rows 0 .. pos-1 plus
+// that new row (held in shared memory); split 0 of the first query head of each
+// kv group appends the new key / value row to the caches (a row no CTA reads
+// from the cache in this launch).  Same arithmetic as the two kernels.
 __global__ void __launch_bounds__(kAttnThreads) rope_attention_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
     const float* __restrict__ bq, const float* __restrict__ bk, const float* __restrict__ bv, float rope_theta,
     const int32_t* __restrict__ pos_ptr, int64_t max_ctx, float* __restrict__ k_cache, float* __restrict__ v_cache,
-    int nq, int nkv, int hd, float* __restrict__ out) {
-    extern __shared__ float sc[];  // [kv_len] scores, then probabilities
+    int nq, int nkv, int hd, float* __restrict__ ws, int* __restrict__ tickets, float* __restrict__ out) {
+    extern __shared__ float sc[];  // the CTA's scores, then probabilities
     __shared__ float qs[kAttnMaxHd], kn[kAttnMaxHd], vn[kAttnMaxHd];
     __shared__ float red[32];
     __shared__ float part[kAttnThreads / 32][kAttnMaxHd];
@@ -245,7 +306,6 @@ __global__ void __launch_bounds__(kAttnThreads) rope_attention_kernel(
     const int kv_len = (int)min((int64_t)max(pos + 1, 1), max_ctx);  // rows 0 .. kv_len-2 cached, kv_len-1 new
     const int ld = nkv * hd;
     const int half = hd / 2;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < half; i += kAttnThreads) {
         const float theta = 1.0f / powf(rope_theta, (float)(2 * i) / (float)hd);
         const float freq = __fmul_rn((float)pos, theta);
@@ -264,59 +324,12 @@ __global__ void __launch_bounds__(kAttnThreads) rope_attention_kernel(
         vn[i + half] = bv ? __fadd_rn(v[kb], bv[kb]) : v[kb];
     }
     __syncthreads();
-    if (head % group == 0 && pos >= 0 && pos < max_ctx)
+    if (head % group == 0 && blockIdx.y == 0 && pos >= 0 && pos < max_ctx)
         for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
             k_cache[(int64_t)pos * ld + kvh * hd + d] = kn[d];
             v_cache[(int64_t)pos * ld + kvh * hd + d] = vn[d];
         }
-    const float scale = 1.0f / sqrtf((float)hd);
-    float mx = -INFINITY;
-    for (int t = threadIdx.x; t < kv_len; t += kAttnThreads) {
-        const float* kr = t == kv_len - 1 ? kn : k_cache + (int64_t)t * ld + kvh * hd;
-        float dot = 0.f;
-        for (int d = 0; d < hd; ++d) dot = __fadd_rn(dot, __fmul_rn(qs[d], kr[d]));
-        const float sv = __fmul_rn(dot, scale);
-        sc[t] = sv;
-        mx = fmaxf(mx, sv);
-    }
-    mx = warp_max(mx);
-    if (lane == 0) red[warp] = mx;
-    __syncthreads();
-    mx = lane < kAttnThreads / 32 ? red[lane] : -INFINITY;
-    mx = warp_max(mx);
-    __syncthreads();
-    float sum = 0.f;
-    for (int t = threadIdx.x; t < kv_len; t += kAttnThreads) {
-        const float p = expf(sc[t] - mx);
-        sc[t] = p;
-        sum = __fadd_rn(sum, p);
-    }
-    sum = block_sum<kAttnThreads>(sum, red);
-    float acc[kAttnMaxHd / 32];
-#pragma unroll
-    for (int j = 0; j < kAttnMaxHd / 32; ++j) acc[j] = 0.f;
-    for (int t = warp; t < kv_len; t += kAttnThreads / 32) {
-        const float p = sc[t];
-        const float* vr = t == kv_len - 1 ? vn : v_cache + (int64_t)t * ld + kvh * hd;
-#pragma unroll
-        for (int j = 0; j < kAttnMaxHd / 32; ++j) {
-            const int d = lane + 32 * j;
-            if (d < hd) acc[j] = __fadd_rn(acc[j], __fmul_rn(p, vr[d]));
-        }
-    }
-#pragma unroll
-    for (int j = 0; j < kAttnMaxHd / 32; ++j) {
-        const int d = lane + 32 * j;
-        if (d < hd) part[warp][d] = acc[j];
-    }
-    __syncthreads();
-    const float inv = 1.0f / sum;
-    for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
-        float o = 0.f;
-#pragma unroll
-        for (int w = 0; w < kAttnThreads / 32; ++w) o = __fadd_rn(o, part[w][d]);
-        out[head * hd + d] = __fmul_rn(o, inv);
-    }
+    attend_split(qs, kn, vn, k_cache, v_cache, kvh, ld, hd, kv_len, head, sc, red, part, ws, tickets, out);
 }
 
 // out = silu(g) * u, silu(g) = g * (1 / (1 + exp(-g)))
@@ -426,33 +439,38 @@ cudaError_t launch_qkv_rope(float* q, const float* k, const float* v, const floa
 }
 
 cudaError_t launch_attention(const float* q, const float* k_cache, const float* v_cache, const int32_t* pos, int nq,
-                             int nkv, int hd, int64_t max_ctx, float* out, cudaStream_t st) {
+                             int nkv, int hd, int64_t max_ctx, float* ws, int64_t ws_floats, int* tickets,
+                             int64_t n_tickets, float* out, cudaStream_t st) {
     if (nq <= 0 || nkv <= 0 || nq % nkv || hd <= 0 || hd > kAttnMaxHd || max_ctx <= 0) return cudaErrorInvalidValue;
-    const size_t smem = (size_t)max_ctx * sizeof(float);
+    if (!ws || !tickets || (int64_t)nq * kAttnSplits * kAttnPart > ws_floats || nq > n_tickets)
+        return cudaErrorInvalidValue;
+    const size_t smem = (size_t)((max_ctx + kAttnSplits - 1) / kAttnSplits) * sizeof(float);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    return launch_pdl(attention_kernel, dim3(nq), dim3(kAttnThreads), smem, st, q, k_cache, v_cache, pos, max_ctx, nq,
-                      nkv, hd, out);
+    return launch_pdl(attention_kernel, dim3(nq, kAttnSplits), dim3(kAttnThreads), smem, st, q, k_cache, v_cache, pos,
+                      max_ctx, nq, nkv, hd, ws, tickets, out);
 }
 
 cudaError_t launch_rope_attention(const float* q, const float* k, const float* v, const float* bq, const float* bk,
                                   const float* bv, float rope_theta, const int32_t* pos, int64_t max_ctx,
-                                  float* k_cache, float* v_cache, int nq, int nkv, int hd, float* out,
-                                  cudaStream_t st) {
+                                  float* k_cache, float* v_cache, int nq, int nkv, int hd, float* ws, int64_t ws_floats,
+                                  int* tickets, int64_t n_tickets, float* out, cudaStream_t st) {
     if (nq <= 0 || nkv <= 0 || nq % nkv || hd <= 0 || (hd & 1) || hd > kAttnMaxHd || max_ctx <= 0)
         return cudaErrorInvalidValue;
-    const size_t smem = (size_t)max_ctx * sizeof(float);
+    if (!ws || !tickets || (int64_t)nq * kAttnSplits * kAttnPart > ws_floats || nq > n_tickets)
+        return cudaErrorInvalidValue;
+    const size_t smem = (size_t)((max_ctx + kAttnSplits - 1) / kAttnSplits) * sizeof(float);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     if (smem > 48 * 1024) {
         cudaError_t e =
             cudaFuncSetAttribute(rope_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    return launch_pdl(rope_attention_kernel, dim3(nq), dim3(kAttnThreads), smem, st, q, k, v, bq, bk, bv, rope_theta,
-                      pos, max_ctx, k_cache, v_cache, nq, nkv, hd, out);
+    return launch_pdl(rope_attention_kernel, dim3(nq, kAttnSplits), dim3(kAttnThreads), smem, st, q, k, v, bq, bk, bv,
+                      rope_theta, pos, max_ctx, k_cache, v_cache, nq, nkv, hd, ws, tickets, out);
 }
 
 cudaError_t launch_silu_mul(const float* g, const float* u, int64_t n, float* out, cudaStream_t st) {
