@@ -148,20 +148,28 @@ __global__ void qkv_rope_kernel(float* __restrict__ q, const float* __restrict__
 }
 
 // Single-token attention (grouped-query: query head h reads kv head
-// h / (nq / nkv)), split over the cached tokens: a grid of nq x kAttnSplits CTAs,
-// CTA (h, s) takes the s-th contiguous range of the *pos + 1 tokens.  It computes
+// h / (nq / nkv)), split over the cached tokens: a grid of nq x S CTAs, S =
+// attn_splits(max_ctx), CTA (h, s) takes the s-th contiguous range of the
+// *pos + 1 tokens.  It computes
 // the scores of its range (a warp per token, lanes across the head dims: the key
 // rows are read whole), its own softmax statistics m_s = max score and
 // l_s = sum exp(score - m_s), and o_s = sum exp(score - m_s) v; the last CTA of a
 // head to finish (a ticket) combines the splits in split order:
 // out = sum_s o_s exp(m_s - M) / sum_s l_s exp(m_s - M), M = max_s m_s.  The same
 // softmax as the reference's single pass up to rounding, in a fixed order (bit-
-// reproducible); 14 heads became 112 CTAs on 148 SMs (one CTA per head read
-// 512 key rows with one thread per row before).
+// reproducible).  Measured on the Qwen2-0.5B step (14 heads, 512-640 tokens):
+// one CTA per head 2.23 ms/token, 8 splits 1.67, 16 splits 1.38, 32 splits 1.33,
+// 64 splits 1.49 (the combine and ~10-token ranges start to cost): a split takes
+// about kAttnSplitTokens of the cache's capacity, at most kAttnMaxSplits splits.
 constexpr int kAttnThreads = 128;
 constexpr int kAttnMaxHd = 128;
-constexpr int kAttnSplits = 8;
+constexpr int kAttnSplitTokens = 20;
+constexpr int kAttnMaxSplits = 64;
 constexpr int kAttnPart = 2 + kAttnMaxHd;  // workspace floats per (head, split): m, l, o[hd]
+inline int attn_splits(int64_t max_ctx) {
+    const int64_t s = (max_ctx + kAttnSplitTokens - 1) / kAttnSplitTokens;
+    return (int)(s < 1 ? 1 : s > kAttnMaxSplits ? kAttnMaxSplits : s);
+}
 
 // The attention core of one CTA (see above).  qs: the query head (shared
 // memory); kn / vn: the newest token's key / value row (shared memory) used for
@@ -442,15 +450,15 @@ cudaError_t launch_attention(const float* q, const float* k_cache, const float* 
                              int nkv, int hd, int64_t max_ctx, float* ws, int64_t ws_floats, int* tickets,
                              int64_t n_tickets, float* out, cudaStream_t st) {
     if (nq <= 0 || nkv <= 0 || nq % nkv || hd <= 0 || hd > kAttnMaxHd || max_ctx <= 0) return cudaErrorInvalidValue;
-    if (!ws || !tickets || (int64_t)nq * kAttnSplits * kAttnPart > ws_floats || nq > n_tickets)
-        return cudaErrorInvalidValue;
-    const size_t smem = (size_t)((max_ctx + kAttnSplits - 1) / kAttnSplits) * sizeof(float);
+    const int S = attn_splits(max_ctx);
+    if (!ws || !tickets || (int64_t)nq * S * kAttnPart > ws_floats || nq > n_tickets) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)((max_ctx + S - 1) / S) * sizeof(float);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    return launch_pdl(attention_kernel, dim3(nq, kAttnSplits), dim3(kAttnThreads), smem, st, q, k_cache, v_cache, pos,
+    return launch_pdl(attention_kernel, dim3(nq, S), dim3(kAttnThreads), smem, st, q, k_cache, v_cache, pos,
                       max_ctx, nq, nkv, hd, ws, tickets, out);
 }
 
@@ -460,16 +468,16 @@ cudaError_t launch_rope_attention(const float* q, const float* k, const float* v
                                   int* tickets, int64_t n_tickets, float* out, cudaStream_t st) {
     if (nq <= 0 || nkv <= 0 || nq % nkv || hd <= 0 || (hd & 1) || hd > kAttnMaxHd || max_ctx <= 0)
         return cudaErrorInvalidValue;
-    if (!ws || !tickets || (int64_t)nq * kAttnSplits * kAttnPart > ws_floats || nq > n_tickets)
-        return cudaErrorInvalidValue;
-    const size_t smem = (size_t)((max_ctx + kAttnSplits - 1) / kAttnSplits) * sizeof(float);
+    const int S = attn_splits(max_ctx);
+    if (!ws || !tickets || (int64_t)nq * S * kAttnPart > ws_floats || nq > n_tickets) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)((max_ctx + S - 1) / S) * sizeof(float);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     if (smem > 48 * 1024) {
         cudaError_t e =
             cudaFuncSetAttribute(rope_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    return launch_pdl(rope_attention_kernel, dim3(nq, kAttnSplits), dim3(kAttnThreads), smem, st, q, k, v, bq, bk, bv,
+    return launch_pdl(rope_attention_kernel, dim3(nq, S), dim3(kAttnThreads), smem, st, q, k, v, bq, bk, bv,
                       rope_theta, pos, max_ctx, k_cache, v_cache, nq, nkv, hd, ws, tickets, out);
 }
 

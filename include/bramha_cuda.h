@@ -543,7 +543,8 @@ BRAMHA_API int bramha_cuda_op_qkv_rope(bramha_ctx* ctx, float* q_dev, const floa
 /* Single-token grouped-query attention over cache rows 0 .. *pos_dev
  * (flash_attention_single_into, cpu_engine.rs:1450-1509); head_dim <= 128,
  * max_ctx <= 51200; out [num_q_heads * head_dim].  The tokens are split over
- * 8 CTAs per head whose softmax statistics are combined in a fixed order; the
+ * up to 64 CTAs per head (about 20 tokens of max_ctx each) whose softmax
+ * statistics are combined in a fixed order; the
  * combine uses the context's GEMV workspace, so like a GEMV it runs one at a
  * time per context (stream-ordered). */
 BRAMHA_API int bramha_cuda_op_attention(bramha_ctx* ctx, const float* q_dev, const float* k_cache_dev,
