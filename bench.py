@@ -992,7 +992,17 @@ def main():
     ap.add_argument("--no-moe", action="store_true", help="skip the config-5 MoE measurement")
     ap.add_argument("--moe-only", action="store_true", help="run only the config-5 MoE measurement and print its JSON")
     ap.add_argument("--moe-tokens", type=int, default=256, help="tokens of the MoE measurement")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="run only the config-2 decode-step measurement (profiling case) and print its JSON")
     args = ap.parse_args()
+    if args.decode_only:
+        import torch
+        from bramha_b200 import CudaComputePlane
+        torch.cuda.set_device(0)
+        plane = CudaComputePlane(0)
+        print(json.dumps({"decode_step": decode_step_bench(plane, torch.device("cuda", 0))}))
+        plane.close()
+        return
     if args.moe_only:
         import torch
         from bramha_b200 import CudaComputePlane
