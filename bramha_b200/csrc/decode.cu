@@ -150,51 +150,144 @@ __global__ void qkv_rope_kernel(float* __restrict__ q, const float* __restrict__
 // Single-token attention (grouped-query: query head h reads kv head
 // h / (nq / nkv)), split over the cached tokens: a grid of nq x S CTAs, S =
 // attn_splits(max_ctx), CTA (h, s) takes the s-th contiguous range of the
-// *pos + 1 tokens.  It computes
-// the scores of its range (a warp per token, lanes across the head dims: the key
-// rows are read whole), its own softmax statistics m_s = max score and
+// *pos + 1 tokens.  It computes the scores of its range (a warp per token,
+// lanes across the head dims), its own softmax statistics m_s = max score and
 // l_s = sum exp(score - m_s), and o_s = sum exp(score - m_s) v; the last CTA of a
 // head to finish (a ticket) combines the splits in split order:
 // out = sum_s o_s exp(m_s - M) / sum_s l_s exp(m_s - M), M = max_s m_s.  The same
 // softmax as the reference's single pass up to rounding, in a fixed order (bit-
-// reproducible).  Measured on the Qwen2-0.5B step (14 heads, 512-640 tokens):
-// one CTA per head 2.23 ms/token, 8 splits 1.67, 16 splits 1.38, 32 splits 1.33,
-// 64 splits 1.49 (the combine and ~10-token ranges start to cost): a split takes
-// about kAttnSplitTokens of the cache's capacity, at most kAttnMaxSplits splits.
+// reproducible).
+// A launch is a short chain of dependent memory round trips, so every step
+// issues all its loads before it uses any: before the programmatic-launch wait
+// the CTA prefetches its range's key and value rows into L2 (rows written by
+// earlier steps; a prefetch does not change what a later load returns), the
+// range is copied into shared memory kAttnChunk rows at a time with all loads of
+// a chunk in flight, and the combining CTA copies the head's S partial results
+// into shared memory in one pass.  The arithmetic and its order are those of a
+// plain row-by-row loop (warp w takes rows w, w + 4, ... of the range).
+// Split count measured on the Qwen2-0.5B step (14 heads, 512-640 tokens, loads
+// not yet staged): one CTA per head 2.23 ms/token, 8 splits 1.67, 16 splits
+// 1.38, 32 splits 1.33, 64 splits 1.49: a split takes about kAttnSplitTokens of
+// the cache's capacity, at most kAttnMaxSplits splits.
 constexpr int kAttnThreads = 128;
 constexpr int kAttnMaxHd = 128;
 constexpr int kAttnSplitTokens = 20;
 constexpr int kAttnMaxSplits = 64;
-constexpr int kAttnPart = 2 + kAttnMaxHd;  // workspace floats per (head, split): m, l, o[hd]
+constexpr int kAttnChunk = 32;  // cache rows staged in shared memory at a time
+// workspace floats per (head, split): m, l, two unused, o[hd] (16-byte aligned rows)
+constexpr int kAttnPart = 4 + kAttnMaxHd;
+// shared staging: a chunk of key and value rows, or the S partial results of a head
+constexpr int kAttnStage = 2 * kAttnChunk * kAttnMaxHd > kAttnMaxSplits * kAttnPart ? 2 * kAttnChunk * kAttnMaxHd
+                                                                                       : kAttnMaxSplits * kAttnPart;
+static_assert(kAttnChunk % (kAttnThreads / 32) == 0, "a row keeps its warp from chunk to chunk");
 inline int attn_splits(int64_t max_ctx) {
     const int64_t s = (max_ctx + kAttnSplitTokens - 1) / kAttnSplitTokens;
     return (int)(s < 1 ? 1 : s > kAttnMaxSplits ? kAttnMaxSplits : s);
 }
 
+// Rows [t0, t0 + n) of the kv_len cached tokens belong to split `split` of S.
+__device__ __forceinline__ void attn_range(int kv_len, int S, int split, int& t0, int& n) {
+    const int per = (kv_len + S - 1) / S;
+    t0 = min(kv_len, split * per);
+    n = min(kv_len, t0 + per) - t0;
+}
+
+// L2 prefetch of this CTA's key and value rows, for a position read before the
+// programmatic-launch wait: a hint only (any value read gives rows inside the
+// caches' max_ctx rows).
+__device__ __forceinline__ void attn_prefetch(const int32_t* pos_ptr, int64_t max_ctx, const float* k_cache,
+                                              const float* v_cache, int kvh, int ld, int hd) {
+    const int kv_len = (int)min((int64_t)max(__ldcg(pos_ptr) + 1, 1), max_ctx);
+    int t0, n;
+    attn_range(kv_len, gridDim.y, blockIdx.y, t0, n);
+    const int lines = (hd + 31) / 32;  // 128-byte lines of a row
+    const int per_cache = n * lines;
+    for (int e = threadIdx.x; e < 2 * per_cache; e += kAttnThreads) {
+        const int which = e >= per_cache, rem = which ? e - per_cache : e;
+        const int r = rem / lines, b = rem - r * lines;
+        const float* p = (which ? v_cache : k_cache) + (int64_t)(t0 + r) * ld + kvh * hd + b * 32;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+    }
+}
+
+// Copies rows [c0, c0 + nc) of kv head kvh from cache a into as (row stride hd
+// floats), and from cache b into bs when bs is not null; row `newrow` comes from
+// an / bn instead when they are given.  vec4 (hd % 4 == 0, 16-byte aligned
+// caches and rows): float4 loads, every load of the chunk in flight before the
+// first store.
+__device__ __forceinline__ void attn_stage(const float* __restrict__ a, const float* an, float* as,
+                                           const float* __restrict__ b, const float* bn, float* bs, int newrow,
+                                           int kvh, int ld, int hd, int c0, int nc, bool vec4) {
+    if (vec4) {
+        constexpr int kPer = kAttnChunk * kAttnMaxHd / 4 / kAttnThreads;
+        const int hd4 = hd >> 2, tot = nc * hd4;
+        float4 ra[kPer], rb[kPer];
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int e = threadIdx.x + j * kAttnThreads;
+            if (e < tot) {
+                const int r = e / hd4, c = e - r * hd4, t = c0 + r;
+                const bool fresh = an && t == newrow;
+                const int64_t off = (int64_t)t * ld + kvh * hd;
+                ra[j] = reinterpret_cast<const float4*>(fresh ? an : a + off)[c];
+                if (bs) rb[j] = reinterpret_cast<const float4*>(fresh ? bn : b + off)[c];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int e = threadIdx.x + j * kAttnThreads;
+            if (e < tot) {
+                reinterpret_cast<float4*>(as)[e] = ra[j];
+                if (bs) reinterpret_cast<float4*>(bs)[e] = rb[j];
+            }
+        }
+    } else {
+        for (int e = threadIdx.x; e < nc * hd; e += kAttnThreads) {
+            const int r = e / hd, d = e - r * hd, t = c0 + r;
+            const bool fresh = an && t == newrow;
+            const int64_t off = (int64_t)t * ld + kvh * hd + d;
+            as[e] = fresh ? an[d] : a[off];
+            if (bs) bs[e] = fresh ? bn[d] : b[off];
+        }
+    }
+}
+
 // The attention core of one CTA (see above).  qs: the query head (shared
-// memory); kn / vn: the newest token's key / value row (shared memory) used for
-// token kv_len - 1 instead of the cache, or null; sc: shared scores of the
-// CTA's range.
+// memory); kn / vn: the newest token's key / value row (shared memory, 16-byte
+// aligned) used for token kv_len - 1 instead of the cache, or null; sc: shared
+// scores of the CTA's range; stage: kAttnStage floats of 16-byte aligned shared
+// memory.
 __device__ void attend_split(const float* qs, const float* kn, const float* vn, const float* __restrict__ k_cache,
                              const float* __restrict__ v_cache, int kvh, int ld, int hd, int kv_len, int head,
-                             float* sc, float* red, float (*part)[kAttnMaxHd], float* __restrict__ ws,
+                             float* sc, float* red, float (*part)[kAttnMaxHd], float* stage, float* __restrict__ ws,
                              int* __restrict__ tickets, float* __restrict__ out) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = gridDim.y, split = blockIdx.y;
-    const int per = (kv_len + S - 1) / S;
-    const int t0 = min(kv_len, split * per), n = min(kv_len, t0 + per) - t0;
+    int t0, n;
+    attn_range(kv_len, S, split, t0, n);
     const float scale = 1.0f / sqrtf((float)hd);
-    // scores: warp w takes tokens t0 + w, t0 + w + 4, ...; lane sums dims lane, lane + 32, ...
+    const bool vec4 =
+        (hd & 3) == 0 && ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) == 0;
+    float* ks = stage;
+    float* vs = stage + kAttnChunk * kAttnMaxHd;
+    const bool one_chunk = n <= kAttnChunk;  // the value rows are staged with the key rows
+    const int newrow = kv_len - 1;
+    // scores: warp w takes rows w, w + 4, ...; lane sums dims lane, lane + 32, ...
     float mx = -INFINITY;
-    for (int i = warp; i < n; i += kAttnThreads / 32) {
-        const int t = t0 + i;
-        const float* kr = (kn && t == kv_len - 1) ? kn : k_cache + (int64_t)t * ld + kvh * hd;
-        float dot = 0.f;
-        for (int d = lane; d < hd; d += 32) dot = __fadd_rn(dot, __fmul_rn(qs[d], kr[d]));
-        dot = warp_sum(dot);
-        const float sv = __fmul_rn(dot, scale);
-        if (lane == 0) sc[i] = sv;
-        mx = fmaxf(mx, sv);
+    for (int c0 = 0; c0 < n; c0 += kAttnChunk) {
+        const int nc = min(kAttnChunk, n - c0);
+        attn_stage(k_cache, kn, ks, v_cache, vn, one_chunk ? vs : nullptr, newrow, kvh, ld, hd, t0 + c0, nc, vec4);
+        __syncthreads();
+        for (int i = warp; i < nc; i += kAttnThreads / 32) {
+            const float* kr = ks + i * hd;
+            float dot = 0.f;
+            for (int d = lane; d < hd; d += 32) dot = __fadd_rn(dot, __fmul_rn(qs[d], kr[d]));
+            dot = warp_sum(dot);
+            const float sv = __fmul_rn(dot, scale);
+            if (lane == 0) sc[c0 + i] = sv;
+            mx = fmaxf(mx, sv);
+        }
+        __syncthreads();
     }
     mx = warp_max(mx);
     if (lane == 0) red[warp] = mx;
@@ -209,19 +302,26 @@ __device__ void attend_split(const float* qs, const float* kn, const float* vn, 
         sum = __fadd_rn(sum, p);
     }
     sum = block_sum<kAttnThreads>(sum, red);
-    // weighted values: warp w takes tokens w, w + 4, ...; lanes split the head dims
+    // weighted values: warp w takes rows w, w + 4, ...; lanes split the head dims
     float acc[kAttnMaxHd / 32];
 #pragma unroll
     for (int j = 0; j < kAttnMaxHd / 32; ++j) acc[j] = 0.f;
-    for (int i = warp; i < n; i += kAttnThreads / 32) {
-        const int t = t0 + i;
-        const float p = sc[i];
-        const float* vr = (vn && t == kv_len - 1) ? vn : v_cache + (int64_t)t * ld + kvh * hd;
-#pragma unroll
-        for (int j = 0; j < kAttnMaxHd / 32; ++j) {
-            const int d = lane + 32 * j;
-            if (d < hd) acc[j] = __fadd_rn(acc[j], __fmul_rn(p, vr[d]));
+    for (int c0 = 0; c0 < n; c0 += kAttnChunk) {
+        const int nc = min(kAttnChunk, n - c0);
+        if (!one_chunk) {
+            attn_stage(v_cache, vn, vs, nullptr, nullptr, nullptr, newrow, kvh, ld, hd, t0 + c0, nc, vec4);
+            __syncthreads();
         }
+        for (int i = warp; i < nc; i += kAttnThreads / 32) {
+            const float p = sc[c0 + i];
+            const float* vr = vs + i * hd;
+#pragma unroll
+            for (int j = 0; j < kAttnMaxHd / 32; ++j) {
+                const int d = lane + 32 * j;
+                if (d < hd) acc[j] = __fadd_rn(acc[j], __fmul_rn(p, vr[d]));
+            }
+        }
+        if (!one_chunk) __syncthreads();
     }
 #pragma unroll
     for (int j = 0; j < kAttnMaxHd / 32; ++j) {
@@ -235,7 +335,7 @@ __device__ void attend_split(const float* qs, const float* kn, const float* vn, 
         float o = 0.f;
 #pragma unroll
         for (int w = 0; w < kAttnThreads / 32; ++w) o = __fadd_rn(o, part[w][d]);
-        wp[2 + d] = o;
+        wp[4 + d] = o;
     }
     if (threadIdx.x == 0) {
         wp[0] = mx;   // -inf for an empty range
@@ -248,23 +348,50 @@ __device__ void attend_split(const float* qs, const float* kn, const float* vn, 
     __syncthreads();
     if (!last) return;
     __threadfence();
-    // the head's last CTA: combine the splits in split order
-    const float* hp = ws + (int64_t)head * S * kAttnPart;
-    float M = -INFINITY;
-    for (int q = 0; q < S; ++q)
-        if (__ldcg(hp + q * kAttnPart + 1) > 0.f) M = fmaxf(M, __ldcg(hp + q * kAttnPart));
+    // the head's last CTA: its S partial results -> shared memory (all loads in
+    // flight), then combined in split order
+    const int pw = (4 + hd + 3) / 4;  // float4 of a partial result
+    const int P = 4 * pw;
+    const float4* hp = reinterpret_cast<const float4*>(ws + (int64_t)head * S * kAttnPart);
+    float4* st4 = reinterpret_cast<float4*>(stage);
+    const int tot = S * pw;
+    constexpr int kBatch = 8;
+    for (int base = 0; base < tot; base += kBatch * kAttnThreads) {
+        float4 r[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const int e = base + threadIdx.x + j * kAttnThreads;
+            if (e < tot) {
+                const int q = e / pw;
+                r[j] = __ldcg(hp + q * (kAttnPart / 4) + (e - q * pw));
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const int e = base + threadIdx.x + j * kAttnThreads;
+            if (e < tot) st4[e] = r[j];
+        }
+    }
+    __shared__ float wq[kAttnMaxSplits];  // exp(m_s - M) of each split with l_s > 0
+    __syncthreads();
+    if (warp == 0) {
+        float M = -INFINITY;
+        for (int q = lane; q < S; q += 32)
+            if (stage[q * P + 1] > 0.f) M = fmaxf(M, stage[q * P]);
+        M = warp_max(M);
+        for (int q = lane; q < S; q += 32) wq[q] = stage[q * P + 1] > 0.f ? expf(stage[q * P] - M) : 0.f;
+    }
+    __syncthreads();
     float L = 0.f;
     for (int q = 0; q < S; ++q) {
-        const float l = __ldcg(hp + q * kAttnPart + 1);
-        if (l > 0.f) L = __fadd_rn(L, __fmul_rn(l, expf(__ldcg(hp + q * kAttnPart) - M)));
+        const float l = stage[q * P + 1];
+        if (l > 0.f) L = __fadd_rn(L, __fmul_rn(l, wq[q]));
     }
     const float inv = 1.0f / L;
     for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
         float o = 0.f;
-        for (int q = 0; q < S; ++q) {
-            const float l = __ldcg(hp + q * kAttnPart + 1);
-            if (l > 0.f) o = __fadd_rn(o, __fmul_rn(__ldcg(hp + q * kAttnPart + 2 + d), expf(__ldcg(hp + q * kAttnPart) - M)));
-        }
+        for (int q = 0; q < S; ++q)
+            if (stage[q * P + 1] > 0.f) o = __fadd_rn(o, __fmul_rn(stage[q * P + 4 + d], wq[q]));
         out[head * hd + d] = __fmul_rn(o, inv);
     }
     if (threadIdx.x == 0) tickets[head] = 0;  // ready for the next launch
@@ -278,17 +405,19 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __
                                                                  int nq, int nkv, int hd, float* __restrict__ ws,
                                                                  int* __restrict__ tickets, float* __restrict__ out) {
     extern __shared__ float sc[];  // the CTA's scores, then probabilities
+    __shared__ __align__(16) float stage[kAttnStage];
     __shared__ float qs[kAttnMaxHd];
     __shared__ float red[32];
     __shared__ float part[kAttnThreads / 32][kAttnMaxHd];
-    pdl_entry();
     const int head = blockIdx.x;
     const int kvh = head / (nq / nkv);
+    attn_prefetch(pos_ptr, max_ctx, k_cache, v_cache, kvh, nkv * hd, hd);
+    pdl_entry();
     const int kv_len = (int)min((int64_t)max(*pos_ptr + 1, 1), max_ctx);
     for (int d = threadIdx.x; d < hd; d += kAttnThreads) qs[d] = q[head * hd + d];
     __syncthreads();
-    attend_split(qs, nullptr, nullptr, k_cache, v_cache, kvh, nkv * hd, hd, kv_len, head, sc, red, part, ws, tickets,
-                 out);
+    attend_split(qs, nullptr, nullptr, k_cache, v_cache, kvh, nkv * hd, hd, kv_len, head, sc, red, part, stage, ws,
+                 tickets, out);
 }
 
 // Fused form of qkv_rope_kernel + attention_kernel: every CTA of a query head
@@ -303,16 +432,20 @@ __global__ void __launch_bounds__(kAttnThreads) rope_attention_kernel(
     const int32_t* __restrict__ pos_ptr, int64_t max_ctx, float* __restrict__ k_cache, float* __restrict__ v_cache,
     int nq, int nkv, int hd, float* __restrict__ ws, int* __restrict__ tickets, float* __restrict__ out) {
     extern __shared__ float sc[];  // the CTA's scores, then probabilities
-    __shared__ float qs[kAttnMaxHd], kn[kAttnMaxHd], vn[kAttnMaxHd];
+    __shared__ __align__(16) float stage[kAttnStage];
+    __shared__ __align__(16) float kn[kAttnMaxHd];
+    __shared__ __align__(16) float vn[kAttnMaxHd];
+    __shared__ float qs[kAttnMaxHd];
     __shared__ float red[32];
     __shared__ float part[kAttnThreads / 32][kAttnMaxHd];
-    pdl_entry();
     const int head = blockIdx.x;
     const int group = nq / nkv;
     const int kvh = head / group;
+    const int ld = nkv * hd;
+    attn_prefetch(pos_ptr, max_ctx, k_cache, v_cache, kvh, ld, hd);
+    pdl_entry();
     const int pos = *pos_ptr;
     const int kv_len = (int)min((int64_t)max(pos + 1, 1), max_ctx);  // rows 0 .. kv_len-2 cached, kv_len-1 new
-    const int ld = nkv * hd;
     const int half = hd / 2;
     for (int i = threadIdx.x; i < half; i += kAttnThreads) {
         const float theta = 1.0f / powf(rope_theta, (float)(2 * i) / (float)hd);
@@ -337,7 +470,7 @@ __global__ void __launch_bounds__(kAttnThreads) rope_attention_kernel(
             k_cache[(int64_t)pos * ld + kvh * hd + d] = kn[d];
             v_cache[(int64_t)pos * ld + kvh * hd + d] = vn[d];
         }
-    attend_split(qs, kn, vn, k_cache, v_cache, kvh, ld, hd, kv_len, head, sc, red, part, ws, tickets, out);
+    attend_split(qs, kn, vn, k_cache, v_cache, kvh, ld, hd, kv_len, head, sc, red, part, stage, ws, tickets, out);
 }
 
 // out = silu(g) * u, silu(g) = g * (1 / (1 + exp(-g)))
@@ -446,15 +579,26 @@ cudaError_t launch_qkv_rope(float* q, const float* k, const float* v, const floa
                       bv, nq, nkv, hd, rope_theta, pos, max_ctx, k_cache, v_cache);
 }
 
+// The attention kernels hold about 38 KB of static shared memory; dynamic
+// shared memory (the scores of a split) beyond what is left of the default 48 KB
+// is opted into per launch.
+constexpr size_t kAttnDefaultDynSmem = 8 * 1024;
+constexpr size_t kAttnMaxDynSmem = 160 * 1024;
+// The split workspace holds nq x S partial results in 16-byte aligned rows.
+inline bool attn_ws_ok(const float* ws, int64_t ws_floats, const int* tickets, int64_t n_tickets, int nq, int S) {
+    return ws && tickets && (reinterpret_cast<uintptr_t>(ws) & 15) == 0 && (int64_t)nq * S * kAttnPart <= ws_floats &&
+           nq <= n_tickets;
+}
+
 cudaError_t launch_attention(const float* q, const float* k_cache, const float* v_cache, const int32_t* pos, int nq,
                              int nkv, int hd, int64_t max_ctx, float* ws, int64_t ws_floats, int* tickets,
                              int64_t n_tickets, float* out, cudaStream_t st) {
     if (nq <= 0 || nkv <= 0 || nq % nkv || hd <= 0 || hd > kAttnMaxHd || max_ctx <= 0) return cudaErrorInvalidValue;
     const int S = attn_splits(max_ctx);
-    if (!ws || !tickets || (int64_t)nq * S * kAttnPart > ws_floats || nq > n_tickets) return cudaErrorInvalidValue;
+    if (!attn_ws_ok(ws, ws_floats, tickets, n_tickets, nq, S)) return cudaErrorInvalidValue;
     const size_t smem = (size_t)((max_ctx + S - 1) / S) * sizeof(float);
-    if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    if (smem > 48 * 1024) {
+    if (smem > kAttnMaxDynSmem) return cudaErrorInvalidValue;
+    if (smem > kAttnDefaultDynSmem) {
         cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
@@ -469,10 +613,10 @@ cudaError_t launch_rope_attention(const float* q, const float* k, const float* v
     if (nq <= 0 || nkv <= 0 || nq % nkv || hd <= 0 || (hd & 1) || hd > kAttnMaxHd || max_ctx <= 0)
         return cudaErrorInvalidValue;
     const int S = attn_splits(max_ctx);
-    if (!ws || !tickets || (int64_t)nq * S * kAttnPart > ws_floats || nq > n_tickets) return cudaErrorInvalidValue;
+    if (!attn_ws_ok(ws, ws_floats, tickets, n_tickets, nq, S)) return cudaErrorInvalidValue;
     const size_t smem = (size_t)((max_ctx + S - 1) / S) * sizeof(float);
-    if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    if (smem > 48 * 1024) {
+    if (smem > kAttnMaxDynSmem) return cudaErrorInvalidValue;
+    if (smem > kAttnDefaultDynSmem) {
         cudaError_t e =
             cudaFuncSetAttribute(rope_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;

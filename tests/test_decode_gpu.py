@@ -175,6 +175,61 @@ def test_rope_attention_fused_equals_two_kernels(plane):
     assert normwise_err(o2.cpu().numpy(), ref) <= 1e-5
 
 
+@pytest.mark.parametrize("nq,nkv,hd,max_ctx,pos", [
+    (14, 2, 64, 640, 0),        # one row: 31 of the 32 splits empty
+    (14, 2, 64, 640, 511),      # the config-2 shape
+    (14, 2, 64, 640, 639),      # the cache's last row
+    (28, 4, 128, 4096, 3000),   # 64 splits of 47 rows: two staged chunks each
+    (8, 2, 96, 51200, 20000),   # the largest cache: 64 splits of 313 rows
+    (4, 1, 6, 100, 57),         # head_dim % 4 != 0: scalar staging
+    (6, 3, 33, 50, 49),         # odd head_dim (the unfused attention only)
+])
+def test_attention_splits_vs_oracle(plane, nq, nkv, hd, max_ctx, pos):
+    """bramha_cuda_op_attention within 1e-5 (normwise) of the oracle's single
+    pass over rows 0 .. pos (flash_attention_single_into,
+    cpu_engine.rs:1450-1509) and bit-identical run to run, across split counts,
+    empty splits, multi-chunk ranges and head sizes; for an even head_dim,
+    bramha_cuda_op_rope_attention equals op_qkv_rope then op_attention bit for
+    bit, the appended cache row included."""
+    from bramha_b200 import lib
+    from bramha_b200._lib import check
+    r = rng(pos + hd)
+    dev = torch.device("cuda", 0)
+    mk = lambda *shape: torch.from_numpy(r.normal(0, 1, shape).astype(np.float32)).to(dev)
+    L, c = lib(), plane.ctx
+    q = mk(nq * hd)
+    kc, vc = mk(max_ctx, nkv * hd), mk(max_ctx, nkv * hd)
+    p = torch.tensor([pos], dtype=torch.int32, device=dev)
+    outs = []
+    for _ in range(2):
+        o = torch.empty(nq * hd, device=dev)
+        check(L.bramha_cuda_op_attention(c, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), p.data_ptr(), nq, nkv, hd,
+                                         max_ctx, o.data_ptr(), None))
+        outs.append(o)
+    plane.stream_sync()
+    assert torch.equal(outs[0], outs[1])
+    ref = oracle.attention(q.cpu().numpy(), kc[:pos + 1].cpu().numpy(), vc[:pos + 1].cpu().numpy(), pos + 1, nq, nkv,
+                           hd)
+    assert normwise_err(outs[0].cpu().numpy(), ref) <= 1e-5
+    if hd % 2:
+        return
+    k, v = mk(nkv * hd), mk(nkv * hd)
+    bq, bk, bv = mk(nq * hd), mk(nkv * hd), mk(nkv * hd)
+    q1, kc1, vc1, o1 = q.clone(), kc.clone(), vc.clone(), torch.empty(nq * hd, device=dev)
+    check(L.bramha_cuda_op_qkv_rope(c, q1.data_ptr(), k.data_ptr(), v.data_ptr(), bq.data_ptr(), bk.data_ptr(),
+                                    bv.data_ptr(), nq, nkv, hd, 1e6, p.data_ptr(), max_ctx, kc1.data_ptr(),
+                                    vc1.data_ptr(), None))
+    check(L.bramha_cuda_op_attention(c, q1.data_ptr(), kc1.data_ptr(), vc1.data_ptr(), p.data_ptr(), nq, nkv, hd,
+                                     max_ctx, o1.data_ptr(), None))
+    kc2, vc2, o2 = kc.clone(), vc.clone(), torch.empty(nq * hd, device=dev)
+    check(L.bramha_cuda_op_rope_attention(c, q.data_ptr(), k.data_ptr(), v.data_ptr(), bq.data_ptr(), bk.data_ptr(),
+                                          bv.data_ptr(), nq, nkv, hd, 1e6, p.data_ptr(), max_ctx, kc2.data_ptr(),
+                                          vc2.data_ptr(), o2.data_ptr(), None))
+    plane.stream_sync()
+    assert torch.equal(o1, o2)
+    assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
+
+
 @pytest.mark.parametrize("fmt", ["log4", "w4zp8", "w8"])
 def test_gemv_swiglu_equals_silu_then_gemv(plane, fmt):
     """bramha_cuda_gemv_swiglu_dev == bramha_cuda_op_silu_mul then the GEMV, bit
