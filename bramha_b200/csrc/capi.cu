@@ -11,6 +11,7 @@
 // the boundary.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -56,6 +57,10 @@ struct bramha_ctx {
     float* dev_x = nullptr;
     float* dev_y = nullptr;
     size_t dev_x_cap = 0, dev_y_cap = 0;
+    // host-buffer chains: input and output copies on their own streams, ordered
+    // against the GEMV launches block by block through events (created on first use)
+    cudaStream_t copy_in = nullptr, copy_out = nullptr;
+    std::vector<cudaEvent_t> events;
     DevStatus* d_status = nullptr;       // error word, wait bound, test fault switch (device)
     int* d_err = nullptr;                // &d_status->err: what kernels are handed
     int* h_err = nullptr;                // pinned host copy of the error word
@@ -774,6 +779,19 @@ int ensure_staging(bramha_ctx* ctx, size_t x_elems, size_t y_elems) {
     return BRAMHA_OK;
 }
 
+// The host-buffer chain's copy streams and at least n events (caller holds io_mu).
+int ensure_copy_streams(bramha_ctx* ctx, size_t n_events) {
+    if (!ctx->copy_in) CK(cudaStreamCreateWithFlags(&ctx->copy_in, cudaStreamNonBlocking), "cudaStreamCreate(copy in)");
+    if (!ctx->copy_out)
+        CK(cudaStreamCreateWithFlags(&ctx->copy_out, cudaStreamNonBlocking), "cudaStreamCreate(copy out)");
+    while (ctx->events.size() < n_events) {
+        cudaEvent_t ev;
+        CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "cudaEventCreate");
+        ctx->events.push_back(ev);
+    }
+    return BRAMHA_OK;
+}
+
 // Host-buffer GEMV/GEMM: H2D x, launch, D2H y, wait.
 int gemv_host(bramha_ctx* ctx, const bramha_weight* w, const float* x_host, int64_t batch, float* y_host) {
     if (batch < 0) return fail(BRAMHA_ERR_INVALID, "negative batch");
@@ -887,6 +905,9 @@ int bramha_cuda_destroy(bramha_ctx* ctx) {
     for (int r = 0; r < ctx->shard_world; ++r)
         if (r != ctx->shard_rank && ctx->peer_arena[r]) cudaIpcCloseMemHandle(ctx->peer_arena[r]);
     if (ctx->arena) cudaFree(ctx->arena);
+    for (cudaEvent_t ev : ctx->events) cudaEventDestroy(ev);
+    if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);
+    if (ctx->copy_out) cudaStreamDestroy(ctx->copy_out);
     cudaStreamDestroy(ctx->stream);
     delete ctx;
     return BRAMHA_OK;
@@ -1077,10 +1098,12 @@ int check_chain_op(bramha_ctx* ctx, const bramha_gemv_op& op, int64_t batch, boo
 
 // Launches the ops in order; op i also prefetches op i+1's weights.  xs / ups /
 // ldxs override the ops' input pointers (device staging of the host chain).
-int chain_device(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch, cudaStream_t st,
-                 const float* const* xs = nullptr, const float* const* ups = nullptr, const int64_t* ldxs = nullptr,
-                 float* const* const* ys = nullptr) {
-    for (int i = 0; i < n_ops; ++i) {
+// Launches ops [i0, i1) of an n_ops chain; each launch requests the next op's
+// weights into L2 (also across i1 when i1 < n_ops).
+int chain_range(bramha_ctx* ctx, int i0, int i1, int n_ops, const bramha_gemv_op* ops, int64_t batch,
+                cudaStream_t st, const float* const* xs = nullptr, const float* const* ups = nullptr,
+                const int64_t* ldxs = nullptr, float* const* const* ys = nullptr) {
+    for (int i = i0; i < i1; ++i) {
         const bramha_gemv_op& op = ops[i];
         const int nn = i + 1 < n_ops ? ops[i + 1].n_weights : 0;
         const bramha_weight* const* nw = i + 1 < n_ops ? ops[i + 1].weights : nullptr;
@@ -1091,6 +1114,12 @@ int chain_device(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t 
         if (rc) return rc;
     }
     return BRAMHA_OK;
+}
+
+int chain_device(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch, cudaStream_t st,
+                 const float* const* xs = nullptr, const float* const* ups = nullptr, const int64_t* ldxs = nullptr,
+                 float* const* const* ys = nullptr) {
+    return chain_range(ctx, 0, n_ops, n_ops, ops, batch, st, xs, ups, ldxs, ys);
 }
 }  // namespace
 
@@ -1164,39 +1193,107 @@ int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops
     std::vector<float* const*> ys((size_t)n_ops);
     size_t yi = 0;
     for (int i = 0; i < n_ops; ++i) {
-        const int64_t K = ops[i].weights[0]->K;
-        float* xd = ctx->dev_x + xo[(size_t)i];
-        xs[(size_t)i] = xd;
-        if (K > 0) {
-            CK(cudaMemcpy2DAsync(xd, (size_t)ldx[(size_t)i] * sizeof(float), ops[i].x, (size_t)K * sizeof(float),
-                                 (size_t)K * sizeof(float), (size_t)batch, cudaMemcpyHostToDevice, st),
-               "H2D x");
-            if (ops[i].x_up) {
-                float* ud = ctx->dev_x + uo[(size_t)i];
-                ups[(size_t)i] = ud;
-                CK(cudaMemcpy2DAsync(ud, (size_t)ldx[(size_t)i] * sizeof(float), ops[i].x_up,
-                                     (size_t)K * sizeof(float), (size_t)K * sizeof(float), (size_t)batch,
-                                     cudaMemcpyHostToDevice, st),
-                   "H2D x_up");
-            }
-        }
+        xs[(size_t)i] = ctx->dev_x + xo[(size_t)i];
+        if (ops[i].x_up) ups[(size_t)i] = ctx->dev_x + uo[(size_t)i];
         for (int j = 0; j < ops[i].n_weights; ++j, ++yi)
             yv[(size_t)i].push_back((in_arena_y[yi] ? arena_y : ctx->dev_y) + yo[yi]);
         ys[(size_t)i] = yv[(size_t)i].data();
     }
-    rc = chain_device(ctx, n_ops, ops, batch, st, xs.data(), ups.data(), ldx.data(), ys.data());
-    if (rc) return rc;
-    if (any_shard) CK(launch_shard_signal(shard_args(ctx), ctx->d_err, 0, st), "shard sync launch");
-    yi = 0;
-    for (int i = 0; i < n_ops; ++i)
-        for (int j = 0; j < ops[i].n_weights; ++j, ++yi) {
+    std::vector<size_t> y0((size_t)n_ops + 1, 0);  // first output index of each op
+    for (int i = 0; i < n_ops; ++i) y0[(size_t)i + 1] = y0[(size_t)i] + (size_t)ops[i].n_weights;
+    auto h2d = [&](int i, cudaStream_t cs) -> int {  // op i's inputs
+        const int64_t K = ops[i].weights[0]->K;
+        if (K <= 0) return BRAMHA_OK;
+        const size_t pitch = (size_t)ldx[(size_t)i] * sizeof(float), row = (size_t)K * sizeof(float);
+        CK(cudaMemcpy2DAsync(const_cast<float*>(xs[(size_t)i]), pitch, ops[i].x, row, row, (size_t)batch,
+                             cudaMemcpyHostToDevice, cs),
+           "H2D x");
+        if (ops[i].x_up)
+            CK(cudaMemcpy2DAsync(const_cast<float*>(ups[(size_t)i]), pitch, ops[i].x_up, row, row, (size_t)batch,
+                                 cudaMemcpyHostToDevice, cs),
+               "H2D x_up");
+        return BRAMHA_OK;
+    };
+    auto d2h = [&](int i, cudaStream_t cs) -> int {  // op i's outputs
+        for (int j = 0; j < ops[i].n_weights; ++j) {
+            const size_t k = y0[(size_t)i] + (size_t)j;
             const bramha_weight* w = ops[i].weights[j];
             const size_t n = (size_t)((w->shard ? w->n_full : w->N) * batch);
             if (n > 0)
-                CK(cudaMemcpyAsync(ops[i].y[j], (in_arena_y[yi] ? arena_y : ctx->dev_y) + yo[yi], n * sizeof(float),
-                                   cudaMemcpyDeviceToHost, st),
+                CK(cudaMemcpyAsync(ops[i].y[j], (in_arena_y[k] ? arena_y : ctx->dev_y) + yo[k], n * sizeof(float),
+                                   cudaMemcpyDeviceToHost, cs),
                    "D2H y");
         }
+        return BRAMHA_OK;
+    };
+    if (any_shard) {  // every copy on the chain's stream; outputs after every rank's rows landed
+        for (int i = 0; i < n_ops; ++i)
+            if ((rc = h2d(i, st))) return rc;
+        rc = chain_device(ctx, n_ops, ops, batch, st, xs.data(), ups.data(), ldx.data(), ys.data());
+        if (rc) return rc;
+        CK(launch_shard_signal(shard_args(ctx), ctx->d_err, 0, st), "shard sync launch");
+        for (int i = 0; i < n_ops; ++i)
+            if ((rc = d2h(i, st))) return rc;
+        return check_device_error(ctx, st);
+    }
+    // Copies overlap the launches: ops in blocks of 1, 2, 4, 8, 16, ..., 16, 8,
+    // 4, 2, 1 (short blocks at both ends: the first launch waits only for its
+    // own inputs, the last outputs start back as soon as their launch is done);
+    // block k's inputs go in on copy_in (one block ahead of the launches), its
+    // launches wait for them, and its outputs come back on copy_out while the
+    // later blocks run.
+    std::vector<int> head, tail;
+    for (int lo = 0, hi = n_ops, size = 1; lo < hi; size = size < 16 ? size * 2 : 16) {
+        int t = std::min(size, hi - lo);
+        head.push_back(t);
+        lo += t;
+        if (lo >= hi) break;
+        t = std::min(size, hi - lo);
+        tail.push_back(t);
+        hi -= t;
+    }
+    std::vector<int> bs{0};
+    for (int t : head) bs.push_back(bs.back() + t);
+    for (auto it = tail.rbegin(); it != tail.rend(); ++it) bs.push_back(bs.back() + *it);
+    const int nb = (int)bs.size() - 1;
+    if ((rc = ensure_copy_streams(ctx, (size_t)(2 * nb + 2)))) return rc;
+    cudaEvent_t* ev = ctx->events.data();  // [0] start, [1] outputs copied, [2 + k] block k in, [2 + nb + k] done
+    auto overlapped = [&]() -> int {
+        CK(cudaEventRecord(ev[0], st), "event record");
+        CK(cudaStreamWaitEvent(ctx->copy_in, ev[0], 0), "stream wait");
+        CK(cudaStreamWaitEvent(ctx->copy_out, ev[0], 0), "stream wait");
+        auto in_block = [&](int k) -> int {
+            for (int i = bs[(size_t)k]; i < bs[(size_t)k + 1]; ++i)
+                if (int r = h2d(i, ctx->copy_in)) return r;
+            CK(cudaEventRecord(ev[2 + k], ctx->copy_in), "event record");
+            return BRAMHA_OK;
+        };
+        if (int r = in_block(0)) return r;
+        for (int k = 0; k < nb; ++k) {
+            if (k + 1 < nb)
+                if (int r = in_block(k + 1)) return r;
+            CK(cudaStreamWaitEvent(st, ev[2 + k], 0), "stream wait");
+            if (int r = chain_range(ctx, bs[(size_t)k], bs[(size_t)k + 1], n_ops, ops, batch, st, xs.data(), ups.data(),
+                                    ldx.data(), ys.data()))
+                return r;
+            CK(cudaEventRecord(ev[2 + nb + k], st), "event record");
+        }
+        for (int k = 0; k < nb; ++k) {
+            CK(cudaStreamWaitEvent(ctx->copy_out, ev[2 + nb + k], 0), "stream wait");
+            for (int i = bs[(size_t)k]; i < bs[(size_t)k + 1]; ++i)
+                if (int r = d2h(i, ctx->copy_out)) return r;
+        }
+        CK(cudaEventRecord(ev[1], ctx->copy_out), "event record");
+        CK(cudaStreamWaitEvent(st, ev[1], 0), "stream wait");
+        return BRAMHA_OK;
+    };
+    rc = overlapped();
+    if (rc) {  // nothing may still read or write the caller's buffers after the return
+        cudaStreamSynchronize(ctx->copy_in);
+        cudaStreamSynchronize(st);
+        cudaStreamSynchronize(ctx->copy_out);
+        return rc;
+    }
     return check_device_error(ctx, st);
 }
 

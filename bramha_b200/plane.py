@@ -372,14 +372,14 @@ class CudaComputePlane:
 
     def gemv_chain(self, ops, batch: int = 1):
         """The same chain on host buffers (numpy arrays or pinned torch CPU tensors):
-        inputs copied in, the chain run, outputs copied back; synchronous."""
-        for op in ops:
-            for a in (op[1],) + tuple(op[2]) + ((op[3],) if len(op) > 3 and op[3] is not None else ()):
-                if isinstance(a, np.ndarray) and (a.dtype != np.float32 or not a.flags.c_contiguous):
-                    raise BramhaError(-1, "gemv_chain: host buffers must be contiguous float32")
-        arr, keep = self._chain_ops(ops)
-        check(lib().bramha_cuda_gemv_chain(self._ctx, len(ops), arr, batch))
-        del keep
+        inputs copied in, the chain run, outputs copied back; synchronous.  The
+        copies run on their own streams, overlapping the launches block by block."""
+        HostGemvChain(self, ops, batch).run()
+
+    def prepare_chain(self, ops, batch: int = 1) -> "HostGemvChain":
+        """gemv_chain on fixed host buffers with the op list built once: each
+        run() copies the buffers' current contents in and the outputs back."""
+        return HostGemvChain(self, ops, batch)
 
     def stream_sync(self, stream=None):
         """Wait for the stream and raise if a kernel reported a device-side failure."""
@@ -389,6 +389,22 @@ class CudaComputePlane:
         n, k = w.shape
         check(lib().bramha_cuda_quantize_dev(self._ctx, FMT[fmt], n, k, w.data_ptr(), q.data_ptr(),
                                              scales.data_ptr(), _stream(stream)))
+
+
+class HostGemvChain:
+    """A host-buffer GEMV chain (bramha_cuda_gemv_chain) whose op array is built
+    once; the buffers are held and must keep their addresses."""
+
+    def __init__(self, plane: "CudaComputePlane", ops, batch: int = 1):
+        for op in ops:
+            for a in (op[1],) + tuple(op[2]) + ((op[3],) if len(op) > 3 and op[3] is not None else ()):
+                if isinstance(a, np.ndarray) and (a.dtype != np.float32 or not a.flags.c_contiguous):
+                    raise BramhaError(-1, "gemv_chain: host buffers must be contiguous float32")
+        self.plane, self.batch, self._ops = plane, batch, ops
+        self._arr, self._keep = CudaComputePlane._chain_ops(ops)
+
+    def run(self):
+        check(lib().bramha_cuda_gemv_chain(self.plane.ctx, len(self._ops), self._arr, self.batch))
 
 
 class GemvProgram:

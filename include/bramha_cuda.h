@@ -259,7 +259,11 @@ BRAMHA_API int bramha_cuda_gemv_chain_dev(bramha_ctx* ctx, int n_ops, const bram
 /* Host buffers (any alignment), synchronous: every op's x is copied to the
  * device, the chain runs, every y is copied back, and the call returns once
  * they are in host memory (one wait for the whole chain, which also reports a
- * device-side failure). */
+ * device-side failure).  The copies run on two streams of the context beside
+ * its launch stream, in blocks of ops (1, 2, 4, 8, 16, ..., 16, 8, 4, 2, 1):
+ * a block's launches wait only for its own inputs, and its outputs are copied
+ * back while the later blocks run, so with pinned host buffers the copies hide
+ * behind the launches.  Pageable buffers work too (the driver stages them). */
 BRAMHA_API int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch);
 
 /* The same chain as ONE persistent launch (no counterpart in the reference,
