@@ -867,7 +867,7 @@ def run_ours(args, ws, rank, local):
             traffic = None
 
     # ---- e2e: the public host-buffer call for the whole step: one
-    # bramha_cuda_gemv_chain call per step (pinned host inputs copied in, the
+    # bramha_cuda_host_chain_run per step (pinned host inputs copied in, the
     # 113 launches, every output copied back, one wait)
     h2d = d2h = 0
     host_ops = []
@@ -880,7 +880,7 @@ def run_ours(args, ws, rank, local):
             h2d += xh.numel() * 4
             d2h += sum(y.numel() * 4 for y in yhs)
 
-    host_chain = plane.prepare_chain(host_ops, B)  # the op list built once, as a host program would
+    host_chain = plane.prepare_chain(host_ops, B)  # bound once (bramha_cuda_host_chain_create), as a host program would
 
     def e2e_step():
         host_chain.run()  # N > 1: every rank's host buffers receive the full outputs
@@ -947,8 +947,9 @@ def run_ours(args, ws, rank, local):
             "per_linear": per_linear,
             "clocks": clocks.summary(),
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "api": "bramha_cuda_gemv_chain (pinned host buffers, synchronous; copies overlapped with "
-                           "the launches on two copy streams), one call per step through HostGemvChain.run",
+                    "api": "bramha_cuda_host_chain_run (the step's host-buffer GEMV chain bound once; pinned "
+                           "host buffers; copies and launches replayed as one CUDA graph, the copies overlapping "
+                           "the launches; synchronous), one call per step",
                     "tokens_per_s": round(B / e2e_s, 2)},
             "spread": spread,
             "cpu_baseline": cpu,

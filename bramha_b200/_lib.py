@@ -94,6 +94,10 @@ _SIGNATURES = {
     "bramha_cuda_shard_sync_dev": [_vp, _vp],
     "bramha_cuda_gemv_chain_dev": [_vp, _int, _vp, _i64, _vp],
     "bramha_cuda_gemv_chain": [_vp, _int, _vp, _i64],
+    "bramha_cuda_host_chain_create": [_vp, _int, _vp, _i64, ctypes.POINTER(_vp)],
+    "bramha_cuda_host_chain_run": [_vp, _vp],
+    "bramha_cuda_host_chain_uses_graph": [_vp, _vp, ctypes.POINTER(_int)],
+    "bramha_cuda_host_chain_destroy": [_vp, _vp],
     "bramha_cuda_gemv_program_create": [_vp, _int, _vp, _i64, ctypes.POINTER(_vp)],
     "bramha_cuda_gemv_program_run_dev": [_vp, _vp, _vp],
     "bramha_cuda_gemv_program_destroy": [_vp, _vp],

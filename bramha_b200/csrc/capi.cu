@@ -1096,10 +1096,9 @@ int check_chain_op(bramha_ctx* ctx, const bramha_gemv_op& op, int64_t batch, boo
     return BRAMHA_OK;
 }
 
-// Launches the ops in order; op i also prefetches op i+1's weights.  xs / ups /
-// ldxs override the ops' input pointers (device staging of the host chain).
-// Launches ops [i0, i1) of an n_ops chain; each launch requests the next op's
-// weights into L2 (also across i1 when i1 < n_ops).
+// Launches ops [i0, i1) of an n_ops chain in order; each launch requests the
+// next op's weights into L2 (also across i1 when i1 < n_ops).  xs / ups / ldxs /
+// ys override the ops' pointers (device staging of the host chain).
 int chain_range(bramha_ctx* ctx, int i0, int i1, int n_ops, const bramha_gemv_op* ops, int64_t batch,
                 cudaStream_t st, const float* const* xs = nullptr, const float* const* ups = nullptr,
                 const int64_t* ldxs = nullptr, float* const* const* ys = nullptr) {
@@ -1136,112 +1135,53 @@ int bramha_cuda_gemv_chain_dev(bramha_ctx* ctx, int n_ops, const bramha_gemv_op*
     return chain_device(ctx, n_ops, ops, batch, st);
 }
 
-int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch) {
-    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
-    if (n_ops < 0 || (n_ops > 0 && !ops)) return fail(BRAMHA_ERR_INVALID, "gemv chain: bad op list");
-    if (batch < 0) return fail(BRAMHA_ERR_INVALID, "negative batch");
-    for (int i = 0; i < n_ops; ++i) {
-        int rc = check_chain_op(ctx, ops[i], batch, false);
-        if (rc) return rc;
-    }
-    if (n_ops == 0 || batch == 0) return BRAMHA_OK;
-    DeviceGuard g(ctx->device);
-    std::lock_guard<std::mutex> lk(ctx->io_mu);
-    // device staging: every op's x (and x_up) at a 16-byte aligned pitch, then
-    // every output, back to back
-    // (outputs of sharded ops -- every rank's rows -- are staged at the top of
-    // the shard arena, where the other ranks' GEMVs can store theirs)
-    std::vector<int64_t> ldx((size_t)n_ops), xo((size_t)n_ops), uo((size_t)n_ops);
-    std::vector<int64_t> yo;
+namespace {
+// Device staging of a host-buffer chain: every op's x (and x_up) at a 16-byte
+// aligned pitch, then every output, back to back (outputs of sharded ops --
+// every rank's rows -- are staged at the top of the shard arena, where the
+// other ranks' GEMVs can store theirs).
+struct ChainLayout {
+    std::vector<int64_t> ldx, xo, uo, yo;
     std::vector<char> in_arena_y;
+    std::vector<size_t> y0;  // index of each op's first output in yo
     size_t xe = 0, ye = 0, ya = 0;
     bool any_shard = false;
+};
+
+ChainLayout chain_layout(int n_ops, const bramha_gemv_op* ops, int64_t batch) {
+    ChainLayout L;
+    L.ldx.resize((size_t)n_ops);
+    L.xo.resize((size_t)n_ops);
+    L.uo.resize((size_t)n_ops);
+    L.y0.assign((size_t)n_ops + 1, 0);
     for (int i = 0; i < n_ops; ++i) {
         const int64_t K = ops[i].weights[0]->K;
-        ldx[(size_t)i] = (K + 3) / 4 * 4;
-        xo[(size_t)i] = (int64_t)xe;
-        xe += (size_t)(ldx[(size_t)i] * batch);
-        uo[(size_t)i] = ops[i].x_up ? (int64_t)xe : -1;
-        if (ops[i].x_up) xe += (size_t)(ldx[(size_t)i] * batch);
+        L.ldx[(size_t)i] = (K + 3) / 4 * 4;
+        L.xo[(size_t)i] = (int64_t)L.xe;
+        L.xe += (size_t)(L.ldx[(size_t)i] * batch);
+        L.uo[(size_t)i] = ops[i].x_up ? (int64_t)L.xe : -1;
+        if (ops[i].x_up) L.xe += (size_t)(L.ldx[(size_t)i] * batch);
         for (int j = 0; j < ops[i].n_weights; ++j) {
             const bramha_weight* w = ops[i].weights[j];
             if (w->shard) {
-                any_shard = true;
-                yo.push_back((int64_t)ya);
-                ya += (size_t)(w->n_full * batch);
+                L.any_shard = true;
+                L.yo.push_back((int64_t)L.ya);
+                L.ya += (size_t)(w->n_full * batch);
             } else {
-                yo.push_back((int64_t)ye);
-                ye += (size_t)(w->N * batch);
+                L.yo.push_back((int64_t)L.ye);
+                L.ye += (size_t)(w->N * batch);
             }
-            in_arena_y.push_back(w->shard ? 1 : 0);
+            L.in_arena_y.push_back(w->shard ? 1 : 0);
         }
+        L.y0[(size_t)i + 1] = L.y0[(size_t)i] + (size_t)ops[i].n_weights;
     }
-    int rc = ensure_staging(ctx, xe, ye > 0 ? ye : 1);
-    if (rc) return rc;
-    float* arena_y = nullptr;
-    if (any_shard) {
-        if (!ctx->arena || ctx->shard_world < 2) return fail(BRAMHA_ERR_INVALID, "sharded weights need a shard group");
-        const size_t need = (ya * sizeof(float) + 255) / 256 * 256;
-        if (need > ctx->arena_bytes - ctx->arena_used)
-            return fail(BRAMHA_ERR_OOM, "shard arena too small to stage this chain's outputs (%zu bytes)", need);
-        if (ctx->arena_bytes - need < ctx->arena_top) ctx->arena_top = ctx->arena_bytes - need;
-        arena_y = reinterpret_cast<float*>(ctx->arena + (ctx->arena_bytes - need));
-    }
-    cudaStream_t st = ctx->stream;
-    std::vector<const float*> xs((size_t)n_ops), ups((size_t)n_ops, nullptr);
-    std::vector<std::vector<float*>> yv((size_t)n_ops);
-    std::vector<float* const*> ys((size_t)n_ops);
-    size_t yi = 0;
-    for (int i = 0; i < n_ops; ++i) {
-        xs[(size_t)i] = ctx->dev_x + xo[(size_t)i];
-        if (ops[i].x_up) ups[(size_t)i] = ctx->dev_x + uo[(size_t)i];
-        for (int j = 0; j < ops[i].n_weights; ++j, ++yi)
-            yv[(size_t)i].push_back((in_arena_y[yi] ? arena_y : ctx->dev_y) + yo[yi]);
-        ys[(size_t)i] = yv[(size_t)i].data();
-    }
-    std::vector<size_t> y0((size_t)n_ops + 1, 0);  // first output index of each op
-    for (int i = 0; i < n_ops; ++i) y0[(size_t)i + 1] = y0[(size_t)i] + (size_t)ops[i].n_weights;
-    auto h2d = [&](int i, cudaStream_t cs) -> int {  // op i's inputs
-        const int64_t K = ops[i].weights[0]->K;
-        if (K <= 0) return BRAMHA_OK;
-        const size_t pitch = (size_t)ldx[(size_t)i] * sizeof(float), row = (size_t)K * sizeof(float);
-        CK(cudaMemcpy2DAsync(const_cast<float*>(xs[(size_t)i]), pitch, ops[i].x, row, row, (size_t)batch,
-                             cudaMemcpyHostToDevice, cs),
-           "H2D x");
-        if (ops[i].x_up)
-            CK(cudaMemcpy2DAsync(const_cast<float*>(ups[(size_t)i]), pitch, ops[i].x_up, row, row, (size_t)batch,
-                                 cudaMemcpyHostToDevice, cs),
-               "H2D x_up");
-        return BRAMHA_OK;
-    };
-    auto d2h = [&](int i, cudaStream_t cs) -> int {  // op i's outputs
-        for (int j = 0; j < ops[i].n_weights; ++j) {
-            const size_t k = y0[(size_t)i] + (size_t)j;
-            const bramha_weight* w = ops[i].weights[j];
-            const size_t n = (size_t)((w->shard ? w->n_full : w->N) * batch);
-            if (n > 0)
-                CK(cudaMemcpyAsync(ops[i].y[j], (in_arena_y[k] ? arena_y : ctx->dev_y) + yo[k], n * sizeof(float),
-                                   cudaMemcpyDeviceToHost, cs),
-                   "D2H y");
-        }
-        return BRAMHA_OK;
-    };
-    if (any_shard) {  // every copy on the chain's stream; outputs after every rank's rows landed
-        for (int i = 0; i < n_ops; ++i)
-            if ((rc = h2d(i, st))) return rc;
-        rc = chain_device(ctx, n_ops, ops, batch, st, xs.data(), ups.data(), ldx.data(), ys.data());
-        if (rc) return rc;
-        CK(launch_shard_signal(shard_args(ctx), ctx->d_err, 0, st), "shard sync launch");
-        for (int i = 0; i < n_ops; ++i)
-            if ((rc = d2h(i, st))) return rc;
-        return check_device_error(ctx, st);
-    }
-    // Copies overlap the launches: ops in blocks of 1, 2, 4, 8, 16, ..., 16, 8,
-    // 4, 2, 1 (short blocks at both ends: the first launch waits only for its
-    // own inputs, the last outputs start back as soon as their launch is done);
-    // block k's inputs go in on copy_in (one block ahead of the launches), its
-    // launches wait for them, and its outputs come back on copy_out while the
-    // later blocks run.
+    return L;
+}
+
+// Boundaries of the copy blocks of an n-op host chain: 1, 2, 4, 8, 16, ..., 16,
+// 8, 4, 2, 1 ops (short blocks at both ends: the first launch waits only for
+// its own inputs, the last outputs start back as soon as their launch is done).
+std::vector<int> chain_blocks(int n_ops) {
     std::vector<int> head, tail;
     for (int lo = 0, hi = n_ops, size = 1; lo < hi; size = size < 16 ? size * 2 : 16) {
         int t = std::min(size, hi - lo);
@@ -1255,6 +1195,70 @@ int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops
     std::vector<int> bs{0};
     for (int t : head) bs.push_back(bs.back() + t);
     for (auto it = tail.rbegin(); it != tail.rend(); ++it) bs.push_back(bs.back() + *it);
+    return bs;
+}
+
+// Enqueues a host-buffer chain staged in dev_x / dev_y (arena_y for sharded
+// outputs): inputs in, the launches, outputs out, on the context's stream (and,
+// unsharded, its two copy streams, joined back into the stream at the end).
+// No wait; capturable into a CUDA graph when unsharded.
+int host_chain_enqueue(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch, const ChainLayout& lay,
+                       float* dev_x, float* dev_y, float* arena_y) {
+    cudaStream_t st = ctx->stream;
+    std::vector<const float*> xs((size_t)n_ops), ups((size_t)n_ops, nullptr);
+    std::vector<std::vector<float*>> yv((size_t)n_ops);
+    std::vector<float* const*> ys((size_t)n_ops);
+    size_t yi = 0;
+    for (int i = 0; i < n_ops; ++i) {
+        xs[(size_t)i] = dev_x + lay.xo[(size_t)i];
+        if (ops[i].x_up) ups[(size_t)i] = dev_x + lay.uo[(size_t)i];
+        for (int j = 0; j < ops[i].n_weights; ++j, ++yi)
+            yv[(size_t)i].push_back((lay.in_arena_y[yi] ? arena_y : dev_y) + lay.yo[yi]);
+        ys[(size_t)i] = yv[(size_t)i].data();
+    }
+    auto h2d = [&](int i, cudaStream_t cs) -> int {  // op i's inputs
+        const int64_t K = ops[i].weights[0]->K;
+        if (K <= 0) return BRAMHA_OK;
+        const size_t pitch = (size_t)lay.ldx[(size_t)i] * sizeof(float), row = (size_t)K * sizeof(float);
+        CK(cudaMemcpy2DAsync(const_cast<float*>(xs[(size_t)i]), pitch, ops[i].x, row, row, (size_t)batch,
+                             cudaMemcpyHostToDevice, cs),
+           "H2D x");
+        if (ops[i].x_up)
+            CK(cudaMemcpy2DAsync(const_cast<float*>(ups[(size_t)i]), pitch, ops[i].x_up, row, row, (size_t)batch,
+                                 cudaMemcpyHostToDevice, cs),
+               "H2D x_up");
+        return BRAMHA_OK;
+    };
+    auto d2h = [&](int i, cudaStream_t cs) -> int {  // op i's outputs
+        for (int j = 0; j < ops[i].n_weights; ++j) {
+            const size_t k = lay.y0[(size_t)i] + (size_t)j;
+            const bramha_weight* w = ops[i].weights[j];
+            const size_t n = (size_t)((w->shard ? w->n_full : w->N) * batch);
+            if (n > 0)
+                CK(cudaMemcpyAsync(ops[i].y[j], (lay.in_arena_y[k] ? arena_y : dev_y) + lay.yo[k], n * sizeof(float),
+                                   cudaMemcpyDeviceToHost, cs),
+                   "D2H y");
+        }
+        return BRAMHA_OK;
+    };
+    int rc = BRAMHA_OK;
+    if (lay.any_shard) {  // every copy on the chain's stream; outputs after every rank's rows landed
+        for (int i = 0; i < n_ops; ++i)
+            if ((rc = h2d(i, st))) return rc;
+        rc = chain_device(ctx, n_ops, ops, batch, st, xs.data(), ups.data(), lay.ldx.data(), ys.data());
+        if (rc) return rc;
+        CK(launch_shard_signal(shard_args(ctx), ctx->d_err, 0, st), "shard sync launch");
+        for (int i = 0; i < n_ops; ++i)
+            if ((rc = d2h(i, st))) return rc;
+        return BRAMHA_OK;
+    }
+    // Copies overlap the launches: ops in blocks of 1, 2, 4, 8, 16, ..., 16, 8,
+    // 4, 2, 1 (short blocks at both ends: the first launch waits only for its
+    // own inputs, the last outputs start back as soon as their launch is done);
+    // block k's inputs go in on copy_in (one block ahead of the launches), its
+    // launches wait for them, and its outputs come back on copy_out while the
+    // later blocks run.
+    const std::vector<int> bs = chain_blocks(n_ops);
     const int nb = (int)bs.size() - 1;
     if ((rc = ensure_copy_streams(ctx, (size_t)(2 * nb + 2)))) return rc;
     cudaEvent_t* ev = ctx->events.data();  // [0] start, [1] outputs copied, [2 + k] block k in, [2 + nb + k] done
@@ -1274,7 +1278,7 @@ int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops
                 if (int r = in_block(k + 1)) return r;
             CK(cudaStreamWaitEvent(st, ev[2 + k], 0), "stream wait");
             if (int r = chain_range(ctx, bs[(size_t)k], bs[(size_t)k + 1], n_ops, ops, batch, st, xs.data(), ups.data(),
-                                    ldx.data(), ys.data()))
+                                    lay.ldx.data(), ys.data()))
                 return r;
             CK(cudaEventRecord(ev[2 + nb + k], st), "event record");
         }
@@ -1287,14 +1291,170 @@ int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops
         CK(cudaStreamWaitEvent(st, ev[1], 0), "stream wait");
         return BRAMHA_OK;
     };
-    rc = overlapped();
-    if (rc) {  // nothing may still read or write the caller's buffers after the return
-        cudaStreamSynchronize(ctx->copy_in);
-        cudaStreamSynchronize(st);
-        cudaStreamSynchronize(ctx->copy_out);
+    return overlapped();
+}
+
+// After a failed enqueue: nothing may still read or write the caller's buffers.
+void host_chain_drain(bramha_ctx* ctx) {
+    if (ctx->copy_in) cudaStreamSynchronize(ctx->copy_in);
+    cudaStreamSynchronize(ctx->stream);
+    if (ctx->copy_out) cudaStreamSynchronize(ctx->copy_out);
+}
+}  // namespace
+
+int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (n_ops < 0 || (n_ops > 0 && !ops)) return fail(BRAMHA_ERR_INVALID, "gemv chain: bad op list");
+    if (batch < 0) return fail(BRAMHA_ERR_INVALID, "negative batch");
+    for (int i = 0; i < n_ops; ++i) {
+        int rc = check_chain_op(ctx, ops[i], batch, false);
+        if (rc) return rc;
+    }
+    if (n_ops == 0 || batch == 0) return BRAMHA_OK;
+    DeviceGuard g(ctx->device);
+    std::lock_guard<std::mutex> lk(ctx->io_mu);
+    const ChainLayout lay = chain_layout(n_ops, ops, batch);
+    int rc = ensure_staging(ctx, lay.xe, lay.ye > 0 ? lay.ye : 1);
+    if (rc) return rc;
+    float* arena_y = nullptr;
+    if (lay.any_shard) {
+        if (!ctx->arena || ctx->shard_world < 2) return fail(BRAMHA_ERR_INVALID, "sharded weights need a shard group");
+        const size_t need = (lay.ya * sizeof(float) + 255) / 256 * 256;
+        if (need > ctx->arena_bytes - ctx->arena_used)
+            return fail(BRAMHA_ERR_OOM, "shard arena too small to stage this chain's outputs (%zu bytes)", need);
+        if (ctx->arena_bytes - need < ctx->arena_top) ctx->arena_top = ctx->arena_bytes - need;
+        arena_y = reinterpret_cast<float*>(ctx->arena + (ctx->arena_bytes - need));
+    }
+    rc = host_chain_enqueue(ctx, n_ops, ops, batch, lay, ctx->dev_x, ctx->dev_y, arena_y);
+    if (rc) {
+        host_chain_drain(ctx);
         return rc;
     }
-    return check_device_error(ctx, st);
+    return check_device_error(ctx, ctx->stream);
+}
+
+struct bramha_host_chain {
+    int n_ops = 0;
+    int64_t batch = 0;
+    std::vector<std::vector<const bramha_weight*>> w;
+    std::vector<std::vector<float*>> y;
+    std::vector<bramha_gemv_op> ops;  // views of w / y and the caller's x, x_up
+    ChainLayout lay;
+    float* dev_x = nullptr;           // the chain's own staging
+    float* dev_y = nullptr;
+    cudaGraphExec_t exec = nullptr;   // null: launched eagerly every run
+};
+
+namespace {
+bool is_pinned(const void* p) {
+    if (!p) return true;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+void host_chain_free(bramha_host_chain* c) {
+    if (c->exec) cudaGraphExecDestroy(c->exec);
+    if (c->dev_x) cudaFree(c->dev_x);
+    if (c->dev_y) cudaFree(c->dev_y);
+    delete c;
+}
+}  // namespace
+
+int bramha_cuda_host_chain_create(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch,
+                                  bramha_host_chain** out) {
+    if (!ctx || !out) return fail(BRAMHA_ERR_INVALID, "null argument");
+    *out = nullptr;
+    if (n_ops < 1 || !ops) return fail(BRAMHA_ERR_INVALID, "host chain: needs at least one op");
+    if (batch < 1) return fail(BRAMHA_ERR_INVALID, "host chain: batch must be at least 1");
+    for (int i = 0; i < n_ops; ++i) {
+        int rc = check_chain_op(ctx, ops[i], batch, false);
+        if (rc) return rc;
+        for (int j = 0; j < ops[i].n_weights; ++j)
+            if (ops[i].weights[j]->shard)
+                return fail(BRAMHA_ERR_UNSUPPORTED, "host chain: sharded weights are not supported; "
+                                                    "use bramha_cuda_gemv_chain");
+    }
+    bramha_host_chain* c = new (std::nothrow) bramha_host_chain();
+    if (!c) return fail(BRAMHA_ERR_OOM, "host allocation failed");
+    c->n_ops = n_ops;
+    c->batch = batch;
+    c->w.resize((size_t)n_ops);
+    c->y.resize((size_t)n_ops);
+    c->ops.resize((size_t)n_ops);
+    bool pinned = true;
+    for (int i = 0; i < n_ops; ++i) {
+        const bramha_gemv_op& op = ops[i];
+        c->w[(size_t)i].assign(op.weights, op.weights + op.n_weights);
+        c->y[(size_t)i].assign(op.y, op.y + op.n_weights);
+        c->ops[(size_t)i] = bramha_gemv_op{op.n_weights, c->w[(size_t)i].data(), op.x, op.x_up, c->y[(size_t)i].data()};
+        pinned = pinned && is_pinned(op.x) && is_pinned(op.x_up);
+        for (int j = 0; j < op.n_weights; ++j) pinned = pinned && is_pinned(op.y[j]);
+    }
+    c->lay = chain_layout(n_ops, c->ops.data(), batch);
+    DeviceGuard g(ctx->device);
+    cudaError_t e = cudaMalloc(&c->dev_x, sizeof(float) * std::max<size_t>(c->lay.xe, 1));
+    if (e == cudaSuccess) e = cudaMalloc(&c->dev_y, sizeof(float) * std::max<size_t>(c->lay.ye, 1));
+    if (e != cudaSuccess) {
+        host_chain_free(c);
+        return cuda_fail(e, "cudaMalloc(host chain staging)");
+    }
+    if (pinned) {  // one CUDA graph of the copies and launches; on any failure, eager runs
+        std::lock_guard<std::mutex> lk(ctx->io_mu);
+        const size_t nb = chain_blocks(n_ops).size() - 1;
+        if (ensure_copy_streams(ctx, 2 * nb + 2) == BRAMHA_OK &&
+            cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            const int rc = host_chain_enqueue(ctx, n_ops, c->ops.data(), batch, c->lay, c->dev_x, c->dev_y, nullptr);
+            cudaGraph_t graph = nullptr;
+            const cudaError_t ee = cudaStreamEndCapture(ctx->stream, &graph);
+            if (rc == BRAMHA_OK && ee == cudaSuccess && graph &&
+                cudaGraphInstantiate(&c->exec, graph, 0) != cudaSuccess)
+                c->exec = nullptr;
+            if (graph) cudaGraphDestroy(graph);
+        }
+        cudaGetLastError();
+        g_last_error.clear();
+    }
+    *out = c;
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_host_chain_uses_graph(bramha_ctx* ctx, const bramha_host_chain* chain, int* out) {
+    if (!ctx || !chain || !out) return fail(BRAMHA_ERR_INVALID, "null argument");
+    *out = chain->exec ? 1 : 0;
+    return BRAMHA_OK;
+}
+
+int bramha_cuda_host_chain_run(bramha_ctx* ctx, bramha_host_chain* c) {
+    if (!ctx || !c) return fail(BRAMHA_ERR_INVALID, "null argument");
+    for (int i = 0; i < c->n_ops; ++i) {  // every weight still registered
+        int rc = check_chain_op(ctx, c->ops[(size_t)i], c->batch, false);
+        if (rc) return rc;
+    }
+    DeviceGuard g(ctx->device);
+    std::lock_guard<std::mutex> lk(ctx->io_mu);
+    if (c->exec) {
+        CK(cudaGraphLaunch(c->exec, ctx->stream), "cudaGraphLaunch(host chain)");
+    } else {
+        const int rc = host_chain_enqueue(ctx, c->n_ops, c->ops.data(), c->batch, c->lay, c->dev_x, c->dev_y, nullptr);
+        if (rc) {
+            host_chain_drain(ctx);
+            return rc;
+        }
+    }
+    return check_device_error(ctx, ctx->stream);
+}
+
+int bramha_cuda_host_chain_destroy(bramha_ctx* ctx, bramha_host_chain* c) {
+    if (!ctx) return fail(BRAMHA_ERR_INVALID, "null context");
+    if (!c) return BRAMHA_OK;
+    DeviceGuard g(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    host_chain_free(c);
+    return BRAMHA_OK;
 }
 
 struct bramha_gemv_program {

@@ -374,11 +374,15 @@ class CudaComputePlane:
         """The same chain on host buffers (numpy arrays or pinned torch CPU tensors):
         inputs copied in, the chain run, outputs copied back; synchronous.  The
         copies run on their own streams, overlapping the launches block by block."""
-        HostGemvChain(self, ops, batch).run()
+        _check_host_buffers(ops)
+        arr, keep = self._chain_ops(ops)
+        check(lib().bramha_cuda_gemv_chain(self._ctx, len(ops), arr, batch))
+        del keep
 
     def prepare_chain(self, ops, batch: int = 1) -> "HostGemvChain":
-        """gemv_chain on fixed host buffers with the op list built once: each
-        run() copies the buffers' current contents in and the outputs back."""
+        """gemv_chain on fixed host buffers, bound once (bramha_cuda_host_chain_*):
+        each run() copies the buffers' current contents in and the outputs back;
+        with pinned buffers the copies and launches replay as one CUDA graph."""
         return HostGemvChain(self, ops, batch)
 
     def stream_sync(self, stream=None):
@@ -391,20 +395,43 @@ class CudaComputePlane:
                                              scales.data_ptr(), _stream(stream)))
 
 
+def _check_host_buffers(ops):
+    for op in ops:
+        for a in (op[1],) + tuple(op[2]) + ((op[3],) if len(op) > 3 and op[3] is not None else ()):
+            if isinstance(a, np.ndarray) and (a.dtype != np.float32 or not a.flags.c_contiguous):
+                raise BramhaError(-1, "gemv_chain: host buffers must be contiguous float32")
+
+
 class HostGemvChain:
-    """A host-buffer GEMV chain (bramha_cuda_gemv_chain) whose op array is built
-    once; the buffers are held and must keep their addresses."""
+    """A host-buffer GEMV chain bound once (bramha_cuda_host_chain_*); the host
+    buffers are held here and keep their addresses while it exists."""
 
     def __init__(self, plane: "CudaComputePlane", ops, batch: int = 1):
-        for op in ops:
-            for a in (op[1],) + tuple(op[2]) + ((op[3],) if len(op) > 3 and op[3] is not None else ()):
-                if isinstance(a, np.ndarray) and (a.dtype != np.float32 or not a.flags.c_contiguous):
-                    raise BramhaError(-1, "gemv_chain: host buffers must be contiguous float32")
-        self.plane, self.batch, self._ops = plane, batch, ops
-        self._arr, self._keep = CudaComputePlane._chain_ops(ops)
+        _check_host_buffers(ops)
+        self.plane, self.batch, self._ops, self.handle = plane, batch, ops, None
+        arr, keep = CudaComputePlane._chain_ops(ops)
+        h = ctypes.c_void_p()
+        check(lib().bramha_cuda_host_chain_create(plane.ctx, len(ops), arr, batch, ctypes.byref(h)))
+        self.handle = h.value
 
     def run(self):
-        check(lib().bramha_cuda_gemv_chain(self.plane.ctx, len(self._ops), self._arr, self.batch))
+        check(lib().bramha_cuda_host_chain_run(self.plane.ctx, self.handle))
+
+    def uses_graph(self) -> bool:
+        g = ctypes.c_int()
+        check(lib().bramha_cuda_host_chain_uses_graph(self.plane.ctx, self.handle, ctypes.byref(g)))
+        return bool(g.value)
+
+    def close(self):
+        if self.handle is not None and self.plane.ctx:
+            lib().bramha_cuda_host_chain_destroy(self.plane.ctx, self.handle)
+        self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class GemvProgram:

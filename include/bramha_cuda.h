@@ -266,6 +266,28 @@ BRAMHA_API int bramha_cuda_gemv_chain_dev(bramha_ctx* ctx, int n_ops, const bram
  * behind the launches.  Pageable buffers work too (the driver stages them). */
 BRAMHA_API int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch);
 
+/* A host-buffer chain bound once and run many times (no counterpart in the
+ * reference, whose host calls each stand alone): the op list -- weights and
+ * the x, x_up and y host pointers -- is copied at creation, the chain gets its
+ * own device staging, and when every x, x_up and y is page-locked host memory
+ * the copies and launches of bramha_cuda_gemv_chain are recorded once into a
+ * CUDA graph that each run replays (otherwise each run enqueues them as
+ * bramha_cuda_gemv_chain does).  A run is synchronous, reads the host inputs'
+ * current contents and reports a device-side failure like
+ * bramha_cuda_gemv_chain.  The host buffers must stay allocated and, when
+ * recorded, page-locked while the chain exists; the weights must stay
+ * registered (each run checks).  The launch choices in force at creation (GEMV
+ * kernel, tuning keys) are kept.  Create a chain while no other thread enqueues
+ * work on the context's own stream (the recording captures that stream).
+ * Sharded weights are not supported. */
+typedef struct bramha_host_chain bramha_host_chain;
+BRAMHA_API int bramha_cuda_host_chain_create(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch,
+                                             bramha_host_chain** out);
+BRAMHA_API int bramha_cuda_host_chain_run(bramha_ctx* ctx, bramha_host_chain* chain);
+/* *out = 1 when the chain replays a recorded CUDA graph, 0 when it runs eagerly. */
+BRAMHA_API int bramha_cuda_host_chain_uses_graph(bramha_ctx* ctx, const bramha_host_chain* chain, int* out);
+BRAMHA_API int bramha_cuda_host_chain_destroy(bramha_ctx* ctx, bramha_host_chain* chain);
+
 /* The same chain as ONE persistent launch (no counterpart in the reference,
  * which runs one GEMV at a time).  One CTA per SM runs every op: the weight
  * stream and its decoding continue across op boundaries, and op i+1 reads its

@@ -156,9 +156,12 @@ def test_chain_errors(plane):
 def test_host_chain_many_blocks_equals_device_chain(plane, pinned):
     """A host-buffer chain of 8 layers (32 launches in nine copy blocks of 1, 2,
     4, 8, 2, 8, 4, 2 and 1 ops, each block's inputs copied in while earlier
-    blocks run and its outputs copied back while later ones run) equals the same chain on device
-    tensors bit for bit, on pageable numpy or pinned torch buffers, and a
-    prepared chain run twice picks up the inputs' new contents."""
+    blocks run and its outputs copied back while later ones run) equals the
+    same chain on device tensors bit for bit, on pageable numpy or pinned torch
+    buffers: through bramha_cuda_gemv_chain, and through a chain bound once
+    (bramha_cuda_host_chain_*, replayed from a CUDA graph when the buffers are
+    pinned) run twice, the second time on new contents of the same buffers."""
+    from bramha_b200 import BramhaError
     layers = [layer_ops(plane, "log4", 2, seed=400 + 31 * i) for i in range(8)]
     ops_d = [op for ops, _ in layers for op in ops]
 
@@ -168,28 +171,46 @@ def test_host_chain_many_blocks_equals_device_chain(plane, pinned):
             return a.pin_memory()
         return a.numpy().copy()
 
-    ops_h = [(ws, host(x), [host(torch.full_like(y, float("nan"))) for y in ys]) + tuple(host(u) for u in up)
-             for ws, x, ys, *up in ops_d]
+    def host_ops():
+        return [(ws, host(x), [host(torch.full_like(y, float("nan"))) for y in ys]) + tuple(host(u) for u in up)
+                for ws, x, ys, *up in ops_d]
+
+    def same(ops_h):
+        for (_, _, ysd, *_), (_, _, ysh, *_) in zip(ops_d, ops_h):
+            for yd, yh in zip(ysd, ysh):
+                assert torch.equal(yd.cpu(), yh if pinned else torch.from_numpy(yh))
+
+    plane.gemv_chain_dev(ops_d, 2)
+    plane.stream_sync()  # the chains share the context's K-split workspace: one at a time
+    once = host_ops()
+    plane.gemv_chain(once, batch=2)
+    same(once)
+    ops_h = host_ops()
     chain = plane.prepare_chain(ops_h, batch=2)
+    assert chain.uses_graph() == pinned
     for rep in range(2):
         if rep:  # new inputs in the same host buffers, and on the device side
             for (ws, xh, *_), (_, xd, *__) in zip(ops_h, ops_d):
                 fresh = torch.from_numpy(make_x(2, xd.shape[1], seed=900 + xd.shape[1]))
                 xd.copy_(fresh.cuda())
                 xh[...] = fresh if pinned else fresh.numpy()
-        plane.gemv_chain_dev(ops_d, 2)
-        plane.stream_sync()  # the two chains share the context's K-split workspace: one at a time
+            plane.gemv_chain_dev(ops_d, 2)
+            plane.stream_sync()
         chain.run()
-        for (_, _, ysd, *_), (_, _, ysh, *_) in zip(ops_d, ops_h):
-            for yd, yh in zip(ysd, ysh):
-                got = yh if pinned else torch.from_numpy(yh)
-                assert torch.equal(yd.cpu(), got)
-    # and against the oracle for one layer
+        same(ops_h)
+    # and against the oracle for one op (layer 0's gate|up)
     (ws, x, ys, *up), (xr, ur, wref) = ops_h[2], layers[0][1][2]
+    xn = x.numpy() if pinned else x
     for (q, s, n), y in zip(wref, ys):
-        yy = y.numpy() if pinned else y
-        assert normwise_err(yy, oracle_gemv("log4", np.asarray(x if not pinned else x.numpy()), q, s, n)) <= GEMV_TOL
+        assert normwise_err(y.numpy() if pinned else y, oracle_gemv("log4", np.asarray(xn), q, s, n)) <= GEMV_TOL
+    # a bound chain whose weight was evicted refuses to run
+    gone = ops_d[-1][0][0].key
+    plane.evict(gone)
+    with pytest.raises(BramhaError):
+        chain.run()
+    chain.close()
     for ops, _ in layers:
         for op in ops:
             for w in op[0]:
-                plane.evict(w.key)
+                if w.key != gone:
+                    plane.evict(w.key)
