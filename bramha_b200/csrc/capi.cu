@@ -1373,10 +1373,6 @@ int bramha_cuda_host_chain_create(bramha_ctx* ctx, int n_ops, const bramha_gemv_
     for (int i = 0; i < n_ops; ++i) {
         int rc = check_chain_op(ctx, ops[i], batch, false);
         if (rc) return rc;
-        for (int j = 0; j < ops[i].n_weights; ++j)
-            if (ops[i].weights[j]->shard)
-                return fail(BRAMHA_ERR_UNSUPPORTED, "host chain: sharded weights are not supported; "
-                                                    "use bramha_cuda_gemv_chain");
     }
     bramha_host_chain* c = new (std::nothrow) bramha_host_chain();
     if (!c) return fail(BRAMHA_ERR_OOM, "host allocation failed");
@@ -1395,6 +1391,10 @@ int bramha_cuda_host_chain_create(bramha_ctx* ctx, int n_ops, const bramha_gemv_
         for (int j = 0; j < op.n_weights; ++j) pinned = pinned && is_pinned(op.y[j]);
     }
     c->lay = chain_layout(n_ops, c->ops.data(), batch);
+    if (c->lay.any_shard) {  // staged in the shard arena by each run's bramha_cuda_gemv_chain
+        *out = c;
+        return BRAMHA_OK;
+    }
     DeviceGuard g(ctx->device);
     cudaError_t e = cudaMalloc(&c->dev_x, sizeof(float) * std::max<size_t>(c->lay.xe, 1));
     if (e == cudaSuccess) e = cudaMalloc(&c->dev_y, sizeof(float) * std::max<size_t>(c->lay.ye, 1));
@@ -1430,6 +1430,7 @@ int bramha_cuda_host_chain_uses_graph(bramha_ctx* ctx, const bramha_host_chain* 
 
 int bramha_cuda_host_chain_run(bramha_ctx* ctx, bramha_host_chain* c) {
     if (!ctx || !c) return fail(BRAMHA_ERR_INVALID, "null argument");
+    if (c->lay.any_shard) return bramha_cuda_gemv_chain(ctx, c->n_ops, c->ops.data(), c->batch);
     for (int i = 0; i < c->n_ops; ++i) {  // every weight still registered
         int rc = check_chain_op(ctx, c->ops[(size_t)i], c->batch, false);
         if (rc) return rc;

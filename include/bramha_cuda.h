@@ -279,7 +279,8 @@ BRAMHA_API int bramha_cuda_gemv_chain(bramha_ctx* ctx, int n_ops, const bramha_g
  * registered (each run checks).  The launch choices in force at creation (GEMV
  * kernel, tuning keys) are kept.  Create a chain while no other thread enqueues
  * work on the context's own stream (the recording captures that stream).
- * Sharded weights are not supported. */
+ * With sharded weights in the list each run is a bramha_cuda_gemv_chain call
+ * on the bound ops (staged in the shard arena, not recorded). */
 typedef struct bramha_host_chain bramha_host_chain;
 BRAMHA_API int bramha_cuda_host_chain_create(bramha_ctx* ctx, int n_ops, const bramha_gemv_op* ops, int64_t batch,
                                              bramha_host_chain** out);

@@ -134,6 +134,13 @@ def gpu_worker(rank, world, port, out_dir, case):
             # host buffers: every rank gets the full output
             yh = sp.gemv(w2, x1.cpu().numpy())
             np.save(os.path.join(out_dir, f"yh_{rank}.npy"), yh)
+            # a host chain bound once over a sharded weight: each run is a per-call chain
+            yb = np.full((2, 1001), np.nan, np.float32)
+            hc = plane.prepare_chain([([w2], x1.cpu().numpy(), [yb])], batch=2)
+            assert not hc.uses_graph()
+            hc.run()
+            hc.close()
+            np.save(os.path.join(out_dir, f"yb_{rank}.npy"), yb)
         elif case == "stop":
             q1, s1, x1 = weight("log4", 512, 1024, seed=21)
             w1 = sp.register("s1", "log4", 512, 1024, q1, s1)
@@ -188,6 +195,7 @@ def test_sharded_gemv_two_gpus(tmp_path):
         assert normwise_err(np.load(tmp_path / f"y3_{r}.npy"), oracle.matvec_mul_into("w4zp8", x3, q3, s3, 1)) <= GEMV_TOL
         rh = np.stack([oracle.matvec_mul_into("w8", xb, q2, s2, 1001) for xb in x1])
         assert normwise_err(np.load(tmp_path / f"yh_{r}.npy"), rh) <= GEMV_TOL
+        assert np.load(tmp_path / f"yb_{r}.npy").tobytes() == np.load(tmp_path / f"yh_{r}.npy").tobytes()
     # both ranks hold identical full outputs
     assert np.load(tmp_path / "lm0.npy").tobytes() == np.load(tmp_path / "lm1.npy").tobytes()
 
