@@ -74,6 +74,7 @@ struct bramha_ctx {
     int64_t pf_next = 8 << 20;           // GEMV chain: bytes of the next launch requested into L2
     int evict_first = 0;                 // GEMV weight copies marked first to be evicted from L2
     int split_cost = 240;                // GEMV K-split plan: cost of splitting, eighths of a block
+    int cc_depth = 4;                    // CUDA-core GEMV: CTAs per SM its K split aims for
     // GEMV programs: L2 lookahead per CTA, bytes (measured on the Qwen2-7B step:
     // 0 -> 1.48 ms, 128 KiB -> 1.52, 256 KiB -> 1.72; off by default)
     int64_t prog_lookahead = 0;
@@ -581,6 +582,8 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
         a.pf_ahead = (int)(ctx->pf_lookahead / (2 * 8192));
         a.evict_first = ctx->evict_first;
         a.split_cost = ctx->split_cost;
+    a.cc_depth = ctx->cc_depth;
+        a.cc_depth = ctx->cc_depth;
         a.pf_next_n = 0;
         a.pf_next_total = 0;
         if (b0 + kMaxGemvBatch >= batch) {  // the last chunk of this op hands over to the next op
@@ -956,6 +959,10 @@ int bramha_cuda_set_gemv_tuning(bramha_ctx* ctx, int what, int64_t value) {
         case BRAMHA_TUNE_NEXT_LAUNCH_BYTES: ctx->pf_next = value; break;
         case BRAMHA_TUNE_EVICT_FIRST: ctx->evict_first = value ? 1 : 0; break;
         case BRAMHA_TUNE_PROGRAM_LOOKAHEAD_BYTES: ctx->prog_lookahead = value; break;
+        case BRAMHA_TUNE_CC_SPLIT_DEPTH:
+            if (value < 1 || value > 64) return fail(BRAMHA_ERR_INVALID, "CUDA-core split depth out of range (1..64)");
+            ctx->cc_depth = (int)value;
+            break;
         case BRAMHA_TUNE_SPLIT_COST:
             if (value > 1 << 20) return fail(BRAMHA_ERR_INVALID, "split cost out of range");
             ctx->split_cost = (int)value;

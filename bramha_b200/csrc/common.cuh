@@ -164,6 +164,7 @@ struct GemvArgs {
     int64_t pf_next_total;
     int evict_first;       // weight copies marked first to be evicted from L2
     int split_cost;        // K-split plan: cost of a split launch, in eighths of a 64-column block
+    int cc_depth;          // CUDA-core GEMV: CTAs per SM its K split aims for (1 = no split unless tiles are few)
     ShardArgs shard;       // column-shard group (shard.world > 1), tensor-core GEMV only
 };
 

@@ -290,9 +290,9 @@ bool gemv_cc_eligible(int fmt, const GemvArgs& a) {
     return bytes <= kCcMaxBytes && a.split_ws && a.split_tickets && tiles <= a.split_tickets_n;
 }
 
-// Splits: enough CTAs to cover the SMs about four deep (CTAs are small), at
-// least one block per split and at most kCcMaxSplit; a workspace slot per
-// (tile, split, row).
+// Splits: enough CTAs to cover the SMs a.cc_depth deep (default 4; CTAs are
+// small), at least one block per split and at most kCcMaxSplit; a workspace
+// slot per (tile, split, row).
 cudaError_t launch_gemv_cc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t st) {
     CcParams p = {};
     int ntiles = 0;
@@ -308,7 +308,7 @@ cudaError_t launch_gemv_cc(int fmt, const GemvArgs& a, int num_sms, cudaStream_t
     p.K = a.K;
     p.ksteps = (int)k_steps(a.K);
     p.ntiles = ntiles;
-    const int64_t want = 4ll * num_sms;
+    const int64_t want = (int64_t)(a.cc_depth > 0 ? a.cc_depth : 4) * num_sms;
     int ks = (int)((want + ntiles - 1) / ntiles);
     if (ks > p.ksteps) ks = p.ksteps;
     if (ks > kCcMaxSplit) ks = kCcMaxSplit;

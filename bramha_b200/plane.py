@@ -331,11 +331,12 @@ class CudaComputePlane:
         check(lib().bramha_cuda_set_prefetch(self._ctx, int(lookahead_bytes), int(next_launch_bytes)))
 
     TUNING = {"lookahead_bytes": 1, "next_launch_bytes": 2, "evict_first": 3, "split_cost": 4,
-              "program_lookahead_bytes": 5}
+              "program_lookahead_bytes": 5, "cc_split_depth": 6}
 
     def set_gemv_tuning(self, **kw):
-        """Tensor-core GEMV tuning (results do not change): lookahead_bytes,
-        next_launch_bytes, evict_first (0/1), split_cost, program_lookahead_bytes."""
+        """GEMV tuning: lookahead_bytes, next_launch_bytes, evict_first (0/1),
+        split_cost, program_lookahead_bytes (tensor-core GEMV; results do not
+        change) and cc_split_depth (CUDA-core GEMV; fp32 grouping only)."""
         for k, v in kw.items():
             check(lib().bramha_cuda_set_gemv_tuning(self._ctx, self.TUNING[k], int(v)))
 

@@ -154,12 +154,16 @@ BRAMHA_API int bramha_cuda_set_prefetch(bramha_ctx* ctx, int64_t lookahead_bytes
  * launch's K range, in eighths of one 64-column weight block;
  * PROGRAM_LOOKAHEAD_BYTES (default 0 = off): how far ahead of its shared-memory
  * copies each CTA of a GEMV program requests its weight stream into L2, so the
- * stream continues while an op waits for the previous op's output. */
+ * stream continues while an op waits for the previous op's output.
+ * CC_SPLIT_DEPTH (default 4, 1..64): the CUDA-core GEMV (batch 1, K <= 1024)
+ * splits K until its CTAs cover the SMs this many deep; the split changes only
+ * the grouping of the fp32 sums (the partials are added in split order). */
 #define BRAMHA_TUNE_LOOKAHEAD_BYTES 1
 #define BRAMHA_TUNE_NEXT_LAUNCH_BYTES 2
 #define BRAMHA_TUNE_EVICT_FIRST 3
 #define BRAMHA_TUNE_SPLIT_COST 4
 #define BRAMHA_TUNE_PROGRAM_LOOKAHEAD_BYTES 5
+#define BRAMHA_TUNE_CC_SPLIT_DEPTH 6
 BRAMHA_API int bramha_cuda_set_gemv_tuning(bramha_ctx* ctx, int what, int64_t value);
 
 /* ---------------------------------------------------------------- weights */
