@@ -139,6 +139,8 @@ def test_rope_attention_fused_equals_two_kernels(plane):
     (outputs and the appended cache row), at a position with cached rows."""
     from bramha_b200 import lib
     from bramha_b200._lib import check
+    from bramha_b200.plane import _stream
+    st = _stream(None)  # torch's current stream: plane.stream_sync() waits for it
     nq, nkv, hd, ctx_len, pos = 14, 2, 64, 64, 37
     r = rng(12)
     dev = torch.device("cuda", 0)
@@ -150,16 +152,17 @@ def test_rope_attention_fused_equals_two_kernels(plane):
     L, c = lib(), plane.ctx
     # two kernels
     q1, kc1, vc1, o1 = q.clone(), kc0.clone(), vc0.clone(), torch.empty(nq * hd, device=dev)
+    kc2, vc2, o2 = kc0.clone(), vc0.clone(), torch.empty(nq * hd, device=dev)
+    torch.cuda.synchronize()  # the ops below run on the context's own stream
     check(L.bramha_cuda_op_qkv_rope(c, q1.data_ptr(), k.data_ptr(), v.data_ptr(), bq.data_ptr(), bk.data_ptr(),
                                     bv.data_ptr(), nq, nkv, hd, 1e6, p.data_ptr(), ctx_len, kc1.data_ptr(),
-                                    vc1.data_ptr(), None))
+                                    vc1.data_ptr(), st))
     check(L.bramha_cuda_op_attention(c, q1.data_ptr(), kc1.data_ptr(), vc1.data_ptr(), p.data_ptr(), nq, nkv, hd,
-                                     ctx_len, o1.data_ptr(), None))
+                                     ctx_len, o1.data_ptr(), st))
     # fused
-    kc2, vc2, o2 = kc0.clone(), vc0.clone(), torch.empty(nq * hd, device=dev)
     check(L.bramha_cuda_op_rope_attention(c, q.data_ptr(), k.data_ptr(), v.data_ptr(), bq.data_ptr(), bk.data_ptr(),
                                           bv.data_ptr(), nq, nkv, hd, 1e6, p.data_ptr(), ctx_len, kc2.data_ptr(),
-                                          vc2.data_ptr(), o2.data_ptr(), None))
+                                          vc2.data_ptr(), o2.data_ptr(), st))
     plane.stream_sync()
     assert torch.equal(o1, o2)
     assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
@@ -193,6 +196,8 @@ def test_attention_splits_vs_oracle(plane, nq, nkv, hd, max_ctx, pos):
     bit, the appended cache row included."""
     from bramha_b200 import lib
     from bramha_b200._lib import check
+    from bramha_b200.plane import _stream
+    st = _stream(None)  # torch's current stream: plane.stream_sync() waits for it
     r = rng(pos + hd)
     dev = torch.device("cuda", 0)
     mk = lambda *shape: torch.from_numpy(r.normal(0, 1, shape).astype(np.float32)).to(dev)
@@ -200,11 +205,12 @@ def test_attention_splits_vs_oracle(plane, nq, nkv, hd, max_ctx, pos):
     q = mk(nq * hd)
     kc, vc = mk(max_ctx, nkv * hd), mk(max_ctx, nkv * hd)
     p = torch.tensor([pos], dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()  # the ops below run on the context's own stream
     outs = []
     for _ in range(2):
         o = torch.empty(nq * hd, device=dev)
         check(L.bramha_cuda_op_attention(c, q.data_ptr(), kc.data_ptr(), vc.data_ptr(), p.data_ptr(), nq, nkv, hd,
-                                         max_ctx, o.data_ptr(), None))
+                                         max_ctx, o.data_ptr(), st))
         outs.append(o)
     plane.stream_sync()
     assert torch.equal(outs[0], outs[1])
@@ -216,15 +222,16 @@ def test_attention_splits_vs_oracle(plane, nq, nkv, hd, max_ctx, pos):
     k, v = mk(nkv * hd), mk(nkv * hd)
     bq, bk, bv = mk(nq * hd), mk(nkv * hd), mk(nkv * hd)
     q1, kc1, vc1, o1 = q.clone(), kc.clone(), vc.clone(), torch.empty(nq * hd, device=dev)
+    kc2, vc2, o2 = kc.clone(), vc.clone(), torch.empty(nq * hd, device=dev)
+    torch.cuda.synchronize()
     check(L.bramha_cuda_op_qkv_rope(c, q1.data_ptr(), k.data_ptr(), v.data_ptr(), bq.data_ptr(), bk.data_ptr(),
                                     bv.data_ptr(), nq, nkv, hd, 1e6, p.data_ptr(), max_ctx, kc1.data_ptr(),
-                                    vc1.data_ptr(), None))
+                                    vc1.data_ptr(), st))
     check(L.bramha_cuda_op_attention(c, q1.data_ptr(), kc1.data_ptr(), vc1.data_ptr(), p.data_ptr(), nq, nkv, hd,
-                                     max_ctx, o1.data_ptr(), None))
-    kc2, vc2, o2 = kc.clone(), vc.clone(), torch.empty(nq * hd, device=dev)
+                                     max_ctx, o1.data_ptr(), st))
     check(L.bramha_cuda_op_rope_attention(c, q.data_ptr(), k.data_ptr(), v.data_ptr(), bq.data_ptr(), bk.data_ptr(),
                                           bv.data_ptr(), nq, nkv, hd, 1e6, p.data_ptr(), max_ctx, kc2.data_ptr(),
-                                          vc2.data_ptr(), o2.data_ptr(), None))
+                                          vc2.data_ptr(), o2.data_ptr(), st))
     plane.stream_sync()
     assert torch.equal(o1, o2)
     assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
