@@ -582,7 +582,6 @@ int gemv_device(bramha_ctx* ctx, int n, const bramha_weight* const* ws, const fl
         a.pf_ahead = (int)(ctx->pf_lookahead / (2 * 8192));
         a.evict_first = ctx->evict_first;
         a.split_cost = ctx->split_cost;
-    a.cc_depth = ctx->cc_depth;
         a.cc_depth = ctx->cc_depth;
         a.pf_next_n = 0;
         a.pf_next_total = 0;
@@ -708,6 +707,7 @@ int gemv_device_sharded(bramha_ctx* ctx, int n, const bramha_weight* const* ws, 
     a.pf_ahead = (int)(ctx->pf_lookahead / (2 * 8192));
     a.evict_first = ctx->evict_first;
     a.split_cost = ctx->split_cost;
+    a.cc_depth = ctx->cc_depth;
     for (int i = 0; i < next_n && i < kMaxSegments; ++i) {
         const bramha_weight* nw = next_ws[i];
         if (!nw || !is_tiled(nw->fmt) || nw->N == 0 || nw->K == 0) continue;
