@@ -9,7 +9,8 @@ rank r holds experts [r E/W, (r+1) E/W) and, for its own T tokens:
 2. dispatches: the (token, choice) pairs with a positive weight, grouped by
    the rank owning the expert (token order inside each group), go out with
    one ``all_to_all_single`` of activations and one of local expert ids, after
-   an ``all_to_all_single`` of the pair counts;
+   an ``all_to_all_single`` of the pair counts (the sizes of the exchanges: the
+   layer's only host synchronisation);
 3. computes its experts on the rows it received (``experts_fn``);
 4. returns the expert outputs with the reverse ``all_to_all_single``;
 5. combines: out[t] = sum over j of y(t, j) * weight[t][j] in the sorted
@@ -54,14 +55,14 @@ class ExpertParallelMoE:
         dest = torch.where(valid, ids.long() // self.e_local, torch.full_like(ids, self.world, dtype=torch.long))
         flat_dest = dest.reshape(-1)
         order = torch.argsort(flat_dest, stable=True)           # grouped by rank, (t, j) order inside
-        n_send = int(valid.sum().item())
-        order = order[:n_send]
-        send_counts = torch.bincount(flat_dest[order], minlength=self.world).to(torch.int64)
+        # pairs per destination rank (index world: skipped pairs, sorted last)
+        send_counts = torch.bincount(flat_dest, minlength=self.world + 1)[:self.world].to(torch.int64)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        send_splits = send_counts.tolist()
-        recv_splits = recv_counts.tolist()
-        n_recv = sum(recv_splits)
+        counts = torch.cat([send_counts, recv_counts]).tolist()  # the layer's one host synchronisation
+        send_splits, recv_splits = counts[:self.world], counts[self.world:]
+        n_send, n_recv = sum(send_splits), sum(recv_splits)
+        order = order[:n_send]
         send_x = x.index_select(0, order // k).contiguous()
         send_e = (ids.reshape(-1).long()[order] - flat_dest[order] * self.e_local).to(torch.int32).contiguous()
         recv_x = torch.empty((n_recv, H), dtype=x.dtype, device=dev)
